@@ -1,0 +1,103 @@
+"""Seeded input generators shared by the golden-fixture script and the tests.
+
+Every tensor is drawn from an explicit ``torch.Generator`` in a fixed order,
+so the GPU box (same torch build) regenerates bit-identical parameters and
+inputs without the reference tree; the fixtures store checksums of what was
+generated so a drift in torch's CPU generator is caught instead of silently
+changing the case.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+# BASELINE config 0 (``pkm/memory.py:41-68`` argument names).
+CONFIG0 = dict(input_dim=512, output_dim=512, mem_k_dim=256, mem_v_dim=512, mem_heads=4,
+               mem_knn=32, mem_n_keys=128)
+# BASELINE config 2 geometry (bf16, query BatchNorm).
+CONFIG2 = dict(input_dim=1024, output_dim=1024, mem_k_dim=512, mem_v_dim=1024, mem_heads=4,
+               mem_knn=32, mem_n_keys=512, mem_query_batchnorm=True, mem_query_rmsnorm=False)
+
+
+def _u(g, shape, bound):
+    return (torch.rand(shape, generator=g, dtype=torch.float32) * 2 - 1) * bound
+
+
+def _n(g, shape, std):
+    return torch.randn(shape, generator=g, dtype=torch.float32) * std
+
+
+def pkm_state(cfg: dict, seed: int = 0) -> dict:
+    """Parameters of a ``HashingMemory`` built with ``cfg``.
+
+    Init follows ``HashingMemory.reset_parameters`` (``pkm/memory.py:169-188``)
+    for keys (U(+-1/sqrt(k_dim))), values (N(0, v_dim^-1/2)) and the SwiLU /
+    value projections (N(0, output_dim^-1/2)); the query Linear and all biases
+    keep nn.Linear's default U(+-1/sqrt(fan_in)), as BASELINE config 0 states.
+    """
+    g = torch.Generator().manual_seed(seed)
+    C = cfg["input_dim"]
+    O = cfg["output_dim"]
+    kd = cfg["mem_k_dim"]
+    H = cfg["mem_heads"]
+    n = cfg["mem_n_keys"]
+    v = cfg["mem_v_dim"] if cfg.get("mem_v_dim", -1) > 0 else O
+    st = {}
+    st["keys"] = _u(g, (2 * H * n, kd // 2), 1 / math.sqrt(kd))
+    st["values.weight"] = _n(g, (n * n, v), v ** -0.5)
+    st["value_proj.weight"] = _n(g, (O, v), O ** -0.5)
+    st["value_proj.bias"] = _u(g, (O,), 1 / math.sqrt(v))
+    st["swilu_projection.weight"] = _n(g, (v, C), O ** -0.5)
+    st["swilu_projection.bias"] = _u(g, (v,), 1 / math.sqrt(C))
+    st["query_proj.query_mlps.0.weight"] = _u(g, (H * kd, C), 1 / math.sqrt(C))
+    st["query_proj.query_mlps.0.bias"] = _u(g, (H * kd,), 1 / math.sqrt(C))
+    if cfg.get("mem_query_batchnorm", False):
+        st["query_proj.norm.weight"] = torch.ones(H * kd)
+        st["query_proj.norm.bias"] = torch.zeros(H * kd)
+        st["query_proj.norm.running_mean"] = torch.zeros(H * kd)
+        st["query_proj.norm.running_var"] = torch.ones(H * kd)
+        st["query_proj.norm.num_batches_tracked"] = torch.tensor(0, dtype=torch.int64)
+    elif cfg.get("mem_query_rmsnorm", True):
+        st["query_proj.norm.weight"] = torch.ones(H * kd)
+    return st
+
+
+def pkm_input(shape, seed: int = 0) -> torch.Tensor:
+    g = torch.Generator().manual_seed(10_000 + seed)
+    return torch.randn(shape, generator=g, dtype=torch.float32)
+
+
+def embbag_case(B: int, L: int, K: int, D: int, seed: int = 0, heads: int = 1,
+                w_std: float = 0.03):
+    """Embedding-bag inputs in the style of BASELINE config 1.
+
+    Indices uniform in [0, K) with replacement, per-bag weights the softmax of
+    N(0,1) logits normalised per head (``heads`` groups of L/heads), table
+    N(0, w_std), upstream gradient N(0,1).  All fp32; callers cast.
+    """
+    g = torch.Generator().manual_seed(20_000 + seed)
+    idx = torch.randint(0, K, (B, L), generator=g, dtype=torch.int64)
+    logits = torch.randn((B, heads, L // heads if heads > 1 else L), generator=g)
+    psw = torch.softmax(logits, dim=-1).reshape(B, L)
+    W = torch.randn((K, D), generator=g) * w_std
+    gout = torch.randn((B, D), generator=g)
+    return idx, psw, W, gout
+
+
+def fwpkm_case(seed: int = 0, B=2, T=16, heads=2, k_dim=16, v_dim=32, n_sub=16, topk=4):
+    """Tiny FwPKM inputs: q [B,T,H*k_dim], ref_v [B,T,v_dim], keys, values."""
+    g = torch.Generator().manual_seed(30_000 + seed)
+    keys = _u(g, (2 * heads * n_sub, k_dim // 2), 1 / math.sqrt(k_dim))
+    values = _n(g, (n_sub * n_sub, v_dim), v_dim ** -0.5)
+    q = torch.randn((B, T, heads * k_dim), generator=g)
+    ref_v = torch.randn((B, T, v_dim), generator=g)
+    return keys, values, q, ref_v
+
+
+def checksum(t: torch.Tensor) -> np.ndarray:
+    """(sum, sum|x|, sum x*i) in float64: a cheap fingerprint of a tensor."""
+    a = t.detach().double().reshape(-1)
+    w = torch.arange(a.numel(), dtype=torch.float64) / max(1, a.numel())
+    return np.array([a.sum().item(), a.abs().sum().item(), (a * w).sum().item()])

@@ -1,0 +1,235 @@
+"""Generate the golden fixtures in this folder from the reference itself.
+
+Run in a container that has the reference tree (read-only) at
+``$MODELOS_REF`` (default ``/root/reference``)::
+
+    python tests/golden/make_golden.py
+
+The reference's ``pkm/`` and ``fwpkm/`` packages are imported in place
+through a synthetic namespace package (no file is written into the reference
+tree) and run on CPU, which is their stock path: ``F.embedding_bag`` for the
+PKM bag (``pkm/xformer_embeddingbag.py:436-437``) and the torch gather plus
+``_embedding_bag_bw_native`` for FwPKM
+(``fwpkm/xformer_embeddingbag_legacy.py:177-178``).  Inputs come from
+``tests/cases.py`` so the GPU tests can regenerate them without the reference.
+"""
+from __future__ import annotations
+
+import importlib
+import os
+import sys
+import types
+
+sys.dont_write_bytecode = True
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(HERE))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+import cases  # noqa: E402
+
+REF = os.environ.get("MODELOS_REF", "/root/reference")
+
+
+def _import_ref():
+    pkg = types.ModuleType("refmodelos")
+    pkg.__path__ = [REF]
+    sys.modules["refmodelos"] = pkg
+    mem = importlib.import_module("refmodelos.pkm.memory")
+    xeb = importlib.import_module("refmodelos.pkm.xformer_embeddingbag")
+    fw = importlib.import_module("refmodelos.fwpkm.fwpkm")
+    gw = importlib.import_module("refmodelos.fwpkm.xformer_embeddingbag_grad_wrapper")
+    leg = importlib.import_module("refmodelos.fwpkm.xformer_embeddingbag_legacy")
+    return mem, xeb, fw, gw, leg
+
+
+def _np(t):
+    t = t.detach()
+    if t.dtype == torch.bfloat16:
+        t = t.float()
+    return t.cpu().numpy()
+
+
+def _rows_summary(prefix, t, out, nsample=64, seed=0):
+    """Row norms of a big gradient plus a few full rows, to keep fixtures small."""
+    t = t.detach().double()
+    out[prefix + "_rownorm"] = t.norm(dim=1).numpy()
+    g = np.random.default_rng(seed)
+    rows = np.sort(g.choice(t.shape[0], size=min(nsample, t.shape[0]), replace=False))
+    out[prefix + "_rows_idx"] = rows
+    out[prefix + "_rows"] = t[torch.from_numpy(rows)].numpy()
+
+
+def gen_pkm(mem, cfg, name, batch_shape, dtype, seed=0):
+    torch.manual_seed(0)
+    m = mem.HashingMemory(**cfg)
+    st = cases.pkm_state(cfg, seed)
+    m.load_state_dict(st)
+    m = m.to(dtype).train()
+    x = cases.pkm_input(batch_shape, seed).to(dtype).requires_grad_(True)
+    out = {}
+    out["param_checksums"] = np.stack([cases.checksum(st[k]) for k in sorted(st)])
+    out["x_checksum"] = cases.checksum(x)
+    # query and get_indices on their own (no grad)
+    with torch.no_grad():
+        q = m.query_proj(x.view(-1, cfg["input_dim"]))
+        s, i = m.get_indices(q, cfg["mem_knn"])
+    out["query"] = _np(q)
+    out["gi_scores"] = _np(s)
+    out["gi_indices"] = i.numpy()
+    y, idx = m(x)
+    loss = (y.float() ** 2).sum()
+    loss.backward()
+    out["out"] = _np(y)
+    out["indices"] = idx.numpy()
+    out["loss"] = np.array(loss.item())
+    out["x_grad"] = _np(x.grad)
+    out["keys_grad"] = _np(m.keys.grad)
+    _rows_summary("values_grad", m.values.weight.grad.float(), out)
+    _rows_summary("wq_grad", m.query_proj.query_mlps[0].weight.grad.float(), out)
+    out["bq_grad"] = _np(m.query_proj.query_mlps[0].bias.grad)
+    out["value_proj_w_grad_norm"] = np.array(m.value_proj.weight.grad.float().norm().item())
+    np.savez_compressed(os.path.join(HERE, name), **out)
+    print("wrote", name)
+
+
+def gen_indices_seeds(mem, name, seeds=(1, 2)):
+    cfg = cases.CONFIG0
+    out = {}
+    for sd in seeds:
+        torch.manual_seed(0)
+        m = mem.HashingMemory(**cfg)
+        m.load_state_dict(cases.pkm_state(cfg, sd))
+        g = torch.Generator().manual_seed(40_000 + sd)
+        q = torch.randn((256 * cfg["mem_heads"], cfg["mem_k_dim"]), generator=g)
+        with torch.no_grad():
+            s, i = m.get_indices(q, cfg["mem_knn"])
+        out[f"s{sd}_q_checksum"] = cases.checksum(q)
+        out[f"s{sd}_scores"] = _np(s)
+        out[f"s{sd}_indices"] = i.numpy()
+    np.savez_compressed(os.path.join(HERE, name), **out)
+    print("wrote", name)
+
+
+def gen_ties(mem, name):
+    """Quantised queries/keys so that many scores tie exactly."""
+    cfg = dict(cases.CONFIG0)
+    cfg.update(mem_n_keys=32, mem_knn=8, mem_k_dim=16)
+    torch.manual_seed(0)
+    m = mem.HashingMemory(**cfg)
+    g = torch.Generator().manual_seed(50_000)
+    keys = torch.randint(-1, 2, m.keys.shape, generator=g).float() * 0.25
+    q = torch.randint(-1, 2, (64 * cfg["mem_heads"], cfg["mem_k_dim"]), generator=g).float() * 0.5
+    with torch.no_grad():
+        m.keys.copy_(keys)
+        s, i = m.get_indices(q, cfg["mem_knn"])
+    np.savez_compressed(os.path.join(HERE, name), keys=keys.numpy(), q=q.numpy(),
+                        scores=_np(s), indices=i.numpy(), n_keys=32, knn=8, heads=cfg["mem_heads"])
+    print("wrote", name)
+
+
+EMB_CASES = {
+    # name: (B, L, K, D, dtype, heads, seed, hot)
+    "f32_small": (64, 16, 512, 64, torch.float32, 1, 1, False),
+    "f32_ragged": (37, 7, 100, 48, torch.float32, 1, 2, False),
+    "f32_hot": (50, 20, 64, 32, torch.float32, 1, 3, True),
+    "f32_L1": (5, 1, 8, 16, torch.float32, 1, 4, False),
+    "bf16_c1like": (96, 128, 4096, 128, torch.bfloat16, 4, 5, False),
+}
+
+
+def gen_embbag(xeb, gw, leg, name):
+    out = {}
+    for cname, (B, L, K, D, dt, heads, sd, hot) in EMB_CASES.items():
+        idx, psw, W, gout = cases.embbag_case(B, L, K, D, seed=sd, heads=heads)
+        if hot:  # few distinct rows, long segments
+            idx = idx % 5
+        W = W.to(dt)
+        psw = psw.to(dt)
+        gout = gout.to(dt)
+        # PKM module path: xformers_embedding_bag -> F.embedding_bag on CPU
+        Wp = W.clone().requires_grad_(True)
+        pp = psw.clone().requires_grad_(True)
+        y = xeb.xformers_embedding_bag(idx, Wp, pp, mode="sum")
+        y.backward(gout)
+        # FwPKM first-order kernel (CPU path) and the double-backward wrapper
+        dW_n, dp_n = leg.embedding_bag_bw_rev_indices(idx, W, psw, gout)
+        g2 = torch.Generator().manual_seed(60_000 + sd)
+        gbar = torch.randn((K, D), generator=g2).to(dt)
+        Wf = W.clone().requires_grad_(True)
+        pf = psw.clone().requires_grad_(True)
+        go = gout.clone().requires_grad_(True)
+        yf = gw.xformers_embedding_bag(idx, Wf, pf)
+        (dWf,) = torch.autograd.grad(yf, Wf, grad_outputs=go, create_graph=True)
+        dgo, dpf = torch.autograd.grad((dWf * gbar).sum(), (go, pf))
+        pre = f"{cname}__"
+        out[pre + "idx"] = idx.numpy()
+        out[pre + "psw"] = _np(psw)
+        out[pre + "W"] = _np(W)
+        out[pre + "g"] = _np(gout)
+        out[pre + "gbar"] = _np(gbar)
+        out[pre + "bf16"] = np.array(dt == torch.bfloat16)
+        out[pre + "out"] = _np(y)
+        out[pre + "dW"] = _np(Wp.grad)
+        out[pre + "dpsw"] = _np(pp.grad)
+        out[pre + "dW_native"] = _np(dW_n)
+        out[pre + "dpsw_native"] = _np(dp_n)
+        out[pre + "out_fw"] = _np(yf)
+        out[pre + "bw2_dg"] = _np(dgo)
+        out[pre + "bw2_da"] = _np(dpf)
+    np.savez_compressed(os.path.join(HERE, name), **out)
+    print("wrote", name)
+
+
+FW_KW = dict(mem_k_dim=16, mem_v_dim=32, mem_heads=2, mem_topk=4, mem_n_subkeys=16,
+             lookahead=1, learning_rate=0.1)
+
+
+def gen_fwpkm(fw, name, score_type, seed=0):
+    torch.manual_seed(0)
+    m = fw.FastWeightProductKeyMemory(qk_score_type=score_type, **FW_KW).train()
+    keys, values, q, ref_v = cases.fwpkm_case(seed)
+    with torch.no_grad():
+        m.keys.copy_(keys)
+        m.values.copy_(values)
+    q = q.clone().requires_grad_(True)
+    ref_v = ref_v.clone().requires_grad_(True)
+    res = m(q, ref_v, None, 8)
+    loss = (res["output"] ** 2).sum() + res["addr_loss"]
+    loss.backward()
+    out = {
+        "output": _np(res["output"]),
+        "indices": res["indices"].numpy(),
+        "scores": _np(res["scores"]),
+        "losses": _np(res["losses"]),
+        "addr_loss": np.array(res["addr_loss"].item()),
+        "grad_norms": np.array([g.item() for g in res["grad_norms"]]),
+        "final_keys": _np(m.keys),
+        "final_values": _np(m.values),
+        "q_grad": _np(q.grad),
+        "ref_v_grad": _np(ref_v.grad),
+        "keys_grad": _np(m.keys.grad),
+        "values_grad": _np(m.values.grad),
+        "loss": np.array(loss.item()),
+    }
+    np.savez_compressed(os.path.join(HERE, name), **out)
+    print("wrote", name)
+
+
+def main():
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    mem, xeb, fw, gw, leg = _import_ref()
+    gen_pkm(mem, cases.CONFIG0, "c0_pkm.npz", (2, 128, 512), torch.float32)
+    gen_indices_seeds(mem, "c0_indices_seeds.npz")
+    gen_ties(mem, "ties.npz")
+    gen_embbag(xeb, gw, leg, "embbag.npz")
+    gen_fwpkm(fw, "fwpkm_dot.npz", "dot_product")
+    gen_fwpkm(fw, "fwpkm_idw.npz", "idw")
+    c2 = dict(cases.CONFIG2)
+    c2.update(mem_n_keys=64)  # same layer, smaller table so the fixture stays small
+    gen_pkm(mem, c2, "c2_small_bf16.npz", (2, 32, 1024), torch.bfloat16)
+
+
+if __name__ == "__main__":
+    main()
