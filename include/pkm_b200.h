@@ -1,0 +1,161 @@
+/*
+ * pkm_b200.h - C ABI of the B200 (sm_100a) product-key-memory kernels.
+ *
+ * Every entry point takes raw device pointers, int64 sizes, dtype codes and
+ * a CUDA stream (as void*, i.e. a cudaStream_t), enqueues its kernels on that
+ * stream and returns a pkm_status code.  Nothing here allocates device
+ * memory: scratch space is passed in by the caller after a *_workspace query.
+ * All tensors are dense row-major (C-contiguous).  Shape, dtype and alignment
+ * errors are reported before any launch (the reference raises AssertionError
+ * for the same conditions, pkm/xformer_embeddingbag.py:226-233).
+ *
+ * Indices are int64 as in the reference (fwpkm/xformer_embeddingbag_grad_wrapper.py:94).
+ * An index outside [0, num_rows) is skipped (contributes nothing, its
+ * per-sample gradient is 0) and sets PKM_DEVERR_INDEX in *dev_err when
+ * dev_err is not NULL; the host reads that word when it wants to know.
+ *
+ * Slot numbering of the product keys follows pkm/memory.py:278-281:
+ * slot = i1 * n_keys + i2.  Query rows are token*heads + head; keys are
+ * [2*heads*n_keys, k_dim/2] viewed as (heads, 2, n_keys, k_dim/2)
+ * (pkm/memory.py:257).
+ */
+#ifndef PKM_B200_H
+#define PKM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PKM_API __attribute__((visibility("default")))
+#else
+#define PKM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types. */
+enum {
+  PKM_DT_F32 = 0,
+  PKM_DT_BF16 = 1,
+  PKM_DT_F16 = 2,
+};
+
+/* Return codes. */
+enum {
+  PKM_OK = 0,
+  PKM_ERR_INVALID_ARG = 1, /* shape / dtype / alignment / null pointer */
+  PKM_ERR_UNSUPPORTED = 2, /* a size outside what the kernels implement */
+  PKM_ERR_CUDA = 3,        /* the CUDA runtime reported an error at launch */
+  PKM_ERR_WORKSPACE = 4,   /* workspace smaller than the *_workspace query */
+};
+
+/* Bits OR-ed into the optional device error word. */
+#define PKM_DEVERR_INDEX 1u   /* an index outside [0, num_rows) was skipped */
+#define PKM_DEVERR_TIMEOUT 2u /* a bounded wait inside a kernel gave up */
+
+/* Library version (major*10000 + minor*100 + patch). */
+PKM_API int pkm_version(void);
+/* Static description of a status code. */
+PKM_API const char* pkm_status_string(int status);
+/* Detail message of the last failing call on this host thread. */
+PKM_API const char* pkm_last_error(void);
+
+/*
+ * K3 - weighted embedding-bag forward.
+ *   out[b, :] = sum_j psw[b, j] * weight[indices[b, j], :]   (fp32 accumulate)
+ * Replaces embedding_bag_k / embedding_bag_triton
+ * (pkm/xformer_embeddingbag.py:97-138, fwpkm/xformer_embeddingbag_legacy.py:33-74)
+ * and the fwpkm torch gather (fwpkm/xformer_embeddingbag_grad_wrapper.py:99-103).
+ * psw may be NULL (all weights 1).  weight rows must be 16-byte multiples and
+ * at most 4096 bytes; out_dtype may differ from weight_dtype.
+ */
+PKM_API int pkm_bag_fwd(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                int weight_dtype, int64_t n_bags, int64_t bag_size, int64_t num_rows, int64_t dim,
+                void* out, int out_dtype, uint32_t* dev_err, void* stream);
+
+/*
+ * K4 - first-order backward of the bag, atomic-free and deterministic.
+ *   grad_weight[k] = sum_{(b,j): idx=k} psw[b,j] * grad_out[b]  (dense; 0 for
+ *                    untouched rows; summed in ascending (b, j) order)
+ *   grad_psw[b,j]  = <weight[idx[b,j]], grad_out[b]>
+ *   row_counts[k]  = number of occurrences of k (optional; the bincount of
+ *                    fwpkm/fwpkm.py:343)
+ * Replaces embedding_bag_bw_rev_indices (pkm/xformer_embeddingbag.py:331-386,
+ * fwpkm/xformer_embeddingbag_legacy.py:170-227).  grad_psw and row_counts may
+ * be NULL; weight may be NULL when grad_psw is NULL.  grad_out must have the
+ * weight's dtype.  workspace must hold pkm_bag_bwd_workspace() bytes,
+ * 256-byte aligned.
+ */
+PKM_API int pkm_bag_bwd_workspace(int64_t n_bags, int64_t bag_size, int64_t num_rows, int64_t dim,
+                          size_t* bytes);
+PKM_API int pkm_bag_bwd(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                int64_t num_rows, int64_t dim, void* grad_weight, int grad_weight_dtype,
+                void* grad_psw, int grad_psw_dtype, int32_t* row_counts, void* workspace,
+                size_t workspace_bytes, uint32_t* dev_err, void* stream);
+
+/*
+ * K5 - double-backward of the bag's weight gradient.
+ *   d_grad_out[b] = sum_j a[b,j] * gbar[idx[b,j]]
+ *   d_a[b,j]      = <gbar[idx[b,j]], grad_out[b]>
+ * Replaces EmbeddingBagBW.backward
+ * (fwpkm/xformer_embeddingbag_grad_wrapper.py:43-74).  a may be NULL (ones;
+ * then d_a must be NULL).  grad_out must have gbar's dtype.
+ */
+PKM_API int pkm_bag_bwd2(const int64_t* indices, const void* a, int a_dtype, const void* gbar,
+                 int gbar_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                 int64_t num_rows, int64_t dim, void* d_grad_out, int d_grad_out_dtype, void* d_a,
+                 int d_a_dtype, uint32_t* dev_err, void* stream);
+
+/*
+ * K1 - sub-key scores for both halves of every (token, head) query.
+ *   scores[r, p, m] = score(query[r, p*half:(p+1)*half], keys[(h*2+p)*n + m])
+ * with r = token*heads + h.  mode 0: dot product (pkm/memory.py:267-268,
+ * fwpkm/fwpkm.py:861); mode 1: idw, -log(1e-3 + |q-k|^2) (fwpkm/fwpkm.py:862-866).
+ * fp32 inputs use a sequential fp32 sum without fused multiply-add (the
+ * oracle's definition); bf16 inputs accumulate in fp32 and round to bf16.
+ * query and keys must share a dtype; scores has that dtype.
+ */
+PKM_API int pkm_subkey_scores(const void* query, const void* keys, int dtype, int64_t n_tokens,
+                      int64_t heads, int64_t k_dim, int64_t n_keys, int mode, void* scores,
+                      void* stream);
+
+/*
+ * K2 - product top-k over precomputed sub-key scores [rows, 2, n_keys].
+ * Stage 1 keeps the knn best sub-keys of each half, stage 2 the knn best of
+ * the knn*knn sums (pkm/memory.py:270-285, fwpkm/fwpkm.py:908-923).  Order:
+ * score descending, ties to the lowest index (sub-key index, then slot).
+ * Outputs (rows x knn): indices (slot, int64), top_scores (score dtype),
+ * optional psw = per-row softmax of top_scores computed in fp32 and stored
+ * in the score dtype (pkm/memory.py:218), and optional stage-1 lists
+ * sub_indices1/2 (int64, sorted like the stage-1 top-k).
+ * knn <= 32, knn <= n_keys <= 1024.
+ */
+PKM_API int pkm_product_topk(const void* scores, int dtype, int64_t rows, int64_t n_keys, int64_t knn,
+                     int64_t* indices, void* top_scores, void* psw, int64_t* sub_indices1,
+                     int64_t* sub_indices2, void* stream);
+
+/*
+ * Backward of the per-row softmax plus the sub-key bags used by the scoring
+ * backward.  For each row r (= token*heads + h) of the product top-k:
+ *   ds[r, j] = psw[r,j] * (dpsw[r,j] - sum_i psw[r,i] * dpsw[r,i])  (fp32)
+ * and, for both halves p, the sub-key bag
+ *   sub_idx[2r+p, j] = (h*2+p)*n_keys + (p ? slot % n_keys : slot / n_keys)
+ *   sub_w[2r+p, j]   = ds[r, j]
+ * so that d_query = bag_fwd(sub_idx, sub_w, keys) and d_keys =
+ * bag_bwd(sub_idx, sub_w, grad_out = query) give the gradients of the
+ * cartesian scores (pkm/memory.py:274-285).  group = knn for the PKM
+ * per-head softmax.  Set psw NULL to pass dpsw through as ds (scores that
+ * were not soft-maxed).
+ */
+PKM_API int pkm_score_bwd_prep(const int64_t* indices, const void* psw, const void* dpsw, int dtype,
+                       int64_t rows, int64_t knn, int64_t heads, int64_t n_keys, int64_t* sub_idx,
+                       void* sub_w, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* PKM_B200_H */

@@ -1,0 +1,327 @@
+"""ctypes binding of ``libpkm_b200.so`` and thin tensor-level wrappers.
+
+Every wrapper checks shapes, dtypes and devices the way the reference's
+launchers assert them (``pkm/xformer_embeddingbag.py:226-233``), allocates the
+outputs and any scratch space with torch's caching allocator, and enqueues
+the kernels on the current CUDA stream.  There is no CPU path: the library
+must be built (``python -m modelos_b200.csrc.build``) and tensors must live
+on a CUDA device, otherwise these functions raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional
+
+import torch
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libpkm_b200.so")
+_lib = None
+_lock = threading.Lock()
+
+DT = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+
+_SIGS = {
+    "pkm_version": ([], _I),
+    "pkm_status_string": ([_I], ctypes.c_char_p),
+    "pkm_last_error": ([], ctypes.c_char_p),
+    "pkm_bag_fwd": ([_P, _P, _I, _P, _I, _I64, _I64, _I64, _I64, _P, _I, _P, _P], _I),
+    "pkm_bag_bwd_workspace": ([_I64, _I64, _I64, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
+    "pkm_bag_bwd": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _I, _P, _P,
+                     ctypes.c_size_t, _P, _P], _I),
+    "pkm_bag_bwd2": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _I, _P, _P], _I),
+    "pkm_subkey_scores": ([_P, _P, _I, _I64, _I64, _I64, _I64, _I, _P, _P], _I),
+    "pkm_product_topk": ([_P, _I, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P], _I),
+    "pkm_score_bwd_prep": ([_P, _P, _P, _I, _I64, _I64, _I64, _I64, _P, _P, _P], _I),
+}
+
+EXPORTED = tuple(_SIGS)
+
+
+def library_path() -> str:
+    return _LIB_PATH
+
+
+def lib():
+    """Load the shared library once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(_LIB_PATH):
+                raise RuntimeError(
+                    f"modelos_b200 native library missing at {_LIB_PATH}; "
+                    "build it with `python -m modelos_b200.csrc.build`")
+            L = ctypes.CDLL(_LIB_PATH)
+            for name, (args, res) in _SIGS.items():
+                fn = getattr(L, name)
+                fn.argtypes = args
+                fn.restype = res
+            _lib = L
+    return _lib
+
+
+def _check(rc: int, name: str):
+    if rc != 0:
+        L = lib()
+        detail = L.pkm_last_error().decode(errors="replace")
+        status = L.pkm_status_string(rc).decode()
+        raise RuntimeError(f"{name} failed ({status}): {detail}")
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(dev: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("modelos_b200 kernels need CUDA tensors (there is no CPU path)")
+
+
+# ---------------------------------------------------------------------------
+# optional CUDA-event probe around selected entry points (used by bench.py to
+# time the dominant kernels on their own stream inside the timed region)
+# ---------------------------------------------------------------------------
+class EventProbe:
+    def __init__(self, names, min_rows: int = 0):
+        self.names = set(names)
+        self.min_rows = min_rows
+        self.events: dict = {n: [] for n in names}
+
+    def start(self, name: str, rows: int):
+        if name not in self.names or rows < self.min_rows:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return ev
+
+    def stop(self, name: str, ev0):
+        if ev0 is None:
+            return
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev1.record()
+        self.events[name].append((ev0, ev1))
+
+    def mean_ms(self, name: str) -> float:
+        ev = self.events.get(name, [])
+        if not ev:
+            return float("nan")
+        return sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+
+    def count(self, name: str) -> int:
+        return len(self.events.get(name, []))
+
+
+_probe: Optional[EventProbe] = None
+
+
+def set_probe(probe: Optional[EventProbe]):
+    global _probe
+    _probe = probe
+
+
+def _pstart(name, rows):
+    return _probe.start(name, rows) if _probe is not None else None
+
+
+def _pstop(name, ev):
+    if ev is not None:
+        _probe.stop(name, ev)
+
+
+# ---------------------------------------------------------------------------
+# device error word
+# ---------------------------------------------------------------------------
+_err_words: dict = {}
+
+
+def err_word(dev: torch.device) -> torch.Tensor:
+    """Per-device uint32 word the kernels OR error bits into."""
+    key = (dev.type, dev.index if dev.index is not None else torch.cuda.current_device())
+    w = _err_words.get(key)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=dev)
+        _err_words[key] = w
+    return w
+
+
+DEVERR_INDEX = 1
+DEVERR_TIMEOUT = 2
+
+
+def read_device_errors(dev: Optional[torch.device] = None, reset: bool = True) -> int:
+    """Synchronising read of the error word (bit 1: an index was out of range,
+    bit 2: a bounded wait timed out)."""
+    dev = dev or torch.device("cuda", torch.cuda.current_device())
+    w = err_word(dev)
+    v = int(w.item())
+    if reset:
+        w.zero_()
+    return v
+
+
+def check_device_errors(dev: Optional[torch.device] = None):
+    v = read_device_errors(dev)
+    if v & DEVERR_INDEX:
+        raise IndexError("modelos_b200: an embedding index was outside [0, num_rows)")
+    if v & DEVERR_TIMEOUT:
+        raise RuntimeError("modelos_b200: a bounded wait inside a kernel timed out")
+
+
+# ---------------------------------------------------------------------------
+# embedding bag
+# ---------------------------------------------------------------------------
+def _bag_checks(indices, weight, psw):
+    assert indices.dim() == 2 and indices.dtype == torch.long, "indices must be [B, bag] int64"
+    assert weight.dim() == 2, "weight must be [K, dim]"
+    assert indices.is_contiguous() and weight.is_contiguous()
+    if psw is not None:
+        assert psw.shape == indices.shape, "per_sample_weights must match indices"
+        assert psw.is_contiguous()
+    _need_cuda(indices, weight, psw)
+
+
+def bag_fwd(indices: torch.Tensor, weight: torch.Tensor, psw: Optional[torch.Tensor],
+            out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """K3: ``out[b] = sum_j psw[b,j] * weight[indices[b,j]]``."""
+    _bag_checks(indices, weight, psw)
+    B, L = indices.shape
+    K, D = weight.shape
+    out_dtype = out_dtype or weight.dtype
+    out = torch.empty((B, D), dtype=out_dtype, device=weight.device)
+    ev = _pstart("pkm_bag_fwd", K)
+    rc = lib().pkm_bag_fwd(_ptr(indices), _ptr(psw), DT[psw.dtype] if psw is not None else 0,
+                           _ptr(weight), DT[weight.dtype], B, L, K, D, _ptr(out), DT[out_dtype],
+                           _ptr(err_word(weight.device)), _stream(weight.device))
+    _pstop("pkm_bag_fwd", ev)
+    _check(rc, "pkm_bag_fwd")
+    return out
+
+
+def bag_bwd_workspace(B: int, L: int, K: int, D: int) -> int:
+    n = ctypes.c_size_t(0)
+    _check(lib().pkm_bag_bwd_workspace(B, L, K, D, ctypes.byref(n)), "pkm_bag_bwd_workspace")
+    return int(n.value)
+
+
+def bag_bwd(indices: torch.Tensor, weight: Optional[torch.Tensor], psw: Optional[torch.Tensor],
+            grad_out: torch.Tensor, *, num_rows: Optional[int] = None, need_dpsw: bool = True,
+            want_counts: bool = False, grad_weight_dtype: Optional[torch.dtype] = None):
+    """K4: dense weight gradient, per-sample-weight gradient, row counts."""
+    assert indices.dim() == 2 and indices.dtype == torch.long and indices.is_contiguous()
+    assert grad_out.dim() == 2 and grad_out.shape[0] == indices.shape[0] and grad_out.is_contiguous()
+    _need_cuda(indices, grad_out, weight, psw)
+    B, L = indices.shape
+    D = grad_out.shape[1]
+    if weight is not None:
+        assert weight.dim() == 2 and weight.is_contiguous() and weight.shape[1] == D
+        K = weight.shape[0]
+        row_dtype = weight.dtype
+    else:
+        assert num_rows is not None and not need_dpsw
+        K = num_rows
+        row_dtype = grad_out.dtype
+    assert grad_out.dtype == row_dtype, "grad_out must have the table's dtype"
+    if psw is not None:
+        assert psw.shape == indices.shape and psw.is_contiguous()
+    dev = grad_out.device
+    gw_dtype = grad_weight_dtype or row_dtype
+    grad_weight = torch.empty((K, D), dtype=gw_dtype, device=dev)
+    grad_psw = torch.empty_like(psw) if (need_dpsw and psw is not None) else None
+    counts = torch.empty((K,), dtype=torch.int32, device=dev) if want_counts else None
+    ws_bytes = bag_bwd_workspace(B, L, K, D)
+    ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+    ev = _pstart("pkm_bag_bwd", K)
+    rc = lib().pkm_bag_bwd(_ptr(indices), _ptr(psw), DT[psw.dtype] if psw is not None else 0,
+                           _ptr(weight), DT[row_dtype], _ptr(grad_out), B, L, K, D,
+                           _ptr(grad_weight), DT[gw_dtype], _ptr(grad_psw),
+                           DT[grad_psw.dtype] if grad_psw is not None else 0, _ptr(counts), _ptr(ws),
+                           ws_bytes, _ptr(err_word(dev)), _stream(dev))
+    _pstop("pkm_bag_bwd", ev)
+    _check(rc, "pkm_bag_bwd")
+    return grad_weight, grad_psw, counts
+
+
+def bag_bwd2(indices: torch.Tensor, a: Optional[torch.Tensor], gbar: torch.Tensor,
+             grad_out: torch.Tensor, *, d_grad_out_dtype: Optional[torch.dtype] = None,
+             d_a_dtype: Optional[torch.dtype] = None):
+    """K5: ``dG[b] = sum_j a[b,j] gbar[idx]``, ``da[b,j] = <gbar[idx], g[b]>``."""
+    _bag_checks(indices, gbar, a)
+    assert grad_out.shape == (indices.shape[0], gbar.shape[1]) and grad_out.is_contiguous()
+    _need_cuda(grad_out)
+    B, L = indices.shape
+    K, D = gbar.shape
+    g = grad_out if grad_out.dtype == gbar.dtype else grad_out.to(gbar.dtype)
+    dgo = torch.empty((B, D), dtype=d_grad_out_dtype or grad_out.dtype, device=gbar.device)
+    da = None
+    if a is not None:
+        da = torch.empty((B, L), dtype=d_a_dtype or a.dtype, device=gbar.device)
+    rc = lib().pkm_bag_bwd2(_ptr(indices), _ptr(a), DT[a.dtype] if a is not None else 0,
+                            _ptr(gbar), DT[gbar.dtype], _ptr(g), B, L, K, D, _ptr(dgo),
+                            DT[dgo.dtype], _ptr(da), DT[da.dtype] if da is not None else 0,
+                            _ptr(err_word(gbar.device)), _stream(gbar.device))
+    _check(rc, "pkm_bag_bwd2")
+    return dgo, da
+
+
+# ---------------------------------------------------------------------------
+# scoring and top-k
+# ---------------------------------------------------------------------------
+def subkey_scores(query: torch.Tensor, keys: torch.Tensor, heads: int, mode: str = "dot") -> torch.Tensor:
+    """K1: ``[N*H, k_dim]`` queries x ``[2*H*n, k_dim/2]`` keys -> ``[N*H, 2, n]``."""
+    assert query.dim() == 2 and keys.dim() == 2 and query.is_contiguous() and keys.is_contiguous()
+    assert query.dtype == keys.dtype, "query and keys must share a dtype"
+    _need_cuda(query, keys)
+    NH, kd = query.shape
+    assert NH % heads == 0 and keys.shape[1] * 2 == kd and keys.shape[0] % (2 * heads) == 0
+    n = keys.shape[0] // (2 * heads)
+    out = torch.empty((NH, 2, n), dtype=query.dtype, device=query.device)
+    rc = lib().pkm_subkey_scores(_ptr(query), _ptr(keys), DT[query.dtype], NH // heads, heads, kd, n,
+                                 {"dot": 0, "idw": 1}[mode], _ptr(out), _stream(query.device))
+    _check(rc, "pkm_subkey_scores")
+    return out
+
+
+def product_topk(scores: torch.Tensor, knn: int, want_psw: bool = False, want_sub: bool = False):
+    """K2 on ``[R, 2, n]`` scores -> (indices, top_scores, psw|None, sub1|None, sub2|None)."""
+    assert scores.dim() == 3 and scores.shape[1] == 2 and scores.is_contiguous()
+    _need_cuda(scores)
+    R, _, n = scores.shape
+    dev = scores.device
+    idx = torch.empty((R, knn), dtype=torch.long, device=dev)
+    ts = torch.empty((R, knn), dtype=scores.dtype, device=dev)
+    psw = torch.empty_like(ts) if want_psw else None
+    s1 = torch.empty((R, knn), dtype=torch.long, device=dev) if want_sub else None
+    s2 = torch.empty((R, knn), dtype=torch.long, device=dev) if want_sub else None
+    rc = lib().pkm_product_topk(_ptr(scores), DT[scores.dtype], R, n, knn, _ptr(idx), _ptr(ts),
+                                _ptr(psw), _ptr(s1), _ptr(s2), _stream(dev))
+    _check(rc, "pkm_product_topk")
+    return idx, ts, psw, s1, s2
+
+
+def score_bwd_prep(indices: torch.Tensor, psw: Optional[torch.Tensor], dpsw: torch.Tensor,
+                   heads: int, n_keys: int):
+    """Softmax backward + sub-key bags: returns (sub_idx [2R, knn], sub_w [2R, knn])."""
+    assert indices.dim() == 2 and dpsw.shape == indices.shape
+    _need_cuda(indices, psw, dpsw)
+    R, knn = indices.shape
+    dpsw = dpsw.contiguous()
+    if psw is not None:
+        psw = psw.contiguous().to(dpsw.dtype)
+    sub_idx = torch.empty((2 * R, knn), dtype=torch.long, device=dpsw.device)
+    sub_w = torch.empty((2 * R, knn), dtype=dpsw.dtype, device=dpsw.device)
+    rc = lib().pkm_score_bwd_prep(_ptr(indices), _ptr(psw), _ptr(dpsw), DT[dpsw.dtype], R, knn, heads,
+                                  n_keys, _ptr(sub_idx), _ptr(sub_w), _stream(dpsw.device))
+    _check(rc, "pkm_score_bwd_prep")
+    return sub_idx, sub_w

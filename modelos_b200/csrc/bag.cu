@@ -1,0 +1,400 @@
+// Embedding-bag kernels: forward gather-sum (K3), sorted-segment backward
+// (K4) and the double-backward of the weight gradient (K5), with their C ABI
+// entry points.
+#include <algorithm>
+#include <string>
+
+#include "gather.cuh"
+#include "sort.cuh"
+
+namespace pkm {
+
+// ---------------------------------------------------------------------------
+// gather launch
+// ---------------------------------------------------------------------------
+static int max_dyn_smem() {
+  int dev = 0, v = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  return v;
+}
+
+// Ring depth and per-warp shared-memory stride for rows of rb bytes.
+static bool gather_geometry(int64_t rb, int* slots, int64_t* warp_smem) {
+  const int64_t budget = (int64_t)(max_dyn_smem() - 1024) / kGatherWarps;
+  for (int p = 32; p >= 1; --p) {
+    int64_t ring = ((int64_t)p * rb + 127) & ~(int64_t)127;
+    int64_t tot = ring + kMetaRing * 12 + (int64_t)p * 8;
+    tot = (tot + 127) & ~(int64_t)127;
+    if (tot <= budget) {
+      *slots = p;
+      *warp_smem = tot;
+      return true;
+    }
+  }
+  return false;
+}
+
+template <typename RowT, int VPL, int MODE, bool DOT>
+static int launch_one(GatherArgs a, int64_t items_upper, cudaStream_t st) {
+  int slots;
+  int64_t ws;
+  if (!gather_geometry(a.row_bytes, &slots, &ws)) return fail(PKM_ERR_UNSUPPORTED, "row too large for the gather ring");
+  a.slots = slots;
+  a.warp_smem = ws;
+  const int smem = (int)(ws * kGatherWarps);
+  auto kern = gather_kernel<RowT, VPL, MODE, DOT>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return check_cuda("cudaFuncSetAttribute(gather)");
+  int64_t blocks = (items_upper + kGatherWarps - 1) / kGatherWarps;
+  blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, num_sms()));
+  kern<<<(unsigned)blocks, kGatherWarps * 32, smem, st>>>(a);
+  return check_cuda("gather_kernel");
+}
+
+template <typename RowT, int MODE, bool DOT>
+static int launch_vpl(GatherArgs a, int64_t items_upper, cudaStream_t st) {
+  const int64_t v = (a.row_bytes + 511) / 512;
+  if (v <= 1) return launch_one<RowT, 1, MODE, DOT>(a, items_upper, st);
+  if (v <= 2) return launch_one<RowT, 2, MODE, DOT>(a, items_upper, st);
+  if (v <= 4) return launch_one<RowT, 4, MODE, DOT>(a, items_upper, st);
+  if (v <= 8) return launch_one<RowT, 8, MODE, DOT>(a, items_upper, st);
+  return fail(PKM_ERR_UNSUPPORTED, "rows above 4096 bytes are not supported");
+}
+
+template <typename RowT>
+static int launch_mode(bool seg, bool dot, GatherArgs a, int64_t items_upper, cudaStream_t st) {
+  if (!seg) {
+    return dot ? launch_vpl<RowT, G_BAG, true>(a, items_upper, st)
+               : launch_vpl<RowT, G_BAG, false>(a, items_upper, st);
+  }
+  return dot ? launch_vpl<RowT, G_SEG, true>(a, items_upper, st)
+             : launch_vpl<RowT, G_SEG, false>(a, items_upper, st);
+}
+
+int gather_launch(int row_dtype, bool seg, bool dot, GatherArgs a, int64_t items_upper, cudaStream_t st) {
+  if (row_dtype == PKM_DT_F32) return launch_mode<float>(seg, dot, a, items_upper, st);
+  if (row_dtype == PKM_DT_BF16) return launch_mode<__nv_bfloat16>(seg, dot, a, items_upper, st);
+  return launch_mode<__half>(seg, dot, a, items_upper, st);
+}
+
+// ---------------------------------------------------------------------------
+// K4 helper kernels
+// ---------------------------------------------------------------------------
+// Row key of every occurrence (invalid indices map to the sentinel row K)
+// and the per-row occurrence counts.
+__global__ void bwd_keys_kernel(const int64_t* __restrict__ idx, int64_t M, int64_t K,
+                                uint32_t* __restrict__ keys, int32_t* __restrict__ counts, uint32_t* err) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < M; o += stride) {
+    const int64_t k = idx[o];
+    uint32_t key;
+    if (k < 0 || k >= K) {
+      key = (uint32_t)K;
+      raise_err(err, PKM_DEVERR_INDEX);
+    } else {
+      key = (uint32_t)k;
+    }
+    keys[o] = key;
+    atomicAdd(&counts[key], 1);
+  }
+}
+
+// One descriptor per chunk of at most `chunk` occurrences of a row (one for an
+// empty row, so that its zero gradient row is written too).
+__global__ void items_fill_kernel(const int32_t* __restrict__ counts, const I4* __restrict__ offs, int64_t K,
+                                  int chunk, int4* __restrict__ desc, int32_t* n_items,
+                                  int32_t* __restrict__ row_counts) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < K; k += stride) {
+    const int c = counts[k];
+    const I4 o = offs[k];
+    const int items = offs[k + 1].y - o.y;
+    for (int j = 0; j < items; ++j) {
+      const int b = o.x + j * chunk;
+      const int e = min(o.x + c, b + chunk);
+      desc[o.y + j] = make_int4((int)k, b, e, items > 1 ? o.z + j : -1);
+    }
+    if (row_counts) row_counts[k] = c;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *n_items = offs[K].y;
+}
+
+// Rows split over several chunks: sum the chunk partials in chunk order.
+__global__ void reduce_partials_kernel(const I4* __restrict__ offs, int64_t K, const float* __restrict__ partials,
+                                       int64_t D, void* out, int out_dtype) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t k = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); k < K; k += warps) {
+    const I4 o = offs[k];
+    const int items = offs[k + 1].y - o.y;
+    if (items <= 1) continue;
+    const float* base = partials + (int64_t)o.z * D;
+    for (int64_t e = lane; e < D; e += 32) {
+      float s = 0.f;
+      for (int j = 0; j < items; ++j) s += base[(int64_t)j * D + e];
+      st_f(out, out_dtype, k * D + e, s);
+    }
+  }
+}
+
+constexpr int kChunk = 256;
+
+struct BwdLayout {
+  size_t counts, offs, keys_a, keys_b, vals_a, vals_b, w_sorted, hist, sums_i, sums_4, desc, n_items,
+      partials, total;
+};
+
+static size_t up256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static BwdLayout bwd_layout(int64_t M, int64_t K, int64_t D) {
+  BwdLayout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = off;
+    off += up256(bytes);
+    return at;
+  };
+  const int64_t tiles = sort_tiles(M);
+  const int64_t nh = (int64_t)kRadix * tiles;
+  const int64_t max_items = K + (M + kChunk - 1) / kChunk + 1;
+  const int64_t max_partial = 2 * ((M + kChunk - 1) / kChunk) + 2;
+  L.counts = take(sizeof(int32_t) * (K + 1));
+  L.offs = take(sizeof(I4) * (K + 2));
+  L.keys_a = take(sizeof(uint32_t) * M);
+  L.keys_b = take(sizeof(uint32_t) * M);
+  L.vals_a = take(sizeof(int32_t) * M);
+  L.vals_b = take(sizeof(int32_t) * M);
+  L.w_sorted = take(sizeof(float) * M);
+  L.hist = take(sizeof(int) * (nh + 1));
+  L.sums_i = take(sizeof(int) * (scan_blocks(nh) + 1));
+  L.sums_4 = take(sizeof(I4) * (scan_blocks(K + 1) + 1));
+  L.desc = take(sizeof(int4) * max_items);
+  L.n_items = take(sizeof(int32_t));
+  L.partials = take(sizeof(float) * max_partial * D);
+  L.total = off;
+  return L;
+}
+
+static int bits_for(int64_t v) {
+  int b = 0;
+  while (b < 63 && (int64_t(1) << b) <= v) ++b;
+  return std::max(b, 1);
+}
+
+}  // namespace pkm
+
+using namespace pkm;
+
+// ---------------------------------------------------------------------------
+// argument checks shared by the entry points
+// ---------------------------------------------------------------------------
+static int check_bag_common(const int64_t* indices, int64_t n_bags, int64_t bag_size, int64_t num_rows,
+                            int64_t dim, int row_dtype) {
+  if (n_bags < 0 || bag_size < 0 || num_rows < 0 || dim <= 0)
+    return fail(PKM_ERR_INVALID_ARG, "negative size or dim <= 0");
+  if (!valid_dtype(row_dtype)) return fail(PKM_ERR_INVALID_ARG, "bad table dtype");
+  if (n_bags * bag_size > 0 && indices == nullptr) return fail(PKM_ERR_INVALID_ARG, "indices is NULL");
+  if (n_bags * bag_size >= (int64_t(1) << 31))
+    return fail(PKM_ERR_UNSUPPORTED, "n_bags * bag_size must stay below 2^31");
+  if (num_rows >= (int64_t(1) << 31) - 1) return fail(PKM_ERR_UNSUPPORTED, "num_rows must stay below 2^31-1");
+  const int64_t rb = dim * dtype_size(row_dtype);
+  if (rb % 16 != 0) return fail(PKM_ERR_UNSUPPORTED, "row bytes (dim * element size) must be a multiple of 16");
+  if (rb > 4096) return fail(PKM_ERR_UNSUPPORTED, "row bytes above 4096 are not supported");
+  return PKM_OK;
+}
+
+extern "C" int pkm_bag_fwd(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                           int weight_dtype, int64_t n_bags, int64_t bag_size, int64_t num_rows, int64_t dim,
+                           void* out, int out_dtype, uint32_t* dev_err, void* stream) {
+  int rc = check_bag_common(indices, n_bags, bag_size, num_rows, dim, weight_dtype);
+  if (rc) return rc;
+  if (!valid_dtype(out_dtype) || (psw && !valid_dtype(psw_dtype)))
+    return fail(PKM_ERR_INVALID_ARG, "bad dtype");
+  if (n_bags == 0) return PKM_OK;
+  if (out == nullptr) return fail(PKM_ERR_INVALID_ARG, "out is NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (bag_size == 0 || num_rows == 0) {
+    cudaMemsetAsync(out, 0, (size_t)(n_bags * dim * dtype_size(out_dtype)), st);
+    if (bag_size > 0 && dev_err)  // every index is out of range of an empty table
+      cudaMemsetAsync(dev_err, PKM_DEVERR_INDEX, 1, st);
+    return check_cuda("pkm_bag_fwd memset");
+  }
+  if (weight == nullptr || !aligned16(weight)) return fail(PKM_ERR_INVALID_ARG, "weight NULL or not 16-byte aligned");
+  GatherArgs a{};
+  a.rows = static_cast<const char*>(weight);
+  a.row_bytes = dim * dtype_size(weight_dtype);
+  a.dim = dim;
+  a.num_rows = num_rows;
+  a.idx = indices;
+  a.w = psw;
+  a.w_dtype = psw ? psw_dtype : PKM_DT_F32;
+  a.L = bag_size;
+  a.n_items = n_bags;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  a.err = dev_err;
+  return gather_launch(weight_dtype, false, false, a, n_bags, st);
+}
+
+extern "C" int pkm_bag_bwd2(const int64_t* indices, const void* a_w, int a_dtype, const void* gbar,
+                            int gbar_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                            int64_t num_rows, int64_t dim, void* d_grad_out, int d_grad_out_dtype, void* d_a,
+                            int d_a_dtype, uint32_t* dev_err, void* stream) {
+  int rc = check_bag_common(indices, n_bags, bag_size, num_rows, dim, gbar_dtype);
+  if (rc) return rc;
+  if (!valid_dtype(d_grad_out_dtype) || (a_w && !valid_dtype(a_dtype)) || (d_a && !valid_dtype(d_a_dtype)))
+    return fail(PKM_ERR_INVALID_ARG, "bad dtype");
+  if (d_a && !a_w) return fail(PKM_ERR_INVALID_ARG, "d_a requested without per-sample weights");
+  if (n_bags == 0) return PKM_OK;
+  if (d_grad_out == nullptr) return fail(PKM_ERR_INVALID_ARG, "d_grad_out is NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (bag_size == 0 || num_rows == 0) {
+    cudaMemsetAsync(d_grad_out, 0, (size_t)(n_bags * dim * dtype_size(d_grad_out_dtype)), st);
+    if (d_a && bag_size > 0) cudaMemsetAsync(d_a, 0, (size_t)(n_bags * bag_size * dtype_size(d_a_dtype)), st);
+    if (bag_size > 0 && dev_err) cudaMemsetAsync(dev_err, PKM_DEVERR_INDEX, 1, st);
+    return check_cuda("pkm_bag_bwd2 memset");
+  }
+  if (gbar == nullptr || !aligned16(gbar)) return fail(PKM_ERR_INVALID_ARG, "gbar NULL or not 16-byte aligned");
+  if (d_a && (grad_out == nullptr || !aligned16(grad_out)))
+    return fail(PKM_ERR_INVALID_ARG, "grad_out NULL or not 16-byte aligned");
+  GatherArgs a{};
+  a.rows = static_cast<const char*>(gbar);
+  a.row_bytes = dim * dtype_size(gbar_dtype);
+  a.dim = dim;
+  a.num_rows = num_rows;
+  a.idx = indices;
+  a.w = a_w;
+  a.w_dtype = a_w ? a_dtype : PKM_DT_F32;
+  a.L = bag_size;
+  a.n_items = n_bags;
+  a.out = d_grad_out;
+  a.out_dtype = d_grad_out_dtype;
+  a.dotvec = static_cast<const char*>(grad_out);
+  a.dotout = d_a;
+  a.dotout_dtype = d_a_dtype;
+  a.err = dev_err;
+  return gather_launch(gbar_dtype, false, d_a != nullptr, a, n_bags, st);
+}
+
+extern "C" int pkm_bag_bwd_workspace(int64_t n_bags, int64_t bag_size, int64_t num_rows, int64_t dim,
+                                     size_t* bytes) {
+  if (!bytes) return fail(PKM_ERR_INVALID_ARG, "bytes is NULL");
+  if (n_bags < 0 || bag_size < 0 || num_rows < 0 || dim <= 0) return fail(PKM_ERR_INVALID_ARG, "bad size");
+  *bytes = bwd_layout(n_bags * bag_size, num_rows, dim).total;
+  return PKM_OK;
+}
+
+extern "C" int pkm_bag_bwd(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                           int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                           int64_t num_rows, int64_t dim, void* grad_weight, int grad_weight_dtype,
+                           void* grad_psw, int grad_psw_dtype, int32_t* row_counts, void* workspace,
+                           size_t workspace_bytes, uint32_t* dev_err, void* stream) {
+  int rc = check_bag_common(indices, n_bags, bag_size, num_rows, dim, weight_dtype);
+  if (rc) return rc;
+  if (!valid_dtype(grad_weight_dtype) || (psw && !valid_dtype(psw_dtype)) ||
+      (grad_psw && !valid_dtype(grad_psw_dtype)))
+    return fail(PKM_ERR_INVALID_ARG, "bad dtype");
+  if (grad_psw && !psw) return fail(PKM_ERR_INVALID_ARG, "grad_psw requested without per-sample weights");
+  if (num_rows > 0 && grad_weight == nullptr) return fail(PKM_ERR_INVALID_ARG, "grad_weight is NULL");
+  const int64_t M = n_bags * bag_size;
+  const int64_t K = num_rows;
+  const int64_t D = dim;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (M > 0 && (grad_out == nullptr || !aligned16(grad_out)))
+    return fail(PKM_ERR_INVALID_ARG, "grad_out NULL or not 16-byte aligned");
+  if (grad_psw && (weight == nullptr || !aligned16(weight)))
+    return fail(PKM_ERR_INVALID_ARG, "weight NULL or not 16-byte aligned");
+  const BwdLayout L = bwd_layout(M, K, D);
+  if (M == 0 || K == 0) {
+    if (K > 0) cudaMemsetAsync(grad_weight, 0, (size_t)(K * D * dtype_size(grad_weight_dtype)), st);
+    if (row_counts && K > 0) cudaMemsetAsync(row_counts, 0, sizeof(int32_t) * K, st);
+    if (grad_psw && M > 0) cudaMemsetAsync(grad_psw, 0, (size_t)(M * dtype_size(grad_psw_dtype)), st);
+    if (M > 0 && dev_err) cudaMemsetAsync(dev_err, PKM_DEVERR_INDEX, 1, st);
+    return check_cuda("pkm_bag_bwd memset");
+  }
+  if (workspace == nullptr || workspace_bytes < L.total)
+    return fail(PKM_ERR_WORKSPACE, "workspace smaller than pkm_bag_bwd_workspace()");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(PKM_ERR_INVALID_ARG, "workspace must be 256-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
+  I4* offs = reinterpret_cast<I4*>(ws + L.offs);
+  uint32_t* keys_a = reinterpret_cast<uint32_t*>(ws + L.keys_a);
+  uint32_t* keys_b = reinterpret_cast<uint32_t*>(ws + L.keys_b);
+  int32_t* vals_a = reinterpret_cast<int32_t*>(ws + L.vals_a);
+  int32_t* vals_b = reinterpret_cast<int32_t*>(ws + L.vals_b);
+  float* w_sorted = reinterpret_cast<float*>(ws + L.w_sorted);
+  int* hist = reinterpret_cast<int*>(ws + L.hist);
+  int* sums_i = reinterpret_cast<int*>(ws + L.sums_i);
+  I4* sums_4 = reinterpret_cast<I4*>(ws + L.sums_4);
+  int4* desc = reinterpret_cast<int4*>(ws + L.desc);
+  int32_t* n_items = reinterpret_cast<int32_t*>(ws + L.n_items);
+  float* partials = reinterpret_cast<float*>(ws + L.partials);
+
+  const int nsm = num_sms();
+  // 1. row keys + counts
+  cudaMemsetAsync(counts, 0, sizeof(int32_t) * (K + 1), st);
+  {
+    int64_t blocks = std::min<int64_t>((M + 255) / 256, (int64_t)nsm * 16);
+    bwd_keys_kernel<<<(unsigned)blocks, 256, 0, st>>>(indices, M, K, keys_a, counts, dev_err);
+  }
+  // 2. segment offsets, chunk counts and partial-row offsets per row
+  scan_exclusive<I4>(RowScanLoad{counts, K, kChunk}, K + 1, offs, sums_4, st);
+  // 3. stable radix sort of occurrence ids by row (sentinel row K included)
+  {
+    const int bits = bits_for(K);
+    const int passes = (bits + 7) / 8;
+    const int64_t tiles = sort_tiles(M);
+    const uint32_t* kin = keys_a;
+    const int32_t* vin = nullptr;
+    uint32_t* kbuf[2] = {keys_b, keys_a};
+    int32_t* vbuf[2] = {vals_a, vals_b};
+    for (int p = 0; p < passes; ++p) {
+      const bool last = p == passes - 1;
+      radix_upsweep_kernel<<<(unsigned)tiles, kSortThreads, 0, st>>>(kin, M, 8 * p, hist, tiles);
+      scan_exclusive<int>(IntLoad{hist}, (int64_t)kRadix * tiles, hist, sums_i, st);
+      uint32_t* kout = last ? nullptr : kbuf[p & 1];
+      int32_t* vout = vbuf[p & 1];
+      radix_downsweep_kernel<<<(unsigned)tiles, kSortThreads, 0, st>>>(
+          kin, vin, M, 8 * p, hist, tiles, kout, vout, last ? psw : nullptr, psw_dtype, last ? w_sorted : nullptr);
+      kin = kout;
+      vin = vout;
+    }
+    // vin now holds the sorted occurrence ids
+    // 4. chunk descriptors
+    {
+      int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((K + 255) / 256, (int64_t)nsm * 8));
+      items_fill_kernel<<<(unsigned)blocks, 256, 0, st>>>(counts, offs, K, kChunk, desc, n_items, row_counts);
+    }
+    rc = check_cuda("pkm_bag_bwd prologue");
+    if (rc) return rc;
+    // 5. segment sums (+ per-sample gradient dots)
+    GatherArgs a{};
+    a.rows = static_cast<const char*>(grad_out);
+    a.row_bytes = D * dtype_size(weight_dtype);
+    a.dim = D;
+    a.num_rows = n_bags;
+    a.occ = vin;
+    a.occ_w = w_sorted;
+    a.L = bag_size;
+    a.n_items_dev = n_items;
+    a.item_desc = desc;
+    a.dotvec = static_cast<const char*>(weight);
+    a.dotout = grad_psw;
+    a.dotout_dtype = grad_psw_dtype;
+    a.out = grad_weight;
+    a.out_dtype = grad_weight_dtype;
+    a.partials = partials;
+    a.err = dev_err;
+    const int64_t items_upper = K + (M + kChunk - 1) / kChunk + 1;
+    rc = gather_launch(weight_dtype, true, grad_psw != nullptr, a, items_upper, st);
+    if (rc) return rc;
+  }
+  // 6. rows that were split over several chunks
+  {
+    int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((K + 7) / 8, (int64_t)nsm * 8));
+    reduce_partials_kernel<<<(unsigned)blocks, 256, 0, st>>>(offs, K, partials, D, grad_weight, grad_weight_dtype);
+  }
+  return check_cuda("pkm_bag_bwd");
+}

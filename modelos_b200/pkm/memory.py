@@ -1,0 +1,341 @@
+"""Product-key memory layer on B200 kernels (``pkm/memory.py`` of the reference).
+
+``HashingMemory`` keeps the reference's constructor arguments, parameter
+names and shapes, ``reset_parameters``, ``forward`` and ``get_indices``
+(``pkm/memory.py:37-289``), so a state dict moves between the two and
+``modeling_qwen3pkm.py`` can import this class unchanged.  The memory lookup
+runs on the sm_100a kernels:
+
+* sub-key scores of both halves (K1, ``pkm_subkey_scores``),
+* dual top-k, cartesian top-k and per-head softmax fused in one warp per
+  (token, head) (K2, ``pkm_product_topk``),
+* the weighted bag over the value table (K3/K4 via ``xFormerEmbeddingBag``),
+* and, in the backward, the softmax gradient plus sub-key bags
+  (``pkm_score_bwd_prep``) that turn the sparse score gradient into the query
+  and key gradients with the same bag kernels.
+
+The query projection, its norm, the SwiLU gate and the value projection are
+ordinary ``nn.Linear``/norm modules as in the reference.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from logging import getLogger
+from typing import Optional
+
+import torch
+from torch import nn
+from torch.nn import functional as F
+
+from .. import _native
+from .colwise_embedding_bag import xFormerEmbeddingBag
+
+logger = getLogger()
+
+
+@dataclass
+class ProductKeyArgs:
+    """Configuration record of the reference (``pkm/memory.py:15-28``)."""
+
+    is_enabled: bool = False
+    layers: str = ""
+    mem_n_keys: int = 1024
+    mem_heads: int = 4
+    mem_knn: int = 32
+    mem_share_values: bool = True
+    mem_k_dim: int = 512
+    mem_v_dim: int = -1
+    swilu_projection: bool = True
+    value_fixed_lr: Optional[float] = 0.001
+    mem_gated: bool = False
+    peer_variant: bool = False
+
+
+class AttrDict(dict):
+    def __init__(self, *args, **kwargs):
+        super(AttrDict, self).__init__(*args, **kwargs)
+        self.__dict__ = self
+
+
+# ---------------------------------------------------------------------------
+# autograd nodes of the lookup
+# ---------------------------------------------------------------------------
+def _score_backward(ctx, d_scores, psw):
+    """Gradients of the product-key scores w.r.t. query and keys.
+
+    The score of slot ``i1*n + i2`` is ``s1[i1] + s2[i2]``
+    (``pkm/memory.py:274-281``), so ``dq_half[r] = sum_j ds[r,j] keys_half[sub_j]``
+    and ``dkeys[m] = sum_{(r,j) -> m} ds[r,j] q_half[r]``: a bag forward and a
+    bag backward over the sub-key table.
+    """
+    query, keys, idx = ctx.saved_tensors[:3]
+    R, kd = query.shape
+    half = kd // 2
+    sub_idx, sub_w = _native.score_bwd_prep(idx, psw, d_scores.to(query.dtype), ctx.heads, ctx.n_keys)
+    dq = None
+    dk = None
+    if ctx.needs_input_grad[0]:
+        dq = _native.bag_fwd(sub_idx, keys, sub_w, out_dtype=query.dtype).view(R, kd)
+    if ctx.needs_input_grad[1]:
+        dk, _, _ = _native.bag_bwd(sub_idx, None, sub_w, query.view(2 * R, half), num_rows=keys.shape[0],
+                                   need_dpsw=False, grad_weight_dtype=keys.dtype)
+    return dq, dk
+
+
+class ProductKeyTopK(torch.autograd.Function):
+    """``(scores, indices)`` of ``HashingMemory.get_indices`` (``pkm/memory.py:250-289``)."""
+
+    @staticmethod
+    def forward(ctx, query, keys, heads, knn):
+        scores_all = _native.subkey_scores(query, keys, heads, "dot")
+        n_keys = scores_all.shape[-1]
+        idx, top, _, _, _ = _native.product_topk(scores_all, knn)
+        ctx.save_for_backward(query, keys, idx)
+        ctx.heads, ctx.n_keys = heads, n_keys
+        ctx.mark_non_differentiable(idx)
+        return top, idx
+
+    @staticmethod
+    def backward(ctx, d_top, d_idx):
+        if d_top is None:
+            return None, None, None, None
+        dq, dk = _score_backward(ctx, d_top.contiguous(), None)
+        return dq, dk, None, None
+
+
+class ProductKeyLookup(torch.autograd.Function):
+    """Fused lookup of ``HashingMemory.forward`` (``pkm/memory.py:204-222``):
+    returns per-head softmax weights (differentiable), indices and the raw
+    top-k scores (not differentiable, kept for ``last_scores``)."""
+
+    @staticmethod
+    def forward(ctx, query, keys, heads, knn):
+        scores_all = _native.subkey_scores(query, keys, heads, "dot")
+        n_keys = scores_all.shape[-1]
+        idx, top, psw, _, _ = _native.product_topk(scores_all, knn, want_psw=True)
+        ctx.save_for_backward(query, keys, idx, psw)
+        ctx.heads, ctx.n_keys = heads, n_keys
+        ctx.mark_non_differentiable(idx, top)
+        return psw, idx, top
+
+    @staticmethod
+    def backward(ctx, d_psw, d_idx, d_top):
+        if d_psw is None:
+            return None, None, None, None
+        psw = ctx.saved_tensors[3]
+        dq, dk = _score_backward(ctx, d_psw.contiguous(), psw)
+        return dq, dk, None, None
+
+
+# ---------------------------------------------------------------------------
+# the layer
+# ---------------------------------------------------------------------------
+class HashingMemory(nn.Module):
+    VALUES = None
+    EVAL_MEMORY = True
+
+    def __init__(
+        self,
+        input_dim,
+        output_dim,
+        value_fixed_lr=0.001,
+        mem_k_dim=512,
+        mem_v_dim=-1,
+        mem_heads=4,
+        mem_knn=32,
+        mem_share_values=True,
+        mem_n_keys=1024,
+        mem_query_bias=True,
+        mem_query_batchnorm=False,
+        mem_query_rmsnorm=True,
+        mem_gated=False,
+        mem_input_dropout=0.0,
+        mem_query_dropout=0.0,
+        mem_value_dropout=0.0,
+        peer_variant=False,
+        swilu_projection=True,
+    ):
+        assert mem_k_dim >= 2
+        assert 0 <= mem_input_dropout < 1
+        assert 0 <= mem_query_dropout < 1
+        assert 0 <= mem_value_dropout < 1
+        assert not (peer_variant and mem_v_dim > 0), (
+            "Cannot use PEER variant with a value dimension different from the input dimension (mem_v_dim=-1)"
+        )
+        assert mem_k_dim % 2 == 0
+        assert mem_heads >= 2
+        if peer_variant:
+            raise NotImplementedError("the PEER variant is not part of the B200 product-key path")
+        if mem_query_batchnorm:
+            logger.warning(
+                "WARNING: if you use batch normalization, be sure that you use batches of sentences with the same "
+                "size at training time. Otherwise, the padding token will result in incorrect mean/variance "
+                "estimations in the BatchNorm layer."
+            )
+        assert not (mem_query_batchnorm and mem_query_rmsnorm), "Cannot use both batchnorm and rmsnorm"
+
+        super().__init__()
+        self.use_peer_variant = peer_variant
+        self.input_dim = input_dim
+        self.output_dim = output_dim
+        self.size = mem_n_keys**2
+        self.k_dim = mem_k_dim
+        self.v_dim = mem_v_dim if mem_v_dim > 0 else output_dim
+        self.swilu_proj = swilu_projection
+        self.v_proj = mem_v_dim > 0 or self.swilu_proj
+        self.heads = mem_heads
+        self.knn = mem_knn
+        self.n_keys = mem_n_keys
+        self.input_dropout = mem_input_dropout
+        self.query_dropout = mem_query_dropout
+        self.value_dropout = mem_value_dropout
+
+        self.keys = nn.Parameter(torch.zeros(2 * self.heads * int(self.size**0.5), self.k_dim // 2))
+        self.mem_share_values = mem_share_values
+        self.original = not self.mem_share_values or HashingMemory.VALUES is None
+        if self.original:
+            self.values = xFormerEmbeddingBag(self.size, self.v_dim)
+        else:
+            self.values = None
+        self.value_fixed_lr = value_fixed_lr
+
+        if self.v_proj:
+            proj_input = mem_v_dim
+            if self.swilu_proj and proj_input < 0:
+                proj_input = output_dim
+            self.value_proj = torch.nn.Linear(proj_input, output_dim)
+        if self.swilu_proj:
+            self.swilu_projection = torch.nn.Linear(self.input_dim, proj_input)
+        self.gating = None
+        if mem_gated:
+            self.gating = torch.nn.Linear(input_dim, 1)
+
+        l_sizes = (self.input_dim, self.heads * self.k_dim)
+        self.query_proj = QueryMLP(
+            self.input_dim,
+            self.heads,
+            self.k_dim,
+            l_sizes,
+            bias=mem_query_bias,
+            batchnorm=mem_query_batchnorm,
+            rmsnorm=mem_query_rmsnorm,
+        )
+        self._last_indices_dev = None
+        self._last_scores_dev = None
+
+    # eval-mode usage statistics (pkm/memory.py:213-215); the host copy is
+    # made when the attribute is read instead of on every forward
+    @property
+    def last_indices(self):
+        t = self._last_indices_dev
+        return None if t is None else t.cpu()
+
+    @last_indices.setter
+    def last_indices(self, v):
+        self._last_indices_dev = v
+
+    @property
+    def last_scores(self):
+        t = self._last_scores_dev
+        return None if t is None else t.cpu().float()
+
+    @last_scores.setter
+    def last_scores(self, v):
+        self._last_scores_dev = v
+
+    def reset_parameters(self, init_std=None, factor=1.0):
+        bound = 1 / math.sqrt(self.k_dim)
+        nn.init.uniform_(self.keys, a=-bound, b=bound)
+        if self.original:
+            nn.init.normal_(self.values.weight, mean=0, std=self.v_dim**-0.5)
+        nn.init.xavier_uniform_(self.query_proj.query_mlps[0].weight)
+        if self.v_proj:
+            nn.init.normal_(self.value_proj.weight, mean=0, std=self.output_dim**-0.5)
+        if self.swilu_proj:
+            nn.init.normal_(self.swilu_projection.weight, mean=0, std=self.output_dim**-0.5)
+        if self.gating is not None:
+            nn.init.normal_(self.gating.weight, mean=0, std=self.input_dim**-0.5)
+
+    def forward(self, input):
+        """Read from the memory: ``(out [B,T,output_dim], indices [B,T,H*knn])``."""
+        B, T, C = input.shape
+        input = input.view(-1, self.input_dim)
+        assert input.shape[-1] == self.input_dim
+        bs = input.shape[0]
+        input = F.dropout(input, p=self.input_dropout, training=self.training)
+        query = self.query_proj(input)
+        query = F.dropout(query, p=self.query_dropout, training=self.training)
+        assert query.shape == (bs * self.heads, self.k_dim)
+
+        knn = self.knn
+        psw, indices, scores = ProductKeyLookup.apply(query.contiguous(), self.keys, self.heads, knn)
+        if not self.training and HashingMemory.EVAL_MEMORY:
+            self.last_indices = indices.view(bs, self.heads, knn).detach()
+            self.last_scores = scores.view(bs, self.heads, knn).detach()
+
+        indices = indices.view(bs, self.heads * knn)
+        psw = psw.view(bs, self.heads * knn)
+        output = self.values(indices, psw)
+        if self.v_proj and not self.swilu_proj:
+            output = self.value_proj(output)
+        if self.swilu_proj:
+            output = self.value_proj(output * F.silu(self.swilu_projection(input)))
+        output = F.dropout(output, p=self.value_dropout, training=self.training)
+        if self.gating:
+            output = F.sigmoid(self.gating(input)) * output
+        output = output.view(B, T, -1)
+        indices = indices.view(B, T, -1)
+        return output, indices
+
+    def get_indices(self, query, knn):
+        """``(scores [bs*H, knn], indices [bs*H, knn])`` (``pkm/memory.py:250-289``)."""
+        assert query.dim() == 2 and query.size(1) == self.k_dim
+        bs = len(query) // self.heads
+        scores, indices = ProductKeyTopK.apply(query.contiguous(), self.keys, self.heads, knn)
+        assert scores.shape == indices.shape == (bs * self.heads, knn)
+        return scores, indices
+
+
+class QueryMLP(nn.Module):
+    """Query network (``pkm/memory.py:292-349``)."""
+
+    def __init__(self, input_dim, heads, k_dim, sizes, bias=False, batchnorm=False, rmsnorm=False):
+        super().__init__()
+        self.input_dim = input_dim
+        self.heads = heads
+        self.k_dim = k_dim
+        self.sizes = sizes
+        assert sizes[0] == input_dim
+        assert sizes[-1] == (heads * k_dim)
+        sizes_ = list(sizes)
+        self.query_mlps = QueryMLP.mlp(sizes_, bias=bias)
+        if batchnorm:
+            self.norm = nn.BatchNorm1d(sizes_[-1], affine=True, eps=1e-6, momentum=0.1)
+        elif rmsnorm:
+            from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm
+
+            self.norm = Qwen3RMSNorm(sizes_[-1], eps=1e-6)
+        else:
+            self.norm = None
+
+    @staticmethod
+    def mlp(sizes, bias=True):
+        assert len(sizes) >= 2
+        pairs = [(sizes[i], sizes[i + 1]) for i in range(len(sizes) - 1)]
+        layers = []
+        for i, (dim_in, dim_out) in enumerate(pairs):
+            layers.append(nn.Linear(dim_in, dim_out, bias=bias))
+            if i < len(pairs) - 1:
+                layers.append(nn.ReLU())
+        return nn.Sequential(*layers)
+
+    def forward(self, input):
+        assert input.shape[-1] == self.input_dim
+        input = input.contiguous().view(-1, self.input_dim) if input.dim() > 2 else input
+        bs = len(input)
+        query = self.query_mlps(input)
+        if self.norm is not None:
+            query = self.norm(query)
+        assert query.shape == (bs, self.heads * self.k_dim)
+        return query.view(bs * self.heads, self.k_dim)

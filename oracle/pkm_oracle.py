@@ -247,8 +247,14 @@ def bag_bwd(indices, psw, weight, grad_out, chunk: int = 4096):
         e = min(B, s + chunk)
         rows = W[indices[s:e]].astype(np.float64)
         dpsw[s:e] = np.einsum("bld,bd->bl", rows, g[s:e])
-        contrib = psw[s:e, :, None] * g[s:e, None, :]
-        np.add.at(dW, indices[s:e].reshape(-1), contrib.reshape(-1, D))
+        flat = indices[s:e].reshape(-1)
+        if flat.size == 0:
+            continue
+        order = np.argsort(flat, kind="stable")
+        fs = flat[order]
+        starts = np.flatnonzero(np.r_[True, fs[1:] != fs[:-1]])
+        contrib = (psw[s:e, :, None] * g[s:e, None, :]).reshape(-1, D)[order]
+        dW[fs[starts]] += np.add.reduceat(contrib, starts, axis=0)
     return dW, dpsw
 
 

@@ -175,3 +175,16 @@ def test_bincount_and_fw_update_math():
 def test_bf16_round_matches_torch():
     x = torch.randn(10000) * 3
     np.testing.assert_array_equal(po.bf16_round(x.numpy()), x.bfloat16().float().numpy())
+
+
+def test_numpy_layer_port_matches_reference_step(c0):
+    """The CPU port timed as the baseline computes the reference's step."""
+    from oracle.pkm_layer import layer_step
+    st = {k: v.numpy() for k, v in cases.pkm_state(cases.CONFIG0, 0).items()}
+    x = cases.pkm_input((2, 128, 512), 0).numpy()
+    loss, G = layer_step(st, x, heads=4, knn=32, norm="rms")
+    assert abs(loss - float(c0["loss"])) <= 1e-4 * abs(float(c0["loss"]))
+    assert rel_err(G["x"], c0["x_grad"]) < 1e-4
+    assert rel_err(G["keys"], c0["keys_grad"]) < 1e-4
+    assert rel_err(np.linalg.norm(G["values.weight"], axis=1), c0["values_grad_rownorm"]) < 1e-4
+    assert rel_err(G["query_proj.query_mlps.0.bias"], c0["bq_grad"]) < 1e-4

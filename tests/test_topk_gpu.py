@@ -1,0 +1,116 @@
+"""Parity of the sub-key scores (K1) and the product top-k (K2): fp32 scores
+and indices bit-exact with the oracle's definition, bf16 top-k bit-exact for
+identical input scores, and the reference's indices matched tie-aware."""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from oracle import pkm_oracle as po
+from tiecmp import compare_topk
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+DEV = "cuda"
+
+
+def rel_err(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.mark.parametrize("mode", ["dot", "idw"])
+def test_scores_fp32_bit_exact(mode):
+    from modelos_b200 import _native
+    c0 = np.load(os.path.join(GOLD, "c0_pkm.npz"))
+    q = c0["query"]
+    keys = cases.pkm_state(cases.CONFIG0, 0)["keys"].numpy()
+    got = _native.subkey_scores(torch.from_numpy(q).to(DEV), torch.from_numpy(keys).to(DEV), 4, mode)
+    ref = po.subkey_scores(q, keys, 4, mode=mode)
+    g = got.cpu().numpy()
+    if mode == "dot":
+        np.testing.assert_array_equal(g, ref)
+    else:
+        # the only non-IEEE-exact step is log(): fp64 log rounded to fp32 on
+        # both sides, so mismatches would be isolated 1-ulp cases
+        mism = (g != ref).sum()
+        assert mism <= 2, mism
+        assert rel_err(g, ref) < 1e-6
+
+
+def test_scores_bf16_against_oracle():
+    from modelos_b200 import _native
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn(512 * 4, 512, generator=g).bfloat16()
+    keys = (torch.rand(2 * 4 * 512, 256, generator=g) * 2 - 1).div(512 ** 0.5).bfloat16()
+    got = _native.subkey_scores(q.to(DEV), keys.to(DEV), 4, "dot").float().cpu().numpy()
+    ref = po.subkey_scores(q.float().numpy(), keys.float().numpy(), 4, bf16=True)
+    # same products, same fp32 summation order, same bf16 rounding
+    np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n,knn", [(128, 32), (512, 32), (100, 7), (16, 4), (1024, 32), (33, 1)])
+def test_product_topk_bit_exact(dtype, n, knn):
+    from modelos_b200 import _native
+    g = torch.Generator().manual_seed(n * 100 + knn)
+    s = torch.randn(700, 2, n, generator=g)
+    if dtype == torch.bfloat16:
+        s = s.bfloat16()
+    else:
+        s = (s * 64).round() / 64  # coarse values: many exact ties in both stages
+    idx, top, psw, s1, s2 = _native.product_topk(s.to(DEV).contiguous(), knn, want_psw=True, want_sub=True)
+    ref = po.product_topk(s.float().numpy(), knn, bf16=dtype == torch.bfloat16)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref["indices"])
+    np.testing.assert_array_equal(top.float().cpu().numpy(), ref["scores"])
+    np.testing.assert_array_equal(s1.cpu().numpy(), ref["sub_indices1"])
+    np.testing.assert_array_equal(s2.cpu().numpy(), ref["sub_indices2"])
+    p_ref = po.softmax_rows(ref["scores"], bf16=dtype == torch.bfloat16)
+    assert rel_err(psw.float().cpu().numpy(), p_ref) < (2e-2 if dtype == torch.bfloat16 else 1e-5)
+
+
+def test_config0_indices_bit_exact_and_match_reference():
+    from modelos_b200 import _native
+    c0 = np.load(os.path.join(GOLD, "c0_pkm.npz"))
+    keys = cases.pkm_state(cases.CONFIG0, 0)["keys"]
+    sc = _native.subkey_scores(torch.from_numpy(c0["query"]).to(DEV), keys.to(DEV), 4)
+    idx, top, _, _, _ = _native.product_topk(sc, 32)
+    ref = po.pkm_get_indices(c0["query"], keys.numpy(), 4, 32)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref["indices"])
+    np.testing.assert_array_equal(top.cpu().numpy(), ref["scores"])
+    # the reference's own indices at seed 0 of config 0: identical
+    np.testing.assert_array_equal(idx.cpu().numpy(), c0["gi_indices"])
+
+
+def test_exact_ties_case():
+    from modelos_b200 import _native
+    d = np.load(os.path.join(GOLD, "ties.npz"))
+    heads, knn = int(d["heads"]), int(d["knn"])
+    sc = _native.subkey_scores(torch.from_numpy(d["q"]).to(DEV), torch.from_numpy(d["keys"]).to(DEV), heads)
+    idx, top, _, _, _ = _native.product_topk(sc, knn)
+    ref = po.pkm_get_indices(d["q"], d["keys"], heads, knn)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref["indices"])
+    compare_topk(top.cpu().numpy(), idx.cpu().numpy(), d["scores"], d["indices"], ref["all_scores"], 0.0)
+
+
+def test_score_bwd_prep_matches_softmax_backward():
+    from modelos_b200 import _native
+    g = torch.Generator().manual_seed(11)
+    R, knn, heads, n = 64, 32, 4, 128
+    logits = torch.randn(R, knn, generator=g)
+    psw = torch.softmax(logits, -1)
+    dpsw = torch.randn(R, knn, generator=g)
+    idx = torch.randint(0, n * n, (R, knn), generator=g)
+    sub_idx, sub_w = _native.score_bwd_prep(idx.to(DEV), psw.to(DEV), dpsw.to(DEV), heads, n)
+    ref_ds = psw * (dpsw - (psw * dpsw).sum(-1, keepdim=True))
+    sw = sub_w.cpu()
+    assert rel_err(sw[0::2].numpy(), ref_ds.numpy()) < 1e-6
+    assert torch.equal(sw[0::2], sw[1::2])
+    h = torch.arange(R)[:, None] % heads
+    assert torch.equal(sub_idx.cpu()[0::2], (h * 2) * n + idx // n)
+    assert torch.equal(sub_idx.cpu()[1::2], (h * 2 + 1) * n + idx % n)
