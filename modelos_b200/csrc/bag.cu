@@ -84,14 +84,16 @@ int gather_launch(int row_dtype, bool seg, bool dot, GatherArgs a, int64_t items
 // Row key of every occurrence (invalid indices map to the sentinel row K)
 // and the per-row occurrence counts.
 __global__ void bwd_keys_kernel(const int64_t* __restrict__ idx, int64_t M, int64_t K,
-                                uint32_t* __restrict__ keys, int32_t* __restrict__ counts, uint32_t* err) {
+                                uint32_t* __restrict__ keys, int32_t* __restrict__ counts, void* grad_psw,
+                                int grad_psw_dtype, uint32_t* err) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < M; o += stride) {
     const int64_t k = idx[o];
     uint32_t key;
     if (k < 0 || k >= K) {
-      key = (uint32_t)K;
+      key = (uint32_t)K;  // sentinel row: never aggregated, its per-sample gradient is 0
       raise_err(err, PKM_DEVERR_INDEX);
+      if (grad_psw) st_f(grad_psw, grad_psw_dtype, o, 0.f);
     } else {
       key = (uint32_t)k;
     }
@@ -337,7 +339,8 @@ extern "C" int pkm_bag_bwd(const int64_t* indices, const void* psw, int psw_dtyp
   cudaMemsetAsync(counts, 0, sizeof(int32_t) * (K + 1), st);
   {
     int64_t blocks = std::min<int64_t>((M + 255) / 256, (int64_t)nsm * 16);
-    bwd_keys_kernel<<<(unsigned)blocks, 256, 0, st>>>(indices, M, K, keys_a, counts, dev_err);
+    bwd_keys_kernel<<<(unsigned)blocks, 256, 0, st>>>(indices, M, K, keys_a, counts, grad_psw, grad_psw_dtype,
+                                                      dev_err);
   }
   // 2. segment offsets, chunk counts and partial-row offsets per row
   scan_exclusive<I4>(RowScanLoad{counts, K, kChunk}, K + 1, offs, sums_4, st);
