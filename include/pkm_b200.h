@@ -154,6 +154,18 @@ PKM_API int pkm_score_bwd_prep(const int64_t* indices, const void* psw, const vo
                        int64_t rows, int64_t knn, int64_t heads, int64_t n_keys, int64_t* sub_idx,
                        void* sub_w, void* stream);
 
+/*
+ * Dense gradient of the sub-key scores [rows, 2, n_keys] from the gradient of
+ * the product top-k outputs: the softmax backward of each row (skipped when
+ * psw is NULL), rounded to the score dtype, scattered to the two sub-keys of
+ * each selected slot and summed where slots share a sub-key.  This is the
+ * gradient the reference's autograd forms through topk/gather/expand
+ * (pkm/memory.py:218, 274-285); d_query and d_keys then follow by two dense
+ * GEMMs per (head, half).  Every element of d_scores is written.
+ */
+PKM_API int pkm_score_grad_dense(const int64_t* indices, const void* psw, const void* dpsw, int dtype,
+                                 int64_t rows, int64_t knn, int64_t n_keys, void* d_scores, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -38,6 +38,7 @@ _SIGS = {
     "pkm_subkey_scores": ([_P, _P, _I, _I64, _I64, _I64, _I64, _I, _P, _P], _I),
     "pkm_product_topk": ([_P, _I, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P], _I),
     "pkm_score_bwd_prep": ([_P, _P, _P, _I, _I64, _I64, _I64, _I64, _P, _P, _P], _I),
+    "pkm_score_grad_dense": ([_P, _P, _P, _I, _I64, _I64, _I64, _P, _P], _I),
 }
 
 EXPORTED = tuple(_SIGS)
@@ -325,3 +326,20 @@ def score_bwd_prep(indices: torch.Tensor, psw: Optional[torch.Tensor], dpsw: tor
                                   n_keys, _ptr(sub_idx), _ptr(sub_w), _stream(dpsw.device))
     _check(rc, "pkm_score_bwd_prep")
     return sub_idx, sub_w
+
+
+def score_grad_dense(indices: torch.Tensor, psw: Optional[torch.Tensor], dpsw: torch.Tensor,
+                     n_keys: int) -> torch.Tensor:
+    """Dense ``[R, 2, n]`` gradient of the sub-key scores (softmax backward
+    included when ``psw`` is given)."""
+    assert indices.dim() == 2 and dpsw.shape == indices.shape
+    _need_cuda(indices, psw, dpsw)
+    R, knn = indices.shape
+    dpsw = dpsw.contiguous()
+    if psw is not None:
+        psw = psw.contiguous().to(dpsw.dtype)
+    out = torch.empty((R, 2, n_keys), dtype=dpsw.dtype, device=dpsw.device)
+    rc = lib().pkm_score_grad_dense(_ptr(indices), _ptr(psw), _ptr(dpsw), DT[dpsw.dtype], R, knn, n_keys,
+                                    _ptr(out), _stream(dpsw.device))
+    _check(rc, "pkm_score_grad_dense")
+    return out

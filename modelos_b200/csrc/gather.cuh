@@ -277,11 +277,10 @@ __global__ void __launch_bounds__(kGatherWarps * 32, 1) gather_kernel(const Gath
         dsum = warp_sum(dsum);
         if (lane == 0) st_f(a.dotout, a.dotout_dtype, pos, src >= 0 ? dsum : 0.f);
       }
+      // every lane has read the slot (the values are in registers) before
+      // lane 0 reuses it for the row P entries ahead
       __syncwarp();
-      if (lane == 0 && e + P < E1) {
-        fence_proxy_async_smem();
-        issue(cs, (rel + P) & (kMetaRing - 1), e + P);
-      }
+      if (lane == 0 && e + P < E1) issue(cs, (rel + P) & (kMetaRing - 1), e + P);
       if ((rel & 31) == 31) {
         // page rel/32 is consumed: its ring half now receives page rel/32 + 2
         const int64_t page = rel >> 5;

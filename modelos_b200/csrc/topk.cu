@@ -331,6 +331,57 @@ __global__ void __launch_bounds__(256) score_bwd_prep_kernel(const int64_t* __re
   ScoreT<T>::store(sub_w, base + knn + lane, ds);
 }
 
+// ---------------------------------------------------------------------------
+// dense sub-score gradient
+// ---------------------------------------------------------------------------
+// dS[r, p, m] = sum of ds[r, j] over the selected slots j whose half-p sub-key
+// is m, where ds is the softmax backward of the row (or dpsw itself when psw
+// is NULL), rounded to the score dtype as the reference's autograd does.
+// Entries sharing a sub-key are summed in slot-rank order, so the result is
+// deterministic; the whole [2, n] row is written (zeros included).
+template <typename T>
+__global__ void __launch_bounds__(256) score_grad_dense_kernel(const int64_t* __restrict__ indices,
+                                                               const T* __restrict__ psw, const T* __restrict__ dpsw,
+                                                               int64_t rows, int knn, int n, T* __restrict__ dS) {
+  __shared__ float sh_ds[8][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + warp;
+  if (r >= rows) return;
+  const bool live = lane < knn;
+  const int dt = sizeof(T) == 4 ? PKM_DT_F32 : PKM_DT_BF16;
+  float g = 0.f, p = 0.f;
+  int64_t slot = 0;
+  if (live) {
+    g = ld_f(dpsw, dt, r * knn + lane);
+    if (psw) p = ld_f(psw, dt, r * knn + lane);
+    slot = indices[r * knn + lane];
+  }
+  float ds = g;
+  if (psw) {
+    const float dot = warp_sum(p * g);
+    ds = p * (g - dot);
+  }
+  sh_ds[warp][lane] = live ? ScoreT<T>::round(ds) : 0.f;
+  T* row = dS + r * 2 * (int64_t)n;
+  for (int m = lane; m < 2 * n; m += 32) ScoreT<T>::store(row, m, 0.f);
+  __syncwarp();
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int key = live ? (int)(half ? slot % n : slot / n) : n + lane;
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    if (live && lane == __ffs(peers) - 1) {
+      float s = 0.f;
+      unsigned mrem = peers;
+      while (mrem) {
+        const int b = __ffs(mrem) - 1;
+        s += sh_ds[warp][b];
+        mrem &= mrem - 1;
+      }
+      ScoreT<T>::store(row, (int64_t)half * n + key, s);
+    }
+  }
+}
+
 }  // namespace pkm
 
 using namespace pkm;
@@ -370,4 +421,24 @@ extern "C" int pkm_score_bwd_prep(const int64_t* indices, const void* psw, const
         indices, static_cast<const __nv_bfloat16*>(psw), static_cast<const __nv_bfloat16*>(dpsw), rows, (int)knn,
         (int)heads, n_keys, sub_idx, static_cast<__nv_bfloat16*>(sub_w));
   return check_cuda("score_bwd_prep_kernel");
+}
+
+extern "C" int pkm_score_grad_dense(const int64_t* indices, const void* psw, const void* dpsw, int dtype,
+                                    int64_t rows, int64_t knn, int64_t n_keys, void* d_scores, void* stream) {
+  if (dtype != PKM_DT_F32 && dtype != PKM_DT_BF16) return fail(PKM_ERR_UNSUPPORTED, "dtype must be f32 or bf16");
+  if (rows < 0 || knn <= 0 || knn > 32 || n_keys <= 0 || n_keys > (1 << 30))
+    return fail(PKM_ERR_INVALID_ARG, "bad size");
+  if (rows == 0) return PKM_OK;
+  if (!indices || !dpsw || !d_scores) return fail(PKM_ERR_INVALID_ARG, "NULL pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  if (dtype == PKM_DT_F32)
+    score_grad_dense_kernel<float><<<blocks, 256, 0, st>>>(indices, static_cast<const float*>(psw),
+                                                           static_cast<const float*>(dpsw), rows, (int)knn,
+                                                           (int)n_keys, static_cast<float*>(d_scores));
+  else
+    score_grad_dense_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        indices, static_cast<const __nv_bfloat16*>(psw), static_cast<const __nv_bfloat16*>(dpsw), rows, (int)knn,
+        (int)n_keys, static_cast<__nv_bfloat16*>(d_scores));
+  return check_cuda("score_grad_dense_kernel");
 }

@@ -10,9 +10,9 @@ runs on the sm_100a kernels:
 * dual top-k, cartesian top-k and per-head softmax fused in one warp per
   (token, head) (K2, ``pkm_product_topk``),
 * the weighted bag over the value table (K3/K4 via ``xFormerEmbeddingBag``),
-* and, in the backward, the softmax gradient plus sub-key bags
-  (``pkm_score_bwd_prep``) that turn the sparse score gradient into the query
-  and key gradients with the same bag kernels.
+* and, in the backward, the softmax gradient scattered onto the dense
+  sub-score grid (``pkm_score_grad_dense``) followed by two GEMMs per
+  (head, half) for the query and key gradients.
 
 The query projection, its norm, the SwiLU gate and the value projection are
 ordinary ``nn.Linear``/norm modules as in the reference.
@@ -61,25 +61,43 @@ class AttrDict(dict):
 # ---------------------------------------------------------------------------
 # autograd nodes of the lookup
 # ---------------------------------------------------------------------------
+def subkey_scores(query: torch.Tensor, keys: torch.Tensor, heads: int) -> torch.Tensor:
+    """All sub-key dot scores ``[N*H, 2, n]`` (``pkm/memory.py:267-268``).
+
+    fp32 uses the sequential-sum kernel, whose scores (and therefore top-k
+    indices) are bit-identical to the oracle's definition; bf16 runs the
+    contraction on the tensor cores (fp32 accumulation, bf16 output, as the
+    reference's einsum)."""
+    if query.dtype == torch.float32:
+        return _native.subkey_scores(query, keys, heads, "dot")
+    R, kd = query.shape
+    half = kd // 2
+    n = keys.shape[0] // (2 * heads)
+    q4 = query.view(R // heads, heads, 2, half)
+    k4 = keys.view(heads, 2, n, half)
+    return torch.einsum("thpd,hpnd->thpn", q4, k4).contiguous().view(R, 2, n)
+
+
 def _score_backward(ctx, d_scores, psw):
     """Gradients of the product-key scores w.r.t. query and keys.
 
     The score of slot ``i1*n + i2`` is ``s1[i1] + s2[i2]``
-    (``pkm/memory.py:274-281``), so ``dq_half[r] = sum_j ds[r,j] keys_half[sub_j]``
-    and ``dkeys[m] = sum_{(r,j) -> m} ds[r,j] q_half[r]``: a bag forward and a
-    bag backward over the sub-key table.
+    (``pkm/memory.py:274-281``): the kernel scatters the (softmax-)gradient
+    onto the dense sub-score grid ``[N*H, 2, n]``, then two GEMMs per
+    (head, half) give ``dq = dS @ keys`` and ``dkeys = dS^T @ q``, the same
+    contraction the reference's einsum backward performs.
     """
     query, keys, idx = ctx.saved_tensors[:3]
     R, kd = query.shape
     half = kd // 2
-    sub_idx, sub_w = _native.score_bwd_prep(idx, psw, d_scores.to(query.dtype), ctx.heads, ctx.n_keys)
-    dq = None
-    dk = None
+    H, n = ctx.heads, ctx.n_keys
+    N = R // H
+    dS = _native.score_grad_dense(idx, psw, d_scores.to(query.dtype), n).view(N, H, 2, n)
+    dq = dk = None
     if ctx.needs_input_grad[0]:
-        dq = _native.bag_fwd(sub_idx, keys, sub_w, out_dtype=query.dtype).view(R, kd)
+        dq = torch.einsum("thpn,hpnd->thpd", dS, keys.view(H, 2, n, half)).reshape(R, kd)
     if ctx.needs_input_grad[1]:
-        dk, _, _ = _native.bag_bwd(sub_idx, None, sub_w, query.view(2 * R, half), num_rows=keys.shape[0],
-                                   need_dpsw=False, grad_weight_dtype=keys.dtype)
+        dk = torch.einsum("thpn,thpd->hpnd", dS, query.view(N, H, 2, half)).reshape(keys.shape)
     return dq, dk
 
 
@@ -88,7 +106,7 @@ class ProductKeyTopK(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, query, keys, heads, knn):
-        scores_all = _native.subkey_scores(query, keys, heads, "dot")
+        scores_all = subkey_scores(query, keys, heads)
         n_keys = scores_all.shape[-1]
         idx, top, _, _, _ = _native.product_topk(scores_all, knn)
         ctx.save_for_backward(query, keys, idx)
@@ -111,7 +129,7 @@ class ProductKeyLookup(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, query, keys, heads, knn):
-        scores_all = _native.subkey_scores(query, keys, heads, "dot")
+        scores_all = subkey_scores(query, keys, heads)
         n_keys = scores_all.shape[-1]
         idx, top, psw, _, _ = _native.product_topk(scores_all, knn, want_psw=True)
         ctx.save_for_backward(query, keys, idx, psw)

@@ -129,7 +129,11 @@ def test_config2_geometry_bf16_matches_reference():
     keys_b = po.bf16_round(cases.pkm_state(cfg, 0)["keys"].numpy())
     res = po.pkm_get_indices(d["query"], keys_b, 4, 32, bf16=True)
     s, i = m.get_indices(torch.from_numpy(d["query"]).to(DEV, torch.bfloat16), 32)
-    np.testing.assert_array_equal(i.cpu().numpy(), res["indices"])
+    # tensor-core sums may round a bf16 score one ulp apart from the oracle's
+    # sequential sum; the selection must agree up to such near-ties
+    ulp = 2 * 2.0 ** -8 * np.maximum(np.abs(res["scores"]).max(axis=1), 1e-3)
+    compare_topk(res["scores"], res["indices"], s.detach().float().cpu().numpy(), i.cpu().numpy(),
+                 res["all_scores"], bound=ulp, bf16=True)
     bound = 4 * 2.0 ** -8 * np.maximum(np.abs(d["gi_scores"]).max(axis=1), 1e-3)
     compare_topk(res["scores"], res["indices"], d["gi_scores"], d["gi_indices"], res["all_scores"],
                  bound=bound, bf16=True)

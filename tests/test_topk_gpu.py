@@ -114,3 +114,25 @@ def test_score_bwd_prep_matches_softmax_backward():
     h = torch.arange(R)[:, None] % heads
     assert torch.equal(sub_idx.cpu()[0::2], (h * 2) * n + idx // n)
     assert torch.equal(sub_idx.cpu()[1::2], (h * 2 + 1) * n + idx % n)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_score_grad_dense_matches_scatter_of_softmax_backward(dtype):
+    from modelos_b200 import _native
+    g = torch.Generator().manual_seed(12)
+    R, knn, n = 96, 32, 64
+    # distinct slots per row, many sharing a sub-key
+    idx = torch.stack([torch.randperm(n * n, generator=g)[:knn] for _ in range(R)])
+    idx[:, 1] = (idx[:, 0] // n) * n + (idx[:, 1] % n)  # force a shared half-0 sub-key
+    psw = torch.softmax(torch.randn(R, knn, generator=g), -1).to(dtype)
+    dpsw = torch.randn(R, knn, generator=g).to(dtype)
+    dS = _native.score_grad_dense(idx.to(DEV), psw.to(DEV), dpsw.to(DEV), n).float().cpu()
+    p, d = psw.float(), dpsw.float()
+    ds = (p * (d - (p * d).sum(-1, keepdim=True))).to(dtype).float()
+    ref = torch.zeros(R, 2, n)
+    ref[:, 0].scatter_add_(1, idx // n, ds)
+    ref[:, 1].scatter_add_(1, idx % n, ds)
+    ref = ref.to(dtype).float()
+    tolr = 1e-6 if dtype == torch.float32 else 2e-2
+    assert rel_err(dS.numpy(), ref.numpy()) < tolr
+    assert (dS[ref == 0] == 0).all()
