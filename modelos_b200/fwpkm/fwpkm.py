@@ -1,0 +1,494 @@
+"""Fast-weight product-key memory on B200 kernels (``fwpkm/fwpkm.py`` of the reference).
+
+``FastWeightProductKeyMemory`` keeps the reference's constructor arguments,
+parameters (``keys``, ``values``), ``forward`` signature and returned dict,
+so ``modeling_qwen3pkm.py`` imports it unchanged (``modeling_qwen3pkm.py:23``).
+Per chunk of the sequence it reads the memory with the current fast weights,
+scores the read against a target (MSE memorisation loss plus the
+marginal-entropy addressing loss), differentiates with
+``create_graph=True`` and takes one SGD step on the fast weights, so the outer
+loss back-propagates through every update (``forward_wo_past``, ``:395-558``).
+
+Kernel mapping:
+
+* sub-key scores, dot or idw (K1, ``pkm_subkey_scores``), bit-exact in fp32;
+  their backward is written with differentiable tensor ops so second
+  derivatives exist for the inner updates;
+* dual / cartesian top-k (K2, ``pkm_product_topk``), ties to the lowest index;
+* the bag forward, its sorted-segment backward and the double-backward
+  (K3 / K4 / K5, through ``xformer_embeddingbag_grad_wrapper``).
+"""
+from __future__ import annotations
+
+import math
+from collections import OrderedDict, defaultdict
+from logging import getLogger
+from typing import Optional
+
+import torch
+from torch import nn
+from torch.nn import functional as F
+
+from .. import _native
+from .xformer_embeddingbag_grad_wrapper import xformers_embedding_bag
+
+logger = getLogger()
+
+
+def l2norm(x: torch.FloatTensor, dim: int = -1, eps: float = 1e-6):
+    """``x / sqrt(sum(x^2) + eps)`` (``fwpkm/fwpkm.py:16-19``)."""
+    inv_norm = torch.rsqrt((x * x).sum(dim=dim, keepdim=True) + eps)
+    return x * inv_norm
+
+
+class SubkeyScores(torch.autograd.Function):
+    """All sub-key scores ``[R, 2, n]`` of queries ``[R, k_dim]``.
+
+    Forward: the sequential-sum kernel (dot, or idw = -log(1e-3 + |q-k|^2),
+    ``fwpkm/fwpkm.py:853-869``).  Backward: the analytic gradient in tensor
+    ops on the saved inputs, hence itself differentiable (the inner updates
+    take gradients with ``create_graph=True``).  For idw with
+    ``r = |q|^2 + |k|^2 - 2 q.k``: ``ds/dr = -1 / (1e-3 + r)`` while
+    ``r > 1e-30`` (the clamp of torch's cdist), ``dr/dq = 2(q - k)``.
+    """
+
+    @staticmethod
+    def forward(ctx, query, keys, heads, mode):
+        s = _native.subkey_scores(query.contiguous(), keys.contiguous(), heads, mode)
+        ctx.save_for_backward(query, keys)
+        ctx.heads, ctx.mode = heads, mode
+        return s
+
+    @staticmethod
+    def backward(ctx, dS):
+        q, k = ctx.saved_tensors
+        H = ctx.heads
+        R, kd = q.shape
+        half = kd // 2
+        n = k.shape[0] // (2 * H)
+        N = R // H
+        qv = q.view(N, H, 2, half)
+        kv = k.view(H, 2, n, half)
+        d = dS.view(N, H, 2, n)
+        if ctx.mode == "dot":
+            dq = torch.einsum("thpn,hpnd->thpd", d, kv)
+            dk = torch.einsum("thpn,thpd->hpnd", d, qv)
+        else:
+            qk = torch.einsum("thpd,hpnd->thpn", qv, kv)
+            qq = (qv * qv).sum(-1, keepdim=True)
+            kk = (kv * kv).sum(-1)
+            r = qq - 2 * qk + kk.unsqueeze(0)
+            w = torch.where(r > 1e-30, -d / (1e-3 + r), torch.zeros_like(r))
+            dq = 2 * (w.sum(-1, keepdim=True) * qv - torch.einsum("thpn,hpnd->thpd", w, kv))
+            dk = 2 * (w.sum(0).unsqueeze(-1) * kv - torch.einsum("thpn,thpd->hpnd", w, qv))
+        return dq.reshape(R, kd), dk.reshape(k.shape), None, None
+
+
+class FastWeightProductKeyMemory(nn.Module):
+    def __init__(
+        self,
+        mem_k_dim=512,
+        mem_v_dim=512,
+        mem_heads=1,
+        mem_topk=8,
+        mem_n_subkeys=512,
+        lookahead=1,
+        qk_score_type="idw",
+        score_nonlinear="softmax",
+        score_temperature=1.0,
+        optimizer_type="sgd",
+        learning_rate=1.0,
+        weight_decay=0.0,
+        loss_type="mse",
+        mem_grad_to_values_only=True,
+        grad_clip=False,
+        addr_loss="me",
+        addr_loss_weight=1.0,
+        fp32_fw=True,
+    ):
+        assert mem_k_dim >= 2
+        assert mem_k_dim % 2 == 0
+        super().__init__()
+        self.subsize = mem_n_subkeys
+        self.size = mem_n_subkeys**2
+        self.k_dim = mem_k_dim
+        self.v_dim = mem_v_dim
+        self.heads = mem_heads
+        self.topk = mem_topk
+        self.lookahead = lookahead
+        self.qk_score_type = qk_score_type
+        self.score_nonlinear = score_nonlinear
+        self.score_temperature = score_temperature
+        self.optimizer_type = optimizer_type
+        self.learning_rate = learning_rate
+        self.weight_decay = weight_decay
+        self.loss_type = loss_type
+        self.mem_grad_to_values_only = mem_grad_to_values_only
+        self.grad_clip = grad_clip
+        self.addr_loss = addr_loss
+        self.addr_loss_weight = addr_loss_weight
+        self.fp32_fw = fp32_fw
+        self.ob_mode = None
+        self.ob_idx2log = defaultdict(list)
+        self.keys = nn.Parameter(torch.zeros(2 * self.heads * self.subsize, self.k_dim // 2))
+        self.values = nn.Parameter(torch.zeros(self.size, self.v_dim))
+
+    def reset_parameters(self):
+        bound = 1 / math.sqrt(self.k_dim)
+        nn.init.uniform_(self.keys, a=-bound, b=bound)
+        nn.init.normal_(self.values, mean=0, std=self.v_dim**-0.5)
+
+    # ------------------------------------------------------------------
+    # pieces of one read / update (fwpkm/fwpkm.py:97-367)
+    # ------------------------------------------------------------------
+    def get_fw_named_params(self):
+        out = OrderedDict()
+        for name, p in self.named_parameters():
+            out[name] = p.float() if self.fp32_fw else p
+        return out
+
+    def score_transform(self, scores):
+        scores = scores / self.score_temperature
+        if self.score_nonlinear == "softmax":
+            return F.softmax(scores, dim=-1).type_as(scores)
+        if self.score_nonlinear == "silu":
+            return F.silu(scores).type_as(scores)
+        if self.score_nonlinear == "relu":
+            return F.relu(scores).type_as(scores)
+        raise NotImplementedError(f"Non-linear {self.score_nonlinear} not implemented for scores.")
+
+    def compute_marginal_entropy(self, M, epsilon=1e-8):
+        """Entropy of the batch-mean of a top-k-thresholded softmax of M [N, K]."""
+        in_dtype = M.dtype
+        if self.addr_loss_weight == 0.0:
+            return torch.tensor(0.0, device=M.device, dtype=in_dtype)
+        kth = torch.topk(M, self.topk, dim=1).values[:, -1:]
+        M = torch.where(M >= kth, M, torch.full_like(M, float("-inf"))).float()
+        P_bar = F.softmax(M, dim=1).mean(dim=0)
+        return (-(P_bar * torch.log(P_bar + epsilon)).sum()).to(in_dtype)
+
+    def retrieve_values(self, query: torch.Tensor, fw_named_params: OrderedDict):
+        B, T = query.shape[:2]
+        scores, indices, indices1, indices2, all_scores1, all_scores2 = self.get_indices(
+            query.view(B * T, self.heads, self.k_dim), fw_named_params["keys"])
+        normed_scores = self.score_transform(scores.view(B * T, self.heads * self.topk))
+        vals = xformers_embedding_bag(
+            indices=indices.view(B * T, self.heads * self.topk),
+            weight=fw_named_params["values"],
+            per_sample_weights=normed_scores,
+        )
+        return {
+            "retireved_values": vals,
+            "scores": scores,
+            "normed_scores": normed_scores,
+            "indices": indices,
+            "sub_indices1": indices1,
+            "sub_indices2": indices2,
+            "all_sub_scores1": all_scores1,
+            "all_sub_scores2": all_scores2,
+        }
+
+    def compute_mem_loss(self, hyp_values, ref_values, loss_mask=None, loss_weights=None):
+        if self.loss_type != "mse":
+            raise NotImplementedError(f"Loss type {self.loss_type} not implemented.")
+        mem_losses = F.mse_loss(hyp_values, ref_values, reduction="none").mean(dim=-1)
+        if loss_mask is not None:
+            mem_losses = mem_losses * loss_mask
+        if loss_weights is not None:
+            mem_losses = mem_losses * loss_weights
+        return mem_losses
+
+    def compute_addr_loss(self, sub_indices1, sub_indices2, all_sub_scores1, all_sub_scores2):
+        if self.addr_loss is None:
+            return None
+        if self.addr_loss != "me":
+            raise NotImplementedError(f"Addressing loss {self.addr_loss} not implemented.")
+        s1 = all_sub_scores1.reshape(-1, self.subsize)
+        s2 = all_sub_scores2.reshape(-1, self.subsize)
+        return self.addr_loss_weight * (-self.compute_marginal_entropy(s1) - self.compute_marginal_entropy(s2))
+
+    def update_fw_param(self, p, g, lr, wd):
+        if self.optimizer_type != "sgd":
+            raise NotImplementedError(f"Optimizer {self.optimizer_type} not implemented.")
+        return p - lr * (g + wd * p)
+
+    def update_fw(self, fw_named_params, num_samples, indices, mem_loss, addr_loss=None):
+        """One SGD step on the fast weights (``fwpkm/fwpkm.py:274-367``)."""
+        mem_loss = mem_loss * 0.5
+        names = list(fw_named_params.keys())
+        params = tuple(fw_named_params.values())
+        if self.mem_grad_to_values_only:
+            if addr_loss is not None:
+                addr_grads = torch.autograd.grad(addr_loss, params, create_graph=self.training, allow_unused=True)
+            else:
+                addr_grads = [None] * len(params)
+            (mem_grad,) = torch.autograd.grad(mem_loss, fw_named_params["values"], create_graph=self.training)
+            grads = [mem_grad if n == "values" else addr_grads[i] for i, n in enumerate(names)]
+        else:
+            loss = mem_loss if addr_loss is None else mem_loss + addr_loss
+            grads = list(torch.autograd.grad(loss, params, create_graph=self.training))
+        # the value gradient is a sum over samples, features, heads and top-k,
+        # shared out over the times each slot was read
+        for i, n in enumerate(names):
+            if n == "values":
+                g = grads[i] * (num_samples * self.v_dim * self.topk * self.heads)
+                counts = torch.bincount(indices.reshape(-1), minlength=self.size).to(g.dtype)
+                counts = torch.where(counts == 0, torch.ones_like(counts), counts)
+                grads[i] = g / counts.unsqueeze(-1)
+        used = [torch.clamp(g, min=-1.0, max=1.0) for g in grads] if self.grad_clip else grads
+        updated = OrderedDict(
+            (n, self.update_fw_param(params[i], used[i], self.learning_rate, self.weight_decay))
+            for i, n in enumerate(names))
+        return updated, grads
+
+    def write_ob_log(self, token_ids, indices, scores):
+        """Per-slot observation log (``fwpkm/fwpkm.py:369-393``), host-side."""
+        assert self.ob_mode
+        B, T = token_ids.shape
+        ids = token_ids.tolist()
+        for b in range(B):
+            for t in range(T - self.lookahead):
+                q_id = ids[b][t]
+                v_id = ids[b][t + self.lookahead]
+                lo = max(0, t + self.lookahead - 10)
+                hi = min(T, t + self.lookahead + 10)
+                prev = ids[b][lo:t + self.lookahead]
+                nxt = ids[b][t + self.lookahead + 1:hi]
+                for htk in range(self.heads * self.topk):
+                    entry = (q_id, v_id, prev, nxt, scores[b, t, htk].item())
+                    self.ob_idx2log[indices[b, t, htk].item()].append(entry)
+
+    # ------------------------------------------------------------------
+    # chunked forward
+    # ------------------------------------------------------------------
+    def _lookahead_target(self, ref):
+        """Targets shifted by ``lookahead`` tokens (``fwpkm/fwpkm.py:472-480``)."""
+        return ref if self.lookahead == 0 else ref[:, self.lookahead:]
+
+    def forward_wo_past(self, q, ref_v, chunk_size, gates=None, loss_mask=None, token_ids=None):
+        B, T = q.shape[:2]
+        input_dtype = q.dtype
+        if self.fp32_fw:
+            q = q.float()
+            ref_v = ref_v.float()
+        cut = None if self.lookahead == 0 else -self.lookahead
+        all_grads, output, losses, indices, scores = [], [], [], [], []
+        addr_losses = [] if self.addr_loss is not None else None
+        with torch.enable_grad():
+            fw_params = [self.get_fw_named_params()]
+            for c0 in range(0, T, chunk_size):
+                c1 = min(c0 + chunk_size, T)
+                cT = c1 - c0
+                cq = q[:, c0:c1].contiguous()
+                cref = ref_v[:, c0:c1].contiguous()
+                cgates = gates[:, c0:c1].contiguous() if gates is not None else None
+                cmask = loss_mask[:, c0:c1].contiguous() if loss_mask is not None else None
+                cids = token_ids[:, c0:c1].contiguous() if token_ids is not None else None
+                cur = fw_params[-1]
+                r = self.retrieve_values(cq, cur)
+                hyp = r["retireved_values"].view(B, cT, -1)
+                output.append(hyp)
+                indices.append(r["indices"].view(B, cT, -1))
+                scores.append(r["normed_scores"].view(B, cT, -1))
+                upd_hyp = hyp[:, :cut].contiguous()
+                upd_w = cgates[:, :cut].contiguous() if cgates is not None else None
+                upd_mask = cmask[:, :cut].contiguous() if cmask is not None else None
+                upd_ref = self._lookahead_target(cref).contiguous()
+                mem_losses = self.compute_mem_loss(
+                    upd_hyp.view(-1, upd_hyp.size(-1)), upd_ref.view(-1, upd_ref.size(-1)),
+                    loss_mask=upd_mask.view(-1) if upd_mask is not None else None,
+                    loss_weights=upd_w.view(-1) if upd_w is not None else None)
+                addr_loss = self.compute_addr_loss(r["sub_indices1"], r["sub_indices2"], r["all_sub_scores1"],
+                                                   r["all_sub_scores2"])
+                num_samples = (upd_mask > 0).sum().item() if upd_mask is not None else B * cT
+                new_params, grads = self.update_fw(cur, num_samples, r["indices"], mem_losses.mean(), addr_loss)
+                if self.ob_mode:
+                    self.write_ob_log(cids.view(B, cT), r["indices"].view(B, cT, -1), cgates.view(B, cT, -1))
+                all_grads.append([g.detach() for g in grads])
+                fw_params.append(new_params)
+                losses.append(mem_losses.view(B, -1).detach())
+                if addr_losses is not None:
+                    addr_losses.append(addr_loss.detach())
+        output = torch.cat(output, dim=1)
+        indices = torch.cat(indices, dim=1).view(B, T, self.heads, self.topk)
+        scores = torch.cat(scores, dim=1).view(B, T, self.heads, self.topk)
+        losses = torch.cat(losses, dim=1)
+        addr_loss = torch.stack(addr_losses).mean() if addr_losses is not None else None
+        with torch.no_grad():
+            grad_norms = [torch.stack([g[i].norm() for g in all_grads]).mean() for i in range(len(fw_params[0]))]
+            final = fw_params[-1]
+            for n, p in self.named_parameters():
+                if n in final:
+                    p.data.copy_(final[n].data.to(p.dtype))
+        return {
+            "output": output.to(input_dtype),
+            "indices": indices,
+            "scores": scores,
+            "losses": losses,
+            "addr_loss": addr_loss,
+            "grad_norms": grad_norms,
+            "past_key_values": None,
+        }
+
+    def forward_w_past(self, q, ref_v, gates, chunk_size, loss_mask=None, past_key_values=None, token_ids=None):
+        """Streaming read/update with a carried signal queue (``fwpkm/fwpkm.py:560-820``)."""
+        B, T = q.shape[:2]
+        input_dtype = q.dtype
+        if self.fp32_fw:
+            q = q.float()
+            ref_v = ref_v.float()
+        dev, dt = ref_v.device, ref_v.dtype
+
+        def empty(width=None, dtype=dt):
+            return torch.zeros(B, 0, width, device=dev, dtype=dtype) if width else torch.zeros(B, 0, device=dev,
+                                                                                               dtype=dtype)
+
+        q_queue, hyp_queue, ref_queue = empty(q.size(-1)), empty(ref_v.size(-1)), empty(ref_v.size(-1))
+        gates_queue = empty() if gates is not None else None
+        mask_queue = empty() if loss_mask is not None else None
+        ids_queue = empty(dtype=torch.long) if token_ids is not None else None
+        if past_key_values is not None:
+            pq, ph, pr, pg, pm, pi = past_key_values
+            if ph is not None:
+                assert ph.size(1) < chunk_size + self.lookahead, (
+                    f"Past key values length {ph.size(1)} longer than chunk size + lookahead "
+                    f"({chunk_size} + {self.lookahead}).")
+                q_queue = torch.cat([pq, q_queue], 1)
+                hyp_queue = torch.cat([ph, hyp_queue], 1)
+                ref_queue = torch.cat([pr, ref_queue], 1)
+                gates_queue = torch.cat([pg, gates_queue], 1) if gates is not None else None
+                mask_queue = torch.cat([pm, mask_queue], 1) if loss_mask is not None else None
+                ids_queue = torch.cat([pi, ids_queue], 1) if token_ids is not None else None
+        first_end = min(chunk_size + self.lookahead - ref_queue.size(1), T)
+        bounds = [(0, first_end)] + [(s, min(s + chunk_size, T)) for s in range(first_end, T, chunk_size)]
+        cut = None if self.lookahead == 0 else -self.lookahead
+        updated = False
+        cur = self.get_fw_named_params()
+        output, losses, indices, scores = [], [], [], []
+        addr_losses = [] if self.addr_loss is not None else None
+        mem_losses = addr_loss = update_mask = None
+        for c0, c1 in bounds:
+            cT = c1 - c0
+            cq = q[:, c0:c1].contiguous()
+            cref = ref_v[:, c0:c1].contiguous()
+            cgates = gates[:, c0:c1].contiguous() if gates is not None else None
+            cmask = loss_mask[:, c0:c1].contiguous() if loss_mask is not None else None
+            cids = token_ids[:, c0:c1].contiguous() if token_ids is not None else None
+            r = self.retrieve_values(cq, cur)
+            hyp = r["retireved_values"].view(B, cT, -1)
+            chunk_indices = r["indices"]
+            output.append(hyp)
+            indices.append(chunk_indices.view(B, cT, -1))
+            scores.append(r["normed_scores"].view(B, cT, -1))
+            q_queue = torch.cat([q_queue, cq], 1)
+            hyp_queue = torch.cat([hyp_queue, hyp], 1)
+            ref_queue = torch.cat([ref_queue, cref], 1)
+            gates_queue = torch.cat([gates_queue, cgates], 1) if gates is not None else None
+            mask_queue = torch.cat([mask_queue, cmask], 1) if loss_mask is not None else None
+            ids_queue = torch.cat([ids_queue, cids], 1) if token_ids is not None else None
+            if past_key_values and hyp_queue.size(1) < chunk_size:
+                continue
+            updated = True
+            with torch.enable_grad():
+                cur = {n: p.detach() for n, p in cur.items()}
+                for p in cur.values():
+                    p.requires_grad = True
+                rb = self.retrieve_values(q_queue[:, :cut].contiguous(), cur)
+                update_hyp = rb["retireved_values"].contiguous()
+                update_w = gates_queue[:, :cut].contiguous() if gates_queue is not None else None
+                update_mask = mask_queue[:, :cut].contiguous() if mask_queue is not None else None
+                update_ref = self._lookahead_target(ref_queue).contiguous()
+                mem_losses = self.compute_mem_loss(
+                    update_hyp.view(-1, update_hyp.size(-1)), update_ref.view(-1, update_ref.size(-1)),
+                    loss_mask=update_mask.view(-1) if update_mask is not None else None,
+                    loss_weights=update_w.view(-1) if update_w is not None else None)
+                addr_loss = self.compute_addr_loss(rb["sub_indices1"], rb["sub_indices2"], rb["all_sub_scores1"],
+                                                   rb["all_sub_scores2"])
+                num_samples = (update_mask > 0).sum().item() if update_mask is not None else B * cT
+                cur, _ = self.update_fw(cur, num_samples, chunk_indices, mem_losses.mean(), addr_loss)
+                if self.ob_mode:
+                    pad = torch.zeros(B, self.lookahead, self.heads * self.topk, device=dev,
+                                      dtype=rb["indices"].dtype)
+                    idx_p = torch.cat([rb["indices"].view(B, ids_queue.size(1) - self.lookahead, -1), pad], 1)
+                    sc_p = torch.cat([rb["scores"].view(B, ids_queue.size(1) - self.lookahead, -1),
+                                      pad.to(rb["scores"].dtype)], 1)
+                    self.write_ob_log(ids_queue, idx_p, sc_p)
+            if self.lookahead == 0:
+                q_queue, hyp_queue, ref_queue = empty(q.size(-1)), empty(ref_v.size(-1)), empty(ref_v.size(-1))
+                gates_queue = empty() if gates is not None else None
+                mask_queue = empty() if loss_mask is not None else None
+                ids_queue = empty(dtype=torch.long)
+            else:
+                keep = slice(-self.lookahead, None)
+                q_queue = q_queue[:, keep].contiguous()
+                hyp_queue = hyp_queue[:, keep].contiguous()
+                ref_queue = ref_queue[:, keep].contiguous()
+                gates_queue = gates_queue[:, keep].contiguous() if gates is not None else None
+                mask_queue = mask_queue[:, keep].contiguous() if update_mask is not None else None
+                ids_queue = ids_queue[:, keep].contiguous() if ids_queue is not None else None
+            losses.append(mem_losses.view(B, -1).detach())
+            if addr_losses is not None:
+                addr_losses.append(addr_loss.detach())
+        output = torch.cat(output, 1)
+        indices = torch.cat(indices, 1).view(B, T, self.heads, self.topk)
+        scores = torch.cat(scores, 1).view(B, T, self.heads, self.topk)
+        past = (q_queue, hyp_queue, ref_queue, gates_queue, mask_queue, ids_queue)
+        if updated:
+            losses = torch.cat(losses, 1)
+            addr_out = torch.stack(addr_losses).mean() if addr_losses is not None else None
+            with torch.no_grad():
+                for n, p in self.named_parameters():
+                    if n in cur:
+                        p.data.copy_(cur[n].data.to(p.dtype))
+        else:
+            losses = None
+            addr_out = None
+        return {
+            "output": output.to(input_dtype),
+            "indices": indices,
+            "scores": scores,
+            "losses": losses,
+            "addr_loss": addr_out,
+            "grad_norms": None,
+            "past_key_values": past,
+        }
+
+    @torch.compiler.disable(recursive=True)
+    def forward(self, q, ref_v, gates, chunk_size, loss_mask=None, past_key_values=None, token_ids=None):
+        if past_key_values is None:
+            return self.forward_wo_past(q=q, ref_v=ref_v, gates=gates, chunk_size=chunk_size, loss_mask=loss_mask,
+                                        token_ids=token_ids)
+        return self.forward_w_past(q=q, ref_v=ref_v, gates=gates, chunk_size=chunk_size, loss_mask=loss_mask,
+                                   past_key_values=past_key_values, token_ids=token_ids)
+
+    def compute_qk_scores(self, q, k):
+        """Scores ``(batch, heads, n_keys)`` of queries ``(batch, heads, d)``
+        against keys ``(heads, n_keys, d)`` (``fwpkm/fwpkm.py:853-869``)."""
+        if self.qk_score_type == "dot_product":
+            return torch.einsum("bhd,hnd->bhn", q, k)
+        if self.qk_score_type == "idw":
+            d = torch.cdist(q.permute(1, 0, 2), k, p=2, compute_mode="use_mm_for_euclid_dist").permute(1, 0, 2)
+            return -torch.log(1e-3 + d.pow(2))
+        raise NotImplementedError(f"QK score type {self.qk_score_type} not implemented.")
+
+    def get_indices(self, query: torch.Tensor, keys: torch.Tensor):
+        """``(scores, indices, topk_indices1, topk_indices2, scores1, scores2)``
+        for queries ``(BT, heads, k_dim)`` (``fwpkm/fwpkm.py:871-934``)."""
+        if self.qk_score_type not in ("dot_product", "idw"):
+            raise NotImplementedError(f"QK score type {self.qk_score_type} not implemented.")
+        topk, H, n = self.topk, self.heads, self.subsize
+        BT = query.size(0)
+        q2 = query.reshape(BT * H, self.k_dim)
+        if keys.dtype != q2.dtype:
+            keys = keys.to(q2.dtype)
+        mode = "dot" if self.qk_score_type == "dot_product" else "idw"
+        s_all = SubkeyScores.apply(q2, keys, H, mode)  # [BT*H, 2, n]
+        with torch.no_grad():
+            idx, _, _, sub1, sub2 = _native.product_topk(s_all.detach(), topk, want_sub=True)
+        scores1 = s_all[:, 0].view(BT, H, n)
+        scores2 = s_all[:, 1].view(BT, H, n)
+        iv = idx.view(BT, H, topk)
+        scores = scores1.gather(2, iv // n) + scores2.gather(2, iv % n)
+        assert scores.shape == iv.shape == (BT, H, topk)
+        return (scores.contiguous(), iv.contiguous(), sub1.view(BT, H, topk), sub2.view(BT, H, topk),
+                scores1.contiguous(), scores2.contiguous())
