@@ -113,7 +113,9 @@ PKM_API int pkm_bag_bwd2(const int64_t* indices, const void* a, int a_dtype, con
  * K1 - sub-key scores for both halves of every (token, head) query.
  *   scores[r, p, m] = score(query[r, p*half:(p+1)*half], keys[(h*2+p)*n + m])
  * with r = token*heads + h.  mode 0: dot product (pkm/memory.py:267-268,
- * fwpkm/fwpkm.py:861); mode 1: idw, -log(1e-3 + |q-k|^2) (fwpkm/fwpkm.py:862-866).
+ * fwpkm/fwpkm.py:861); mode 1: idw, -log(1e-3 + |q-k|^2) (fwpkm/fwpkm.py:862-866);
+ * mode 2: the distance |q-k| = sqrt(max(|q|^2 - 2 q.k + |k|^2, 1e-30)) that
+ * torch.cdist(..., compute_mode="use_mm_for_euclid_dist") returns.
  * fp32 inputs use a sequential fp32 sum without fused multiply-add (the
  * oracle's definition); bf16 inputs accumulate in fp32 and round to bf16.
  * query and keys must share a dtype; scores has that dtype.

@@ -289,7 +289,7 @@ def subkey_scores(query: torch.Tensor, keys: torch.Tensor, heads: int, mode: str
     n = keys.shape[0] // (2 * heads)
     out = torch.empty((NH, 2, n), dtype=query.dtype, device=query.device)
     rc = lib().pkm_subkey_scores(_ptr(query), _ptr(keys), DT[query.dtype], NH // heads, heads, kd, n,
-                                 {"dot": 0, "idw": 1}[mode], _ptr(out), _stream(query.device))
+                                 {"dot": 0, "idw": 1, "dist": 2}[mode], _ptr(out), _stream(query.device))
     _check(rc, "pkm_subkey_scores")
     return out
 

@@ -1,7 +1,8 @@
 // Sub-key scores (K1), SIMT path.
 //
 // scores[r, p, m] = <query[r, p*half : (p+1)*half], keys[(h*2+p)*n + m]>,
-// r = token*heads + h, for the dot and idw score types.  Every score is a
+// r = token*heads + h, for the dot and idw score types (and the plain
+// Euclidean distance the idw score is built from).  Every score is a
 // sequential fp32 sum over the half dimension in ascending order; for fp32
 // inputs products and sums are rounded separately (no fused multiply-add),
 // which is the oracle's definition and makes top-k indices bit-exact.
@@ -75,7 +76,7 @@ __global__ void __launch_bounds__(256) subkey_scores_kernel(const T* __restrict_
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], b[j]));
-      if (MODE == 1) {
+      if (MODE >= 1) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) qq[i] = __fadd_rn(qq[i], __fmul_rn(a[i], a[i]));
 #pragma unroll
@@ -94,12 +95,16 @@ __global__ void __launch_bounds__(256) subkey_scores_kernel(const T* __restrict_
       const int m = m0 + tx * 4 + j;
       if (m >= n) continue;
       float s = acc[i][j];
-      if (MODE == 1) {
+      if (MODE >= 1) {
         float rr = __fadd_rn(__fsub_rn(qq[i], __fmul_rn(2.f, s)), kk[j]);
         rr = fmaxf(rr, 1e-30f);
         const float d = __fsqrt_rn(rr);
-        const float t2 = __fadd_rn(1e-3f, __fmul_rn(d, d));
-        s = -(float)log((double)t2);
+        if (MODE == 1) {
+          const float t2 = __fadd_rn(1e-3f, __fmul_rn(d, d));
+          s = -(float)log((double)t2);
+        } else {
+          s = d;  // the Euclidean distance itself
+        }
       }
       const int64_t o = (r * 2 + p) * (int64_t)n + m;
       if (sizeof(T) == 4)
@@ -119,7 +124,7 @@ extern "C" int pkm_subkey_scores(const void* query, const void* keys, int dtype,
   if (dtype != PKM_DT_F32 && dtype != PKM_DT_BF16) return fail(PKM_ERR_UNSUPPORTED, "dtype must be f32 or bf16");
   if (n_tokens < 0 || heads <= 0 || k_dim < 2 || (k_dim & 1) || n_keys <= 0)
     return fail(PKM_ERR_INVALID_ARG, "bad size (k_dim must be even)");
-  if (mode != 0 && mode != 1) return fail(PKM_ERR_INVALID_ARG, "mode must be 0 (dot) or 1 (idw)");
+  if (mode < 0 || mode > 2) return fail(PKM_ERR_INVALID_ARG, "mode must be 0 (dot), 1 (idw) or 2 (distance)");
   if (heads * 2 > 65535) return fail(PKM_ERR_UNSUPPORTED, "too many heads");
   if (n_tokens == 0) return PKM_OK;
   if (!query || !keys || !scores) return fail(PKM_ERR_INVALID_ARG, "NULL pointer");
@@ -133,13 +138,17 @@ extern "C" int pkm_subkey_scores(const void* query, const void* keys, int dtype,
   if (dtype == PKM_DT_F32) {
     if (mode == 0)
       PKM_SC(float, 0);
-    else
+    else if (mode == 1)
       PKM_SC(float, 1);
+    else
+      PKM_SC(float, 2);
   } else {
     if (mode == 0)
       PKM_SC(__nv_bfloat16, 0);
-    else
+    else if (mode == 1)
       PKM_SC(__nv_bfloat16, 1);
+    else
+      PKM_SC(__nv_bfloat16, 2);
   }
 #undef PKM_SC
   return check_cuda("subkey_scores_kernel");

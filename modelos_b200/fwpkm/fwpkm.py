@@ -11,9 +11,10 @@ loss back-propagates through every update (``forward_wo_past``, ``:395-558``).
 
 Kernel mapping:
 
-* sub-key scores, dot or idw (K1, ``pkm_subkey_scores``), bit-exact in fp32;
-  their backward is written with differentiable tensor ops so second
-  derivatives exist for the inner updates;
+* sub-key scores, dot or idw (K1, ``pkm_subkey_scores``; idw is built from
+  the distance mode), bit-exact in fp32; their backward is written with
+  differentiable tensor ops so second derivatives exist for the inner
+  updates, and reads the same saved tensors as the reference's autograd;
 * dual / cartesian top-k (K2, ``pkm_product_topk``), ties to the lowest index;
 * the bag forward, its sorted-segment backward and the double-backward
   (K3 / K4 / K5, through ``xformer_embeddingbag_grad_wrapper``).
@@ -42,21 +43,19 @@ def l2norm(x: torch.FloatTensor, dim: int = -1, eps: float = 1e-6):
 
 
 class SubkeyScores(torch.autograd.Function):
-    """All sub-key scores ``[R, 2, n]`` of queries ``[R, k_dim]``.
+    """Dot-product sub-key scores ``[R, 2, n]`` of queries ``[R, k_dim]``
+    (``fwpkm/fwpkm.py:861``).
 
-    Forward: the sequential-sum kernel (dot, or idw = -log(1e-3 + |q-k|^2),
-    ``fwpkm/fwpkm.py:853-869``).  Backward: the analytic gradient in tensor
-    ops on the saved inputs, hence itself differentiable (the inner updates
-    take gradients with ``create_graph=True``).  For idw with
-    ``r = |q|^2 + |k|^2 - 2 q.k``: ``ds/dr = -1 / (1e-3 + r)`` while
-    ``r > 1e-30`` (the clamp of torch's cdist), ``dr/dq = 2(q - k)``.
-    """
+    Forward: the sequential-sum kernel.  Backward: two einsums on the saved
+    query and keys, like the reference's einsum backward, and itself
+    differentiable (the inner updates take gradients with
+    ``create_graph=True``)."""
 
     @staticmethod
-    def forward(ctx, query, keys, heads, mode):
-        s = _native.subkey_scores(query.contiguous(), keys.contiguous(), heads, mode)
+    def forward(ctx, query, keys, heads):
+        s = _native.subkey_scores(query.contiguous(), keys.contiguous(), heads, "dot")
         ctx.save_for_backward(query, keys)
-        ctx.heads, ctx.mode = heads, mode
+        ctx.heads = heads
         return s
 
     @staticmethod
@@ -66,22 +65,59 @@ class SubkeyScores(torch.autograd.Function):
         R, kd = q.shape
         half = kd // 2
         n = k.shape[0] // (2 * H)
-        N = R // H
-        qv = q.view(N, H, 2, half)
+        d = dS.view(R // H, H, 2, n)
+        dq = torch.einsum("thpn,hpnd->thpd", d, k.view(H, 2, n, half))
+        dk = torch.einsum("thpn,thpd->hpnd", d, q.view(R // H, H, 2, half))
+        return dq.reshape(R, kd), dk.reshape(k.shape), None
+
+
+class SubkeyDist(torch.autograd.Function):
+    """Euclidean distances ``[R, 2, n]`` between query halves and sub-keys,
+    ``sqrt(max(|q|^2 - 2 q.k + |k|^2, 1e-30))`` as torch's ``cdist`` with
+    ``use_mm_for_euclid_dist`` (``fwpkm/fwpkm.py:864``).
+
+    Backward follows that op's own derivative: with ``ratio = grad / dist``,
+    ``dq = q * sum(ratio) - ratio @ k`` and ``dk = k * sum(ratio) - ratio^T @ q``,
+    using the saved distances and the saved query/keys tensors, so it reads
+    exactly what the reference's autograd reads."""
+
+    @staticmethod
+    def forward(ctx, query, keys, heads):
+        dist = _native.subkey_scores(query.contiguous(), keys.contiguous(), heads, "dist")
+        ctx.save_for_backward(query, keys, dist)
+        ctx.heads = heads
+        return dist
+
+    @staticmethod
+    def backward(ctx, grad):
+        q, k, dist = ctx.saved_tensors
+        H = ctx.heads
+        R, kd = q.shape
+        half = kd // 2
+        n = k.shape[0] // (2 * H)
+        ratio = (grad / dist).view(R // H, H, 2, n)
+        qv = q.view(R // H, H, 2, half)
         kv = k.view(H, 2, n, half)
-        d = dS.view(N, H, 2, n)
-        if ctx.mode == "dot":
-            dq = torch.einsum("thpn,hpnd->thpd", d, kv)
-            dk = torch.einsum("thpn,thpd->hpnd", d, qv)
-        else:
-            qk = torch.einsum("thpd,hpnd->thpn", qv, kv)
-            qq = (qv * qv).sum(-1, keepdim=True)
-            kk = (kv * kv).sum(-1)
-            r = qq - 2 * qk + kk.unsqueeze(0)
-            w = torch.where(r > 1e-30, -d / (1e-3 + r), torch.zeros_like(r))
-            dq = 2 * (w.sum(-1, keepdim=True) * qv - torch.einsum("thpn,hpnd->thpd", w, kv))
-            dk = 2 * (w.sum(0).unsqueeze(-1) * kv - torch.einsum("thpn,thpd->hpnd", w, qv))
-        return dq.reshape(R, kd), dk.reshape(k.shape), None, None
+        dq = qv * ratio.sum(-1, keepdim=True) - torch.einsum("thpn,hpnd->thpd", ratio, kv)
+        dk = kv * ratio.sum(0).unsqueeze(-1) - torch.einsum("thpn,thpd->hpnd", ratio, qv)
+        return dq.reshape(R, kd), dk.reshape(k.shape), None
+
+
+class IdwScore(torch.autograd.Function):
+    """``-log(1e-3 + dist^2)`` (``fwpkm/fwpkm.py:866``); the log is taken in
+    fp64 and rounded, the oracle's definition, and the backward is
+    ``-grad / (1e-3 + dist^2) * 2 dist`` in differentiable tensor ops."""
+
+    @staticmethod
+    def forward(ctx, dist):
+        t = 1e-3 + dist * dist
+        ctx.save_for_backward(dist)
+        return (-torch.log(t.double())).to(dist.dtype)
+
+    @staticmethod
+    def backward(ctx, grad):
+        (dist,) = ctx.saved_tensors
+        return (-grad / (1e-3 + dist.pow(2))) * (2 * dist)
 
 
 class FastWeightProductKeyMemory(nn.Module):
@@ -235,9 +271,12 @@ class FastWeightProductKeyMemory(nn.Module):
                 counts = torch.bincount(indices.reshape(-1), minlength=self.size).to(g.dtype)
                 counts = torch.where(counts == 0, torch.ones_like(counts), counts)
                 grads[i] = g / counts.unsqueeze(-1)
-        used = [torch.clamp(g, min=-1.0, max=1.0) for g in grads] if self.grad_clip else grads
+        used = [None if g is None else (torch.clamp(g, min=-1.0, max=1.0) if self.grad_clip else g) for g in grads]
+        # a parameter without a gradient (keys when there is no addressing
+        # loss) is left as it is; the reference fails with a TypeError there
         updated = OrderedDict(
-            (n, self.update_fw_param(params[i], used[i], self.learning_rate, self.weight_decay))
+            (n, params[i] if used[i] is None else
+             self.update_fw_param(params[i], used[i], self.learning_rate, self.weight_decay))
             for i, n in enumerate(names))
         return updated, grads
 
@@ -304,7 +343,7 @@ class FastWeightProductKeyMemory(nn.Module):
                 new_params, grads = self.update_fw(cur, num_samples, r["indices"], mem_losses.mean(), addr_loss)
                 if self.ob_mode:
                     self.write_ob_log(cids.view(B, cT), r["indices"].view(B, cT, -1), cgates.view(B, cT, -1))
-                all_grads.append([g.detach() for g in grads])
+                all_grads.append([None if g is None else g.detach() for g in grads])
                 fw_params.append(new_params)
                 losses.append(mem_losses.view(B, -1).detach())
                 if addr_losses is not None:
@@ -315,7 +354,8 @@ class FastWeightProductKeyMemory(nn.Module):
         losses = torch.cat(losses, dim=1)
         addr_loss = torch.stack(addr_losses).mean() if addr_losses is not None else None
         with torch.no_grad():
-            grad_norms = [torch.stack([g[i].norm() for g in all_grads]).mean() for i in range(len(fw_params[0]))]
+            grad_norms = [torch.stack([g[i].norm() if g[i] is not None else torch.zeros((), device=q.device)
+                                       for g in all_grads]).mean() for i in range(len(fw_params[0]))]
             final = fw_params[-1]
             for n, p in self.named_parameters():
                 if n in final:
@@ -481,8 +521,15 @@ class FastWeightProductKeyMemory(nn.Module):
         q2 = query.reshape(BT * H, self.k_dim)
         if keys.dtype != q2.dtype:
             keys = keys.to(q2.dtype)
-        mode = "dot" if self.qk_score_type == "dot_product" else "idw"
-        s_all = SubkeyScores.apply(q2, keys, H, mode)  # [BT*H, 2, n]
+        if self.qk_score_type == "dot_product":
+            s_all = SubkeyScores.apply(q2, keys, H)  # [BT*H, 2, n]
+        else:
+            # The reference's cdist backward works on its own copy of the keys,
+            # so an in-place overwrite of the key parameter after the forward
+            # (the write-back at the end of ``forward_wo_past``, which aliases
+            # the first chunk's fast weights when they are fp32) does not reach
+            # it; the clone gives the same behaviour.
+            s_all = IdwScore.apply(SubkeyDist.apply(q2, keys.clone(), H))
         with torch.no_grad():
             idx, _, _, sub1, sub2 = _native.product_topk(s_all.detach(), topk, want_sub=True)
         scores1 = s_all[:, 0].view(BT, H, n)

@@ -124,15 +124,18 @@ def subkey_scores(query: np.ndarray, keys: np.ndarray, heads: int, mode: str = "
             kb = kv[h, p]
             if mode == "dot":
                 s = _seq_dot(qa, kb)
-            elif mode == "idw":
+            elif mode in ("idw", "dist"):
                 qk = _seq_dot(qa, kb)
                 qq = _seq_sqnorm(qa)
                 kk = _seq_sqnorm(kb)
                 r = (qq[:, None] - np.float32(2.0) * qk) + kk[None, :]
                 r = np.maximum(r, np.float32(1e-30))
                 d = np.sqrt(r)
-                t = np.float32(1e-3) + d * d
-                s = -(np.log(t.astype(np.float64)).astype(np.float32))
+                if mode == "dist":
+                    s = d
+                else:
+                    t = np.float32(1e-3) + d * d
+                    s = -(np.log(t.astype(np.float64)).astype(np.float32))
             else:
                 raise ValueError(mode)
             out[:, h, p, :] = _round_to(s, bf16)

@@ -1,0 +1,95 @@
+"""CPU stand-in for ``modelos_b200._native`` (test infrastructure only).
+
+Implements the tensor-level wrappers with torch CPU ops and the numpy oracle
+so the host-side module logic (autograd wiring, chunk loop, update rule) can
+be exercised without a GPU.  Tests install it with ``monkeypatch``; the
+product package never imports it.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from oracle import pkm_oracle as po
+
+DEVERR_INDEX = 1
+DEVERR_TIMEOUT = 2
+
+
+def bag_fwd(indices, weight, psw, out_dtype=None):
+    rows = weight.double()[indices]
+    w = torch.ones(indices.shape, dtype=torch.float64) if psw is None else psw.double()
+    return (w[..., None] * rows).sum(1).to(out_dtype or weight.dtype)
+
+
+def bag_bwd(indices, weight, psw, grad_out, *, num_rows=None, need_dpsw=True, want_counts=False,
+            grad_weight_dtype=None):
+    K = weight.shape[0] if weight is not None else num_rows
+    D = grad_out.shape[1]
+    g = grad_out.double()
+    w = torch.ones(indices.shape, dtype=torch.float64) if psw is None else psw.double()
+    dW = torch.zeros(K, D, dtype=torch.float64)
+    dW.index_add_(0, indices.reshape(-1), (w[..., None] * g[:, None, :]).reshape(-1, D))
+    dpsw = None
+    if need_dpsw and psw is not None:
+        dpsw = (weight.double()[indices] * g[:, None, :]).sum(-1).to(psw.dtype)
+    counts = torch.bincount(indices.reshape(-1), minlength=K).int() if want_counts else None
+    dt = grad_weight_dtype or (weight.dtype if weight is not None else grad_out.dtype)
+    return dW.to(dt), dpsw, counts
+
+
+def bag_bwd2(indices, a, gbar, grad_out, *, d_grad_out_dtype=None, d_a_dtype=None):
+    rows = gbar.double()[indices]
+    w = torch.ones(indices.shape, dtype=torch.float64) if a is None else a.double()
+    dgo = (w[..., None] * rows).sum(1).to(d_grad_out_dtype or grad_out.dtype)
+    da = None
+    if a is not None:
+        da = (rows * grad_out.double()[:, None, :]).sum(-1).to(d_a_dtype or a.dtype)
+    return dgo, da
+
+
+def subkey_scores(query, keys, heads, mode="dot"):
+    bf16 = query.dtype == torch.bfloat16
+    s = po.subkey_scores(query.float().numpy(), keys.float().numpy(), heads, mode=mode, bf16=bf16)
+    return torch.from_numpy(s).to(query.dtype)
+
+
+def product_topk(scores, knn, want_psw=False, want_sub=False):
+    bf16 = scores.dtype == torch.bfloat16
+    r = po.product_topk(scores.float().numpy(), knn, bf16=bf16)
+    idx = torch.from_numpy(r["indices"]).long()
+    top = torch.from_numpy(r["scores"]).to(scores.dtype)
+    psw = torch.from_numpy(po.softmax_rows(r["scores"], bf16=bf16)).to(scores.dtype) if want_psw else None
+    s1 = torch.from_numpy(r["sub_indices1"]).long() if want_sub else None
+    s2 = torch.from_numpy(r["sub_indices2"]).long() if want_sub else None
+    return idx, top, psw, s1, s2
+
+
+def score_grad_dense(indices, psw, dpsw, n_keys):
+    d = dpsw.float()
+    if psw is not None:
+        p = psw.float()
+        d = p * (d - (p * d).sum(-1, keepdim=True))
+    d = d.to(dpsw.dtype).float()
+    R = indices.shape[0]
+    out = torch.zeros(R, 2, n_keys)
+    out[:, 0].scatter_add_(1, indices // n_keys, d)
+    out[:, 1].scatter_add_(1, indices % n_keys, d)
+    return out.to(dpsw.dtype)
+
+
+def read_device_errors(dev=None, reset=True):
+    return 0
+
+
+def check_device_errors(dev=None):
+    return None
+
+
+def install(monkeypatch):
+    """Route ``modelos_b200._native`` calls to this module for one test."""
+    from modelos_b200 import _native
+    for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense",
+                 "read_device_errors", "check_device_errors"):
+        monkeypatch.setattr(_native, name, globals()[name])
+    return np
