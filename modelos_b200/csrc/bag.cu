@@ -19,12 +19,16 @@ static int max_dyn_smem() {
   return v;
 }
 
-// Ring depth and per-warp shared-memory stride for rows of rb bytes.
-static bool gather_geometry(int64_t rb, int* slots, int64_t* warp_smem) {
-  const int64_t budget = (int64_t)(max_dyn_smem() - 1024) / kGatherWarps;
-  for (int p = 32; p >= 1; --p) {
+// Ring depth and per-warp shared-memory stride for rows of rb bytes with nw
+// warps per block (segment mode adds the item-descriptor ring, and the dot
+// vector ring when dots are requested).
+static bool gather_geometry(int64_t rb, int nw, bool seg, bool dot, int* slots, int64_t* warp_smem) {
+  const int64_t budget = (int64_t)(max_dyn_smem() - 1024) / nw;
+  const int64_t dvb = (seg && dot) ? (((int64_t)kDvSlots * rb + 127) & ~(int64_t)127) : 0;
+  const int64_t fixed = dvb + kMetaRing * 12 + (seg ? kMetaRing * 16 : 0) + kDvSlots * 8;
+  for (int p = 32; p >= 2; --p) {
     int64_t ring = ((int64_t)p * rb + 127) & ~(int64_t)127;
-    int64_t tot = ring + kMetaRing * 12 + (int64_t)p * 8;
+    int64_t tot = ring + fixed + (int64_t)p * 8;
     tot = (tot + 127) & ~(int64_t)127;
     if (tot <= budget) {
       *slots = p;
@@ -35,30 +39,38 @@ static bool gather_geometry(int64_t rb, int* slots, int64_t* warp_smem) {
   return false;
 }
 
-template <typename RowT, int VPL, int MODE, bool DOT>
+template <typename RowT, int VPL, int MODE, bool DOT, bool FULL>
 static int launch_one(GatherArgs a, int64_t items_upper, cudaStream_t st) {
+  constexpr int NW = DOT ? 12 : 16;
   int slots;
   int64_t ws;
-  if (!gather_geometry(a.row_bytes, &slots, &ws)) return fail(PKM_ERR_UNSUPPORTED, "row too large for the gather ring");
+  if (!gather_geometry(a.row_bytes, NW, MODE == G_SEG, DOT, &slots, &ws))
+    return fail(PKM_ERR_UNSUPPORTED, "row too large for the gather ring");
   a.slots = slots;
   a.warp_smem = ws;
-  const int smem = (int)(ws * kGatherWarps);
-  auto kern = gather_kernel<RowT, VPL, MODE, DOT>;
+  const int smem = (int)(ws * NW);
+  auto kern = gather_kernel<RowT, VPL, MODE, DOT, NW, FULL>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return check_cuda("cudaFuncSetAttribute(gather)");
-  int64_t blocks = (items_upper + kGatherWarps - 1) / kGatherWarps;
+  int64_t blocks = (items_upper + NW - 1) / NW;
   blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, num_sms()));
-  kern<<<(unsigned)blocks, kGatherWarps * 32, smem, st>>>(a);
+  kern<<<(unsigned)blocks, NW * 32, smem, st>>>(a);
   return check_cuda("gather_kernel");
+}
+
+template <typename RowT, int VPL, int MODE, bool DOT>
+static int launch_full(GatherArgs a, int64_t items_upper, cudaStream_t st) {
+  if (a.row_bytes == (int64_t)VPL * 512) return launch_one<RowT, VPL, MODE, DOT, true>(a, items_upper, st);
+  return launch_one<RowT, VPL, MODE, DOT, false>(a, items_upper, st);
 }
 
 template <typename RowT, int MODE, bool DOT>
 static int launch_vpl(GatherArgs a, int64_t items_upper, cudaStream_t st) {
   const int64_t v = (a.row_bytes + 511) / 512;
-  if (v <= 1) return launch_one<RowT, 1, MODE, DOT>(a, items_upper, st);
-  if (v <= 2) return launch_one<RowT, 2, MODE, DOT>(a, items_upper, st);
-  if (v <= 4) return launch_one<RowT, 4, MODE, DOT>(a, items_upper, st);
-  if (v <= 8) return launch_one<RowT, 8, MODE, DOT>(a, items_upper, st);
+  if (v <= 1) return launch_full<RowT, 1, MODE, DOT>(a, items_upper, st);
+  if (v <= 2) return launch_full<RowT, 2, MODE, DOT>(a, items_upper, st);
+  if (v <= 4) return launch_full<RowT, 4, MODE, DOT>(a, items_upper, st);
+  if (v <= 8) return launch_full<RowT, 8, MODE, DOT>(a, items_upper, st);
   return fail(PKM_ERR_UNSUPPORTED, "rows above 4096 bytes are not supported");
 }
 

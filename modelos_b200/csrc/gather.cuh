@@ -8,14 +8,17 @@
 // shared-memory slots: lane 0 issues one cp.async.bulk per row, `slots`
 // entries ahead of the consumer, and each slot's mbarrier flips when the
 // bytes land.  The whole warp then accumulates weight * row into fp32
-// registers (lane l owns 16-byte vectors l, l+32, ...) in entry order, so
-// every output row is summed in a fixed, deterministic order, and reduces
+// registers (lane l owns 16-byte vectors l, l+32, ...; pairs of elements are
+// accumulated with the packed fma.rn.f32x2) in entry order, so every output
+// row is summed in a fixed, deterministic order, and reduces
 // <row, dot_vector> across the warp when a dot output is requested.
 //
-// Entry metadata (row id, weight, dot position) is staged through a 64-entry
-// shared ring, filled one 32-entry page ahead from registers that were loaded
-// another page earlier, so neither the copy issue nor the consumer waits on
-// a metadata load.
+// Entry metadata (row id, weight, dot position) and, in segment mode, item
+// descriptors are staged through 64-entry shared rings filled one 32-entry
+// page ahead from registers loaded another page earlier.  In segment mode the
+// per-item dot vector (a row of the table) also streams through a small ring
+// of its own, issued a few items ahead, so no global load is waited on at an
+// item boundary.
 #pragma once
 
 #include "common.cuh"
@@ -23,8 +26,8 @@
 namespace pkm {
 
 enum { G_BAG = 0, G_SEG = 1 };
-constexpr int kGatherWarps = 8;
 constexpr int kMetaRing = 64;
+constexpr int kDvSlots = 3;
 
 struct GatherArgs {
   const char* rows;  // gathered table
@@ -55,6 +58,61 @@ struct GatherArgs {
   int64_t warp_smem;
 };
 
+// ---------------------------------------------------------------------------
+// packed fp32 pairs
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t r, float& lo, float& hi) {
+  uint32_t a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(r));
+  lo = __uint_as_float(a);
+  hi = __uint_as_float(b);
+}
+// acc = a * b + acc on both halves, each rounded like fmaf
+__device__ __forceinline__ void ffma2(uint64_t& acc, uint64_t a, uint64_t b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+
+template <typename T>
+struct Pairs;
+template <>
+struct Pairs<float> {
+  static constexpr int NP = 2;  // fp32 pairs per 16-byte vector
+  __device__ static __forceinline__ void unpack(const uint4& v, uint64_t* p) {
+    p[0] = pack2(v.x, v.y);
+    p[1] = pack2(v.z, v.w);
+  }
+};
+template <>
+struct Pairs<__nv_bfloat16> {
+  static constexpr int NP = 4;
+  __device__ static __forceinline__ void unpack(const uint4& v, uint64_t* p) {
+    p[0] = pack2(v.x << 16, v.x & 0xffff0000u);
+    p[1] = pack2(v.y << 16, v.y & 0xffff0000u);
+    p[2] = pack2(v.z << 16, v.z & 0xffff0000u);
+    p[3] = pack2(v.w << 16, v.w & 0xffff0000u);
+  }
+};
+template <>
+struct Pairs<__half> {
+  static constexpr int NP = 4;
+  __device__ static __forceinline__ void unpack(const uint4& v, uint64_t* p) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 t = __half22float2(h[i]);
+      p[i] = pack2(__float_as_uint(t.x), __float_as_uint(t.y));
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// metadata pages
+// ---------------------------------------------------------------------------
 struct GatherPrefetch {
   int64_t a;   // bag: index; seg: occurrence id
   uint32_t b;  // weight bits (bag: raw dtype bits; seg: fp32 bits)
@@ -84,8 +142,7 @@ __device__ __forceinline__ GatherPrefetch gather_prefetch(const GatherArgs& a, i
 
 template <int MODE>
 __device__ __forceinline__ void gather_commit(const GatherArgs& a, const GatherPrefetch& p, int64_t e,
-                                              int64_t E1, int32_t* m_src, float* m_w, int32_t* m_pos,
-                                              int mi) {
+                                              int64_t E1, int2* m_sp, float* m_w, int mi) {
   int32_t src = -1, pos = -1;
   float w = 0.f;
   if (e < E1) {
@@ -108,51 +165,42 @@ __device__ __forceinline__ void gather_commit(const GatherArgs& a, const GatherP
       pos = static_cast<int32_t>(p.a);
     }
   }
-  m_src[mi] = src;
+  m_sp[mi] = make_int2(src, pos);
   m_w[mi] = w;
-  m_pos[mi] = pos;
 }
 
-template <typename RowT, int VPL>
-__device__ __forceinline__ void load_row_f(const char* row, int64_t row_bytes, int lane,
-                                           float (&f)[VPL][VecTraits<RowT>::EPV]) {
-  constexpr int EPV = VecTraits<RowT>::EPV;
-#pragma unroll
-  for (int v = 0; v < VPL; ++v) {
-    const int64_t off = (int64_t)(v * 32 + lane) * 16;
-    if (off < row_bytes) {
-      uint4 raw = *reinterpret_cast<const uint4*>(row + off);
-      VecTraits<RowT>::unpack(raw, f[v]);
-    } else {
-#pragma unroll
-      for (int t = 0; t < EPV; ++t) f[v][t] = 0.f;
-    }
-  }
-}
-
-template <typename RowT, int VPL, int MODE, bool DOT>
-__global__ void __launch_bounds__(kGatherWarps * 32, 1) gather_kernel(const GatherArgs a) {
-  constexpr int EPV = VecTraits<RowT>::EPV;
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <typename RowT, int VPL, int MODE, bool DOT, int NW, bool FULL>
+__global__ void __launch_bounds__(NW * 32, 1) gather_kernel(const GatherArgs a) {
+  constexpr int NP = Pairs<RowT>::NP;
+  constexpr bool SEGDV = (MODE == G_SEG) && DOT;
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int P = a.slots;
   const int64_t RB = a.row_bytes;
 
+  // per-warp shared layout: ring | dv ring | meta | item descs | barriers
   unsigned char* wbase = smem + warp * a.warp_smem;
   unsigned char* ring = wbase;
   const int64_t ring_bytes = ((int64_t)P * RB + 127) & ~(int64_t)127;
-  int32_t* m_src = reinterpret_cast<int32_t*>(wbase + ring_bytes);
-  float* m_w = reinterpret_cast<float*>(m_src + kMetaRing);
-  int32_t* m_pos = reinterpret_cast<int32_t*>(m_w + kMetaRing);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(m_pos + kMetaRing);
+  unsigned char* dvring = wbase + ring_bytes;
+  const int64_t dv_bytes = SEGDV ? (((int64_t)kDvSlots * RB + 127) & ~(int64_t)127) : 0;
+  int2* m_sp = reinterpret_cast<int2*>(dvring + dv_bytes);
+  float* m_w = reinterpret_cast<float*>(m_sp + kMetaRing);
+  int4* m_items = reinterpret_cast<int4*>(m_w + kMetaRing);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(m_items + (MODE == G_SEG ? kMetaRing : 0));
+  uint64_t* dvbars = bars + P;
 
-  const int64_t nw = (int64_t)gridDim.x * kGatherWarps;
-  const int64_t gw = (int64_t)blockIdx.x * kGatherWarps + warp;
+  const int64_t nw = (int64_t)gridDim.x * NW;
+  const int64_t gw = (int64_t)blockIdx.x * NW + warp;
   const int64_t n_items = (MODE == G_BAG) ? a.n_items : (int64_t)(*a.n_items_dev);
   const int64_t i0 = n_items * gw / nw;
   const int64_t i1 = n_items * (gw + 1) / nw;
   if (i0 >= i1) return;  // warp-uniform; no block-wide barrier follows
+  const int64_t ni = i1 - i0;
 
   int64_t E0, E1;
   if (MODE == G_BAG) {
@@ -165,127 +213,154 @@ __global__ void __launch_bounds__(kGatherWarps * 32, 1) gather_kernel(const Gath
 
   if (lane == 0) {
     for (int s = 0; s < P; ++s) mbar_init(&bars[s], 1);
+    if (SEGDV)
+      for (int s = 0; s < kDvSlots; ++s) mbar_init(&dvbars[s], 1);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
-  // metadata pages 0 and 1, registers hold page 2
+  // entry metadata pages 0 and 1; registers hold page 2
   {
     GatherPrefetch p0 = gather_prefetch<MODE>(a, E0 + lane, E1);
     GatherPrefetch p1 = gather_prefetch<MODE>(a, E0 + 32 + lane, E1);
-    gather_commit<MODE>(a, p0, E0 + lane, E1, m_src, m_w, m_pos, lane);
-    gather_commit<MODE>(a, p1, E0 + 32 + lane, E1, m_src, m_w, m_pos, 32 + lane);
+    gather_commit<MODE>(a, p0, E0 + lane, E1, m_sp, m_w, lane);
+    gather_commit<MODE>(a, p1, E0 + 32 + lane, E1, m_sp, m_w, 32 + lane);
   }
   GatherPrefetch pf = gather_prefetch<MODE>(a, E0 + 64 + lane, E1);
+  // item descriptor pages (segment mode)
+  int4 ipf = make_int4(0, 0, 0, -1);
+  if (MODE == G_SEG) {
+    m_items[lane] = lane < ni ? a.item_desc[i0 + lane] : make_int4(0, 0, 0, -1);
+    m_items[32 + lane] = 32 + lane < ni ? a.item_desc[i0 + 32 + lane] : make_int4(0, 0, 0, -1);
+    if (64 + lane < ni) ipf = a.item_desc[i0 + 64 + lane];
+  }
   __syncwarp();
 
-  // issue entry `e` (metadata at ring index mi) into slot `s`
-  auto issue = [&](int s, int mi, int64_t e) {
-    const int32_t src = m_src[mi];
+  // issue the entry whose metadata sits at ring index mi into slot s
+  auto issue = [&](int s, int mi) {
+    const int32_t src = m_sp[mi].x;
     if (src >= 0) {
       mbar_arrive_expect_tx(&bars[s], (uint32_t)RB);
       bulk_g2s(ring + (int64_t)s * RB, a.rows + (int64_t)src * RB, (uint32_t)RB, &bars[s]);
     } else {
       mbar_arrive(&bars[s]);
     }
-    (void)e;
+  };
+  // issue the dot-vector row of item j (relative) into its dv slot
+  auto issue_dv = [&](int64_t j) {
+    const int s = (int)(j % kDvSlots);
+    const int64_t k = m_items[j & (kMetaRing - 1)].x;
+    mbar_arrive_expect_tx(&dvbars[s], (uint32_t)RB);
+    bulk_g2s(dvring + (int64_t)s * RB, a.dotvec + k * RB, (uint32_t)RB, &dvbars[s]);
   };
   if (lane == 0) {
-    for (int r = 0; r < P && E0 + r < E1; ++r) issue(r, r & (kMetaRing - 1), E0 + r);
+    for (int r = 0; r < P && E0 + r < E1; ++r) issue(r, r & (kMetaRing - 1));
+    if (SEGDV)
+      for (int j = 0; j < kDvSlots - 1 && j < ni; ++j) issue_dv(j);
   }
 
-  // seg mode: item descriptors and dot vectors run ahead of the consumer
-  int4 desc_cur = make_int4(0, 0, 0, -1), desc_nxt = make_int4(0, 0, 0, -1);
-  if (MODE == G_SEG) {
-    desc_cur = a.item_desc[i0];
-    if (i0 + 1 < i1) desc_nxt = a.item_desc[i0 + 1];
-  }
+  // bag mode: the dot vector of the next bag is prefetched into registers
   uint4 dv_raw_nxt[VPL];
-  auto dot_row_ptr = [&](int64_t item, const int4& d) -> const char* {
-    const int64_t r = (MODE == G_BAG) ? item : (int64_t)d.x;
-    return a.dotvec + r * RB;
-  };
-  auto fetch_dv = [&](int64_t item, const int4& d, uint4 (&raw)[VPL]) {
-    const char* row = dot_row_ptr(item, d);
+  auto fetch_dv = [&](int64_t item, uint4 (&raw)[VPL]) {
+    const char* row = a.dotvec + item * RB;
 #pragma unroll
     for (int v = 0; v < VPL; ++v) {
       const int64_t off = (int64_t)(v * 32 + lane) * 16;
-      raw[v] = (off < RB) ? *reinterpret_cast<const uint4*>(row + off) : make_uint4(0, 0, 0, 0);
+      raw[v] = (FULL || off < RB) ? *reinterpret_cast<const uint4*>(row + off) : make_uint4(0, 0, 0, 0);
     }
   };
-  if (DOT) fetch_dv(i0, desc_cur, dv_raw_nxt);
+  if (DOT && MODE == G_BAG) fetch_dv(i0, dv_raw_nxt);
 
   int64_t e = E0;
   int32_t rel = 0;  // consumer position relative to E0
   int cs = 0;       // consumer slot
   uint32_t cpar = 0;
   bool failed = false;
-  for (int64_t it = i0; it < i1 && !failed; ++it) {
+  int64_t jfail = ni;
+  for (int64_t j = 0; j < ni && !failed; ++j) {
+    jfail = j;
+    const int64_t it = i0 + j;
     int64_t ee, out_row;
     int pslot = -1;
-    int4 d_this = desc_cur;
     if (MODE == G_BAG) {
       ee = (it + 1) * a.L;
       out_row = it;
     } else {
-      ee = d_this.z;
-      out_row = d_this.x;
-      pslot = d_this.w;
-      // advance the descriptor window: next item, and load the one after
-      desc_cur = desc_nxt;
-      if (it + 2 < i1) desc_nxt = a.item_desc[it + 2];
+      const int4 d = m_items[j & (kMetaRing - 1)];
+      ee = d.z;
+      out_row = d.x;
+      pslot = d.w;
     }
-    float dv[VPL][EPV];
+    uint64_t dv[VPL][NP];
     if (DOT) {
+      if (MODE == G_BAG) {
 #pragma unroll
-      for (int v = 0; v < VPL; ++v) VecTraits<RowT>::unpack(dv_raw_nxt[v], dv[v]);
-      if (it + 1 < i1) fetch_dv(it + 1, desc_cur, dv_raw_nxt);
+        for (int v = 0; v < VPL; ++v) Pairs<RowT>::unpack(dv_raw_nxt[v], dv[v]);
+        if (j + 1 < ni) fetch_dv(it + 1, dv_raw_nxt);
+      } else {
+        const int s = (int)(j % kDvSlots);
+        if (!mbar_wait(&dvbars[s], (uint32_t)((j / kDvSlots) & 1), a.err)) {
+          failed = true;
+          break;
+        }
+        const unsigned char* row = dvring + (int64_t)s * RB;
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) {
+          const int64_t off = (int64_t)(v * 32 + lane) * 16;
+          const uint4 raw = (FULL || off < RB) ? *reinterpret_cast<const uint4*>(row + off) : make_uint4(0, 0, 0, 0);
+          Pairs<RowT>::unpack(raw, dv[v]);
+        }
+        __syncwarp();
+        if (lane == 0 && j + kDvSlots - 1 < ni) issue_dv(j + kDvSlots - 1);
+      }
     }
-    float acc[VPL][EPV];
+    uint64_t acc[VPL][NP];
 #pragma unroll
     for (int v = 0; v < VPL; ++v)
 #pragma unroll
-      for (int t = 0; t < EPV; ++t) acc[v][t] = 0.f;
+      for (int t = 0; t < NP; ++t) acc[v][t] = 0ull;
 
     for (; e < ee; ++e, ++rel) {
       const int mi = rel & (kMetaRing - 1);
-      const int32_t src = m_src[mi];
+      const int2 sp = m_sp[mi];
       const float w = m_w[mi];
-      const int32_t pos = m_pos[mi];
       if (!mbar_wait(&bars[cs], cpar, a.err)) {
         failed = true;
         break;
       }
-      float dsum = 0.f;
-      if (src >= 0) {
+      uint64_t dsum = 0ull;
+      if (sp.x >= 0) {
         const unsigned char* slot = ring + (int64_t)cs * RB;
+        const uint64_t w2 = pack2(__float_as_uint(w), __float_as_uint(w));
 #pragma unroll
         for (int v = 0; v < VPL; ++v) {
           const int64_t off = (int64_t)(v * 32 + lane) * 16;
-          if (off < RB) {
-            uint4 raw = *reinterpret_cast<const uint4*>(slot + off);
-            float f[EPV];
-            VecTraits<RowT>::unpack(raw, f);
+          if (FULL || off < RB) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(slot + off);
+            uint64_t f[NP];
+            Pairs<RowT>::unpack(raw, f);
 #pragma unroll
-            for (int t = 0; t < EPV; ++t) {
-              acc[v][t] = fmaf(w, f[t], acc[v][t]);
-              if (DOT) dsum = fmaf(dv[v][t], f[t], dsum);
+            for (int t = 0; t < NP; ++t) {
+              ffma2(acc[v][t], w2, f[t]);
+              if (DOT) ffma2(dsum, dv[v][t], f[t]);
             }
           }
         }
       }
       if (DOT && a.dotout != nullptr) {
-        dsum = warp_sum(dsum);
-        if (lane == 0) st_f(a.dotout, a.dotout_dtype, pos, src >= 0 ? dsum : 0.f);
+        float d0, d1;
+        unpack2(dsum, d0, d1);
+        const float dt = warp_sum(d0 + d1);
+        if (lane == 0) st_f(a.dotout, a.dotout_dtype, sp.y, sp.x >= 0 ? dt : 0.f);
       }
       // every lane has read the slot (the values are in registers) before
       // lane 0 reuses it for the row P entries ahead
       __syncwarp();
-      if (lane == 0 && e + P < E1) issue(cs, (rel + P) & (kMetaRing - 1), e + P);
+      if (lane == 0 && e + P < E1) issue(cs, (rel + P) & (kMetaRing - 1));
       if ((rel & 31) == 31) {
         // page rel/32 is consumed: its ring half now receives page rel/32 + 2
         const int64_t page = rel >> 5;
         const int64_t e2 = E0 + (page + 2) * 32 + lane;
-        gather_commit<MODE>(a, pf, e2, E1, m_src, m_w, m_pos, (int)((e2 - E0) & (kMetaRing - 1)));
+        gather_commit<MODE>(a, pf, e2, E1, m_sp, m_w, (int)((e2 - E0) & (kMetaRing - 1)));
         pf = gather_prefetch<MODE>(a, E0 + (page + 3) * 32 + lane, E1);
         __syncwarp();
       }
@@ -300,14 +375,25 @@ __global__ void __launch_bounds__(kGatherWarps * 32, 1) gather_kernel(const Gath
 #pragma unroll
     for (int v = 0; v < VPL; ++v) {
       const int64_t c = (int64_t)(v * 32 + lane);
-      if (c * 16 < RB) {
-        const int64_t e0 = c * EPV;
+      if (FULL || c * 16 < RB) {
+        float o[2 * NP];
+#pragma unroll
+        for (int t = 0; t < NP; ++t) unpack2(acc[v][t], o[2 * t], o[2 * t + 1]);
+        const int64_t e0 = c * (2 * NP);
         if (MODE == G_SEG && pslot >= 0) {
-          st_run(a.partials, PKM_DT_F32, (int64_t)pslot * a.dim + e0, acc[v], EPV);
+          st_run(a.partials, PKM_DT_F32, (int64_t)pslot * a.dim + e0, o, 2 * NP);
         } else {
-          st_run(a.out, a.out_dtype, out_row * a.dim + e0, acc[v], EPV);
+          st_run(a.out, a.out_dtype, out_row * a.dim + e0, o, 2 * NP);
         }
       }
+    }
+    if (MODE == G_SEG && (j & 31) == 31) {
+      // item page j/32 is done: its half receives page j/32 + 2
+      const int64_t ip = j >> 5;
+      m_items[((ip + 2) * 32 + lane) & (kMetaRing - 1)] = ipf;
+      ipf = make_int4(0, 0, 0, -1);
+      if ((ip + 3) * 32 + lane < ni) ipf = a.item_desc[i0 + (ip + 3) * 32 + lane];
+      __syncwarp();
     }
   }
 
@@ -322,13 +408,16 @@ __global__ void __launch_bounds__(kGatherWarps * 32, 1) gather_kernel(const Gath
         dp ^= 1u;
       }
     }
+    if (SEGDV) {
+      for (int64_t q = jfail; q < ni && q < jfail + kDvSlots - 1; ++q)
+        if (!mbar_wait(&dvbars[q % kDvSlots], (uint32_t)((q / kDvSlots) & 1), nullptr)) break;
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
 // host launcher
 // ---------------------------------------------------------------------------
-int gather_launch(int row_dtype, bool seg, bool dot, GatherArgs a, int64_t items_upper,
-                  cudaStream_t stream);
+int gather_launch(int row_dtype, bool seg, bool dot, GatherArgs a, int64_t items_upper, cudaStream_t stream);
 
 }  // namespace pkm
