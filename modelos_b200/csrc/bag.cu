@@ -41,7 +41,9 @@ static bool gather_geometry(int64_t rb, int nw, bool seg, bool dot, int* slots, 
 
 template <typename RowT, int VPL, int MODE, bool DOT, bool FULL>
 static int launch_one(GatherArgs a, int64_t items_upper, cudaStream_t st) {
-  constexpr int NW = DOT ? 12 : 16;
+  // warps per block: as many as the registers allow, fewer for 4 KB rows so
+  // that every warp still keeps a few rows in flight
+  constexpr int NW = VPL >= 8 ? 8 : (DOT ? 12 : 16);
   int slots;
   int64_t ws;
   if (!gather_geometry(a.row_bytes, NW, MODE == G_SEG, DOT, &slots, &ws))
