@@ -115,14 +115,18 @@ PKM_API int pkm_bag_bwd2(const int64_t* indices, const void* a, int a_dtype, con
  * with r = token*heads + h.  mode 0: dot product (pkm/memory.py:267-268,
  * fwpkm/fwpkm.py:861); mode 1: idw, -log(1e-3 + |q-k|^2) (fwpkm/fwpkm.py:862-866);
  * mode 2: the distance |q-k| = sqrt(max(|q|^2 - 2 q.k + |k|^2, 1e-30)) that
- * torch.cdist(..., compute_mode="use_mm_for_euclid_dist") returns.
- * fp32 inputs use a sequential fp32 sum without fused multiply-add (the
- * oracle's definition); bf16 inputs accumulate in fp32 and round to bf16.
- * query and keys must share a dtype; scores has that dtype.
+ * torch.cdist(..., compute_mode="use_mm_for_euclid_dist") returns; mode 3:
+ * dot product with the sequential sum below.
+ * fp32 inputs (all modes) and mode 3 use a sequential fp32 sum over the half
+ * dimension without fused multiply-add (the oracle's definition).  bf16 dot
+ * products (mode 0) with half % 64 == 0 and n_keys % 8 == 0 run on the
+ * tcgen05 tensor cores (fp32 accumulation, rounded to bf16).
+ * query and keys must share a dtype; scores has that dtype.  dev_err may be
+ * NULL (see PKM_DEVERR_TIMEOUT).
  */
 PKM_API int pkm_subkey_scores(const void* query, const void* keys, int dtype, int64_t n_tokens,
                       int64_t heads, int64_t k_dim, int64_t n_keys, int mode, void* scores,
-                      void* stream);
+                      uint32_t* dev_err, void* stream);
 
 /*
  * K2 - product top-k over precomputed sub-key scores [rows, 2, n_keys].

@@ -35,7 +35,7 @@ _SIGS = {
     "pkm_bag_bwd": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _I, _P, _P,
                      ctypes.c_size_t, _P, _P], _I),
     "pkm_bag_bwd2": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _I, _P, _P], _I),
-    "pkm_subkey_scores": ([_P, _P, _I, _I64, _I64, _I64, _I64, _I, _P, _P], _I),
+    "pkm_subkey_scores": ([_P, _P, _I, _I64, _I64, _I64, _I64, _I, _P, _P, _P], _I),
     "pkm_product_topk": ([_P, _I, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P], _I),
     "pkm_score_bwd_prep": ([_P, _P, _P, _I, _I64, _I64, _I64, _I64, _P, _P, _P], _I),
     "pkm_score_grad_dense": ([_P, _P, _P, _I, _I64, _I64, _I64, _P, _P], _I),
@@ -280,7 +280,10 @@ def bag_bwd2(indices: torch.Tensor, a: Optional[torch.Tensor], gbar: torch.Tenso
 # scoring and top-k
 # ---------------------------------------------------------------------------
 def subkey_scores(query: torch.Tensor, keys: torch.Tensor, heads: int, mode: str = "dot") -> torch.Tensor:
-    """K1: ``[N*H, k_dim]`` queries x ``[2*H*n, k_dim/2]`` keys -> ``[N*H, 2, n]``."""
+    """K1: ``[N*H, k_dim]`` queries x ``[2*H*n, k_dim/2]`` keys -> ``[N*H, 2, n]``.
+
+    ``mode``: "dot" (bf16 on the tensor cores), "dot_seq" (sequential fp32
+    sum), "idw" or "dist" (distance)."""
     assert query.dim() == 2 and keys.dim() == 2 and query.is_contiguous() and keys.is_contiguous()
     assert query.dtype == keys.dtype, "query and keys must share a dtype"
     _need_cuda(query, keys)
@@ -289,7 +292,8 @@ def subkey_scores(query: torch.Tensor, keys: torch.Tensor, heads: int, mode: str
     n = keys.shape[0] // (2 * heads)
     out = torch.empty((NH, 2, n), dtype=query.dtype, device=query.device)
     rc = lib().pkm_subkey_scores(_ptr(query), _ptr(keys), DT[query.dtype], NH // heads, heads, kd, n,
-                                 {"dot": 0, "idw": 1, "dist": 2}[mode], _ptr(out), _stream(query.device))
+                                 {"dot": 0, "idw": 1, "dist": 2, "dot_seq": 3}[mode], _ptr(out),
+                                 _ptr(err_word(query.device)), _stream(query.device))
     _check(rc, "pkm_subkey_scores")
     return out
 

@@ -14,6 +14,11 @@
 
 namespace pkm {
 
+bool subkey_scores_tc_eligible(int64_t heads, int64_t k_dim, int64_t n_keys, const void* query, const void* keys,
+                               const void* scores);
+int subkey_scores_tc(const void* query, const void* keys, int64_t n_tokens, int64_t heads, int64_t k_dim,
+                     int64_t n_keys, void* scores, uint32_t* err, cudaStream_t st);
+
 constexpr int kTR = 64, kTM = 64, kKC = 32;
 
 template <typename T>
@@ -120,15 +125,20 @@ __global__ void __launch_bounds__(256) subkey_scores_kernel(const T* __restrict_
 using namespace pkm;
 
 extern "C" int pkm_subkey_scores(const void* query, const void* keys, int dtype, int64_t n_tokens, int64_t heads,
-                                 int64_t k_dim, int64_t n_keys, int mode, void* scores, void* stream) {
+                                 int64_t k_dim, int64_t n_keys, int mode, void* scores, uint32_t* dev_err,
+                                 void* stream) {
   if (dtype != PKM_DT_F32 && dtype != PKM_DT_BF16) return fail(PKM_ERR_UNSUPPORTED, "dtype must be f32 or bf16");
   if (n_tokens < 0 || heads <= 0 || k_dim < 2 || (k_dim & 1) || n_keys <= 0)
     return fail(PKM_ERR_INVALID_ARG, "bad size (k_dim must be even)");
-  if (mode < 0 || mode > 2) return fail(PKM_ERR_INVALID_ARG, "mode must be 0 (dot), 1 (idw) or 2 (distance)");
+  if (mode < 0 || mode > 3)
+    return fail(PKM_ERR_INVALID_ARG, "mode must be 0 (dot), 1 (idw), 2 (distance) or 3 (dot, sequential sum)");
   if (heads * 2 > 65535) return fail(PKM_ERR_UNSUPPORTED, "too many heads");
   if (n_tokens == 0) return PKM_OK;
   if (!query || !keys || !scores) return fail(PKM_ERR_INVALID_ARG, "NULL pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (mode == 0 && dtype == PKM_DT_BF16 && subkey_scores_tc_eligible(heads, k_dim, n_keys, query, keys, scores))
+    return subkey_scores_tc(query, keys, n_tokens, heads, k_dim, n_keys, scores, dev_err, st);
+  if (mode == 3) mode = 0;
   dim3 grid((unsigned)((n_tokens + kTR - 1) / kTR), (unsigned)((n_keys + kTM - 1) / kTM), (unsigned)(heads * 2));
   if (grid.y > 65535) return fail(PKM_ERR_UNSUPPORTED, "n_keys too large");
 #define PKM_SC(T, M)                                                                                              \

@@ -66,16 +66,9 @@ def subkey_scores(query: torch.Tensor, keys: torch.Tensor, heads: int) -> torch.
 
     fp32 uses the sequential-sum kernel, whose scores (and therefore top-k
     indices) are bit-identical to the oracle's definition; bf16 runs the
-    contraction on the tensor cores (fp32 accumulation, bf16 output, as the
-    reference's einsum)."""
-    if query.dtype == torch.float32:
-        return _native.subkey_scores(query, keys, heads, "dot")
-    R, kd = query.shape
-    half = kd // 2
-    n = keys.shape[0] // (2 * heads)
-    q4 = query.view(R // heads, heads, 2, half)
-    k4 = keys.view(heads, 2, n, half)
-    return torch.einsum("thpd,hpnd->thpn", q4, k4).contiguous().view(R, 2, n)
+    contraction on the tcgen05 tensor cores (fp32 accumulation, bf16 output,
+    as the reference's einsum)."""
+    return _native.subkey_scores(query, keys, heads, "dot")
 
 
 def _score_backward(ctx, d_scores, psw):

@@ -48,10 +48,30 @@ def test_scores_bf16_against_oracle():
     g = torch.Generator().manual_seed(3)
     q = torch.randn(512 * 4, 512, generator=g).bfloat16()
     keys = (torch.rand(2 * 4 * 512, 256, generator=g) * 2 - 1).div(512 ** 0.5).bfloat16()
-    got = _native.subkey_scores(q.to(DEV), keys.to(DEV), 4, "dot").float().cpu().numpy()
+    got = _native.subkey_scores(q.to(DEV), keys.to(DEV), 4, "dot_seq").float().cpu().numpy()
     ref = po.subkey_scores(q.float().numpy(), keys.float().numpy(), 4, bf16=True)
     # same products, same fp32 summation order, same bf16 rounding
     np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("N,H,kd,n", [(2048, 4, 512, 512), (300, 4, 512, 512), (1000, 2, 128, 200),
+                                      (16384, 4, 512, 512)])
+def test_scores_bf16_tensor_cores(N, H, kd, n):
+    """tcgen05 path: fp32 accumulation in the tensor core's order, rounded to
+    bf16 -- equal to the sequential oracle up to one bf16 ulp, and within
+    fp32-accumulation error of an fp64 evaluation."""
+    from modelos_b200 import _native
+    g = torch.Generator().manual_seed(N + n)
+    q = torch.randn(N * H, kd, generator=g).bfloat16()
+    keys = (torch.rand(2 * H * n, kd // 2, generator=g) * 2 - 1).div(kd ** 0.5).bfloat16()
+    got = _native.subkey_scores(q.to(DEV), keys.to(DEV), H, "dot").float().cpu()
+    q64 = q.double().view(N, H, 2, kd // 2)
+    k64 = keys.double().view(H, 2, n, kd // 2)
+    exact = torch.einsum("thpd,hpnd->thpn", q64, k64).reshape(N * H, 2, n)
+    ref = exact.float().bfloat16().double()
+    ulp = torch.clamp(exact.abs(), min=1e-3) * 2.0 ** -7
+    assert ((got.double() - exact).abs() <= ulp).all()
+    assert (got.double() == ref).float().mean().item() > 0.99
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
