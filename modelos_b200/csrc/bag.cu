@@ -20,12 +20,11 @@ static int max_dyn_smem() {
 }
 
 // Ring depth and per-warp shared-memory stride for rows of rb bytes with nw
-// warps per block (segment mode adds the item-descriptor ring, and the dot
-// vector ring when dots are requested).
+// warps per block (segment mode adds the item-descriptor ring).
 static bool gather_geometry(int64_t rb, int nw, bool seg, bool dot, int* slots, int64_t* warp_smem) {
   const int64_t budget = (int64_t)(max_dyn_smem() - 1024) / nw;
-  const int64_t dvb = (seg && dot) ? (((int64_t)kDvSlots * rb + 127) & ~(int64_t)127) : 0;
-  const int64_t fixed = dvb + kMetaRing * 12 + (seg ? kMetaRing * 16 : 0) + kDvSlots * 8;
+  (void)dot;
+  const int64_t fixed = kMetaRing * 12 + (seg ? kMetaRing * 16 : 0);
   for (int p = 32; p >= 2; --p) {
     int64_t ring = ((int64_t)p * rb + 127) & ~(int64_t)127;
     int64_t tot = ring + fixed + (int64_t)p * 8;

@@ -15,10 +15,8 @@
 //
 // Entry metadata (row id, weight, dot position) and, in segment mode, item
 // descriptors are staged through 64-entry shared rings filled one 32-entry
-// page ahead from registers loaded another page earlier.  In segment mode the
-// per-item dot vector (a row of the table) also streams through a small ring
-// of its own, issued a few items ahead, so no global load is waited on at an
-// item boundary.
+// page ahead from registers loaded another page earlier; the per-item dot
+// vector is loaded into registers one item ahead.
 #pragma once
 
 #include "common.cuh"
@@ -27,7 +25,6 @@ namespace pkm {
 
 enum { G_BAG = 0, G_SEG = 1 };
 constexpr int kMetaRing = 64;
-constexpr int kDvSlots = 3;
 
 struct GatherArgs {
   const char* rows;  // gathered table
@@ -175,24 +172,20 @@ __device__ __forceinline__ void gather_commit(const GatherArgs& a, const GatherP
 template <typename RowT, int VPL, int MODE, bool DOT, int NW, bool FULL>
 __global__ void __launch_bounds__(NW * 32, 1) gather_kernel(const GatherArgs a) {
   constexpr int NP = Pairs<RowT>::NP;
-  constexpr bool SEGDV = (MODE == G_SEG) && DOT;
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int P = a.slots;
   const int64_t RB = a.row_bytes;
 
-  // per-warp shared layout: ring | dv ring | meta | item descs | barriers
+  // per-warp shared layout: ring | meta | item descs | barriers
   unsigned char* wbase = smem + warp * a.warp_smem;
   unsigned char* ring = wbase;
   const int64_t ring_bytes = ((int64_t)P * RB + 127) & ~(int64_t)127;
-  unsigned char* dvring = wbase + ring_bytes;
-  const int64_t dv_bytes = SEGDV ? (((int64_t)kDvSlots * RB + 127) & ~(int64_t)127) : 0;
-  int2* m_sp = reinterpret_cast<int2*>(dvring + dv_bytes);
+  int2* m_sp = reinterpret_cast<int2*>(wbase + ring_bytes);
   float* m_w = reinterpret_cast<float*>(m_sp + kMetaRing);
   int4* m_items = reinterpret_cast<int4*>(m_w + kMetaRing);
   uint64_t* bars = reinterpret_cast<uint64_t*>(m_items + (MODE == G_SEG ? kMetaRing : 0));
-  uint64_t* dvbars = bars + P;
 
   const int64_t nw = (int64_t)gridDim.x * NW;
   const int64_t gw = (int64_t)blockIdx.x * NW + warp;
@@ -213,8 +206,6 @@ __global__ void __launch_bounds__(NW * 32, 1) gather_kernel(const GatherArgs a) 
 
   if (lane == 0) {
     for (int s = 0; s < P; ++s) mbar_init(&bars[s], 1);
-    if (SEGDV)
-      for (int s = 0; s < kDvSlots; ++s) mbar_init(&dvbars[s], 1);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -245,39 +236,30 @@ __global__ void __launch_bounds__(NW * 32, 1) gather_kernel(const GatherArgs a) 
       mbar_arrive(&bars[s]);
     }
   };
-  // issue the dot-vector row of item j (relative) into its dv slot
-  auto issue_dv = [&](int64_t j) {
-    const int s = (int)(j % kDvSlots);
-    const int64_t k = m_items[j & (kMetaRing - 1)].x;
-    mbar_arrive_expect_tx(&dvbars[s], (uint32_t)RB);
-    bulk_g2s(dvring + (int64_t)s * RB, a.dotvec + k * RB, (uint32_t)RB, &dvbars[s]);
-  };
   if (lane == 0) {
     for (int r = 0; r < P && E0 + r < E1; ++r) issue(r, r & (kMetaRing - 1));
-    if (SEGDV)
-      for (int j = 0; j < kDvSlots - 1 && j < ni; ++j) issue_dv(j);
   }
 
-  // bag mode: the dot vector of the next bag is prefetched into registers
+  // the dot vector of the next item is prefetched into registers (bag mode:
+  // the bag's upstream-gradient row; segment mode: the item's table row)
   uint4 dv_raw_nxt[VPL];
-  auto fetch_dv = [&](int64_t item, uint4 (&raw)[VPL]) {
-    const char* row = a.dotvec + item * RB;
+  auto fetch_dv = [&](int64_t j, uint4 (&raw)[VPL]) {
+    const int64_t r = (MODE == G_BAG) ? i0 + j : (int64_t)m_items[j & (kMetaRing - 1)].x;
+    const char* row = a.dotvec + r * RB;
 #pragma unroll
     for (int v = 0; v < VPL; ++v) {
       const int64_t off = (int64_t)(v * 32 + lane) * 16;
       raw[v] = (FULL || off < RB) ? *reinterpret_cast<const uint4*>(row + off) : make_uint4(0, 0, 0, 0);
     }
   };
-  if (DOT && MODE == G_BAG) fetch_dv(i0, dv_raw_nxt);
+  if (DOT) fetch_dv(0, dv_raw_nxt);
 
   int64_t e = E0;
   int32_t rel = 0;  // consumer position relative to E0
   int cs = 0;       // consumer slot
   uint32_t cpar = 0;
   bool failed = false;
-  int64_t jfail = ni;
   for (int64_t j = 0; j < ni && !failed; ++j) {
-    jfail = j;
     const int64_t it = i0 + j;
     int64_t ee, out_row;
     int pslot = -1;
@@ -292,26 +274,9 @@ __global__ void __launch_bounds__(NW * 32, 1) gather_kernel(const GatherArgs a) 
     }
     uint64_t dv[VPL][NP];
     if (DOT) {
-      if (MODE == G_BAG) {
 #pragma unroll
-        for (int v = 0; v < VPL; ++v) Pairs<RowT>::unpack(dv_raw_nxt[v], dv[v]);
-        if (j + 1 < ni) fetch_dv(it + 1, dv_raw_nxt);
-      } else {
-        const int s = (int)(j % kDvSlots);
-        if (!mbar_wait(&dvbars[s], (uint32_t)((j / kDvSlots) & 1), a.err)) {
-          failed = true;
-          break;
-        }
-        const unsigned char* row = dvring + (int64_t)s * RB;
-#pragma unroll
-        for (int v = 0; v < VPL; ++v) {
-          const int64_t off = (int64_t)(v * 32 + lane) * 16;
-          const uint4 raw = (FULL || off < RB) ? *reinterpret_cast<const uint4*>(row + off) : make_uint4(0, 0, 0, 0);
-          Pairs<RowT>::unpack(raw, dv[v]);
-        }
-        __syncwarp();
-        if (lane == 0 && j + kDvSlots - 1 < ni) issue_dv(j + kDvSlots - 1);
-      }
+      for (int v = 0; v < VPL; ++v) Pairs<RowT>::unpack(dv_raw_nxt[v], dv[v]);
+      if (j + 1 < ni) fetch_dv(j + 1, dv_raw_nxt);
     }
     uint64_t acc[VPL][NP];
 #pragma unroll
@@ -407,10 +372,6 @@ __global__ void __launch_bounds__(NW * 32, 1) gather_kernel(const GatherArgs a) 
         ds = 0;
         dp ^= 1u;
       }
-    }
-    if (SEGDV) {
-      for (int64_t q = jfail; q < ni && q < jfail + kDvSlots - 1; ++q)
-        if (!mbar_wait(&dvbars[q % kDvSlots], (uint32_t)((q / kDvSlots) & 1), nullptr)) break;
     }
   }
 }
