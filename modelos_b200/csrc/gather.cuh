@@ -284,53 +284,99 @@ __global__ void __launch_bounds__(NW * 32, 1) gather_kernel(const GatherArgs a) 
 #pragma unroll
       for (int t = 0; t < NP; ++t) acc[v][t] = 0ull;
 
-    for (; e < ee; ++e, ++rel) {
-      const int mi = rel & (kMetaRing - 1);
-      const int2 sp = m_sp[mi];
-      const float w = m_w[mi];
-      if (!mbar_wait(&bars[cs], cpar, a.err)) {
+    // entries are consumed two at a time where the item allows: the two rows'
+    // loads and FMAs interleave, and their two dot products share one
+    // butterfly reduction
+    while (e < ee) {
+      const bool two = e + 1 < ee;
+      const int cs1 = (cs + 1 == P) ? 0 : cs + 1;
+      const uint32_t cpar1 = (cs + 1 == P) ? (cpar ^ 1u) : cpar;
+      const int mi0 = rel & (kMetaRing - 1);
+      const int mi1 = (rel + 1) & (kMetaRing - 1);
+      const int2 sp0 = m_sp[mi0];
+      const float w0 = m_w[mi0];
+      int2 sp1 = make_int2(-1, -1);
+      float w1 = 0.f;
+      if (two) {
+        sp1 = m_sp[mi1];
+        w1 = m_w[mi1];
+      }
+      if (!mbar_wait(&bars[cs], cpar, a.err) || (two && !mbar_wait(&bars[cs1], cpar1, a.err))) {
         failed = true;
         break;
       }
-      uint64_t dsum = 0ull;
-      if (sp.x >= 0) {
-        const unsigned char* slot = ring + (int64_t)cs * RB;
-        const uint64_t w2 = pack2(__float_as_uint(w), __float_as_uint(w));
+      uint64_t ds0 = 0ull, ds1 = 0ull;
+      const unsigned char* slot0 = ring + (int64_t)cs * RB;
+      const unsigned char* slot1 = ring + (int64_t)cs1 * RB;
+      const uint64_t w20 = pack2(__float_as_uint(w0), __float_as_uint(w0));
+      const uint64_t w21 = pack2(__float_as_uint(w1), __float_as_uint(w1));
 #pragma unroll
-        for (int v = 0; v < VPL; ++v) {
-          const int64_t off = (int64_t)(v * 32 + lane) * 16;
-          if (FULL || off < RB) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(slot + off);
-            uint64_t f[NP];
-            Pairs<RowT>::unpack(raw, f);
+      for (int v = 0; v < VPL; ++v) {
+        const int64_t off = (int64_t)(v * 32 + lane) * 16;
+        if (FULL || off < RB) {
+          uint64_t f0[NP], f1[NP];
+          if (sp0.x >= 0) Pairs<RowT>::unpack(*reinterpret_cast<const uint4*>(slot0 + off), f0);
+          if (sp1.x >= 0) Pairs<RowT>::unpack(*reinterpret_cast<const uint4*>(slot1 + off), f1);
+          if (sp0.x >= 0) {
 #pragma unroll
             for (int t = 0; t < NP; ++t) {
-              ffma2(acc[v][t], w2, f[t]);
-              if (DOT) ffma2(dsum, dv[v][t], f[t]);
+              ffma2(acc[v][t], w20, f0[t]);
+              if (DOT) ffma2(ds0, dv[v][t], f0[t]);
+            }
+          }
+          if (sp1.x >= 0) {
+#pragma unroll
+            for (int t = 0; t < NP; ++t) {
+              ffma2(acc[v][t], w21, f1[t]);
+              if (DOT) ffma2(ds1, dv[v][t], f1[t]);
             }
           }
         }
       }
       if (DOT && a.dotout != nullptr) {
-        float d0, d1;
-        unpack2(dsum, d0, d1);
-        const float dt = warp_sum(d0 + d1);
-        if (lane == 0) st_f(a.dotout, a.dotout_dtype, sp.y, sp.x >= 0 ? dt : 0.f);
+        float a0, a1, b0, b1;
+        unpack2(ds0, a0, a1);
+        unpack2(ds1, b0, b1);
+        const float d0 = a0 + a1, d1 = b0 + b1;
+        if (two) {
+          // lanes 0-15 reduce entry e, lanes 16-31 entry e+1
+          const bool hi = (lane & 16) != 0;
+          float keep = hi ? d1 : d0;
+          keep += __shfl_xor_sync(0xffffffffu, hi ? d0 : d1, 16);
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+          if (lane == 0) st_f(a.dotout, a.dotout_dtype, sp0.y, sp0.x >= 0 ? keep : 0.f);
+          if (lane == 16) st_f(a.dotout, a.dotout_dtype, sp1.y, sp1.x >= 0 ? keep : 0.f);
+        } else {
+          const float dt = warp_sum(d0);
+          if (lane == 0) st_f(a.dotout, a.dotout_dtype, sp0.y, sp0.x >= 0 ? dt : 0.f);
+        }
       }
-      // every lane has read the slot (the values are in registers) before
-      // lane 0 reuses it for the row P entries ahead
+      // every lane has read the slots (the values are in registers) before
+      // they are refilled
       __syncwarp();
-      if (lane == 0 && e + P < E1) issue(cs, (rel + P) & (kMetaRing - 1));
-      if ((rel & 31) == 31) {
-        // page rel/32 is consumed: its ring half now receives page rel/32 + 2
-        const int64_t page = rel >> 5;
-        const int64_t e2 = E0 + (page + 2) * 32 + lane;
+      int64_t done_page = -1;  // a metadata page whose last entry was just consumed
+      if ((rel & 31) == 31)
+        done_page = rel >> 5;
+      else if (two && ((rel + 1) & 31) == 31)
+        done_page = (rel + 1) >> 5;
+      if (done_page >= 0) {
+        // its ring half now receives page done_page + 2
+        const int64_t e2 = E0 + (done_page + 2) * 32 + lane;
         gather_commit<MODE>(a, pf, e2, E1, m_sp, m_w, (int)((e2 - E0) & (kMetaRing - 1)));
-        pf = gather_prefetch<MODE>(a, E0 + (page + 3) * 32 + lane, E1);
+        pf = gather_prefetch<MODE>(a, E0 + (done_page + 3) * 32 + lane, E1);
         __syncwarp();
       }
-      if (++cs == P) {
-        cs = 0;
+      if (lane == 0) {
+        if (e + P < E1) issue(cs, (rel + P) & (kMetaRing - 1));
+        if (two && e + 1 + P < E1) issue(cs1, (rel + 1 + P) & (kMetaRing - 1));
+      }
+      const int adv = two ? 2 : 1;
+      e += adv;
+      rel += adv;
+      cs += adv;
+      if (cs >= P) {
+        cs -= P;
         cpar ^= 1u;
       }
     }
