@@ -50,7 +50,7 @@ static int launch_one(GatherArgs a, int64_t items_upper, cudaStream_t st) {
   a.slots = slots;
   a.warp_smem = ws;
   const int smem = (int)(ws * NW);
-  auto kern = gather_kernel<RowT, VPL, MODE, DOT, NW, FULL>;
+  auto kern = MODE == G_SEG ? gather_seg_kernel<RowT, VPL, DOT, NW, FULL> : gather_kernel<RowT, VPL, MODE, DOT, NW, FULL>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return check_cuda("cudaFuncSetAttribute(gather)");
   int64_t blocks = (items_upper + NW - 1) / NW;
