@@ -305,13 +305,15 @@ __global__ void __launch_bounds__(NW * 32, 1) gather_kernel(const GatherArgs a) 
         failed = true;
         break;
       }
-      uint64_t ds0 = 0ull, ds1 = 0ull;
+      uint64_t ds0[VPL], ds1[VPL];  // per-vector partial dots: short dependency chains
       const unsigned char* slot0 = ring + (int64_t)cs * RB;
       const unsigned char* slot1 = ring + (int64_t)cs1 * RB;
       const uint64_t w20 = pack2(__float_as_uint(w0), __float_as_uint(w0));
       const uint64_t w21 = pack2(__float_as_uint(w1), __float_as_uint(w1));
 #pragma unroll
       for (int v = 0; v < VPL; ++v) {
+        ds0[v] = 0ull;
+        ds1[v] = 0ull;
         const int64_t off = (int64_t)(v * 32 + lane) * 16;
         if (FULL || off < RB) {
           uint64_t f0[NP], f1[NP];
@@ -321,23 +323,28 @@ __global__ void __launch_bounds__(NW * 32, 1) gather_kernel(const GatherArgs a) 
 #pragma unroll
             for (int t = 0; t < NP; ++t) {
               ffma2(acc[v][t], w20, f0[t]);
-              if (DOT) ffma2(ds0, dv[v][t], f0[t]);
+              if (DOT) ffma2(ds0[v], dv[v][t], f0[t]);
             }
           }
           if (sp1.x >= 0) {
 #pragma unroll
             for (int t = 0; t < NP; ++t) {
               ffma2(acc[v][t], w21, f1[t]);
-              if (DOT) ffma2(ds1, dv[v][t], f1[t]);
+              if (DOT) ffma2(ds1[v], dv[v][t], f1[t]);
             }
           }
         }
       }
       if (DOT && a.dotout != nullptr) {
-        float a0, a1, b0, b1;
-        unpack2(ds0, a0, a1);
-        unpack2(ds1, b0, b1);
-        const float d0 = a0 + a1, d1 = b0 + b1;
+        float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) {
+          float a0, a1, b0, b1;
+          unpack2(ds0[v], a0, a1);
+          unpack2(ds1[v], b0, b1);
+          d0 += a0 + a1;
+          d1 += b0 + b1;
+        }
         if (two) {
           // lanes 0-15 reduce entry e, lanes 16-31 entry e+1
           const bool hi = (lane & 16) != 0;
@@ -558,9 +565,10 @@ __global__ void __launch_bounds__(NW * 32, 1) gather_seg_kernel(const GatherArgs
         }
         const unsigned char* slot = ring + (int64_t)cslot * RB;
         const uint64_t w2 = pack2(__float_as_uint(w), __float_as_uint(w));
-        uint64_t dsum = 0ull;
+        uint64_t dsum[VPL];  // one partial dot per vector: short dependency chains
 #pragma unroll
         for (int v = 0; v < VPL; ++v) {
+          dsum[v] = 0ull;
           const int64_t off = (int64_t)(v * 32 + lane) * 16;
           if (FULL || off < RB) {
             uint64_t f[NP];
@@ -568,13 +576,19 @@ __global__ void __launch_bounds__(NW * 32, 1) gather_seg_kernel(const GatherArgs
 #pragma unroll
             for (int t = 0; t < NP; ++t) {
               ffma2(acc[v][t], w2, f[t]);
-              if (DOT) ffma2(dsum, dv[v][t], f[t]);
+              if (DOT) ffma2(dsum[v], dv[v][t], f[t]);
             }
           }
         }
         if (DOT && a.dotout != nullptr) {
-          float d0, d1;
-          unpack2(dsum, d0, d1);
+          float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+          for (int v = 0; v < VPL; ++v) {
+            float x0, x1;
+            unpack2(dsum[v], x0, x1);
+            d0 += x0;
+            d1 += x1;
+          }
           const float dt = warp_sum(d0 + d1);
           if (lane == 0) st_f(a.dotout, a.dotout_dtype, sp.y, dt);
         }
