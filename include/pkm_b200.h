@@ -97,6 +97,27 @@ PKM_API int pkm_bag_bwd(const int64_t* indices, const void* psw, int psw_dtype, 
                 size_t workspace_bytes, uint32_t* dev_err, void* stream);
 
 /*
+ * Allocation-free K4.  No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory (an FFI binding without a device
+ * allocator of its own, or a latency-critical loop where a cudaMalloc, which
+ * may synchronise the device, is not allowed).  Same arguments and results as
+ * pkm_bag_bwd, without the workspace: the scratch is a 16 MiB static device
+ * array inside the library, held by every GPU that loads it until exit.
+ * Sizes whose pkm_bag_bwd_workspace() exceeds 16 MiB return
+ * PKM_ERR_UNSUPPORTED before any launch.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture.  All calls share the one array, so calls that
+ * overlap on the GPU (other streams, other host threads) race; the kernels
+ * clear what must start at zero on every call.
+ */
+PKM_API int pkm_bag_bwd_noalloc(const int64_t* indices, const void* psw, int psw_dtype,
+                                const void* weight, int weight_dtype, const void* grad_out,
+                                int64_t n_bags, int64_t bag_size, int64_t num_rows, int64_t dim,
+                                void* grad_weight, int grad_weight_dtype, void* grad_psw,
+                                int grad_psw_dtype, int32_t* row_counts, uint32_t* dev_err,
+                                void* stream);
+
+/*
  * K5 - double-backward of the bag's weight gradient.
  *   d_grad_out[b] = sum_j a[b,j] * gbar[idx[b,j]]
  *   d_a[b,j]      = <gbar[idx[b,j]], grad_out[b]>

@@ -34,6 +34,7 @@ _SIGS = {
     "pkm_bag_bwd_workspace": ([_I64, _I64, _I64, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
     "pkm_bag_bwd": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _I, _P, _P,
                      ctypes.c_size_t, _P, _P], _I),
+    "pkm_bag_bwd_noalloc": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _I, _P, _P, _P], _I),
     "pkm_bag_bwd2": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _I, _P, _P], _I),
     "pkm_subkey_scores": ([_P, _P, _I, _I64, _I64, _I64, _I64, _I, _P, _P, _P], _I),
     "pkm_product_topk": ([_P, _I, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P], _I),

@@ -2,6 +2,7 @@
 // (K4) and the double-backward of the weight gradient (K5), with their C ABI
 // entry points.
 #include <algorithm>
+#include <mutex>
 #include <string>
 
 #include "gather.cuh"
@@ -413,4 +414,56 @@ extern "C" int pkm_bag_bwd(const int64_t* indices, const void* psw, int psw_dtyp
     reduce_partials_kernel<<<(unsigned)blocks, 256, 0, st>>>(offs, K, partials, D, grad_weight, grad_weight_dtype);
   }
   return check_cuda("pkm_bag_bwd");
+}
+
+// ---------------------------------------------------------------------------
+// allocation-free variant of the backward
+// ---------------------------------------------------------------------------
+// Some callers cannot allocate device memory at all: an FFI binding that has
+// no device allocator of its own, or a latency-critical serving loop where a
+// cudaMalloc (which may synchronise the device) is not allowed.  For them the
+// backward's scratch lives in this file-scope device array, which every GPU
+// that loads the library holds until the process exits.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of the scratch array on the current device, looked up once
+// per device (the host-side symbol is only a stand-in, never a device address).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return check_cuda("cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(PKM_ERR_UNSUPPORTED, "device ordinal above 63");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess)
+      return check_cuda("cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return PKM_OK;
+}
+}  // namespace
+
+extern "C" int pkm_bag_bwd_noalloc(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                                   int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                                   int64_t num_rows, int64_t dim, void* grad_weight, int grad_weight_dtype,
+                                   void* grad_psw, int grad_psw_dtype, int32_t* row_counts, uint32_t* dev_err,
+                                   void* stream) {
+  size_t need = 0;
+  int rc = pkm_bag_bwd_workspace(n_bags, bag_size, num_rows, dim, &need);
+  if (rc) return rc;
+  if (need > kNoAllocScratchBytes)
+    return fail(PKM_ERR_UNSUPPORTED, "pkm_bag_bwd_noalloc: this size needs " + std::to_string(need) +
+                                         " bytes of scratch; the static scratch holds " +
+                                         std::to_string(kNoAllocScratchBytes) + " (use pkm_bag_bwd with a workspace)");
+  void* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return pkm_bag_bwd(indices, psw, psw_dtype, weight, weight_dtype, grad_out, n_bags, bag_size, num_rows, dim,
+                     grad_weight, grad_weight_dtype, grad_psw, grad_psw_dtype, row_counts, scratch,
+                     kNoAllocScratchBytes, dev_err, stream);
 }
