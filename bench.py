@@ -217,7 +217,12 @@ def run_ours(args, rank, world, local_rank):
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     x = torch.randn((B, T, C), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
     x_host = x.cpu().pin_memory()
-    dense = [p for p in params if p is not m.values.weight]
+    reducer = None
+    if world > 1:
+        from modelos_b200.dist import GradReducer
+        # the value-table gradient is all-reduced as soon as the bag backward
+        # has produced it, overlapping the rest of the backward
+        reducer = GradReducer(params, early=[m.values.weight])
 
     def step(xin):
         for p in params:
@@ -225,15 +230,8 @@ def run_ours(args, rank, world, local_rank):
         y, _ = m(xin)
         loss = (y.float() ** 2).sum()
         loss.backward()
-        if world > 1:
-            dist.all_reduce(m.values.weight.grad)
-            flat = torch.cat([p.grad.reshape(-1) for p in dense])
-            dist.all_reduce(flat)
-            off = 0
-            for p in dense:
-                n = p.numel()
-                p.grad.copy_(flat[off:off + n].view_as(p.grad))
-                off += n
+        if reducer is not None:
+            reducer.finish()
         return loss
 
     for _ in range(args.warmup):

@@ -1,0 +1,69 @@
+"""Worker of the multi-process CPU tests (gloo): one rank of a data-parallel
+HashingMemory step with the kernels replaced by the CPU stand-in."""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+for p in (ROOT, HERE):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+CFG = dict(input_dim=64, output_dim=64, mem_k_dim=32, mem_v_dim=64, mem_heads=2, mem_knn=4, mem_n_keys=16)
+
+
+def install_cpu_kernels():
+    import fake_native
+    from modelos_b200 import _native
+    from modelos_b200.pkm import colwise_embedding_bag, xformer_embeddingbag
+    for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense"):
+        setattr(_native, name, getattr(fake_native, name))
+
+    def bag(indices, weight, per_sample_weights, mode="sum", bw_algo="reverse_indices"):
+        return xformer_embeddingbag.xFormersEmbeddingBag.apply(indices, weight, per_sample_weights, bw_algo)
+
+    xformer_embeddingbag.xformers_embedding_bag = bag
+    colwise_embedding_bag.xformers_embedding_bag = bag
+
+
+def layer_grads(rank_input_seed: int, reducer_world=None):
+    """Gradients of sum(out^2) for one rank's batch (single process)."""
+    import torch
+
+    import cases
+    from modelos_b200.pkm.memory import HashingMemory
+    m = HashingMemory(**CFG)
+    m.load_state_dict(cases.pkm_state(CFG, 0))
+    x = cases.pkm_input((2, 8, 64), rank_input_seed)
+    y, _ = m(x)
+    (y ** 2).sum().backward()
+    return m, {n: p.grad.clone() for n, p in m.named_parameters()}
+
+
+def run(rank: int, world: int, port: int, out_dir: str, mode: str):
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        install_cpu_kernels()
+        import cases
+        from modelos_b200.dist import GradReducer
+        from modelos_b200.pkm.memory import HashingMemory
+        if mode == "fail" and rank == 1:
+            raise RuntimeError("rank 1 fails before its first collective")
+        m = HashingMemory(**CFG)
+        m.load_state_dict(cases.pkm_state(CFG, 0))
+        red = GradReducer(m.parameters(), early=[m.values.weight])
+        x = cases.pkm_input((2, 8, 64), 100 + rank)
+        y, _ = m(x)
+        (y ** 2).sum().backward()
+        red.finish()
+        torch.save({n: p.grad for n, p in m.named_parameters()}, os.path.join(out_dir, f"rank{rank}.pt"))
+    finally:
+        dist.destroy_process_group()

@@ -1,0 +1,62 @@
+"""Data-parallel gradient reduction across processes (gloo, world size 2,
+CPU): the all-reduced gradients equal the sum of the single-process
+gradients of every rank's batch; a rank that dies makes the others fail on
+the process-group timeout instead of hanging."""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _spawn(world, mode, tmp_path):
+    os.environ["PYTHONPATH"] = os.pathsep.join([HERE, os.path.dirname(HERE), os.environ.get("PYTHONPATH", "")])
+    import dist_worker
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=dist_worker.run, args=(r, world, port, str(tmp_path), mode)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    codes = []
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+        codes.append(p.exitcode)
+    return codes
+
+
+def test_grad_reducer_sums_rank_gradients(tmp_path):
+    codes = _spawn(2, "ok", tmp_path)
+    assert codes == [0, 0], codes
+    import dist_worker
+    dist_worker.install_cpu_kernels()
+    ref = None
+    for r in range(2):
+        _, g = dist_worker.layer_grads(100 + r)
+        ref = g if ref is None else {k: ref[k] + g[k] for k in ref}
+    for r in range(2):
+        got = torch.load(os.path.join(tmp_path, f"rank{r}.pt"))
+        for k, v in ref.items():
+            den = max(v.abs().max().item(), 1e-30)
+            assert (got[k] - v).abs().max().item() <= 1e-5 * den, k
+
+
+def test_dead_rank_fails_fast(tmp_path):
+    codes = _spawn(2, "fail", tmp_path)
+    assert codes[1] != 0
+    assert codes[0] != 0  # the surviving rank errors out (connection closed or timeout)
