@@ -281,7 +281,8 @@ def run_ours(args, rank, world, local_rank):
     e2e_ms = float(t.item())
     assert math.isfinite(lv)
 
-    launches_per_step = count_launches(step, x) if rank == 0 else None
+    # every rank runs the counted step: it holds the gradient all-reduce
+    launches_per_step = count_launches(step, x)
     _native.check_device_errors(dev)
 
     if rank != 0:
