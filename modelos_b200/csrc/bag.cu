@@ -6,6 +6,7 @@
 #include <string>
 
 #include "gather.cuh"
+#include "seg.cuh"
 #include "sort.cuh"
 
 namespace pkm {
@@ -39,8 +40,36 @@ static bool gather_geometry(int64_t rb, int nw, bool seg, bool dot, int* slots, 
   return false;
 }
 
+// Segment pass: one block per SM, 12 warps (the register limit: the fp32
+// accumulator, the unpacked table row and the next one), each with about
+// 12 KiB of upstream-gradient rows in flight in its shared ring.
+#ifndef PKM_SEG_WARPS
+#define PKM_SEG_WARPS 12
+#endif
+#ifndef PKM_SEG_BYTES
+#define PKM_SEG_BYTES 12288
+#endif
+template <typename RowT, int VPL, bool DOT, bool FULL>
+static int launch_seg(GatherArgs a, int64_t items_upper, cudaStream_t st) {
+  // 4 KiB rows (VPL 8) need more registers: 8 warps with 16 KiB rings
+  constexpr int NW = VPL >= 8 ? 8 : PKM_SEG_WARPS;
+  constexpr int RING = (VPL >= 8 ? 16384 : PKM_SEG_BYTES) / (VPL * 512);
+  constexpr int DEPTH = RING < 2 ? 2 : (RING > 8 ? 8 : RING);
+  auto kern = seg_direct_kernel<RowT, VPL, DOT, NW, FULL, DEPTH>;
+  a.warp_smem = seg_warp_smem(a.row_bytes, DEPTH, DOT);
+  const int smem = (int)(a.warp_smem * NW);
+  if (smem > max_dyn_smem()) return fail(PKM_ERR_UNSUPPORTED, "row too large for the segment ring");
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return check_cuda("cudaFuncSetAttribute(seg)");
+  int64_t blocks = (items_upper + NW - 1) / NW;
+  blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, num_sms()));
+  kern<<<(unsigned)blocks, NW * 32, smem, st>>>(a);
+  return check_cuda("seg_direct_kernel");
+}
+
 template <typename RowT, int VPL, int MODE, bool DOT, bool FULL>
 static int launch_one(GatherArgs a, int64_t items_upper, cudaStream_t st) {
+  if (MODE == G_SEG) return launch_seg<RowT, VPL, DOT, FULL>(a, items_upper, st);
   // warps per block: as many as the registers allow, fewer for 4 KB rows so
   // that every warp still keeps a few rows in flight
   constexpr int NW = VPL >= 8 ? 8 : (DOT ? 12 : 16);
@@ -51,7 +80,7 @@ static int launch_one(GatherArgs a, int64_t items_upper, cudaStream_t st) {
   a.slots = slots;
   a.warp_smem = ws;
   const int smem = (int)(ws * NW);
-  auto kern = MODE == G_SEG ? gather_seg_kernel<RowT, VPL, DOT, NW, FULL> : gather_kernel<RowT, VPL, MODE, DOT, NW, FULL>;
+  auto kern = gather_kernel<RowT, VPL, MODE, DOT, NW, FULL>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return check_cuda("cudaFuncSetAttribute(gather)");
   int64_t blocks = (items_upper + NW - 1) / NW;
