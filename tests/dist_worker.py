@@ -15,18 +15,20 @@ for p in (ROOT, HERE):
 CFG = dict(input_dim=64, output_dim=64, mem_k_dim=32, mem_v_dim=64, mem_heads=2, mem_knn=4, mem_n_keys=16)
 
 
-def install_cpu_kernels():
+def install_cpu_kernels(set_attr=setattr):
+    """Swap the kernels for the CPU stand-in (``set_attr`` may be pytest's
+    ``monkeypatch.setattr`` so that the swap is undone after a test)."""
     import fake_native
     from modelos_b200 import _native
     from modelos_b200.pkm import colwise_embedding_bag, xformer_embeddingbag
     for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense"):
-        setattr(_native, name, getattr(fake_native, name))
+        set_attr(_native, name, getattr(fake_native, name))
 
     def bag(indices, weight, per_sample_weights, mode="sum", bw_algo="reverse_indices"):
         return xformer_embeddingbag.xFormersEmbeddingBag.apply(indices, weight, per_sample_weights, bw_algo)
 
-    xformer_embeddingbag.xformers_embedding_bag = bag
-    colwise_embedding_bag.xformers_embedding_bag = bag
+    set_attr(xformer_embeddingbag, "xformers_embedding_bag", bag)
+    set_attr(colwise_embedding_bag, "xformers_embedding_bag", bag)
 
 
 def layer_grads(rank_input_seed: int, reducer_world=None):
