@@ -1,12 +1,25 @@
 // Product-key top-k (K2) and the softmax / sub-key-bag preparation for the
 // scoring backward.
 //
-// One warp owns one (token, head) row.  Stage 1 selects the knn best
-// sub-keys of each half with a bitwise radix select on order-preserving
-// integer keys (ties to the lowest sub-key index), sorts them with a warp
-// bitonic network, and stage 2 merges the knn sorted candidate lists
-// s1[i] + s2[.] (one list per lane) with warp max/min reductions, taking
-// equal sums in ascending slot order.  Nothing of the knn*knn product is
+// One warp owns one (token, head) row at a time (a persistent grid walks the
+// rows).  Stage 1 selects the knn best sub-keys of each half: a bitwise radix
+// select on order-preserving integer keys finds the knn-th largest key T,
+// the keys above T and the lowest-index keys equal to T are compacted, and a
+// warp bitonic network sorts them (score descending, index ascending).
+//
+// Stage 2 needs the knn best sums s1[i] + s2[j] (rounded to the score dtype)
+// of the knn x knn product.  With both lists sorted, the pair (i, j) is
+// preceded by the (i+1)(j+1)-1 pairs (i', j') with i' <= i, j' <= j, whose
+// sums are no smaller, so every pair of the top knn in the order
+// (sum descending, (i, j) ascending) has (i+1)(j+1) <= knn: at most 119
+// candidates for knn = 32 instead of 1024.  The knn-th largest sum T of the
+// candidates is therefore the knn-th largest of all pairs, every pair with a
+// larger sum is a candidate, and only pairs equal to T can lie outside the
+// candidate set.  Row i's sums fall with j, so pair (i, knn/(i+1)) tells
+// whether row i has such a pair; if any row has one (rare), the row is
+// finished by an exact k-way merge of the knn sorted rows instead.  Pairs
+// equal to T are taken in ascending slot order (slot = i1 * n + i2), as
+// many as the top knn has room for.  Nothing of the product is
 // materialised.
 #include <algorithm>
 
@@ -20,9 +33,16 @@ __device__ __forceinline__ uint32_t key32(float x) {
   const uint32_t u = __float_as_uint(x);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
-__device__ __forceinline__ uint32_t key16(uint16_t b) {
+__device__ __forceinline__ float unkey32(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+__device__ __forceinline__ uint32_t key16(uint32_t b) {
   if (b == 0x8000u) b = 0;
-  return (b & 0x8000u) ? (uint32_t)(~b & 0xffffu) : (uint32_t)(b | 0x8000u);
+  return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
+}
+__device__ __forceinline__ float unkey16(uint32_t k) {
+  const uint32_t b = (k & 0x8000u) ? (k & 0x7fffu) : (~k & 0xffffu);
+  return __uint_as_float(b << 16);
 }
 
 template <typename T>
@@ -30,22 +50,38 @@ struct ScoreT;
 template <>
 struct ScoreT<float> {
   static constexpr int KEYBITS = 32;
-  __device__ static __forceinline__ void load(const float* p, int64_t i, float& v, uint32_t& k) {
-    v = p[i];
-    k = key32(v);
+  static constexpr int PER_VEC = 4;  // scores per 16-byte load
+  __device__ static __forceinline__ uint32_t key_at(const float* p, int64_t i) { return key32(p[i]); }
+  __device__ static __forceinline__ void keys_of(const uint4& v, uint32_t* k) {
+    k[0] = key32(__uint_as_float(v.x));
+    k[1] = key32(__uint_as_float(v.y));
+    k[2] = key32(__uint_as_float(v.z));
+    k[3] = key32(__uint_as_float(v.w));
   }
+  __device__ static __forceinline__ float value(uint32_t k) { return unkey32(k); }
   __device__ static __forceinline__ float round(float x) { return x; }
+  // key of a value already representable in the score dtype
+  __device__ static __forceinline__ uint32_t key_of(float x) { return key32(x); }
   __device__ static __forceinline__ void store(float* p, int64_t i, float v) { p[i] = v; }
 };
 template <>
 struct ScoreT<__nv_bfloat16> {
   static constexpr int KEYBITS = 16;
-  __device__ static __forceinline__ void load(const __nv_bfloat16* p, int64_t i, float& v, uint32_t& k) {
-    const uint16_t b = reinterpret_cast<const uint16_t*>(p)[i];
-    v = __uint_as_float((uint32_t)b << 16);
-    k = key16(b);
+  static constexpr int PER_VEC = 8;
+  __device__ static __forceinline__ uint32_t key_at(const __nv_bfloat16* p, int64_t i) {
+    return key16(reinterpret_cast<const uint16_t*>(p)[i]);
   }
+  __device__ static __forceinline__ void keys_of(const uint4& v, uint32_t* k) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      k[2 * i] = key16(w[i] & 0xffffu);
+      k[2 * i + 1] = key16(w[i] >> 16);
+    }
+  }
+  __device__ static __forceinline__ float value(uint32_t k) { return unkey16(k); }
   __device__ static __forceinline__ float round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+  __device__ static __forceinline__ uint32_t key_of(float x) { return key16(__float_as_uint(x) >> 16); }
   __device__ static __forceinline__ void store(__nv_bfloat16* p, int64_t i, float v) {
     p[i] = __float2bfloat16_rn(v);
   }
@@ -77,142 +113,96 @@ __device__ __forceinline__ void warp_sort_desc(uint32_t& key, uint32_t& idx, flo
   }
 }
 
-// Stage 1 on one half: lane l holds elements l*EPL .. l*EPL+EPL-1.  Returns,
-// in lane j < knn, the j-th best (key, index, value), sorted.
-template <int EPL, int KEYBITS>
-__device__ __forceinline__ void stage1_select(const uint32_t (&key)[EPL], const float (&val)[EPL], int n, int knn,
-                                              uint32_t* s_key, uint32_t* s_idx, float* s_val, uint32_t& okey,
-                                              uint32_t& oidx, float& oval) {
-  const int lane = threadIdx.x & 31;
-  uint32_t T = 0;
+// The k-th largest key (counting repeats) over the whole warp: bitwise
+// radix select.  Absent elements carry key 0, which no finite score has, so
+// they are never counted.  The caller passes keys lo <= T <= hi that bound
+// the answer: T shares their common high bits, and the search starts below
+// them.
+template <int NE>
+__device__ __forceinline__ uint32_t warp_kth_key(const uint32_t (&key)[NE], int k, uint32_t lo, uint32_t hi) {
+  const uint32_t diff = lo ^ hi;
+  if (diff == 0) return lo;
+  const int top = 31 - __clz(diff);  // highest bit where lo and hi differ
+  uint32_t T = lo & ~((2u << top) - 1u);
 #pragma unroll 1
-  for (int bit = KEYBITS - 1; bit >= 0; --bit) {
+  for (int bit = top; bit >= 0; --bit) {
     const uint32_t cand = T | (1u << bit);
     int c = 0;
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) c += key[e] >= cand;
-    c = __reduce_add_sync(0xffffffffu, c);
-    if (c >= knn) T = cand;
+    for (int e = 0; e < NE; ++e) c += key[e] >= cand;
+    if (__reduce_add_sync(0xffffffffu, c) >= k) T = cand;
   }
+  return T;
+}
+
+__device__ __forceinline__ int warp_excl_prefix(int v) {
+  const int lane = threadIdx.x & 31;
+  int p = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, p, d);
+    if (lane >= d) p += o;
+  }
+  return p - v;
+}
+
+// Stage 1 on one half: lane l holds the keys of elements l*EPL ..
+// l*EPL+EPL-1 (key 0 where the element does not exist).  Returns, in lane
+// j < knn, the j-th best (key, index), sorted.
+template <typename T, int EPL>
+__device__ __forceinline__ void stage1_select(const uint32_t (&key)[EPL], int knn, uint32_t* s_key,
+                                              uint32_t* s_idx, uint32_t& okey, uint32_t& oidx) {
+  const int lane = threadIdx.x & 31;
+  // bounds: the largest key, and the smallest lane maximum (every lane's
+  // maximum is at least that, so at least 32 >= knn keys are)
+  uint32_t lmax = key[0];
+#pragma unroll
+  for (int e = 1; e < EPL; ++e) lmax = max(lmax, key[e]);
+  const uint32_t Tk = warp_kth_key<EPL>(key, knn, __reduce_min_sync(0xffffffffu, lmax),
+                                        __reduce_max_sync(0xffffffffu, lmax));
   int gt = 0, eq = 0;
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
-    gt += key[e] > T;
-    eq += key[e] == T;
+    gt += key[e] > Tk;
+    eq += key[e] == Tk;
   }
-  const int n_gt = __reduce_add_sync(0xffffffffu, gt);
-  const int need_eq = knn - n_gt;
-  // exclusive prefix of equal counts over lanes (lower lanes hold lower indices)
-  int eq_pre = eq;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    const int o = __shfl_up_sync(0xffffffffu, eq_pre, d);
-    if (lane >= d) eq_pre += o;
-  }
-  eq_pre -= eq;
-  // selection flags and compaction
-  int sel = 0;
+  const int need_eq = knn - __reduce_add_sync(0xffffffffu, gt);
+  // lower lanes hold lower indices: equal keys are taken in lane order
+  int eqr = warp_excl_prefix(eq);
   uint32_t selmask = 0;
-  int eqr = eq_pre;
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
-    bool s = key[e] > T;
-    if (key[e] == T) {
+    bool s = key[e] > Tk;
+    if (key[e] == Tk) {
       s = eqr < need_eq;
       ++eqr;
     }
-    if (lane * EPL + e >= n) s = false;
-    if (s) {
-      selmask |= 1u << e;
-      ++sel;
-    }
+    if (s) selmask |= 1u << e;
   }
-  int sel_pre = sel;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    const int o = __shfl_up_sync(0xffffffffu, sel_pre, d);
-    if (lane >= d) sel_pre += o;
-  }
-  sel_pre -= sel;
+  int pos = warp_excl_prefix(__popc(selmask));
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
     if (selmask & (1u << e)) {
-      s_key[sel_pre] = key[e];
-      s_idx[sel_pre] = lane * EPL + e;
-      s_val[sel_pre] = val[e];
-      ++sel_pre;
+      s_key[pos] = key[e];
+      s_idx[pos] = lane * EPL + e;
+      ++pos;
     }
   }
   __syncwarp();
-  if (lane < knn) {
-    okey = s_key[lane];
-    oidx = s_idx[lane];
-    oval = s_val[lane];
-  } else {
-    okey = 0;
-    oidx = 0xffffffffu;
-    oval = -INFINITY;
-  }
+  okey = lane < knn ? s_key[lane] : 0u;
+  oidx = lane < knn ? s_idx[lane] : 0xffffffffu;
   __syncwarp();
-  warp_sort_desc(okey, oidx, oval);
+  float dummy = 0.f;
+  warp_sort_desc(okey, oidx, dummy);
 }
 
-template <typename T, int EPL>
-__global__ void __launch_bounds__(256) product_topk_kernel(const T* __restrict__ scores, int64_t rows, int n, int knn,
-                                                           int64_t* __restrict__ out_idx, T* __restrict__ out_scores,
-                                                           T* __restrict__ out_psw, int64_t* __restrict__ sub1,
-                                                           int64_t* __restrict__ sub2) {
-  __shared__ uint32_t sh_key[8][32];
-  __shared__ uint32_t sh_idx[8][32];
-  __shared__ float sh_val[8][32];
-  __shared__ uint32_t sh_idx2[8][32];
-  __shared__ float sh_val2[8][32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t r = (int64_t)blockIdx.x * 8 + warp;
-  if (r >= rows) return;
-  constexpr int KB = ScoreT<T>::KEYBITS;
-
-  uint32_t k1, i1, k2, i2;
-  float v1, v2;
-  for (int p = 0; p < 2; ++p) {
-    const T* row = scores + (r * 2 + p) * (int64_t)n;
-    uint32_t key[EPL];
-    float val[EPL];
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      const int m = lane * EPL + e;
-      if (m < n) {
-        ScoreT<T>::load(row, m, val[e], key[e]);
-      } else {
-        val[e] = -INFINITY;
-        key[e] = 0;
-      }
-    }
-    uint32_t ok, oi;
-    float ov;
-    stage1_select<EPL, KB>(key, val, n, knn, sh_key[warp], sh_idx[warp], sh_val[warp], ok, oi, ov);
-    if (p == 0) {
-      k1 = ok;
-      i1 = oi;
-      v1 = ov;
-    } else {
-      k2 = ok;
-      i2 = oi;
-      v2 = ov;
-    }
-  }
-  (void)k1;
-  (void)k2;
-  if (sub1 && lane < knn) {
-    sub1[r * knn + lane] = i1;
-    sub2[r * knn + lane] = i2;
-  }
-  // stage 2: lane i owns candidates (i, j), j < knn, non-increasing in j
-  sh_idx2[warp][lane] = i2;
-  sh_val2[warp][lane] = v2;
-  __syncwarp();
-  const uint32_t* idx2 = sh_idx2[warp];
-  const float* val2 = sh_val2[warp];
+// Exact stage 2 by a k-way merge of the knn sorted rows s1[i] + s2[.] (one
+// row per lane, equal sums in ascending slot order).  Used for rows where
+// pairs equal to the knn-th sum lie outside the candidate set.
+template <typename T>
+__device__ void stage2_merge(float v1, uint32_t i1, const uint32_t* idx2, const float* val2, int knn, int n,
+                             uint32_t& my_slot, float& my_val) {
+  const int lane = threadIdx.x & 31;
   const bool live = lane < knn;
   uint32_t done = 0;
   const uint32_t all = knn == 32 ? 0xffffffffu : ((1u << knn) - 1u);
@@ -245,8 +235,8 @@ __global__ void __launch_bounds__(256) product_topk_kernel(const T* __restrict__
   int hj;
   float hval;
   head(hkey, hslot, hj, hval);
-  uint32_t my_slot = 0;
-  float my_val = -INFINITY;
+  my_slot = 0;
+  my_val = -INFINITY;
   for (int t = 0; t < knn; ++t) {
     const uint32_t best = __reduce_max_sync(0xffffffffu, hkey);
     const uint32_t cslot = (hkey == best) ? hslot : 0xffffffffu;
@@ -262,31 +252,200 @@ __global__ void __launch_bounds__(256) product_topk_kernel(const T* __restrict__
       head(hkey, hslot, hj, hval);
     }
   }
-  // outputs + per-row softmax (fp32, stored in the score dtype)
-  if (live) {
-    out_idx[r * knn + lane] = my_slot;
-    ScoreT<T>::store(out_scores, r * knn + lane, my_val);
+}
+
+constexpr int kTopkWarps = 8;
+constexpr int kPairCap = 128;  // candidate pairs for knn <= 32 (119 at knn = 32)
+
+template <typename T, int EPL>
+__global__ void __launch_bounds__(kTopkWarps * 32) product_topk_kernel(const T* __restrict__ scores, int64_t rows,
+                                                                        int n, int knn,
+                                                                        int64_t* __restrict__ out_idx,
+                                                                        T* __restrict__ out_scores,
+                                                                        T* __restrict__ out_psw,
+                                                                        int64_t* __restrict__ sub1,
+                                                                        int64_t* __restrict__ sub2, bool vec_ok) {
+  __shared__ uint32_t sh_key[kTopkWarps][32];
+  __shared__ uint32_t sh_idx[kTopkWarps][32];
+  __shared__ float sh_v1[kTopkWarps][32];
+  __shared__ uint32_t sh_i1[kTopkWarps][32];
+  __shared__ float sh_v2[kTopkWarps][32];
+  __shared__ uint32_t sh_i2[kTopkWarps][32];
+  __shared__ uint16_t sh_pair[kTopkWarps][kPairCap];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int KB = ScoreT<T>::KEYBITS;
+  constexpr int PV = ScoreT<T>::PER_VEC;
+  constexpr int NV = (EPL % PV == 0) ? EPL / PV : 0;  // 16-byte loads per lane and half
+  const bool full = n == 32 * EPL;
+
+  // candidate pairs (i, j) with (i+1)(j+1) <= knn, packed i | j << 8
+  int n_pairs;
+  {
+    const int cnt = lane < knn ? knn / (lane + 1) : 0;
+    const int off = warp_excl_prefix(cnt);
+    for (int j = 0; j < cnt; ++j) sh_pair[warp][off + j] = (uint16_t)(lane | (j << 8));
+    n_pairs = __shfl_sync(0xffffffffu, off + cnt, 31);
+    __syncwarp();
   }
-  if (out_psw) {
-    const float mx = __shfl_sync(0xffffffffu, my_val, 0);
-    const float ex = live ? expf(my_val - mx) : 0.f;
-    const float sum = warp_sum(ex);
-    if (live) ScoreT<T>::store(out_psw, r * knn + lane, ex / sum);
+  uint32_t* s_key = sh_key[warp];
+  uint32_t* s_idx = sh_idx[warp];
+
+  const int64_t warps_total = (int64_t)gridDim.x * kTopkWarps;
+  for (int64_t r = (int64_t)blockIdx.x * kTopkWarps + warp; r < rows; r += warps_total) {
+    uint32_t k1, i1, k2, i2;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const T* row = scores + (r * 2 + p) * (int64_t)n;
+      uint32_t key[EPL];
+      if (NV > 0 && full && vec_ok) {
+        const uint4* vp = reinterpret_cast<const uint4*>(row + (int64_t)lane * EPL);
+#pragma unroll
+        for (int v = 0; v < (NV > 0 ? NV : 1); ++v) ScoreT<T>::keys_of(__ldg(vp + v), key + v * PV);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          const int m = lane * EPL + e;
+          key[e] = m < n ? ScoreT<T>::key_at(row, m) : 0u;
+        }
+      }
+      uint32_t ok, oi;
+      stage1_select<T, EPL>(key, knn, s_key, s_idx, ok, oi);
+      if (p == 0) {
+        k1 = ok;
+        i1 = oi;
+      } else {
+        k2 = ok;
+        i2 = oi;
+      }
+    }
+    const bool live = lane < knn;
+    const float v1 = live ? ScoreT<T>::value(k1) : -INFINITY;
+    const float v2 = live ? ScoreT<T>::value(k2) : -INFINITY;
+    if (sub1 && live) {
+      sub1[r * knn + lane] = i1;
+      sub2[r * knn + lane] = i2;
+    }
+    sh_v1[warp][lane] = v1;
+    sh_i1[warp][lane] = i1;
+    sh_v2[warp][lane] = v2;
+    sh_i2[warp][lane] = i2;
+    __syncwarp();
+
+    // stage 2 over the candidate pairs, four per lane
+    uint32_t ck[4], cs[4];
+    float cv[4];
+    uint32_t cvalid = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int c = lane + 32 * t;
+      ck[t] = 0;
+      cs[t] = 0xffffffffu;
+      cv[t] = -INFINITY;
+      if (c < n_pairs) {
+        const uint32_t pr = sh_pair[warp][c];
+        const int pi = pr & 0xff, pj = pr >> 8;
+        cv[t] = ScoreT<T>::round(sh_v1[warp][pi] + sh_v2[warp][pj]);
+        ck[t] = ScoreT<T>::key_of(cv[t]);
+        cs[t] = sh_i1[warp][pi] * (uint32_t)n + sh_i2[warp][pj];
+        cvalid |= 1u << t;
+      }
+    }
+    // bounds: the best pair (0, 0), and the knn pairs (i, 0) or (0, j)
+    const float b0 = sh_v2[warp][0], a0 = sh_v1[warp][0];
+    const uint32_t hi_k = ScoreT<T>::key_of(ScoreT<T>::round(a0 + b0));
+    const uint32_t lo_k = max(ScoreT<T>::key_of(ScoreT<T>::round(sh_v1[warp][knn - 1] + b0)),
+                              ScoreT<T>::key_of(ScoreT<T>::round(a0 + sh_v2[warp][knn - 1])));
+    const uint32_t Tk = warp_kth_key<4>(ck, knn, lo_k, hi_k);
+    // a row with a pair equal to Tk outside the candidates?
+    bool outside = false;
+    if (live) {
+      const int jb = knn / (lane + 1);
+      if (jb < knn) outside = ScoreT<T>::key_of(ScoreT<T>::round(v1 + sh_v2[warp][jb])) == Tk;
+    }
+    uint32_t my_slot;
+    float my_val;
+    if (__any_sync(0xffffffffu, outside)) {
+      stage2_merge<T>(v1, i1, sh_i2[warp], sh_v2[warp], knn, n, my_slot, my_val);
+    } else {
+      int gt = 0, eq = 0;
+      uint32_t sel = 0, tie = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const bool v = (cvalid >> t) & 1u;
+        if (v && ck[t] > Tk) {
+          sel |= 1u << t;
+          ++gt;
+        }
+        if (v && ck[t] == Tk) {
+          tie |= 1u << t;
+          ++eq;
+        }
+      }
+      const int need = knn - __reduce_add_sync(0xffffffffu, gt);
+      if (__reduce_add_sync(0xffffffffu, eq) == need) {
+        sel |= tie;
+      } else {
+        // the `need` lowest slots among the tied pairs
+        for (int q = 0; q < need; ++q) {
+          uint32_t mine = 0xffffffffu;
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            if ((tie >> t) & 1u) mine = min(mine, cs[t]);
+          const uint32_t m = __reduce_min_sync(0xffffffffu, mine);
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            if (((tie >> t) & 1u) && cs[t] == m) {
+              tie &= ~(1u << t);
+              sel |= 1u << t;
+            }
+        }
+      }
+      int pos = warp_excl_prefix(__popc(sel));
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        if ((sel >> t) & 1u) {
+          s_key[pos] = ck[t];
+          s_idx[pos] = cs[t];
+          sh_v1[warp][pos] = cv[t];  // the stage-1 values are no longer needed
+          ++pos;
+        }
+      }
+      __syncwarp();
+      uint32_t ok = live ? s_key[lane] : 0u;
+      my_slot = live ? s_idx[lane] : 0xffffffffu;
+      my_val = live ? sh_v1[warp][lane] : -INFINITY;
+      __syncwarp();
+      warp_sort_desc(ok, my_slot, my_val);
+    }
+    // outputs + per-row softmax (fp32, stored in the score dtype)
+    if (live) {
+      out_idx[r * knn + lane] = my_slot;
+      ScoreT<T>::store(out_scores, r * knn + lane, my_val);
+    }
+    if (out_psw) {
+      const float mx = __shfl_sync(0xffffffffu, my_val, 0);
+      const float ex = live ? expf(my_val - mx) : 0.f;
+      const float sum = warp_sum(ex);
+      if (live) ScoreT<T>::store(out_psw, r * knn + lane, ex / sum);
+    }
+    __syncwarp();
   }
 }
 
 template <typename T>
 static int launch_topk(const void* scores, int64_t rows, int64_t n, int64_t knn, int64_t* idx, void* ts, void* psw,
                        int64_t* s1, int64_t* s2, cudaStream_t st) {
-  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  const int64_t want = (rows + kTopkWarps - 1) / kTopkWarps;
+  const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)num_sms() * 8));
   const T* sc = static_cast<const T*>(scores);
   T* o = static_cast<T*>(ts);
   T* pw = static_cast<T*>(psw);
   const int ni = (int)n, ki = (int)knn;
-#define PKM_TOPK_CASE(E)                                                                      \
-  if (n <= 32 * (E)) {                                                                        \
-    product_topk_kernel<T, E><<<blocks, 256, 0, st>>>(sc, rows, ni, ki, idx, o, pw, s1, s2); \
-    return check_cuda("product_topk_kernel");                                                 \
+  const bool vec_ok = aligned16(scores);  // 16-byte loads of whole rows
+#define PKM_TOPK_CASE(E)                                                                                          \
+  if (n <= 32 * (E)) {                                                                                            \
+    product_topk_kernel<T, E><<<blocks, kTopkWarps * 32, 0, st>>>(sc, rows, ni, ki, idx, o, pw, s1, s2, vec_ok); \
+    return check_cuda("product_topk_kernel");                                                                     \
   }
   PKM_TOPK_CASE(1)
   PKM_TOPK_CASE(2)

@@ -94,6 +94,38 @@ def test_product_topk_bit_exact(dtype, n, knn):
     assert rel_err(psw.float().cpu().numpy(), p_ref) < (2e-2 if dtype == torch.bfloat16 else 1e-5)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("kind", ["integers", "zeros", "two_levels", "unaligned"])
+def test_product_topk_heavy_ties(dtype, kind):
+    """Rows whose knn-th pair sum is shared by pairs outside the pruned
+    candidate set (the exact-merge path), all-equal rows, and a score
+    tensor that does not start on a 16-byte boundary (scalar loads)."""
+    from modelos_b200 import _native
+    g = torch.Generator().manual_seed(5)
+    n, knn = 512, 32
+    if kind == "integers":
+        s = torch.randint(-3, 4, (300, 2, n), generator=g).float()
+    elif kind == "zeros":
+        s = torch.zeros(40, 2, n)
+    elif kind == "two_levels":
+        s = (torch.rand(300, 2, n, generator=g) < 0.1).float()
+    else:
+        s = torch.randn(300, 2, n, generator=g)
+    s = s.to(dtype)
+    if kind == "unaligned":
+        buf = torch.empty(s.numel() + 1, dtype=dtype, device=DEV)
+        dev = buf[1:].view(s.shape)
+        dev.copy_(s.to(DEV))
+    else:
+        dev = s.to(DEV).contiguous()
+    idx, top, psw, s1, s2 = _native.product_topk(dev, knn, want_psw=True, want_sub=True)
+    ref = po.product_topk(s.float().numpy(), knn, bf16=dtype == torch.bfloat16)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref["indices"])
+    np.testing.assert_array_equal(top.float().cpu().numpy(), ref["scores"])
+    np.testing.assert_array_equal(s1.cpu().numpy(), ref["sub_indices1"])
+    np.testing.assert_array_equal(s2.cpu().numpy(), ref["sub_indices2"])
+
+
 def test_config0_indices_bit_exact_and_match_reference():
     from modelos_b200 import _native
     c0 = np.load(os.path.join(GOLD, "c0_pkm.npz"))
