@@ -193,6 +193,35 @@ PKM_API int pkm_score_bwd_prep(const int64_t* indices, const void* psw, const vo
 PKM_API int pkm_score_grad_dense(const int64_t* indices, const void* psw, const void* dpsw, int dtype,
                                  int64_t rows, int64_t knn, int64_t n_keys, void* d_scores, void* stream);
 
+/*
+ * Batch normalisation of the query projection, x [n, c] row-major (rows =
+ * tokens, c a multiple of 8, x / out / dy / dx 16-byte aligned; x f32 or
+ * bf16).  Replaces the query network's nn.BatchNorm1d(heads * k_dim,
+ * eps=1e-6, momentum=0.1) (pkm/memory.py:308-309), i.e. ATen's
+ * native_batch_norm (training and evaluation) and
+ * native_batch_norm_backward.
+ *
+ * pkm_batchnorm_fwd, training != 0: batch statistics (biased variance for
+ * the normalisation), save_mean / save_rstd [c] fp32 receive the mean and
+ * 1/sqrt(var + eps), and running_mean / running_var (either may be NULL) are
+ * updated with `momentum` and the unbiased variance.  training == 0: the
+ * running statistics normalise, save_* receive them (mean, 1/sqrt(var +
+ * eps)), and no workspace is needed.  weight / bias (p_dtype) may be NULL.
+ * pkm_batchnorm_bwd: from the saved statistics, dx (NULL to skip), dweight
+ * and dbias (p_dtype, NULL to skip).  Both reduce in a fixed order: results
+ * are deterministic.
+ */
+PKM_API int pkm_batchnorm_workspace(int64_t n, int64_t c, size_t* bytes);
+PKM_API int pkm_batchnorm_fwd(const void* x, int x_dtype, int64_t n, int64_t c, const void* weight,
+                              const void* bias, int p_dtype, void* running_mean, void* running_var,
+                              int r_dtype, int training, double momentum, double eps, void* out,
+                              float* save_mean, float* save_rstd, void* workspace, size_t workspace_bytes,
+                              void* stream);
+PKM_API int pkm_batchnorm_bwd(const void* dy, const void* x, int x_dtype, int64_t n, int64_t c,
+                              const float* save_mean, const float* save_rstd, const void* weight,
+                              int p_dtype, void* dx, void* dweight, void* dbias, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -40,6 +40,10 @@ _SIGS = {
     "pkm_product_topk": ([_P, _I, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P], _I),
     "pkm_score_bwd_prep": ([_P, _P, _P, _I, _I64, _I64, _I64, _I64, _P, _P, _P], _I),
     "pkm_score_grad_dense": ([_P, _P, _P, _I, _I64, _I64, _I64, _P, _P], _I),
+    "pkm_batchnorm_workspace": ([_I64, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
+    "pkm_batchnorm_fwd": ([_P, _I, _I64, _I64, _P, _P, _I, _P, _P, _I, _I, ctypes.c_double, ctypes.c_double,
+                           _P, _P, _P, _P, ctypes.c_size_t, _P], _I),
+    "pkm_batchnorm_bwd": ([_P, _P, _I, _I64, _I64, _P, _P, _P, _I, _P, _P, _P, _P, ctypes.c_size_t, _P], _I),
 }
 
 EXPORTED = tuple(_SIGS)
@@ -348,3 +352,51 @@ def score_grad_dense(indices: torch.Tensor, psw: Optional[torch.Tensor], dpsw: t
                                     _ptr(out), _stream(dpsw.device))
     _check(rc, "pkm_score_grad_dense")
     return out
+
+
+# ---------------------------------------------------------------------------
+# batch normalisation of the query projection
+# ---------------------------------------------------------------------------
+def batchnorm_workspace(n: int, c: int) -> int:
+    nb = ctypes.c_size_t(0)
+    _check(lib().pkm_batchnorm_workspace(n, c, ctypes.byref(nb)), "pkm_batchnorm_workspace")
+    return int(nb.value)
+
+
+def batchnorm_fwd(x: torch.Tensor, weight, bias, running_mean, running_var, training: bool, momentum: float,
+                  eps: float):
+    """``(out, save_mean, save_rstd)`` of ``F.batch_norm`` on a [n, c] tensor;
+    the running statistics are updated in place when training."""
+    assert x.dim() == 2 and x.is_contiguous()
+    n, c = x.shape
+    out = torch.empty_like(x)
+    mean = torch.empty(c, dtype=torch.float32, device=x.device)
+    rstd = torch.empty(c, dtype=torch.float32, device=x.device)
+    p = weight if weight is not None else bias
+    r = running_mean if running_mean is not None else running_var
+    ws = torch.empty(batchnorm_workspace(n, c) if training else 0, dtype=torch.uint8, device=x.device)
+    _need_cuda(x, weight, bias, running_mean, running_var)
+    _check(lib().pkm_batchnorm_fwd(_ptr(x), DT[x.dtype], n, c, _ptr(weight), _ptr(bias),
+                                   DT[p.dtype] if p is not None else 0, _ptr(running_mean), _ptr(running_var),
+                                   DT[r.dtype] if r is not None else 0, int(training), float(momentum), float(eps),
+                                   _ptr(out), _ptr(mean), _ptr(rstd), _ptr(ws) if ws.numel() else None, ws.numel(),
+                                   _stream(x.device)), "pkm_batchnorm_fwd")
+    return out, mean, rstd
+
+
+def batchnorm_bwd(dy: torch.Tensor, x: torch.Tensor, mean: torch.Tensor, rstd: torch.Tensor, weight,
+                  need_dx: bool = True, need_dw: bool = True, need_db: bool = True, param_dtype=None):
+    """``(dx, dweight, dbias)`` of the training-mode batch normalisation."""
+    assert x.dim() == 2 and x.is_contiguous() and dy.shape == x.shape
+    dy = dy.contiguous()
+    n, c = x.shape
+    pdt = param_dtype if param_dtype is not None else (weight.dtype if weight is not None else x.dtype)
+    dx = torch.empty_like(x) if need_dx else None
+    dw = torch.empty(c, dtype=pdt, device=x.device) if need_dw else None
+    db = torch.empty(c, dtype=pdt, device=x.device) if need_db else None
+    ws = torch.empty(batchnorm_workspace(n, c), dtype=torch.uint8, device=x.device)
+    _need_cuda(dy, x, mean, rstd, weight)
+    _check(lib().pkm_batchnorm_bwd(_ptr(dy), _ptr(x), DT[x.dtype], n, c, _ptr(mean), _ptr(rstd), _ptr(weight),
+                                   DT[pdt], _ptr(dx), _ptr(dw), _ptr(db), _ptr(ws), ws.numel(), _stream(x.device)),
+           "pkm_batchnorm_bwd")
+    return dx, dw, db

@@ -14,8 +14,10 @@ runs on the sm_100a kernels:
   sub-score grid (``pkm_score_grad_dense``) followed by two GEMMs per
   (head, half) for the query and key gradients.
 
-The query projection, its norm, the SwiLU gate and the value projection are
-ordinary ``nn.Linear``/norm modules as in the reference.
+The query projection, the SwiLU gate and the value projection are ordinary
+``nn.Linear`` modules as in the reference; the query batch norm keeps
+``nn.BatchNorm1d``'s parameters and buffers and runs on the library's
+batch-normalisation kernels (``QueryBatchNorm``).
 """
 from __future__ import annotations
 
@@ -85,12 +87,16 @@ def _score_backward(ctx, d_scores, psw):
     half = kd // 2
     H, n = ctx.heads, ctx.n_keys
     N = R // H
-    dS = _native.score_grad_dense(idx, psw, d_scores.to(query.dtype), n).view(N, H, 2, n)
+    dS = _native.score_grad_dense(idx, psw, d_scores.to(query.dtype), n).view(N, H * 2, n)
     dq = dk = None
     if ctx.needs_input_grad[0]:
-        dq = torch.einsum("thpn,hpnd->thpd", dS, keys.view(H, 2, n, half)).reshape(R, kd)
+        # one strided batched GEMM over the H*2 (head, half) blocks, written
+        # straight into the token-major [N, H, 2, half] layout of the query
+        dq = torch.empty((N, H * 2, half), dtype=query.dtype, device=query.device)
+        torch.bmm(dS.transpose(0, 1), keys.view(H * 2, n, half), out=dq.transpose(0, 1))
+        dq = dq.view(R, kd)
     if ctx.needs_input_grad[1]:
-        dk = torch.einsum("thpn,thpd->hpnd", dS, query.view(N, H, 2, half)).reshape(keys.shape)
+        dk = torch.bmm(dS.permute(1, 2, 0), query.view(N, H * 2, half).transpose(0, 1)).reshape(keys.shape)
     return dq, dk
 
 
@@ -308,6 +314,58 @@ class HashingMemory(nn.Module):
         return scores, indices
 
 
+class _QueryBatchNormFn(torch.autograd.Function):
+    """Training/evaluation batch normalisation of a [n, c] tensor on the
+    library's kernels (``F.batch_norm`` semantics)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, running_mean, running_var, training, momentum, eps):
+        out, mean, rstd = _native.batchnorm_fwd(x, weight, bias, running_mean, running_var, training, momentum, eps)
+        ctx.training = training
+        ctx.save_for_backward(x, weight, mean, rstd)
+        ctx.param_dtype = weight.dtype if weight is not None else (bias.dtype if bias is not None else x.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, d_out):
+        x, weight, mean, rstd = ctx.saved_tensors
+        if not ctx.training:
+            # evaluation: an affine map of x with the running statistics
+            scale = rstd * (weight.float() if weight is not None else 1.0)
+            dx = (d_out.float() * scale).to(x.dtype) if ctx.needs_input_grad[0] else None
+            dw = (d_out.float() * (x.float() - mean) * rstd).sum(0).to(ctx.param_dtype) \
+                if ctx.needs_input_grad[1] else None
+            db = d_out.float().sum(0).to(ctx.param_dtype) if ctx.needs_input_grad[2] else None
+            return dx, dw, db, None, None, None, None, None
+        dx, dw, db = _native.batchnorm_bwd(d_out, x, mean, rstd, weight, need_dx=ctx.needs_input_grad[0],
+                                           need_dw=ctx.needs_input_grad[1], need_db=ctx.needs_input_grad[2],
+                                           param_dtype=ctx.param_dtype)
+        return dx, dw, db, None, None, None, None, None
+
+
+class QueryBatchNorm(nn.BatchNorm1d):
+    """``nn.BatchNorm1d`` of the query network (``pkm/memory.py:308-309``)
+    with the same parameters, buffers and running-statistics rule
+    (``torch.nn.modules.batchnorm._BatchNorm.forward``), computed by the
+    library's batch-normalisation kernels.  Inputs are [n, c] CUDA tensors."""
+
+    def forward(self, input):
+        self._check_input_dim(input)
+        if not input.is_cuda:
+            raise RuntimeError("modelos_b200 QueryBatchNorm needs CUDA tensors (no CPU path)")
+        if input.dim() != 2:
+            raise NotImplementedError("QueryBatchNorm takes [n, c] inputs")
+        factor = 0.0 if self.momentum is None else self.momentum
+        if self.training and self.track_running_stats and self.num_batches_tracked is not None:
+            self.num_batches_tracked.add_(1)
+            factor = 1.0 / float(self.num_batches_tracked) if self.momentum is None else self.momentum
+        bn_training = self.training or (self.running_mean is None and self.running_var is None)
+        use_running = not self.training or self.track_running_stats
+        return _QueryBatchNormFn.apply(input.contiguous(), self.weight, self.bias,
+                                       self.running_mean if use_running else None,
+                                       self.running_var if use_running else None, bn_training, factor, self.eps)
+
+
 class QueryMLP(nn.Module):
     """Query network (``pkm/memory.py:292-349``)."""
 
@@ -322,7 +380,7 @@ class QueryMLP(nn.Module):
         sizes_ = list(sizes)
         self.query_mlps = QueryMLP.mlp(sizes_, bias=bias)
         if batchnorm:
-            self.norm = nn.BatchNorm1d(sizes_[-1], affine=True, eps=1e-6, momentum=0.1)
+            self.norm = QueryBatchNorm(sizes_[-1], affine=True, eps=1e-6, momentum=0.1)
         elif rmsnorm:
             from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm
 
