@@ -84,9 +84,6 @@ __device__ __forceinline__ void seg_store_vec(void* p, int dt, int64_t e0, const
 // Per-lane asynchronous 16-byte copies global -> shared (L2 only), grouped
 // per occurrence; each lane later reads back exactly the vectors it copied,
 // so completion is tracked per thread with wait_group and no warp barrier.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -119,42 +116,71 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const GatherArgs
   const int64_t i0 = n_items * gw / nw;
   const int64_t i1 = n_items * (gw + 1) / nw;
   if (i0 >= i1) return;  // warp-uniform; the block has no barrier
-  const int64_t ni = i1 - i0;
+  const int ni = (int)(i1 - i0);
   const int64_t E0 = a.item_desc[i0].y;
-  const int64_t NE = (int64_t)a.item_desc[i1 - 1].z - E0;
+  const int NE = (int)((int64_t)a.item_desc[i1 - 1].z - E0);  // < 2^31: checked on the host
+  const uint32_t L = (uint32_t)a.L;
+  const uint32_t n_occ = (uint32_t)(a.num_rows * a.L);
 
   const uint64_t stream = l2_policy_evict_first();
 
+  // entry metadata: {bag, occurrence} and weight; an occurrence id outside
+  // [0, n_bags * L) is reported and read as bag 0 (never out of bounds)
+  auto fetch_meta = [&](int e, int32_t& occ, float& w) {
+    occ = -1;
+    w = 0.f;
+    if (e < NE) {
+      occ = a.occ[E0 + e];
+      w = a.occ_w[E0 + e];
+    }
+  };
+  auto commit_meta = [&](int e, int32_t occ, float w) {
+    int32_t bag = 0;
+    if (e < NE) {
+      if ((uint32_t)occ < n_occ) {
+        bag = (int32_t)((uint32_t)occ / L);
+      } else {
+        raise_err(a.err, PKM_DEVERR_INDEX);
+        occ = 0;
+        w = 0.f;
+      }
+    }
+    m_sp[e & (kMetaRing - 1)] = make_int2(bag, occ);
+    m_w[e & (kMetaRing - 1)] = w;
+  };
   // metadata pages 0 and 1 in shared memory, page 2 in registers
   {
-    GatherPrefetch p0 = gather_prefetch<G_SEG>(a, E0 + lane, E0 + NE);
-    GatherPrefetch p1 = gather_prefetch<G_SEG>(a, E0 + 32 + lane, E0 + NE);
-    gather_commit<G_SEG>(a, p0, E0 + lane, E0 + NE, m_sp, m_w, lane);
-    gather_commit<G_SEG>(a, p1, E0 + 32 + lane, E0 + NE, m_sp, m_w, 32 + lane);
+    int32_t o0, o1;
+    float w0, w1;
+    fetch_meta(lane, o0, w0);
+    fetch_meta(32 + lane, o1, w1);
+    commit_meta(lane, o0, w0);
+    commit_meta(32 + lane, o1, w1);
   }
-  GatherPrefetch pf = gather_prefetch<G_SEG>(a, E0 + 64 + lane, E0 + NE);
+  int32_t pf_occ;
+  float pf_w;
+  fetch_meta(64 + lane, pf_occ, pf_w);
   m_items[lane] = lane < ni ? a.item_desc[i0 + lane] : make_int4(0, 0, 0, -1);
   m_items[32 + lane] = 32 + lane < ni ? a.item_desc[i0 + 32 + lane] : make_int4(0, 0, 0, -1);
   int4 ipf = (64 + lane < ni) ? a.item_desc[i0 + 64 + lane] : make_int4(0, 0, 0, -1);
   __syncwarp();
 
-  // copy this lane's vectors of entry `rel` into ring slot `slot` (= rel mod
-  // DEPTH); one group per entry (empty past the end) keeps the group count
-  // uniform
+  // this lane's 16-byte vectors: global row offset lane*16 + v*512, ring
+  // offset slot*RB + lane*16 + v*512
   const int rb = (int)RB;
-  auto issue = [&](int64_t rel, int slot) {
-    if (rel < NE) {
-      const int32_t bag = m_sp[rel & (kMetaRing - 1)].x;
-      if (bag >= 0 && bag < a.num_rows) {
-        const char* src = a.rows + (int64_t)bag * RB;
-        unsigned char* dst = ring + slot * rb;
+  const char* src_lane = a.rows + lane * 16;
+  const uint32_t ring_lane = smem_u32(ring) + lane * 16;
+  // copy entry e's vectors into ring slot `slot` (= e mod DEPTH); one group
+  // per entry, empty past the end, keeps the group count uniform
+  auto issue = [&](int e, int slot) {
+    if (e < NE) {
+      const char* src = src_lane + (int64_t)m_sp[e & (kMetaRing - 1)].x * RB;
+      const uint32_t dst = ring_lane + slot * rb;
 #pragma unroll
-        for (int v = 0; v < VPL; ++v) {
-          const int off = (v * 32 + lane) * 16;
-          if (FULL || off < RB) cp_async16(dst + off, src + off);
-        }
-      } else {
-        raise_err(a.err, PKM_DEVERR_INDEX);
+      for (int v = 0; v < VPL; ++v) {
+        if (FULL || (v * 32 + lane) * 16 < rb)
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + v * 512), "l"(src + v * 512)
+                       : "memory");
       }
     }
     cp_async_commit();
@@ -166,18 +192,18 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const GatherArgs
 #pragma unroll
     for (int v = 0; v < VPL; ++v) {
       const int off = (v * 32 + lane) * 16;
-      r[v] = (FULL || off < RB) ? ld_nc_hint(base + off, pol) : make_uint4(0, 0, 0, 0);
+      r[v] = (FULL || off < rb) ? ld_nc_hint(base + off, pol) : make_uint4(0, 0, 0, 0);
     }
   };
 
   // item state
-  int64_t j = 0;         // current item (relative)
-  int64_t item_end = 0;  // its end (relative entry index)
+  int j = 0;         // current item (relative)
+  int item_end = 0;  // its end (relative entry index)
   int4 cur = make_int4(0, 0, 0, -1);
   uint64_t acc[VPL][NP];
   uint64_t dv[VPL][NP];
   uint4 dv_raw[VPL];
-  int64_t dv_item = -1;  // item whose table row sits in dv_raw
+  int dv_item = -1;  // item whose table row sits in dv_raw
   if (DOT) {
     load_row(a.dotvec + (int64_t)m_items[0].x * RB, dv_raw, stream);
     dv_item = 0;
@@ -199,7 +225,7 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const GatherArgs
   // item page bookkeeping after item j is finished
   auto item_done = [&]() {
     if ((j & 31) == 31) {
-      const int64_t ip = j >> 5;
+      const int ip = j >> 5;
       __syncwarp();
       m_items[((ip + 2) * 32 + lane) & (kMetaRing - 1)] = ipf;
       ipf = make_int4(0, 0, 0, -1);
@@ -221,7 +247,7 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const GatherArgs
       item_done();
     }
     if (j >= ni) return;
-    item_end = (int64_t)cur.z - E0;
+    item_end = (int)((int64_t)cur.z - E0);
     if (DOT) {
       if (dv_item != j) load_row(a.dotvec + (int64_t)cur.x * RB, dv_raw, stream);
 #pragma unroll
@@ -235,65 +261,87 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const GatherArgs
   };
 
   open_item();
-  int cslot = 0;  // ring slot of entry rel
-#pragma unroll 1
-  for (int64_t rel = 0; rel < NE; ++rel) {
-    if (rel == item_end) {
+  int cslot = 0;  // ring slot of entry e
+  int e = 0;
+  while (e < NE) {
+    if (e == item_end) {
       write_row(cur, acc);
       item_done();
       open_item();
     }
-    cp_async_wait<DEPTH - 1>();  // this lane's copies of entry rel have landed
-    const unsigned char* slot = ring + cslot * rb;
-    const float w = m_w[rel & (kMetaRing - 1)];
-    const uint64_t w2 = pack2(__float_as_uint(w), __float_as_uint(w));
-    uint64_t ds[VPL];
-#pragma unroll
-    for (int v = 0; v < VPL; ++v) {
-      ds[v] = 0ull;
-      const int off = (v * 32 + lane) * 16;
-      if (FULL || off < RB) {
-        uint64_t f[NP];
-        Pairs<RowT>::unpack(*reinterpret_cast<const uint4*>(slot + off), f);
-#pragma unroll
-        for (int t = 0; t < NP; ++t) {
-          ffma2(acc[v][t], w2, f[t]);
-          if (DOT) ffma2(ds[v], dv[v][t], f[t]);
-        }
-      }
-    }
-    issue(rel + DEPTH, cslot);  // the slot's values are in registers now
-    cslot = cslot + 1 == DEPTH ? 0 : cslot + 1;
-    if (DOT) {
-      float d0 = 0.f, d1 = 0.f;
+    // a run of entries with no item or page boundary inside
+    const int stop = min(min(item_end, NE), (e | 31) + 1);
+    const bool all_issue = stop + DEPTH <= NE;
+#pragma unroll 1
+    for (; e < stop; ++e) {
+      cp_async_wait<DEPTH - 1>();  // this lane's copies of entry e have landed
+      const uint32_t slot = ring_lane + cslot * rb;
+      const float w = m_w[e & (kMetaRing - 1)];
+      const uint64_t w2 = pack2(__float_as_uint(w), __float_as_uint(w));
+      uint64_t ds[VPL];
 #pragma unroll
       for (int v = 0; v < VPL; ++v) {
-        float x0, x1;
-        unpack2(ds[v], x0, x1);
-        d0 += x0;
-        d1 += x1;
+        ds[v] = 0ull;
+        if (FULL || (v * 32 + lane) * 16 < rb) {
+          uint4 raw;
+          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w)
+                       : "r"(slot + v * 512));
+          uint64_t f[NP];
+          Pairs<RowT>::unpack(raw, f);
+#pragma unroll
+          for (int t = 0; t < NP; ++t) {
+            ffma2(acc[v][t], w2, f[t]);
+            if (DOT) ffma2(ds[v], dv[v][t], f[t]);
+          }
+        }
       }
-      m_dot[rel & 31][lane] = d0 + d1;
+      // the slot's values are in registers: refill it with entry e + DEPTH
+      if (all_issue) {
+        const char* src = src_lane + (int64_t)m_sp[(e + DEPTH) & (kMetaRing - 1)].x * RB;
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) {
+          if (FULL || (v * 32 + lane) * 16 < rb)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(slot + v * 512), "l"(src + v * 512)
+                         : "memory");
+        }
+        cp_async_commit();
+      } else {
+        issue(e + DEPTH, cslot);
+      }
+      cslot = cslot + 1 == DEPTH ? 0 : cslot + 1;
+      if (DOT) {
+        float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) {
+          float x0, x1;
+          unpack2(ds[v], x0, x1);
+          d0 += x0;
+          d1 += x1;
+        }
+        m_dot[e & 31][lane] = d0 + d1;
+      }
     }
-    if ((rel & 31) == 31 || rel + 1 == NE) {
+    if ((e & 31) == 0 || e == NE) {
+      // the page of entries (e - 1) / 32 is consumed (or the stream ended)
+      const int last = e - 1;
+      const int first = last & ~31;
       __syncwarp();
       if (DOT) {
-        // the page's dots: row r of the transpose is entry r's lane partials
-        const int64_t first = rel & ~(int64_t)31;
-        if (lane <= (int)(rel - first)) {
-          float s = 0.f;
+        // row r of the transpose holds entry r's lane partials
+        if (lane <= last - first) {
+          float sum = 0.f;
 #pragma unroll 8
-          for (int l = 0; l < 32; ++l) s += m_dot[lane][l];
-          st_f(a.dotout, a.dotout_dtype, m_sp[(first + lane) & (kMetaRing - 1)].y, s);
+          for (int l = 0; l < 32; ++l) sum += m_dot[lane][l];
+          st_f(a.dotout, a.dotout_dtype, m_sp[(first + lane) & (kMetaRing - 1)].y, sum);
         }
         __syncwarp();
       }
-      if ((rel & 31) == 31) {
-        // metadata page rel/32 is consumed: its half receives page rel/32 + 2
-        const int64_t page = rel >> 5;
-        const int64_t e2 = E0 + (page + 2) * 32 + lane;
-        gather_commit<G_SEG>(a, pf, e2, E0 + NE, m_sp, m_w, (int)((e2 - E0) & (kMetaRing - 1)));
-        pf = gather_prefetch<G_SEG>(a, E0 + (page + 3) * 32 + lane, E0 + NE);
+      if ((e & 31) == 0) {
+        // its half of the metadata ring receives page last/32 + 2
+        const int page = last >> 5;
+        commit_meta((page + 2) * 32 + lane, pf_occ, pf_w);
+        fetch_meta((page + 3) * 32 + lane, pf_occ, pf_w);
         __syncwarp();
       }
     }
