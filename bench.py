@@ -216,11 +216,19 @@ def run_ours(args, rank, world, local_rank):
     x = torch.randn((B, T, C), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
     x_host = x.cpu().pin_memory()
     reducer = None
+    exchange = "none"
     if world > 1:
-        from modelos_b200.dist import GradReducer
-        # the value-table gradient is all-reduced as soon as the bag backward
-        # has produced it, overlapping the rest of the backward
-        reducer = GradReducer(params, early=[m.values.weight])
+        from modelos_b200.dist import GradReducer, ShardedTableGrad
+        if args.grad_exchange == "fused":
+            # the value-table gradient goes to its row owners over NVLink while
+            # the bag backward computes it; owners reduce and all-gather beside
+            # the rest of the backward
+            reducer = GradReducer(params, sharded=[ShardedTableGrad(m.values.weight)])
+            exchange = "fused: segment-pass stores to row owners (symmetric memory) + owner reduce/all-gather"
+        else:
+            # NCCL all-reduce started as soon as the bag backward produced it
+            reducer = GradReducer(params, early=[m.values.weight])
+            exchange = "nccl all-reduce from a post-accumulate hook"
 
     def step(xin):
         for p in params:
@@ -331,7 +339,7 @@ def run_ours(args, rank, world, local_rank):
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded normal x, reset_parameters init)",
-        "config": config_obj(world),
+        "config": dict(config_obj(world), grad_exchange=exchange),
         "e2e": {"value": round(B * T * world / (e2e_ms / 1000.0), 1), "unit": UNIT,
                 "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4,
                 "ms_per_step": round(e2e_ms, 4)},
@@ -353,6 +361,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--grad-exchange", default="fused", choices=["fused", "nccl"],
+                    help="data-parallel exchange of the value-table gradient (N > 1)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -194,6 +194,42 @@ PKM_API int pkm_score_grad_dense(const int64_t* indices, const void* psw, const 
                                  int64_t rows, int64_t knn, int64_t n_keys, void* d_scores, void* stream);
 
 /*
+ * Data-parallel bag backward: K4 fused with the reduce-scatter of the table
+ * gradient over NVLink.  Rank o owns table rows [o*shard_rows,
+ * (o+1)*shard_rows) and holds a receive buffer [world][shard_rows][dim] (dtype
+ * grad_weight_dtype) that every rank can store to (IPC or symmetric memory);
+ * recv_bases is a HOST array of the world buffers' device addresses.  Instead
+ * of writing a local dense gradient, the segment pass stores this rank's
+ * gradient of row r into recv_bases[r / shard_rows] at row
+ * rank*shard_rows + r % shard_rows while it computes, so the transfer overlaps
+ * the pass.  Every other argument is pkm_bag_bwd's; world <= 8 (one NVLink
+ * domain).  Replaces embedding_bag_bw_rev_indices
+ * (pkm/xformer_embeddingbag.py:331-386) followed by the data-parallel
+ * all-reduce of values.weight.grad (its reduce-scatter half).
+ */
+PKM_API int pkm_bag_bwd_sharded(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                                int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                                int64_t num_rows, int64_t dim, void* const* recv_bases, int world, int rank,
+                                int64_t shard_rows, int grad_weight_dtype, void* grad_psw, int grad_psw_dtype,
+                                int32_t* row_counts, void* workspace, size_t workspace_bytes, uint32_t* dev_err,
+                                void* stream);
+
+/*
+ * Owner side of the exchange (the all-gather half): sums the world partial
+ * copies of this rank's shard in its receive buffer `recv` (fixed source
+ * order, fp32), multiplies by `scale` (1/world averages), and stores the
+ * rows into rows [rank*shard_rows, ...) of every rank's gradient
+ * grad_bases[d] (HOST array of world peer-writable device addresses).
+ * max_blocks > 0 bounds the grid so that the kernel can run beside the rest
+ * of the backward on another stream.  The caller orders this after every
+ * rank's pkm_bag_bwd_sharded (a barrier), and readers of the gradient after
+ * every rank's pkm_grad_shard_reduce (a second barrier).  dtype f32 or bf16.
+ */
+PKM_API int pkm_grad_shard_reduce(const void* recv, int dtype, int64_t num_rows, int64_t dim, int world, int rank,
+                                  int64_t shard_rows, void* const* grad_bases, float scale, int max_blocks,
+                                  void* stream);
+
+/*
  * Batch normalisation of the query projection, x [n, c] row-major (rows =
  * tokens, c a multiple of 8, x / out / dy / dx 16-byte aligned; x f32 or
  * bf16).  Replaces the query network's nn.BatchNorm1d(heads * k_dim,

@@ -40,6 +40,9 @@ _SIGS = {
     "pkm_product_topk": ([_P, _I, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P], _I),
     "pkm_score_bwd_prep": ([_P, _P, _P, _I, _I64, _I64, _I64, _I64, _P, _P, _P], _I),
     "pkm_score_grad_dense": ([_P, _P, _P, _I, _I64, _I64, _I64, _P, _P], _I),
+    "pkm_bag_bwd_sharded": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _I, _I64, _I, _P, _I, _P, _P,
+                             ctypes.c_size_t, _P, _P], _I),
+    "pkm_grad_shard_reduce": ([_P, _I, _I64, _I64, _I, _I, _I64, _P, ctypes.c_float, _I, _P], _I),
     "pkm_batchnorm_workspace": ([_I64, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
     "pkm_batchnorm_fwd": ([_P, _I, _I64, _I64, _P, _P, _I, _P, _P, _I, _I, ctypes.c_double, ctypes.c_double,
                            _P, _P, _P, _P, ctypes.c_size_t, _P], _I),
@@ -257,6 +260,51 @@ def bag_bwd(indices: torch.Tensor, weight: Optional[torch.Tensor], psw: Optional
     _pstop("pkm_bag_bwd", ev)
     _check(rc, "pkm_bag_bwd")
     return grad_weight, grad_psw, counts
+
+
+def _ptr_array(ptrs):
+    return (ctypes.c_void_p * len(ptrs))(*[ctypes.c_void_p(int(p)) for p in ptrs])
+
+
+def bag_bwd_sharded(indices: torch.Tensor, weight: torch.Tensor, psw: Optional[torch.Tensor],
+                    grad_out: torch.Tensor, recv_bases, rank: int, shard_rows: int, *, need_dpsw: bool = True):
+    """K4 with the table gradient stored into the owners' receive buffers
+    (``recv_bases[o]``: device address of rank o's [world, shard_rows, D]
+    buffer).  Returns the per-sample-weight gradient (or None)."""
+    assert indices.dim() == 2 and indices.dtype == torch.long and indices.is_contiguous()
+    assert grad_out.dim() == 2 and grad_out.shape[0] == indices.shape[0] and grad_out.is_contiguous()
+    assert weight.dim() == 2 and weight.is_contiguous() and weight.shape[1] == grad_out.shape[1]
+    assert grad_out.dtype == weight.dtype, "grad_out must have the table's dtype"
+    _need_cuda(indices, grad_out, weight, psw)
+    B, L = indices.shape
+    K, D = weight.shape
+    dev = grad_out.device
+    grad_psw = torch.empty_like(psw) if (need_dpsw and psw is not None) else None
+    ws_bytes = bag_bwd_workspace(B, L, K, D)
+    ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+    world = len(recv_bases)
+    ev = _pstart("pkm_bag_bwd", K)
+    rc = lib().pkm_bag_bwd_sharded(_ptr(indices), _ptr(psw), DT[psw.dtype] if psw is not None else 0, _ptr(weight),
+                                   DT[weight.dtype], _ptr(grad_out), B, L, K, D, _ptr_array(recv_bases), world, rank,
+                                   shard_rows, DT[weight.dtype], _ptr(grad_psw),
+                                   DT[grad_psw.dtype] if grad_psw is not None else 0, None, _ptr(ws), ws_bytes,
+                                   _ptr(err_word(dev)), _stream(dev))
+    _pstop("pkm_bag_bwd", ev)
+    _check(rc, "pkm_bag_bwd_sharded")
+    return grad_psw
+
+
+def grad_shard_reduce(recv: torch.Tensor, num_rows: int, rank: int, shard_rows: int, grad_bases, scale: float = 1.0,
+                      max_blocks: int = 0):
+    """Sum this rank's received partial shard rows and store them into every
+    rank's gradient (``grad_bases``: device addresses, one per rank)."""
+    _need_cuda(recv)
+    world = len(grad_bases)
+    assert recv.is_contiguous() and recv.shape[0] == world and recv.shape[1] == shard_rows
+    D = recv.shape[2]
+    _check(lib().pkm_grad_shard_reduce(_ptr(recv), DT[recv.dtype], num_rows, D, world, rank, shard_rows,
+                                       _ptr_array(grad_bases), float(scale), int(max_blocks), _stream(recv.device)),
+           "pkm_grad_shard_reduce")
 
 
 def bag_bwd2(indices: torch.Tensor, a: Optional[torch.Tensor], gbar: torch.Tensor,

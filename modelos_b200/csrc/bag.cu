@@ -165,9 +165,24 @@ __global__ void items_fill_kernel(const int32_t* __restrict__ counts, const I4* 
   if (blockIdx.x == 0 && threadIdx.x == 0) *n_items = offs[K].y;
 }
 
+// Destination rows of the bag backward's weight gradient: the local gradient,
+// or (data-parallel) row r of the table goes to rank r / shard_rows, row
+// rank * shard_rows + r % shard_rows of that rank's receive buffer.
+struct GradDest {
+  void* out;
+  int64_t shard_rows;  // 0: local
+  int rank;
+  char* base[kMaxShards];
+  __device__ __forceinline__ void* row(int64_t r, int64_t D, int dt) const {
+    if (shard_rows == 0) return static_cast<char*>(out) + r * D * dtype_size_dev(dt);
+    const int64_t o = r / shard_rows;
+    return base[o] + (rank * shard_rows + (r - o * shard_rows)) * D * dtype_size_dev(dt);
+  }
+};
+
 // Rows split over several chunks: sum the chunk partials in chunk order.
 __global__ void reduce_partials_kernel(const I4* __restrict__ offs, int64_t K, const float* __restrict__ partials,
-                                       int64_t D, void* out, int out_dtype) {
+                                       int64_t D, const __grid_constant__ GradDest dest, int out_dtype) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t k = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); k < K; k += warps) {
@@ -175,12 +190,58 @@ __global__ void reduce_partials_kernel(const I4* __restrict__ offs, int64_t K, c
     const int items = offs[k + 1].y - o.y;
     if (items <= 1) continue;
     const float* base = partials + (int64_t)o.z * D;
+    void* row = dest.row(k, D, out_dtype);
     for (int64_t e = lane; e < D; e += 32) {
       float s = 0.f;
       for (int j = 0; j < items; ++j) s += base[(int64_t)j * D + e];
-      st_f(out, out_dtype, k * D + e, s);
+      st_f(row, out_dtype, e, s);
     }
   }
+  if (dest.shard_rows > 0) __threadfence_system();
+}
+
+// Zero rows for every table row (data-parallel backward of an empty bag set:
+// this rank's slots of all owners' receive buffers).
+__global__ void zero_rows_kernel(int64_t K, int64_t D, const __grid_constant__ GradDest dest, int out_dtype) {
+  const int64_t vec = D * dtype_size_dev(out_dtype) / 16;
+  const int64_t total = K * vec;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / vec;
+    reinterpret_cast<uint4*>(dest.row(r, D, out_dtype))[i - r * vec] = make_uint4(0, 0, 0, 0);
+  }
+  if (dest.shard_rows > 0) __threadfence_system();
+}
+
+// Owner side of the data-parallel exchange: sum the world partial copies of
+// this rank's shard rows (fixed source order, fp32), scale, and store the
+// result into row (rank * shard_rows + r) of every rank's gradient.
+template <typename T>
+__global__ void shard_reduce_kernel(const T* __restrict__ recv, int64_t shard_rows, int64_t rows, int64_t D,
+                                    int world, int rank, float scale, const __grid_constant__ GradDest dest) {
+  constexpr int EPV = 16 / sizeof(T);
+  const int64_t vec = D / EPV;
+  const int64_t total = rows * vec;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / vec, v = i - r * vec;
+    float acc[EPV];
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) acc[k] = 0.f;
+    for (int s = 0; s < world; ++s) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(recv + ((int64_t)s * shard_rows + r) * D + v * EPV);
+      float f[EPV];
+      VecTraits<T>::unpack(raw, f);
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) acc[k] += f[k];
+    }
+#pragma unroll
+    for (int k = 0; k < EPV; ++k) acc[k] *= scale;
+    const int64_t grow = rank * shard_rows + r;
+    for (int d = 0; d < world; ++d) {
+      T* dst = reinterpret_cast<T*>(dest.base[d]) + grow * D + v * EPV;
+      st_run(dst, DtOf<T>::value, 0, acc, EPV);
+    }
+  }
+  __threadfence_system();
 }
 
 constexpr int kChunk = 256;
@@ -330,18 +391,19 @@ extern "C" int pkm_bag_bwd_workspace(int64_t n_bags, int64_t bag_size, int64_t n
   return PKM_OK;
 }
 
-extern "C" int pkm_bag_bwd(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
-                           int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
-                           int64_t num_rows, int64_t dim, void* grad_weight, int grad_weight_dtype,
-                           void* grad_psw, int grad_psw_dtype, int32_t* row_counts, void* workspace,
-                           size_t workspace_bytes, uint32_t* dev_err, void* stream) {
+static int bag_bwd_impl(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                        int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size, int64_t num_rows,
+                        int64_t dim, const GradDest& dest, int grad_weight_dtype, void* grad_psw,
+                        int grad_psw_dtype, int32_t* row_counts, void* workspace, size_t workspace_bytes,
+                        uint32_t* dev_err, void* stream) {
   int rc = check_bag_common(indices, n_bags, bag_size, num_rows, dim, weight_dtype);
   if (rc) return rc;
   if (!valid_dtype(grad_weight_dtype) || (psw && !valid_dtype(psw_dtype)) ||
       (grad_psw && !valid_dtype(grad_psw_dtype)))
     return fail(PKM_ERR_INVALID_ARG, "bad dtype");
   if (grad_psw && !psw) return fail(PKM_ERR_INVALID_ARG, "grad_psw requested without per-sample weights");
-  if (num_rows > 0 && grad_weight == nullptr) return fail(PKM_ERR_INVALID_ARG, "grad_weight is NULL");
+  if (num_rows > 0 && dest.shard_rows == 0 && dest.out == nullptr)
+    return fail(PKM_ERR_INVALID_ARG, "grad_weight is NULL");
   const int64_t M = n_bags * bag_size;
   const int64_t K = num_rows;
   const int64_t D = dim;
@@ -352,7 +414,12 @@ extern "C" int pkm_bag_bwd(const int64_t* indices, const void* psw, int psw_dtyp
     return fail(PKM_ERR_INVALID_ARG, "weight NULL or not 16-byte aligned");
   const BwdLayout L = bwd_layout(M, K, D);
   if (M == 0 || K == 0) {
-    if (K > 0) cudaMemsetAsync(grad_weight, 0, (size_t)(K * D * dtype_size(grad_weight_dtype)), st);
+    if (K > 0 && dest.shard_rows > 0) {
+      const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((K * D / 8 + 255) / 256, (int64_t)num_sms() * 8));
+      zero_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(K, D, dest, grad_weight_dtype);
+    } else if (K > 0) {
+      cudaMemsetAsync(dest.out, 0, (size_t)(K * D * dtype_size(grad_weight_dtype)), st);
+    }
     if (row_counts && K > 0) cudaMemsetAsync(row_counts, 0, sizeof(int32_t) * K, st);
     if (grad_psw && M > 0) cudaMemsetAsync(grad_psw, 0, (size_t)(M * dtype_size(grad_psw_dtype)), st);
     if (M > 0 && dev_err) cudaMemsetAsync(dev_err, PKM_DEVERR_INDEX, 1, st);
@@ -429,10 +496,13 @@ extern "C" int pkm_bag_bwd(const int64_t* indices, const void* psw, int psw_dtyp
     a.dotvec = static_cast<const char*>(weight);
     a.dotout = grad_psw;
     a.dotout_dtype = grad_psw_dtype;
-    a.out = grad_weight;
+    a.out = dest.out;
     a.out_dtype = grad_weight_dtype;
     a.partials = partials;
     a.err = dev_err;
+    a.shard_rows = dest.shard_rows;
+    a.shard_rank = dest.rank;
+    for (int i = 0; i < kMaxShards; ++i) a.shard_base[i] = dest.base[i];
     const int64_t items_upper = K + (M + kChunk - 1) / kChunk + 1;
     rc = gather_launch(weight_dtype, true, grad_psw != nullptr, a, items_upper, st);
     if (rc) return rc;
@@ -440,9 +510,77 @@ extern "C" int pkm_bag_bwd(const int64_t* indices, const void* psw, int psw_dtyp
   // 6. rows that were split over several chunks
   {
     int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((K + 7) / 8, (int64_t)nsm * 8));
-    reduce_partials_kernel<<<(unsigned)blocks, 256, 0, st>>>(offs, K, partials, D, grad_weight, grad_weight_dtype);
+    reduce_partials_kernel<<<(unsigned)blocks, 256, 0, st>>>(offs, K, partials, D, dest, grad_weight_dtype);
   }
   return check_cuda("pkm_bag_bwd");
+}
+
+extern "C" int pkm_bag_bwd(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                           int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                           int64_t num_rows, int64_t dim, void* grad_weight, int grad_weight_dtype,
+                           void* grad_psw, int grad_psw_dtype, int32_t* row_counts, void* workspace,
+                           size_t workspace_bytes, uint32_t* dev_err, void* stream) {
+  GradDest dest{};
+  dest.out = grad_weight;
+  return bag_bwd_impl(indices, psw, psw_dtype, weight, weight_dtype, grad_out, n_bags, bag_size, num_rows, dim, dest,
+                      grad_weight_dtype, grad_psw, grad_psw_dtype, row_counts, workspace, workspace_bytes, dev_err,
+                      stream);
+}
+
+static int shard_dest(GradDest& dest, void* const* bases, int world, int rank, int64_t shard_rows, int64_t num_rows,
+                      int64_t dim, int dtype) {
+  if (world < 1 || world > kMaxShards || rank < 0 || rank >= world)
+    return fail(PKM_ERR_INVALID_ARG, "need 1 <= world <= 8 and 0 <= rank < world");
+  if (!bases) return fail(PKM_ERR_INVALID_ARG, "shard base pointers are NULL");
+  if (shard_rows <= 0 || shard_rows * world < num_rows)
+    return fail(PKM_ERR_INVALID_ARG, "shard_rows * world must cover num_rows");
+  if ((dim * dtype_size(dtype)) % 16 != 0) return fail(PKM_ERR_UNSUPPORTED, "row bytes must be a multiple of 16");
+  dest.out = nullptr;
+  dest.shard_rows = shard_rows;
+  dest.rank = rank;
+  for (int i = 0; i < kMaxShards; ++i) dest.base[i] = nullptr;
+  for (int i = 0; i < world; ++i) {
+    if (!bases[i] || !aligned16(bases[i])) return fail(PKM_ERR_INVALID_ARG, "shard base NULL or not 16-byte aligned");
+    dest.base[i] = static_cast<char*>(bases[i]);
+  }
+  return PKM_OK;
+}
+
+extern "C" int pkm_bag_bwd_sharded(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                                   int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                                   int64_t num_rows, int64_t dim, void* const* recv_bases, int world, int rank,
+                                   int64_t shard_rows, int grad_weight_dtype, void* grad_psw, int grad_psw_dtype,
+                                   int32_t* row_counts, void* workspace, size_t workspace_bytes, uint32_t* dev_err,
+                                   void* stream) {
+  GradDest dest{};
+  int rc = shard_dest(dest, recv_bases, world, rank, shard_rows, num_rows, dim, grad_weight_dtype);
+  if (rc) return rc;
+  return bag_bwd_impl(indices, psw, psw_dtype, weight, weight_dtype, grad_out, n_bags, bag_size, num_rows, dim, dest,
+                      grad_weight_dtype, grad_psw, grad_psw_dtype, row_counts, workspace, workspace_bytes, dev_err,
+                      stream);
+}
+
+extern "C" int pkm_grad_shard_reduce(const void* recv, int dtype, int64_t num_rows, int64_t dim, int world, int rank,
+                                     int64_t shard_rows, void* const* grad_bases, float scale, int max_blocks,
+                                     void* stream) {
+  if (dtype != PKM_DT_F32 && dtype != PKM_DT_BF16) return fail(PKM_ERR_UNSUPPORTED, "dtype must be f32 or bf16");
+  GradDest dest{};
+  int rc = shard_dest(dest, grad_bases, world, rank, shard_rows, num_rows, dim, dtype);
+  if (rc) return rc;
+  if (!recv || !aligned16(recv)) return fail(PKM_ERR_INVALID_ARG, "recv NULL or not 16-byte aligned");
+  const int64_t rows = std::min<int64_t>(shard_rows, num_rows - (int64_t)rank * shard_rows);
+  if (rows <= 0) return PKM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t total = rows * dim * dtype_size(dtype) / 16;
+  int64_t blocks = std::max<int64_t>(1, (total + 255) / 256);
+  if (max_blocks > 0) blocks = std::min<int64_t>(blocks, max_blocks);
+  if (dtype == PKM_DT_F32)
+    shard_reduce_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const float*>(recv), shard_rows, rows,
+                                                                 dim, world, rank, scale, dest);
+  else
+    shard_reduce_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(recv), shard_rows, rows, dim, world, rank, scale, dest);
+  return check_cuda("pkm_grad_shard_reduce");
 }
 
 // ---------------------------------------------------------------------------

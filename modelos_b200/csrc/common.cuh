@@ -24,6 +24,7 @@ int num_sms();
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool valid_dtype(int dt) { return dt == PKM_DT_F32 || dt == PKM_DT_BF16 || dt == PKM_DT_F16; }
 inline int dtype_size(int dt) { return dt == PKM_DT_F32 ? 4 : 2; }
+__host__ __device__ inline int dtype_size_dev(int dt) { return dt == PKM_DT_F32 ? 4 : 2; }
 
 // ---------------------------------------------------------------------------
 // device side: scalar conversions
@@ -43,6 +44,21 @@ __device__ __forceinline__ void st_f(void* p, int dt, int64_t i, float v) {
     static_cast<__half*>(p)[i] = __float2half_rn(v);
   }
 }
+
+template <typename T>
+struct DtOf;
+template <>
+struct DtOf<float> {
+  static constexpr int value = PKM_DT_F32;
+};
+template <>
+struct DtOf<__nv_bfloat16> {
+  static constexpr int value = PKM_DT_BF16;
+};
+template <>
+struct DtOf<__half> {
+  static constexpr int value = PKM_DT_F16;
+};
 
 template <typename T>
 struct VecTraits;

@@ -24,6 +24,7 @@
 namespace pkm {
 
 enum { G_BAG = 0, G_SEG = 1 };
+constexpr int kMaxShards = 8;  // ranks of one NVLink domain
 constexpr int kMetaRing = 64;
 
 struct GatherArgs {
@@ -53,6 +54,12 @@ struct GatherArgs {
   uint32_t* err;
   int slots;
   int64_t warp_smem;
+  // segment mode, data-parallel: row r's gradient goes to rank r / shard_rows,
+  // at row (shard_rank * shard_rows + r % shard_rows) of that rank's receive
+  // buffer shard_base[r / shard_rows] (peer memory); shard_rows == 0: `out`
+  int64_t shard_rows;
+  int shard_rank;
+  char* shard_base[kMaxShards];
 };
 
 // ---------------------------------------------------------------------------

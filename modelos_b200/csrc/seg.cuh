@@ -52,8 +52,11 @@ __device__ __forceinline__ void st_hint(void* p, const uint4& v, uint64_t pol) {
                : "memory");
 }
 
-// Store 2*NP fp32 values (NP packed pairs) as dtype dt at element e0 of p.
-// The vectors here are 16-byte aligned (whole rows of 16-byte multiples).
+__device__ __forceinline__ void st_plain(void* p, const uint4& v) { *reinterpret_cast<uint4*>(p) = v; }
+
+// Store 2*NP fp32 values (NP packed pairs) as dtype dt at element e0 of p,
+// with the L2 evict-first policy `pol` (local memory) or a plain store
+// (peer memory, pol == 0).  The vectors here are 16-byte aligned.
 template <int NP>
 __device__ __forceinline__ void seg_store_vec(void* p, int dt, int64_t e0, const uint64_t (&acc)[NP],
                                               uint64_t pol) {
@@ -71,11 +74,17 @@ __device__ __forceinline__ void seg_store_vec(void* p, int dt, int64_t e0, const
     v.z = *reinterpret_cast<uint32_t*>(&h);
     h = __floats2bfloat162_rn(o[6], o[7]);
     v.w = *reinterpret_cast<uint32_t*>(&h);
-    st_hint(static_cast<__nv_bfloat16*>(p) + e0, v, pol);
+    if (pol)
+      st_hint(static_cast<__nv_bfloat16*>(p) + e0, v, pol);
+    else
+      st_plain(static_cast<__nv_bfloat16*>(p) + e0, v);
   } else if (dt == PKM_DT_F32 && NP == 2) {
-    st_hint(static_cast<float*>(p) + e0,
-            make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]), __float_as_uint(o[3])),
-            pol);
+    const uint4 v =
+        make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]), __float_as_uint(o[3]));
+    if (pol)
+      st_hint(static_cast<float*>(p) + e0, v, pol);
+    else
+      st_plain(static_cast<float*>(p) + e0, v);
   } else {
     st_run(p, dt, e0, o, 2 * NP);
   }
@@ -96,7 +105,7 @@ __host__ __device__ constexpr int64_t seg_warp_smem(int64_t rb, int depth, bool 
 }
 
 template <typename RowT, int VPL, bool DOT, int NW, bool FULL, int DEPTH>
-__global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const GatherArgs a) {
+__global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const __grid_constant__ GatherArgs a) {
   static_assert(DEPTH >= 2 && DEPTH <= 8, "at most 8 copy groups in flight per thread");
   constexpr int NP = Pairs<RowT>::NP;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -210,6 +219,17 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const GatherArgs
   }
 
   auto write_row = [&](const int4& d, const uint64_t (&row)[VPL][NP]) {
+    // destination of a finished row: the local gradient, or the owner rank's
+    // receive buffer in data-parallel mode
+    void* dst = a.out;
+    int64_t drow = d.x;
+    uint64_t pol = stream;
+    if (a.shard_rows > 0) {
+      const int64_t o = d.x / a.shard_rows;
+      dst = a.shard_base[o];
+      drow = a.shard_rank * a.shard_rows + (d.x - o * a.shard_rows);
+      pol = 0;
+    }
 #pragma unroll
     for (int v = 0; v < VPL; ++v) {
       const int64_t c = (int64_t)(v * 32 + lane);
@@ -218,7 +238,7 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const GatherArgs
         if (d.w >= 0)
           seg_store_vec<NP>(a.partials, PKM_DT_F32, (int64_t)d.w * a.dim + e0, row[v], stream);
         else
-          seg_store_vec<NP>(a.out, a.out_dtype, (int64_t)d.x * a.dim + e0, row[v], stream);
+          seg_store_vec<NP>(dst, a.out_dtype, drow * a.dim + e0, row[v], pol);
       }
     }
   };
@@ -353,6 +373,8 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const GatherArgs
     item_done();
   }
   open_item();
+  // peer stores are ordered before whatever this GPU signals to its peers next
+  if (a.shard_rows > 0) __threadfence_system();
 }
 
 }  // namespace pkm

@@ -19,6 +19,86 @@ import torch
 import torch.distributed as dist
 
 
+class ShardedTableGrad:
+    """Data-parallel gradient of a value table, exchanged while it is computed.
+
+    Rank ``o`` owns table rows ``[o*S, (o+1)*S)`` (``S = ceil(K / world)``).
+    In the bag backward, the segment pass stores each row's gradient straight
+    into the owner's receive buffer over NVLink (``pkm_bag_bwd_sharded``:
+    the reduce-scatter runs inside the compute).  On a side stream, after a
+    barrier, every owner sums the ``world`` partial copies of its rows and
+    stores the result into every rank's gradient buffer
+    (``pkm_grad_shard_reduce``: the all-gather), beside the rest of the
+    backward; a second barrier completes the exchange.  Both buffers are
+    symmetric memory (peer-addressable).  ``wait()`` orders the caller's
+    stream after the exchange; the gradient is the symmetric buffer itself.
+
+    Replaces the data-parallel all-reduce of ``values.weight.grad`` that the
+    reference gets from DDP around ``embedding_bag_bw_rev_indices``.
+    """
+
+    def __init__(self, weight: torch.nn.Parameter, group: Optional[dist.ProcessGroup] = None,
+                 average: bool = False, max_blocks: int = 48):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if self.world > 8:
+            raise ValueError("the fused exchange spans one NVLink domain (at most 8 ranks)")
+        K, D = weight.shape
+        self.K, self.D = K, D
+        self.shard_rows = -(-K // self.world)
+        dev = weight.device
+        self.recv = symm_mem.empty((self.world, self.shard_rows, D), dtype=weight.dtype, device=dev)
+        self.full = symm_mem.empty((self.world * self.shard_rows, D), dtype=weight.dtype, device=dev)
+        h_recv = symm_mem.rendezvous(self.recv, self.group)
+        h_full = symm_mem.rendezvous(self.full, self.group)
+        self.recv_ptrs = [int(h_recv.buffer_ptrs[i]) for i in range(self.world)]
+        self.full_ptrs = [int(h_full.buffer_ptrs[i]) for i in range(self.world)]
+        self._handles = (h_recv, h_full)
+        self.scale = 1.0 / self.world if average else 1.0
+        self.max_blocks = max_blocks
+        self.side = torch.cuda.Stream(dev)
+        self.flag = torch.zeros(1, device=dev)
+        self.done = None
+        self.weight = weight
+        weight._pkm_grad_exchange = self
+
+    def backward(self, indices, weight, psw, grad_out, need_dpsw: bool):
+        """Bag backward of one step: returns (table gradient, psw gradient);
+        the table gradient is complete after ``wait()``."""
+        from . import _native
+
+        dpsw = _native.bag_bwd_sharded(indices, weight, psw, grad_out, self.recv_ptrs, self.rank, self.shard_rows,
+                                       need_dpsw=need_dpsw)
+        self.side.wait_stream(torch.cuda.current_stream(weight.device))
+        with torch.cuda.stream(self.side):
+            dist.all_reduce(self.flag, group=self.group)  # every rank's rows are in the receive buffers
+            _native.grad_shard_reduce(self.recv, self.K, self.rank, self.shard_rows, self.full_ptrs, self.scale,
+                                      self.max_blocks)
+            dist.all_reduce(self.flag, group=self.group)  # every shard is in every rank's gradient
+            self.done = torch.cuda.Event()
+            self.done.record(self.side)
+        return self.full[: self.K], dpsw
+
+    def wait(self):
+        """Order the current stream after this step's exchange."""
+        if self.done is None:
+            return
+        torch.cuda.current_stream(self.weight.device).wait_event(self.done)
+        self.done = None
+        g = self.weight.grad
+        if g is not None and g.data_ptr() != self.full.data_ptr():
+            # autograd copied (or accumulated into) the gradient before the
+            # exchange finished: redo it from the completed buffer
+            g.copy_(self.full[: self.K])
+
+    def close(self):
+        if getattr(self.weight, "_pkm_grad_exchange", None) is self:
+            del self.weight._pkm_grad_exchange
+
+
 class GradReducer:
     """Sum gradients of ``params`` over ``group`` (``average`` divides by the
     world size).  ``early`` names the parameters whose all-reduce starts from
@@ -26,12 +106,14 @@ class GradReducer:
     ``finish()``, which also waits for the early reductions."""
 
     def __init__(self, params: Iterable[torch.nn.Parameter], early: Iterable[torch.nn.Parameter] = (),
-                 group: Optional[dist.ProcessGroup] = None, average: bool = False):
+                 group: Optional[dist.ProcessGroup] = None, average: bool = False,
+                 sharded: Iterable[ShardedTableGrad] = ()):
         self.group = group
         self.average = average
         early = list(early)
-        early_ids = {id(p) for p in early}
-        self.rest: List[torch.nn.Parameter] = [p for p in params if id(p) not in early_ids and p.requires_grad]
+        self.sharded = list(sharded)
+        skip = {id(p) for p in early} | {id(x.weight) for x in self.sharded}
+        self.rest: List[torch.nn.Parameter] = [p for p in params if id(p) not in skip and p.requires_grad]
         self.pending = []
         self.handles = []
         for p in early:
@@ -63,6 +145,8 @@ class GradReducer:
             if self.average:
                 g /= self.world()
         self.pending = []
+        for x in self.sharded:
+            x.wait()
 
     def remove(self):
         for h in self.handles:

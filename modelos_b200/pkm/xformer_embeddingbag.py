@@ -59,6 +59,9 @@ class xFormersEmbeddingBag(torch.autograd.Function):
     def forward(ctx, indices, weight, per_sample_weights, bw_algo):
         ctx.save_for_backward(indices, weight, per_sample_weights)
         ctx.bw_algo = bw_algo
+        # data-parallel training may attach a fused gradient exchange to the
+        # table (modelos_b200.dist.ShardedTableGrad)
+        ctx.exchange = getattr(weight, "_pkm_grad_exchange", None)
         return embedding_bag_b200(indices, weight, per_sample_weights)
 
     @staticmethod
@@ -67,6 +70,11 @@ class xFormersEmbeddingBag(torch.autograd.Function):
         # every bw_algo of the reference ("reverse_indices", "atomics", "lock")
         # computes the same gradients; all map to the sorted-segment kernel
         assert ctx.bw_algo in ("reverse_indices", "atomics", "lock")
+        if ctx.exchange is not None and ctx.needs_input_grad[1]:
+            g = gradient.contiguous().to(weight.dtype)
+            weight_g, per_sample_weights_g = ctx.exchange.backward(
+                indices, weight, per_sample_weights, g, need_dpsw=ctx.needs_input_grad[2])
+            return None, weight_g, per_sample_weights_g, None
         weight_g, per_sample_weights_g = embedding_bag_bw_rev_indices(
             indices, weight, per_sample_weights, gradient.contiguous())
         return None, weight_g, per_sample_weights_g, None

@@ -1,0 +1,47 @@
+"""Fused data-parallel exchange of the value-table gradient on two GPUs:
+the table gradient equals the NCCL all-reduce of the ranks' local
+gradients, bit for bit at two ranks (one fp32 addition per element), in
+fp32 and bf16."""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("dtype_name", ["float32", "bfloat16"])
+def test_sharded_table_grad_two_ranks(tmp_path, dtype_name):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    sys.path.insert(0, HERE)
+    import dist_gpu_worker
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=dist_gpu_worker.run, args=(r, 2, port, str(tmp_path), dtype_name)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert [p.exitcode for p in procs] == [0, 0]
+    for r in range(2):
+        d = torch.load(os.path.join(tmp_path, f"rank{r}.pt"))
+        assert d["aliased"]
+        assert torch.equal(d["got"], d["ref"])
+        assert torch.equal(d["got_keys"], d["ref_keys"])
