@@ -216,8 +216,10 @@ PKM_API int pkm_bag_bwd_sharded(const int64_t* indices, const void* psw, int psw
 
 /*
  * Owner side of the exchange (the all-gather half): sums the world partial
- * copies of this rank's shard in its receive buffer `recv` (fixed source
- * order, fp32), multiplies by `scale` (1/world averages), and stores the
+ * copies of this rank's shard in its receive buffer `recv` in source order
+ * 0..world-1 (bf16 as packed pairs, each addition rounded to bf16 like a
+ * bf16 all-reduce; fp32 in fp32), multiplies by `scale` (1/world averages),
+ * and stores the
  * rows into rows [rank*shard_rows, ...) of every rank's gradient
  * grad_bases[d] (HOST array of world peer-writable device addresses).
  * max_blocks > 0 bounds the grid so that the kernel can run beside the rest

@@ -213,34 +213,82 @@ __global__ void zero_rows_kernel(int64_t K, int64_t D, const __grid_constant__ G
 }
 
 // Owner side of the data-parallel exchange: sum the world partial copies of
-// this rank's shard rows (fixed source order, fp32), scale, and store the
-// result into row (rank * shard_rows + r) of every rank's gradient.
-template <typename T>
-__global__ void shard_reduce_kernel(const T* __restrict__ recv, int64_t shard_rows, int64_t rows, int64_t D,
-                                    int world, int rank, float scale, const __grid_constant__ GradDest dest) {
-  constexpr int EPV = 16 / sizeof(T);
-  const int64_t vec = D / EPV;
-  const int64_t total = rows * vec;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / vec, v = i - r * vec;
-    float acc[EPV];
+// this rank's shard rows in source order 0..world-1, scale, and store the
+// result into row (rank * shard_rows + r) of every rank's gradient.  bf16
+// copies are added as packed pairs (each addition rounded to bf16, as a
+// bf16 all-reduce does; with two ranks that is the single rounding of the
+// exact sum), fp32 in fp32.  Each thread handles kShardVec 16-byte vectors
+// with all their loads in flight before the additions.
+constexpr int kShardVec = 4;
+__device__ __forceinline__ uint32_t add_pair(uint32_t a, uint32_t b, bool bf16) {
+  if (bf16) {
+    __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&a), y = *reinterpret_cast<__nv_bfloat162*>(&b);
+    __nv_bfloat162 r = __hadd2(x, y);
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+  return __float_as_uint(__uint_as_float(a) + __uint_as_float(b));
+}
+__device__ __forceinline__ uint4 add_vec(const uint4& a, const uint4& b, bool bf16) {
+  return make_uint4(add_pair(a.x, b.x, bf16), add_pair(a.y, b.y, bf16), add_pair(a.z, b.z, bf16),
+                    add_pair(a.w, b.w, bf16));
+}
+__device__ __forceinline__ uint4 scale_vec(const uint4& a, float s, bool bf16) {
+  if (bf16) {
+    float f[8];
+    VecTraits<__nv_bfloat16>::unpack(a, f);
+    uint4 r;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&r);
 #pragma unroll
-    for (int k = 0; k < EPV; ++k) acc[k] = 0.f;
-    for (int s = 0; s < world; ++s) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(recv + ((int64_t)s * shard_rows + r) * D + v * EPV);
-      float f[EPV];
-      VecTraits<T>::unpack(raw, f);
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i] * s, f[2 * i + 1] * s);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return r;
+  }
+  return make_uint4(__float_as_uint(__uint_as_float(a.x) * s), __float_as_uint(__uint_as_float(a.y) * s),
+                    __float_as_uint(__uint_as_float(a.z) * s), __float_as_uint(__uint_as_float(a.w) * s));
+}
+
+__global__ void __launch_bounds__(256) shard_reduce_kernel(const uint4* __restrict__ recv, int64_t shard_vecs,
+                                                           int64_t n_vecs, int64_t row_vecs, int world, int rank,
+                                                           bool bf16, float scale,
+                                                           const __grid_constant__ GradDest dest) {
+  const int64_t n_chunks = (n_vecs + (int64_t)blockDim.x * kShardVec - 1) / ((int64_t)blockDim.x * kShardVec);
+  for (int64_t chunk = blockIdx.x; chunk < n_chunks; chunk += gridDim.x) {
+  const int64_t v0 = (chunk * blockDim.x) * kShardVec + threadIdx.x;
+  uint4 acc[kShardVec];
+  bool live[kShardVec];
 #pragma unroll
-      for (int k = 0; k < EPV; ++k) acc[k] += f[k];
+  for (int u = 0; u < kShardVec; ++u) {
+    const int64_t v = v0 + (int64_t)u * blockDim.x;
+    live[u] = v < n_vecs;
+    acc[u] = live[u] ? recv[v] : make_uint4(0, 0, 0, 0);
+  }
+  for (int s = 1; s < world; ++s) {
+    uint4 x[kShardVec];
+#pragma unroll
+    for (int u = 0; u < kShardVec; ++u) {
+      const int64_t v = v0 + (int64_t)u * blockDim.x;
+      x[u] = live[u] ? recv[(int64_t)s * shard_vecs + v] : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int k = 0; k < EPV; ++k) acc[k] *= scale;
-    const int64_t grow = rank * shard_rows + r;
-    for (int d = 0; d < world; ++d) {
-      T* dst = reinterpret_cast<T*>(dest.base[d]) + grow * D + v * EPV;
-      st_run(dst, DtOf<T>::value, 0, acc, EPV);
+    for (int u = 0; u < kShardVec; ++u) acc[u] = add_vec(acc[u], x[u], bf16);
+  }
+  if (scale != 1.f) {
+#pragma unroll
+    for (int u = 0; u < kShardVec; ++u) acc[u] = scale_vec(acc[u], scale, bf16);
+  }
+  const int64_t base = (int64_t)rank * shard_vecs;  // this shard's first vector in a full gradient
+  for (int d = 0; d < world; ++d) {
+    uint4* dst = reinterpret_cast<uint4*>(dest.base[d]) + base;
+#pragma unroll
+    for (int u = 0; u < kShardVec; ++u) {
+      const int64_t v = v0 + (int64_t)u * blockDim.x;
+      if (live[u]) dst[v] = acc[u];
     }
   }
+  }
+  (void)row_vecs;
   __threadfence_system();
 }
 
@@ -571,15 +619,14 @@ extern "C" int pkm_grad_shard_reduce(const void* recv, int dtype, int64_t num_ro
   const int64_t rows = std::min<int64_t>(shard_rows, num_rows - (int64_t)rank * shard_rows);
   if (rows <= 0) return PKM_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t total = rows * dim * dtype_size(dtype) / 16;
-  int64_t blocks = std::max<int64_t>(1, (total + 255) / 256);
+  const int64_t row_vecs = dim * dtype_size(dtype) / 16;
+  const int64_t n_vecs = rows * row_vecs;
+  const int64_t per_block = 256 * kShardVec;
+  int64_t blocks = (n_vecs + per_block - 1) / per_block;
   if (max_blocks > 0) blocks = std::min<int64_t>(blocks, max_blocks);
-  if (dtype == PKM_DT_F32)
-    shard_reduce_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const float*>(recv), shard_rows, rows,
-                                                                 dim, world, rank, scale, dest);
-  else
-    shard_reduce_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(recv), shard_rows, rows, dim, world, rank, scale, dest);
+  shard_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const uint4*>(recv), shard_rows * row_vecs,
+                                                        n_vecs, row_vecs, world, rank, dtype == PKM_DT_BF16, scale,
+                                                        dest);
   return check_cuda("pkm_grad_shard_reduce");
 }
 

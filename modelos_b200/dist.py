@@ -4,12 +4,14 @@ Tokens are independent in the memory lookup, so the layer shards over the
 batch: every rank holds the full (replicated) value table and runs its own
 tokens, and the gradients are summed across ranks.  The value table's
 gradient is the large one (``[n_keys^2, v_dim]``, 512 MiB in bf16 at
-BASELINE config 2) and is produced in the middle of the backward, by the bag
-backward; ``GradReducer`` starts its all-reduce as soon as it is accumulated,
-so the transfer overlaps the rest of the backward (scoring and query
-projection), and reduces the small dense gradients together in one flattened
-bucket at the end.  BatchNorm statistics stay per rank, as the reference's
-``nn.BatchNorm1d`` does under data parallelism.
+BASELINE config 2); ``ShardedTableGrad`` fuses its exchange into the bag
+backward (rows stored to their owners over NVLink while the segment pass
+computes, owner-side reduction and all-gather beside the rest of the
+backward).  ``GradReducer`` all-reduces every other gradient from its
+post-accumulate hook as soon as it exists, and without a
+``ShardedTableGrad`` the table's too (plain NCCL).  BatchNorm statistics
+stay per rank, as the reference's ``nn.BatchNorm1d`` does under data
+parallelism.
 """
 from __future__ import annotations
 
@@ -30,7 +32,9 @@ class ShardedTableGrad:
     stores the result into every rank's gradient buffer
     (``pkm_grad_shard_reduce``: the all-gather), beside the rest of the
     backward; a second barrier completes the exchange.  Both buffers are
-    symmetric memory (peer-addressable).  ``wait()`` orders the caller's
+    symmetric memory (peer-addressable).  ``max_blocks`` > 0 caps the owner
+    kernel's grid (0: one pass over the shard with a full grid).  ``wait()``
+    orders the caller's
     stream after the exchange; the gradient is the symmetric buffer itself.
 
     Replaces the data-parallel all-reduce of ``values.weight.grad`` that the
@@ -38,7 +42,7 @@ class ShardedTableGrad:
     """
 
     def __init__(self, weight: torch.nn.Parameter, group: Optional[dist.ProcessGroup] = None,
-                 average: bool = False, max_blocks: int = 48):
+                 average: bool = False, max_blocks: int = 0):
         import torch.distributed._symmetric_memory as symm_mem
 
         self.group = group if group is not None else dist.group.WORLD
@@ -101,23 +105,24 @@ class ShardedTableGrad:
 
 class GradReducer:
     """Sum gradients of ``params`` over ``group`` (``average`` divides by the
-    world size).  ``early`` names the parameters whose all-reduce starts from
-    a post-accumulate-grad hook; the rest are flattened into one bucket by
-    ``finish()``, which also waits for the early reductions."""
+    world size).  Every parameter's all-reduce starts, asynchronously and in
+    the gradient's own dtype, from a post-accumulate-grad hook, so the
+    transfers overlap the rest of the backward; ``finish()`` waits for them.
+    Tables handled by a ``ShardedTableGrad`` (``sharded``) are skipped here
+    and ``finish()`` orders the caller after their exchange.  ``early`` is
+    kept for callers that list the first parameters explicitly; every
+    parameter is reduced from its hook either way."""
 
     def __init__(self, params: Iterable[torch.nn.Parameter], early: Iterable[torch.nn.Parameter] = (),
                  group: Optional[dist.ProcessGroup] = None, average: bool = False,
                  sharded: Iterable[ShardedTableGrad] = ()):
         self.group = group
         self.average = average
-        early = list(early)
         self.sharded = list(sharded)
-        skip = {id(p) for p in early} | {id(x.weight) for x in self.sharded}
-        self.rest: List[torch.nn.Parameter] = [p for p in params if id(p) not in skip and p.requires_grad]
+        skip = {id(x.weight) for x in self.sharded}
+        self.params: List[torch.nn.Parameter] = [p for p in params if id(p) not in skip and p.requires_grad]
         self.pending = []
-        self.handles = []
-        for p in early:
-            self.handles.append(p.register_post_accumulate_grad_hook(self._start))
+        self.handles = [p.register_post_accumulate_grad_hook(self._start) for p in self.params]
 
     def world(self) -> int:
         return dist.get_world_size(self.group)
@@ -128,18 +133,7 @@ class GradReducer:
         self.pending.append((p.grad, dist.all_reduce(p.grad, group=self.group, async_op=True)))
 
     def finish(self):
-        """Reduce the remaining gradients and wait for everything."""
-        grads = [p.grad for p in self.rest if p.grad is not None]
-        if grads:
-            flat = torch.cat([g.reshape(-1).to(torch.float32) for g in grads])
-            dist.all_reduce(flat, group=self.group)
-            if self.average:
-                flat /= self.world()
-            off = 0
-            for g in grads:
-                n = g.numel()
-                g.copy_(flat[off:off + n].view_as(g))
-                off += n
+        """Wait for every reduction of this step."""
         for g, work in self.pending:
             work.wait()
             if self.average:
