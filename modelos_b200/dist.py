@@ -33,7 +33,9 @@ class ShardedTableGrad:
     (``pkm_grad_shard_reduce``: the all-gather), beside the rest of the
     backward; a second barrier completes the exchange.  Both buffers are
     symmetric memory (peer-addressable).  ``max_blocks`` > 0 caps the owner
-    kernel's grid (0: one pass over the shard with a full grid).  ``wait()``
+    kernel's grid (0: one pass over the shard with a full grid); the default
+    leaves most SMs to the rest of the backward, which the kernel overlaps
+    (measured best on two B200s).  ``wait()``
     orders the caller's
     stream after the exchange; the gradient is the symmetric buffer itself.
 
@@ -42,7 +44,7 @@ class ShardedTableGrad:
     """
 
     def __init__(self, weight: torch.nn.Parameter, group: Optional[dist.ProcessGroup] = None,
-                 average: bool = False, max_blocks: int = 0):
+                 average: bool = False, max_blocks: int = 64):
         import torch.distributed._symmetric_memory as symm_mem
 
         self.group = group if group is not None else dist.group.WORLD
@@ -105,24 +107,30 @@ class ShardedTableGrad:
 
 class GradReducer:
     """Sum gradients of ``params`` over ``group`` (``average`` divides by the
-    world size).  Every parameter's all-reduce starts, asynchronously and in
-    the gradient's own dtype, from a post-accumulate-grad hook, so the
-    transfers overlap the rest of the backward; ``finish()`` waits for them.
-    Tables handled by a ``ShardedTableGrad`` (``sharded``) are skipped here
-    and ``finish()`` orders the caller after their exchange.  ``early`` is
-    kept for callers that list the first parameters explicitly; every
-    parameter is reduced from its hook either way."""
+    world size).  A gradient of at least ``bucket_bytes`` starts its
+    all-reduce, asynchronously and in its own dtype, from its
+    post-accumulate-grad hook, so the transfer overlaps the rest of the
+    backward; smaller ones are all-reduced together in ``finish()`` as one
+    coalesced NCCL launch.  Tables handled by a ``ShardedTableGrad``
+    (``sharded``) are skipped here and ``finish()`` orders the caller after
+    their exchange.  ``early`` names parameters whose reduction starts from
+    the hook whatever their size."""
 
     def __init__(self, params: Iterable[torch.nn.Parameter], early: Iterable[torch.nn.Parameter] = (),
                  group: Optional[dist.ProcessGroup] = None, average: bool = False,
-                 sharded: Iterable[ShardedTableGrad] = ()):
+                 sharded: Iterable[ShardedTableGrad] = (), bucket_bytes: int = 1 << 20):
         self.group = group
         self.average = average
         self.sharded = list(sharded)
         skip = {id(x.weight) for x in self.sharded}
+        early_ids = {id(p) for p in early}
         self.params: List[torch.nn.Parameter] = [p for p in params if id(p) not in skip and p.requires_grad]
+        self.hooked = [p for p in self.params
+                       if id(p) in early_ids or p.numel() * p.element_size() >= bucket_bytes]
+        hooked_ids = {id(p) for p in self.hooked}
+        self.small = [p for p in self.params if id(p) not in hooked_ids]
         self.pending = []
-        self.handles = [p.register_post_accumulate_grad_hook(self._start) for p in self.params]
+        self.handles = [p.register_post_accumulate_grad_hook(self._start) for p in self.hooked]
 
     def world(self) -> int:
         return dist.get_world_size(self.group)
@@ -133,7 +141,18 @@ class GradReducer:
         self.pending.append((p.grad, dist.all_reduce(p.grad, group=self.group, async_op=True)))
 
     def finish(self):
-        """Wait for every reduction of this step."""
+        """Reduce the small gradients and wait for every reduction of this step."""
+        from torch.distributed.distributed_c10d import _coalescing_manager
+
+        grads = [p.grad for p in self.small if p.grad is not None]
+        if grads:
+            with _coalescing_manager(group=self.group, async_ops=True) as cm:
+                for g in grads:
+                    dist.all_reduce(g, group=self.group)
+            cm.wait()
+            if self.average:
+                for g in grads:
+                    g /= self.world()
         for g, work in self.pending:
             work.wait()
             if self.average:
