@@ -232,6 +232,30 @@ PKM_API int pkm_grad_shard_reduce(const void* recv, int dtype, int64_t num_rows,
                                   void* stream);
 
 /*
+ * Fused FwPKM value update: one SGD step of the fast-weight inner loop on the
+ * value table [rows, dim] (f32 or bf16), replacing the value branch of
+ * update_fw (fwpkm/fwpkm.py:274-367, update_fw_param :266-272):
+ *   counts = bincount(indices)          (int32 [rows], caller's buffer)
+ *   scaled = grad * scale / max(counts, 1)
+ *   new    = values - lr * (u + weight_decay * values),
+ *   u      = clamp(scaled, -1, 1) if grad_clip else scaled
+ * each operation rounded to the table dtype as torch's eager ops round, so
+ * f32 results equal the reference's bit for bit.  scaled_grad may be NULL.
+ * Indices outside [0, rows) set PKM_DEVERR_INDEX and are not counted.
+ * pkm_fw_update_bwd: d_values = d_new * (1 - lr * weight_decay), d_grad =
+ * (scale / max(counts, 1)) * (d_scaled - lr * d_new * [|scaled| <= 1 when
+ * clipping]); d_scaled_grad, d_values, d_grad may be NULL.
+ */
+PKM_API int pkm_fw_update(const void* values, const void* grad, int dtype, int64_t rows, int64_t dim,
+                          const int64_t* indices, int64_t n_indices, double scale, double lr, double weight_decay,
+                          int grad_clip, void* new_values, void* scaled_grad, int32_t* counts, uint32_t* dev_err,
+                          void* stream);
+PKM_API int pkm_fw_update_bwd(const void* d_new_values, const void* d_scaled_grad, const void* scaled_grad,
+                              const int32_t* counts, int dtype, int64_t rows, int64_t dim, double scale,
+                              double lr, double weight_decay, int grad_clip, void* d_values, void* d_grad,
+                              void* stream);
+
+/*
  * Batch normalisation of the query projection, x [n, c] row-major (rows =
  * tokens, c a multiple of 8, x / out / dy / dx 16-byte aligned; x f32 or
  * bf16).  Replaces the query network's nn.BatchNorm1d(heads * k_dim,

@@ -43,6 +43,10 @@ _SIGS = {
     "pkm_bag_bwd_sharded": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _I, _I64, _I, _P, _I, _P, _P,
                              ctypes.c_size_t, _P, _P], _I),
     "pkm_grad_shard_reduce": ([_P, _I, _I64, _I64, _I, _I, _I64, _P, ctypes.c_float, _I, _P], _I),
+    "pkm_fw_update": ([_P, _P, _I, _I64, _I64, _P, _I64, ctypes.c_double, ctypes.c_double, ctypes.c_double, _I,
+                       _P, _P, _P, _P, _P], _I),
+    "pkm_fw_update_bwd": ([_P, _P, _P, _P, _I, _I64, _I64, ctypes.c_double, ctypes.c_double, ctypes.c_double, _I,
+                           _P, _P, _P], _I),
     "pkm_batchnorm_workspace": ([_I64, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
     "pkm_batchnorm_fwd": ([_P, _I, _I64, _I64, _P, _P, _I, _P, _P, _I, _I, ctypes.c_double, ctypes.c_double,
                            _P, _P, _P, _P, ctypes.c_size_t, _P], _I),
@@ -448,3 +452,42 @@ def batchnorm_bwd(dy: torch.Tensor, x: torch.Tensor, mean: torch.Tensor, rstd: t
                                    DT[pdt], _ptr(dx), _ptr(dw), _ptr(db), _ptr(ws), ws.numel(), _stream(x.device)),
            "pkm_batchnorm_bwd")
     return dx, dw, db
+
+
+# ---------------------------------------------------------------------------
+# fused FwPKM value update
+# ---------------------------------------------------------------------------
+def fw_update(values: torch.Tensor, grad: torch.Tensor, indices: torch.Tensor, scale: float, lr: float,
+              weight_decay: float, grad_clip: bool, want_scaled: bool = True):
+    """``(new_values, scaled_grad, counts)`` of the value branch of
+    ``update_fw``; counts are int32 per row."""
+    assert values.shape == grad.shape and values.dim() == 2 and values.dtype == grad.dtype
+    values, grad = values.contiguous(), grad.contiguous()
+    idx = indices.reshape(-1).contiguous()
+    assert idx.dtype == torch.long
+    _need_cuda(values, grad, idx)
+    K, D = values.shape
+    new = torch.empty_like(values)
+    scaled = torch.empty_like(values) if want_scaled else None
+    counts = torch.empty(K, dtype=torch.int32, device=values.device)
+    _check(lib().pkm_fw_update(_ptr(values), _ptr(grad), DT[values.dtype], K, D, _ptr(idx), idx.numel(),
+                               float(scale), float(lr), float(weight_decay), int(bool(grad_clip)), _ptr(new),
+                               _ptr(scaled), _ptr(counts), _ptr(err_word(values.device)), _stream(values.device)),
+           "pkm_fw_update")
+    return new, scaled, counts
+
+
+def fw_update_bwd(d_new: torch.Tensor, d_scaled: Optional[torch.Tensor], scaled: Optional[torch.Tensor],
+                  counts: torch.Tensor, scale: float, lr: float, weight_decay: float, grad_clip: bool,
+                  need_values: bool = True, need_grad: bool = True):
+    """``(d_values, d_grad)`` of ``fw_update``."""
+    d_new = d_new.contiguous()
+    d_scaled = None if d_scaled is None else d_scaled.contiguous().to(d_new.dtype)
+    _need_cuda(d_new, d_scaled, scaled, counts)
+    K, D = d_new.shape
+    dv = torch.empty_like(d_new) if need_values else None
+    dg = torch.empty_like(d_new) if need_grad else None
+    _check(lib().pkm_fw_update_bwd(_ptr(d_new), _ptr(d_scaled), _ptr(scaled), _ptr(counts), DT[d_new.dtype], K, D,
+                                   float(scale), float(lr), float(weight_decay), int(bool(grad_clip)), _ptr(dv),
+                                   _ptr(dg), _stream(d_new.device)), "pkm_fw_update_bwd")
+    return dv, dg

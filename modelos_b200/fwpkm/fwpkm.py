@@ -120,6 +120,31 @@ class IdwScore(torch.autograd.Function):
         return (-grad / (1e-3 + dist.pow(2))) * (2 * dist)
 
 
+class FusedValueUpdate(torch.autograd.Function):
+    """Value branch of ``update_fw`` (``fwpkm/fwpkm.py:274-367``) as one
+    kernel pass: ``scaled = grad * scale / max(bincount(indices), 1)``,
+    ``new = values - lr * (clamp?(scaled) + wd * values)``.  Returns
+    ``(new, scaled)``; differentiable in ``values`` and ``grad`` for the
+    outer backward through the inner update."""
+
+    @staticmethod
+    def forward(ctx, values, grad, indices, scale, lr, weight_decay, grad_clip):
+        new, scaled, counts = _native.fw_update(values, grad, indices, scale, lr, weight_decay, grad_clip)
+        ctx.save_for_backward(scaled if grad_clip else None, counts)
+        ctx.args = (scale, lr, weight_decay, grad_clip)
+        return new, scaled
+
+    @staticmethod
+    def backward(ctx, d_new, d_scaled):
+        scaled, counts = ctx.saved_tensors
+        scale, lr, wd, clip = ctx.args
+        if d_new is None:
+            d_new = torch.zeros_like(d_scaled)
+        dv, dg = _native.fw_update_bwd(d_new, d_scaled, scaled, counts, scale, lr, wd, clip,
+                                       need_values=ctx.needs_input_grad[0], need_grad=ctx.needs_input_grad[1])
+        return dv, dg, None, None, None, None, None
+
+
 class FastWeightProductKeyMemory(nn.Module):
     def __init__(
         self,
@@ -264,18 +289,20 @@ class FastWeightProductKeyMemory(nn.Module):
             loss = mem_loss if addr_loss is None else mem_loss + addr_loss
             grads = list(torch.autograd.grad(loss, params, create_graph=self.training))
         # the value gradient is a sum over samples, features, heads and top-k,
-        # shared out over the times each slot was read
+        # shared out over the times each slot was read; its scaling, the
+        # bincount, the clamp and the SGD step run as one fused kernel pass
+        fused = {}
         for i, n in enumerate(names):
-            if n == "values":
-                g = grads[i] * (num_samples * self.v_dim * self.topk * self.heads)
-                counts = torch.bincount(indices.reshape(-1), minlength=self.size).to(g.dtype)
-                counts = torch.where(counts == 0, torch.ones_like(counts), counts)
-                grads[i] = g / counts.unsqueeze(-1)
+            if n == "values" and grads[i] is not None:
+                scale = num_samples * self.v_dim * self.topk * self.heads
+                new_v, grads[i] = FusedValueUpdate.apply(params[i], grads[i], indices, scale, self.learning_rate,
+                                                         self.weight_decay, self.grad_clip)
+                fused[n] = new_v
         used = [None if g is None else (torch.clamp(g, min=-1.0, max=1.0) if self.grad_clip else g) for g in grads]
         # a parameter without a gradient (keys when there is no addressing
         # loss) is left as it is; the reference fails with a TypeError there
         updated = OrderedDict(
-            (n, params[i] if used[i] is None else
+            (n, fused[n] if n in fused else params[i] if used[i] is None else
              self.update_fw_param(params[i], used[i], self.learning_rate, self.weight_decay))
             for i, n in enumerate(names))
         return updated, grads

@@ -78,6 +78,29 @@ def score_grad_dense(indices, psw, dpsw, n_keys):
     return out.to(dpsw.dtype)
 
 
+def fw_update(values, grad, indices, scale, lr, weight_decay, grad_clip, want_scaled=True):
+    K = values.shape[0]
+    counts = torch.bincount(indices.reshape(-1), minlength=K).to(torch.int32)
+    c = counts.to(grad.dtype)
+    c = torch.where(c == 0, torch.ones_like(c), c)
+    scaled = grad * scale / c.unsqueeze(-1)
+    u = torch.clamp(scaled, min=-1.0, max=1.0) if grad_clip else scaled
+    new = values - lr * (u + weight_decay * values)
+    return new, scaled, counts
+
+
+def fw_update_bwd(d_new, d_scaled, scaled, counts, scale, lr, weight_decay, grad_clip, need_values=True,
+                  need_grad=True):
+    c = counts.to(d_new.dtype)
+    f = (scale / torch.where(c == 0, torch.ones_like(c), c)).unsqueeze(-1)
+    du = -lr * d_new
+    if grad_clip:
+        du = du * ((scaled >= -1) & (scaled <= 1)).to(d_new.dtype)
+    dg = f * (du + (d_scaled if d_scaled is not None else 0))
+    dv = d_new * (1 - lr * weight_decay)
+    return (dv if need_values else None), (dg if need_grad else None)
+
+
 def read_device_errors(dev=None, reset=True):
     return 0
 
@@ -90,6 +113,6 @@ def install(monkeypatch):
     """Route ``modelos_b200._native`` calls to this module for one test."""
     from modelos_b200 import _native
     for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense",
-                 "read_device_errors", "check_device_errors"):
+                 "fw_update", "fw_update_bwd", "read_device_errors", "check_device_errors"):
         monkeypatch.setattr(_native, name, globals()[name])
     return np
