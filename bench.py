@@ -3,9 +3,10 @@
 One step = forward + backward of ``HashingMemory`` at the config-2 shape
 (x [8, 2048, 1024] bf16, heads 4, knn 32, k_dim 512, n_keys 512 -> 262144
 slots, v_dim 1024, query BatchNorm) with loss ``sum(out**2)``; at N GPUs
-every rank runs that step on its own batch (weak scaling) and the value and
-key gradients plus the dense layer gradients are all-reduced over NCCL inside
-the step.  Inputs are synthetic (seeded normal draws; there is no dataset).
+every rank runs that step on its own batch (weak scaling) and the gradients
+are summed over the ranks inside the step: the value table's through the
+fused NVLink exchange of ``modelos_b200.dist.ShardedTableGrad``, the others
+through NCCL.  Inputs are synthetic (seeded normal draws; there is no dataset).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -223,8 +224,10 @@ def run_ours(args, rank, world, local_rank):
             # the value-table gradient goes to its row owners over NVLink while
             # the bag backward computes it; owners reduce and all-gather beside
             # the rest of the backward
-            reducer = GradReducer(params, sharded=[ShardedTableGrad(m.values.weight)])
-            exchange = "fused: segment-pass stores to row owners (symmetric memory) + owner reduce/all-gather"
+            ex = ShardedTableGrad(m.values.weight)
+            reducer = GradReducer(params, sharded=[ex])
+            exchange = {"nvls": "fused nvls: in-switch multimem all-reduce of the table gradient beside the backward",
+                        "p2p": "fused p2p: segment-pass stores to row owners + owner reduce/all-gather"}[ex.mode]
         else:
             # NCCL all-reduce started as soon as the bag backward produced it
             reducer = GradReducer(params, early=[m.values.weight])

@@ -232,6 +232,22 @@ PKM_API int pkm_grad_shard_reduce(const void* recv, int dtype, int64_t num_rows,
                                   void* stream);
 
 /*
+ * In-switch all-reduce of a table gradient over NVLink SHARP (NVLS): every
+ * rank's gradient [num_rows, dim] sits in one symmetric buffer whose
+ * multicast address is mc_src; the owner of rows [rank*shard_rows, ...)
+ * reads each 16-byte vector of them with multimem.ld_reduce (the switch
+ * returns the sum over ranks; bf16 accumulated in fp32) and stores it, times
+ * `scale`, with multimem.st at the same offset of mc_dst (the multicast
+ * address of the gradient buffers), which writes every rank's copy.  Called
+ * by every rank for its own shard, between two barriers (after every rank's
+ * gradient is written, before any rank reads the result).  Replaces the
+ * data-parallel all-reduce of values.weight.grad.
+ */
+PKM_API int pkm_grad_multimem_allreduce(const void* mc_src, void* mc_dst, int dtype, int64_t num_rows,
+                                        int64_t dim, int world, int rank, int64_t shard_rows, float scale,
+                                        int max_blocks, void* stream);
+
+/*
  * Fused FwPKM value update: one SGD step of the fast-weight inner loop on the
  * value table [rows, dim] (f32 or bf16), replacing the value branch of
  * update_fw (fwpkm/fwpkm.py:274-367, update_fw_param :266-272):

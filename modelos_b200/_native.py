@@ -43,6 +43,7 @@ _SIGS = {
     "pkm_bag_bwd_sharded": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _I, _I64, _I, _P, _I, _P, _P,
                              ctypes.c_size_t, _P, _P], _I),
     "pkm_grad_shard_reduce": ([_P, _I, _I64, _I64, _I, _I, _I64, _P, ctypes.c_float, _I, _P], _I),
+    "pkm_grad_multimem_allreduce": ([_P, _P, _I, _I64, _I64, _I, _I, _I64, ctypes.c_float, _I, _P], _I),
     "pkm_fw_update": ([_P, _P, _I, _I64, _I64, _P, _I64, ctypes.c_double, ctypes.c_double, ctypes.c_double, _I,
                        _P, _P, _P, _P, _P], _I),
     "pkm_fw_update_bwd": ([_P, _P, _P, _P, _I, _I64, _I64, ctypes.c_double, ctypes.c_double, ctypes.c_double, _I,
@@ -230,7 +231,8 @@ def bag_bwd_workspace(B: int, L: int, K: int, D: int) -> int:
 
 def bag_bwd(indices: torch.Tensor, weight: Optional[torch.Tensor], psw: Optional[torch.Tensor],
             grad_out: torch.Tensor, *, num_rows: Optional[int] = None, need_dpsw: bool = True,
-            want_counts: bool = False, grad_weight_dtype: Optional[torch.dtype] = None):
+            want_counts: bool = False, grad_weight_dtype: Optional[torch.dtype] = None,
+            out: Optional[torch.Tensor] = None):
     """K4: dense weight gradient, per-sample-weight gradient, row counts."""
     assert indices.dim() == 2 and indices.dtype == torch.long and indices.is_contiguous()
     assert grad_out.dim() == 2 and grad_out.shape[0] == indices.shape[0] and grad_out.is_contiguous()
@@ -250,7 +252,11 @@ def bag_bwd(indices: torch.Tensor, weight: Optional[torch.Tensor], psw: Optional
         assert psw.shape == indices.shape and psw.is_contiguous()
     dev = grad_out.device
     gw_dtype = grad_weight_dtype or row_dtype
-    grad_weight = torch.empty((K, D), dtype=gw_dtype, device=dev)
+    if out is not None:
+        assert out.shape == (K, D) and out.dtype == gw_dtype and out.is_contiguous() and out.device == dev
+        grad_weight = out
+    else:
+        grad_weight = torch.empty((K, D), dtype=gw_dtype, device=dev)
     grad_psw = torch.empty_like(psw) if (need_dpsw and psw is not None) else None
     counts = torch.empty((K,), dtype=torch.int32, device=dev) if want_counts else None
     ws_bytes = bag_bwd_workspace(B, L, K, D)
@@ -309,6 +315,14 @@ def grad_shard_reduce(recv: torch.Tensor, num_rows: int, rank: int, shard_rows: 
     _check(lib().pkm_grad_shard_reduce(_ptr(recv), DT[recv.dtype], num_rows, D, world, rank, shard_rows,
                                        _ptr_array(grad_bases), float(scale), int(max_blocks), _stream(recv.device)),
            "pkm_grad_shard_reduce")
+
+
+def grad_multimem_allreduce(mc_src: int, mc_dst: int, dtype: torch.dtype, num_rows: int, dim: int, world: int,
+                            rank: int, shard_rows: int, device: torch.device, scale: float = 1.0, max_blocks: int = 0):
+    """In-switch all-reduce of this rank's shard (multicast addresses)."""
+    _check(lib().pkm_grad_multimem_allreduce(ctypes.c_void_p(mc_src), ctypes.c_void_p(mc_dst), DT[dtype], num_rows,
+                                             dim, world, rank, shard_rows, float(scale), int(max_blocks),
+                                             _stream(device)), "pkm_grad_multimem_allreduce")
 
 
 def bag_bwd2(indices: torch.Tensor, a: Optional[torch.Tensor], gbar: torch.Tensor,

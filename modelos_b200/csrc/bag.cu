@@ -292,6 +292,54 @@ __global__ void __launch_bounds__(256) shard_reduce_kernel(const uint4* __restri
   __threadfence_system();
 }
 
+// In-switch variant (NVLS): every rank's gradient sits in one symmetric
+// buffer with a multicast mapping.  The owner of a shard reads each 16-byte
+// vector of its rows through the multicast address with
+// multimem.ld_reduce, which returns the sum over all ranks' copies (bf16
+// accumulated in fp32 in the switch), and stores it with multimem.st to the
+// multicast address of the gradient buffer, which writes every rank's copy.
+// Each rank's NVLink carries its own rows out once for the reduction and the
+// reduced shard out once for the broadcast.
+constexpr int kMmVec = 8;
+__global__ void __launch_bounds__(256) multimem_allreduce_kernel(const char* mc_src, char* mc_dst, int64_t v_begin,
+                                                                 int64_t n_vecs, bool bf16, float scale) {
+  const int64_t n_chunks = (n_vecs + (int64_t)blockDim.x * kMmVec - 1) / ((int64_t)blockDim.x * kMmVec);
+  for (int64_t chunk = blockIdx.x; chunk < n_chunks; chunk += gridDim.x) {
+    const int64_t v0 = chunk * blockDim.x * kMmVec + threadIdx.x;
+    uint4 r[kMmVec];
+#pragma unroll
+    for (int u = 0; u < kMmVec; ++u) {
+      const int64_t v = v0 + (int64_t)u * blockDim.x;
+      r[u] = make_uint4(0, 0, 0, 0);
+      if (v < n_vecs) {
+        const char* a = mc_src + (v_begin + v) * 16;
+        if (bf16)
+          asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(r[u].x), "=r"(r[u].y), "=r"(r[u].z), "=r"(r[u].w)
+                       : "l"(a)
+                       : "memory");
+        else
+          asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(r[u].x), "=r"(r[u].y), "=r"(r[u].z), "=r"(r[u].w)
+                       : "l"(a)
+                       : "memory");
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kMmVec; ++u) {
+      const int64_t v = v0 + (int64_t)u * blockDim.x;
+      if (v < n_vecs) {
+        uint4 x = scale != 1.f ? scale_vec(r[u], scale, bf16) : r[u];
+        char* d = mc_dst + (v_begin + v) * 16;
+        asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(d), "r"(x.x), "r"(x.y),
+                     "r"(x.z), "r"(x.w)
+                     : "memory");
+      }
+    }
+  }
+  __threadfence_system();
+}
+
 constexpr int kChunk = 256;
 
 struct BwdLayout {
@@ -680,4 +728,26 @@ extern "C" int pkm_bag_bwd_noalloc(const int64_t* indices, const void* psw, int 
   return pkm_bag_bwd(indices, psw, psw_dtype, weight, weight_dtype, grad_out, n_bags, bag_size, num_rows, dim,
                      grad_weight, grad_weight_dtype, grad_psw, grad_psw_dtype, row_counts, scratch,
                      kNoAllocScratchBytes, dev_err, stream);
+}
+
+extern "C" int pkm_grad_multimem_allreduce(const void* mc_src, void* mc_dst, int dtype, int64_t num_rows, int64_t dim,
+                                           int world, int rank, int64_t shard_rows, float scale, int max_blocks,
+                                           void* stream) {
+  if (dtype != PKM_DT_F32 && dtype != PKM_DT_BF16) return fail(PKM_ERR_UNSUPPORTED, "dtype must be f32 or bf16");
+  if (world < 1 || rank < 0 || rank >= world) return fail(PKM_ERR_INVALID_ARG, "bad world / rank");
+  if (shard_rows <= 0 || shard_rows * world < num_rows || dim <= 0) return fail(PKM_ERR_INVALID_ARG, "bad size");
+  if ((dim * dtype_size(dtype)) % 16 != 0) return fail(PKM_ERR_UNSUPPORTED, "row bytes must be a multiple of 16");
+  if (!mc_src || !mc_dst || !aligned16(mc_src) || !aligned16(mc_dst))
+    return fail(PKM_ERR_INVALID_ARG, "multicast addresses NULL or not 16-byte aligned");
+  const int64_t r0 = (int64_t)rank * shard_rows;
+  const int64_t rows = std::min<int64_t>(shard_rows, num_rows - r0);
+  if (rows <= 0) return PKM_OK;
+  const int64_t row_vecs = dim * dtype_size(dtype) / 16;
+  const int64_t n_vecs = rows * row_vecs;
+  int64_t blocks = (n_vecs + 256 * kMmVec - 1) / (256 * kMmVec);
+  if (max_blocks > 0) blocks = std::min<int64_t>(blocks, max_blocks);
+  multimem_allreduce_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const char*>(mc_src), static_cast<char*>(mc_dst), r0 * row_vecs, n_vecs, dtype == PKM_DT_BF16,
+      scale);
+  return check_cuda("pkm_grad_multimem_allreduce");
 }

@@ -22,31 +22,42 @@ import torch.distributed as dist
 
 
 class ShardedTableGrad:
-    """Data-parallel gradient of a value table, exchanged while it is computed.
+    """Data-parallel gradient of a value table, exchanged over NVLink inside
+    the backward.
 
-    Rank ``o`` owns table rows ``[o*S, (o+1)*S)`` (``S = ceil(K / world)``).
-    In the bag backward, the segment pass stores each row's gradient straight
-    into the owner's receive buffer over NVLink (``pkm_bag_bwd_sharded``:
-    the reduce-scatter runs inside the compute).  On a side stream, after a
-    barrier, every owner sums the ``world`` partial copies of its rows and
-    stores the result into every rank's gradient buffer
-    (``pkm_grad_shard_reduce``: the all-gather), beside the rest of the
-    backward; a second barrier completes the exchange.  Both buffers are
-    symmetric memory (peer-addressable).  ``max_blocks`` > 0 caps the owner
-    kernel's grid (0: one pass over the shard with a full grid); the default
-    leaves most SMs to the rest of the backward, which the kernel overlaps
-    (measured best on two B200s).  ``wait()``
-    orders the caller's
-    stream after the exchange; the gradient is the symmetric buffer itself.
+    Rank ``o`` owns table rows ``[o*S, (o+1)*S)`` (``S = ceil(K / world)``);
+    every buffer below is symmetric memory (peer-addressable, and with a
+    multicast mapping where the system has NVLink SHARP).
+
+    * ``mode="nvls"`` (the default where multicast is available): the bag
+      backward writes this rank's gradient into a symmetric buffer; after a
+      barrier each owner reads its rows through the multicast address with
+      ``multimem.ld_reduce`` (the switch sums the ranks' copies) and stores
+      them with ``multimem.st`` into every rank's gradient
+      (``pkm_grad_multimem_allreduce``); a second barrier ends the exchange.
+      Each rank's link carries its rows out once and the reduced shard out
+      once.
+    * ``mode="p2p"``: the segment pass stores each finished row straight into
+      its owner's receive buffer (``pkm_bag_bwd_sharded``: the reduce-scatter
+      inside the compute); after a barrier each owner sums the ``world``
+      copies and stores the rows into every rank's gradient
+      (``pkm_grad_shard_reduce``); a second barrier.
+
+    The exchange after the bag backward runs on a side stream beside the
+    rest of the backward (``max_blocks`` caps its grid so that the backward
+    keeps most SMs).  ``wait()`` orders the caller's stream after it; the
+    table's ``.grad`` is the symmetric gradient buffer itself.
 
     Replaces the data-parallel all-reduce of ``values.weight.grad`` that the
     reference gets from DDP around ``embedding_bag_bw_rev_indices``.
     """
 
     def __init__(self, weight: torch.nn.Parameter, group: Optional[dist.ProcessGroup] = None,
-                 average: bool = False, max_blocks: int = 64):
+                 average: bool = False, max_blocks: int = 64, mode: str = "auto"):
         import torch.distributed._symmetric_memory as symm_mem
 
+        if mode not in ("auto", "nvls", "p2p"):
+            raise ValueError(mode)
         self.group = group if group is not None else dist.group.WORLD
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
@@ -56,13 +67,28 @@ class ShardedTableGrad:
         self.K, self.D = K, D
         self.shard_rows = -(-K // self.world)
         dev = weight.device
-        self.recv = symm_mem.empty((self.world, self.shard_rows, D), dtype=weight.dtype, device=dev)
-        self.full = symm_mem.empty((self.world * self.shard_rows, D), dtype=weight.dtype, device=dev)
-        h_recv = symm_mem.rendezvous(self.recv, self.group)
+        rows = self.world * self.shard_rows
+        self.full = symm_mem.empty((rows, D), dtype=weight.dtype, device=dev)
         h_full = symm_mem.rendezvous(self.full, self.group)
-        self.recv_ptrs = [int(h_recv.buffer_ptrs[i]) for i in range(self.world)]
-        self.full_ptrs = [int(h_full.buffer_ptrs[i]) for i in range(self.world)]
-        self._handles = (h_recv, h_full)
+        handles = [h_full]
+        self.mode = "p2p"
+        if mode in ("auto", "nvls") and int(h_full.multicast_ptr) != 0:
+            self.local = symm_mem.empty((rows, D), dtype=weight.dtype, device=dev)
+            h_local = symm_mem.rendezvous(self.local, self.group)
+            handles.append(h_local)
+            if int(h_local.multicast_ptr) != 0:
+                self.mode = "nvls"
+                self.mc_local = int(h_local.multicast_ptr) + self._offset(h_local, self.local)
+                self.mc_full = int(h_full.multicast_ptr) + self._offset(h_full, self.full)
+        if mode == "nvls" and self.mode != "nvls":
+            raise RuntimeError("NVLink multicast (NVLS) is not available for symmetric memory here")
+        if self.mode == "p2p":
+            self.recv = symm_mem.empty((self.world, self.shard_rows, D), dtype=weight.dtype, device=dev)
+            h_recv = symm_mem.rendezvous(self.recv, self.group)
+            handles.append(h_recv)
+            self.recv_ptrs = self._peers(h_recv, self.recv)
+            self.full_ptrs = self._peers(h_full, self.full)
+        self._handles = handles
         self.scale = 1.0 / self.world if average else 1.0
         self.max_blocks = max_blocks
         self.side = torch.cuda.Stream(dev)
@@ -71,18 +97,37 @@ class ShardedTableGrad:
         self.weight = weight
         weight._pkm_grad_exchange = self
 
+    def _offset(self, h, t) -> int:
+        off = t.data_ptr() - int(h.buffer_ptrs[self.rank])
+        if off < 0 or off + t.numel() * t.element_size() > int(h.buffer_size):
+            raise RuntimeError("tensor lies outside its symmetric allocation")
+        return off
+
+    def _peers(self, h, t):
+        off = self._offset(h, t)
+        return [int(h.buffer_ptrs[i]) + off for i in range(self.world)]
+
     def backward(self, indices, weight, psw, grad_out, need_dpsw: bool):
         """Bag backward of one step: returns (table gradient, psw gradient);
         the table gradient is complete after ``wait()``."""
         from . import _native
 
-        dpsw = _native.bag_bwd_sharded(indices, weight, psw, grad_out, self.recv_ptrs, self.rank, self.shard_rows,
-                                       need_dpsw=need_dpsw)
+        if self.mode == "nvls":
+            _, dpsw, _ = _native.bag_bwd(indices, weight, psw, grad_out, need_dpsw=need_dpsw,
+                                         out=self.local[: self.K])
+        else:
+            dpsw = _native.bag_bwd_sharded(indices, weight, psw, grad_out, self.recv_ptrs, self.rank,
+                                           self.shard_rows, need_dpsw=need_dpsw)
         self.side.wait_stream(torch.cuda.current_stream(weight.device))
         with torch.cuda.stream(self.side):
-            dist.all_reduce(self.flag, group=self.group)  # every rank's rows are in the receive buffers
-            _native.grad_shard_reduce(self.recv, self.K, self.rank, self.shard_rows, self.full_ptrs, self.scale,
-                                      self.max_blocks)
+            dist.all_reduce(self.flag, group=self.group)  # every rank's rows are written
+            if self.mode == "nvls":
+                _native.grad_multimem_allreduce(self.mc_local, self.mc_full, weight.dtype, self.K, self.D,
+                                                self.world, self.rank, self.shard_rows, weight.device, self.scale,
+                                                self.max_blocks)
+            else:
+                _native.grad_shard_reduce(self.recv, self.K, self.rank, self.shard_rows, self.full_ptrs,
+                                          self.scale, self.max_blocks)
             dist.all_reduce(self.flag, group=self.group)  # every shard is in every rank's gradient
             self.done = torch.cuda.Event()
             self.done.record(self.side)

@@ -17,7 +17,7 @@ CFG = dict(input_dim=256, output_dim=256, mem_k_dim=128, mem_v_dim=256, mem_head
            mem_query_batchnorm=False, mem_query_rmsnorm=True)
 
 
-def run(rank: int, world: int, port: int, out_dir: str, dtype_name: str):
+def run(rank: int, world: int, port: int, out_dir: str, dtype_name: str, mode: str = "p2p"):
     import torch
     import torch.distributed as dist
 
@@ -53,7 +53,11 @@ def run(rank: int, world: int, port: int, out_dir: str, dtype_name: str):
         ref_keys = m.keys.grad.clone()
         dist.all_reduce(ref_keys)
         # fused exchange, two steps (the buffers are reused)
-        ex = ShardedTableGrad(m.values.weight)
+        try:
+            ex = ShardedTableGrad(m.values.weight, mode=mode)
+        except RuntimeError as e:  # no NVLink multicast on this machine
+            torch.save({"skip": str(e)}, os.path.join(out_dir, f"rank{rank}.pt"))
+            return
         red = GradReducer(params, sharded=[ex])
         for _ in range(2):
             step()
@@ -61,7 +65,7 @@ def run(rank: int, world: int, port: int, out_dir: str, dtype_name: str):
         torch.cuda.synchronize()
         got = m.values.weight.grad
         torch.save({"ref": ref.cpu(), "got": got.cpu(), "ref_keys": ref_keys.cpu(), "got_keys": m.keys.grad.cpu(),
-                    "aliased": got.data_ptr() == ex.full.data_ptr()},
+                    "aliased": got.data_ptr() == ex.full.data_ptr(), "mode": ex.mode},
                    os.path.join(out_dir, f"rank{rank}.pt"))
         ex.close()
         del ex, red

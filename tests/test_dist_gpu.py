@@ -1,7 +1,8 @@
-"""Fused data-parallel exchange of the value-table gradient on two GPUs:
+"""Fused data-parallel exchanges of the value-table gradient on two GPUs
+(NVLink stores to the row owners, and the in-switch multimem all-reduce):
 the table gradient equals the NCCL all-reduce of the ranks' local
-gradients, bit for bit at two ranks (one fp32 addition per element), in
-fp32 and bf16."""
+gradients, bit for bit at two ranks (one addition per element, rounded
+once), in fp32 and bf16."""
 from __future__ import annotations
 
 import os
@@ -21,8 +22,9 @@ def _free_port():
         return s.getsockname()[1]
 
 
+@pytest.mark.parametrize("mode", ["p2p", "nvls"])
 @pytest.mark.parametrize("dtype_name", ["float32", "bfloat16"])
-def test_sharded_table_grad_two_ranks(tmp_path, dtype_name):
+def test_sharded_table_grad_two_ranks(tmp_path, dtype_name, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -30,7 +32,7 @@ def test_sharded_table_grad_two_ranks(tmp_path, dtype_name):
     import dist_gpu_worker
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=dist_gpu_worker.run, args=(r, 2, port, str(tmp_path), dtype_name)) for r in range(2)]
+    procs = [ctx.Process(target=dist_gpu_worker.run, args=(r, 2, port, str(tmp_path), dtype_name, mode)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -42,6 +44,8 @@ def test_sharded_table_grad_two_ranks(tmp_path, dtype_name):
     assert [p.exitcode for p in procs] == [0, 0]
     for r in range(2):
         d = torch.load(os.path.join(tmp_path, f"rank{r}.pt"))
-        assert d["aliased"]
+        if "skip" in d:
+            pytest.skip(d["skip"])
+        assert d["mode"] == mode and d["aliased"]
         assert torch.equal(d["got"], d["ref"])
         assert torch.equal(d["got_keys"], d["ref_keys"])
