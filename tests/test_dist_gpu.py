@@ -2,7 +2,8 @@
 (NVLink stores to the row owners, and the in-switch multimem all-reduce):
 the table gradient equals the NCCL all-reduce of the ranks' local
 gradients, bit for bit at two ranks (one addition per element, rounded
-once), in fp32 and bf16."""
+once) in fp32 and for the NVLink-store exchange in bf16, and within one
+bf16 ulp for the in-switch reduction in bf16."""
 from __future__ import annotations
 
 import os
@@ -47,5 +48,12 @@ def test_sharded_table_grad_two_ranks(tmp_path, dtype_name, mode):
         if "skip" in d:
             pytest.skip(d["skip"])
         assert d["mode"] == mode and d["aliased"]
-        assert torch.equal(d["got"], d["ref"])
+        if mode == "nvls" and dtype_name == "bfloat16":
+            # the switch's bf16 reduction (fp32 accumulation, its own final
+            # rounding) may differ from NCCL's by one bf16 ulp
+            got, ref = d["got"].float(), d["ref"].float()
+            assert torch.all((got - ref).abs() <= ref.abs() * 2.0 ** -7)
+            assert ((got - ref).abs().max() / ref.abs().max()).item() < 2e-2
+        else:
+            assert torch.equal(d["got"], d["ref"])
         assert torch.equal(d["got_keys"], d["ref_keys"])
