@@ -29,7 +29,7 @@ class ShardedTableGrad:
     every buffer below is symmetric memory (peer-addressable, and with a
     multicast mapping where the system has NVLink SHARP).
 
-    * ``mode="nvls"`` (the default where multicast is available): the bag
+    * ``mode="nvls"`` (``auto`` above two ranks, where multicast exists): the bag
       backward writes this rank's gradient into a symmetric buffer; after a
       barrier each owner reads its rows through the multicast address with
       ``multimem.ld_reduce`` (the switch sums the ranks' copies) and stores
@@ -37,7 +37,7 @@ class ShardedTableGrad:
       (``pkm_grad_multimem_allreduce``); a second barrier ends the exchange.
       Each rank's link carries its rows out once and the reduced shard out
       once.
-    * ``mode="p2p"``: the segment pass stores each finished row straight into
+    * ``mode="p2p"`` (``auto`` at two ranks): the segment pass stores each finished row straight into
       its owner's receive buffer (``pkm_bag_bwd_sharded``: the reduce-scatter
       inside the compute); after a barrier each owner sums the ``world``
       copies and stores the rows into every rank's gradient
@@ -53,7 +53,7 @@ class ShardedTableGrad:
     """
 
     def __init__(self, weight: torch.nn.Parameter, group: Optional[dist.ProcessGroup] = None,
-                 average: bool = False, max_blocks: int = 64, mode: str = "auto"):
+                 average: bool = False, max_blocks: Optional[int] = None, mode: str = "auto"):
         import torch.distributed._symmetric_memory as symm_mem
 
         if mode not in ("auto", "nvls", "p2p"):
@@ -72,7 +72,11 @@ class ShardedTableGrad:
         h_full = symm_mem.rendezvous(self.full, self.group)
         handles = [h_full]
         self.mode = "p2p"
-        if mode in ("auto", "nvls") and int(h_full.multicast_ptr) != 0:
+        # measured on B200s at config 2: the NVLink stores win at two ranks
+        # (3.24 vs 3.99 ms per step), the in-switch reduction at eight
+        # (3.92 vs 3.97 ms)
+        want_nvls = mode == "nvls" or (mode == "auto" and self.world > 2)
+        if want_nvls and int(h_full.multicast_ptr) != 0:
             self.local = symm_mem.empty((rows, D), dtype=weight.dtype, device=dev)
             h_local = symm_mem.rendezvous(self.local, self.group)
             handles.append(h_local)
@@ -90,6 +94,8 @@ class ShardedTableGrad:
             self.full_ptrs = self._peers(h_full, self.full)
         self._handles = handles
         self.scale = 1.0 / self.world if average else 1.0
+        if max_blocks is None:  # grid cap of the side-stream kernel (measured best per mode / size)
+            max_blocks = 64 if (self.mode == "nvls" or self.world <= 2) else 148
         self.max_blocks = max_blocks
         self.side = torch.cuda.Stream(dev)
         self.flag = torch.zeros(1, device=dev)
