@@ -248,6 +248,26 @@ PKM_API int pkm_grad_multimem_allreduce(const void* mc_src, void* mc_dst, int dt
                                         int max_blocks, void* stream);
 
 /*
+ * SwiGLU gate of the memory output (pkm/memory.py:226-229: output *
+ * silu(swilu_projection(input))) on row-major [n, c] tensors (f32 or bf16,
+ * c a multiple of 8, 16-byte aligned), one pass each way:
+ *   pkm_swiglu_fwd: z = a * silu(h)
+ *   pkm_swiglu_bwd: da = dz * silu(h) (NULL to skip), dh = silu'(h)-chain of
+ *     dz * a, and dbias = column sums of dh (the gate projection's bias
+ *     gradient; NULL to skip; needs pkm_colsum_workspace bytes)
+ * with every intermediate rounded to the activation dtype where torch's eager
+ * ops round it.  pkm_colsum: out[c] = sum over rows (fixed order; the bias
+ * gradient of an nn.Linear).
+ */
+PKM_API int pkm_colsum_workspace(int64_t n, int64_t c, size_t* bytes);
+PKM_API int pkm_swiglu_fwd(const void* a, const void* h, int dtype, int64_t n, int64_t c, void* z, void* stream);
+PKM_API int pkm_swiglu_bwd(const void* dz, const void* a, const void* h, int dtype, int64_t n, int64_t c, void* da,
+                           void* dh, void* dbias, int bias_dtype, void* workspace, size_t workspace_bytes,
+                           void* stream);
+PKM_API int pkm_colsum(const void* x, int dtype, int64_t n, int64_t c, void* out, int out_dtype, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/*
  * Fused FwPKM value update: one SGD step of the fast-weight inner loop on the
  * value table [rows, dim] (f32 or bf16), replacing the value branch of
  * update_fw (fwpkm/fwpkm.py:274-367, update_fw_param :266-272):

@@ -44,6 +44,10 @@ _SIGS = {
                              ctypes.c_size_t, _P, _P], _I),
     "pkm_grad_shard_reduce": ([_P, _I, _I64, _I64, _I, _I, _I64, _P, ctypes.c_float, _I, _P], _I),
     "pkm_grad_multimem_allreduce": ([_P, _P, _I, _I64, _I64, _I, _I, _I64, ctypes.c_float, _I, _P], _I),
+    "pkm_colsum_workspace": ([_I64, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
+    "pkm_swiglu_fwd": ([_P, _P, _I, _I64, _I64, _P, _P], _I),
+    "pkm_swiglu_bwd": ([_P, _P, _P, _I, _I64, _I64, _P, _P, _P, _I, _P, ctypes.c_size_t, _P], _I),
+    "pkm_colsum": ([_P, _I, _I64, _I64, _P, _I, _P, ctypes.c_size_t, _P], _I),
     "pkm_fw_update": ([_P, _P, _I, _I64, _I64, _P, _I64, ctypes.c_double, ctypes.c_double, ctypes.c_double, _I,
                        _P, _P, _P, _P, _P], _I),
     "pkm_fw_update_bwd": ([_P, _P, _P, _P, _I, _I64, _I64, ctypes.c_double, ctypes.c_double, ctypes.c_double, _I,
@@ -505,3 +509,51 @@ def fw_update_bwd(d_new: torch.Tensor, d_scaled: Optional[torch.Tensor], scaled:
                                    float(scale), float(lr), float(weight_decay), int(bool(grad_clip)), _ptr(dv),
                                    _ptr(dg), _stream(d_new.device)), "pkm_fw_update_bwd")
     return dv, dg
+
+
+# ---------------------------------------------------------------------------
+# SwiGLU gate and column sums
+# ---------------------------------------------------------------------------
+def colsum_workspace(n: int, c: int) -> int:
+    nb = ctypes.c_size_t(0)
+    _check(lib().pkm_colsum_workspace(n, c, ctypes.byref(nb)), "pkm_colsum_workspace")
+    return int(nb.value)
+
+
+def swiglu_fwd(a: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+    """``a * silu(h)`` in one pass ([n, c] contiguous, same dtype)."""
+    assert a.shape == h.shape and a.dim() == 2 and a.dtype == h.dtype
+    a, h = a.contiguous(), h.contiguous()
+    _need_cuda(a, h)
+    z = torch.empty_like(a)
+    _check(lib().pkm_swiglu_fwd(_ptr(a), _ptr(h), DT[a.dtype], a.shape[0], a.shape[1], _ptr(z), _stream(a.device)),
+           "pkm_swiglu_fwd")
+    return z
+
+
+def swiglu_bwd(dz: torch.Tensor, a: torch.Tensor, h: torch.Tensor, need_da: bool = True,
+               bias_dtype: Optional[torch.dtype] = None):
+    """``(da, dh, dbias_h)``; dbias_h (column sums of dh) when bias_dtype is given."""
+    dz, a, h = dz.contiguous().to(a.dtype), a.contiguous(), h.contiguous()
+    _need_cuda(dz, a, h)
+    n, c = a.shape
+    da = torch.empty_like(a) if need_da else None
+    dh = torch.empty_like(a)
+    db = torch.empty(c, dtype=bias_dtype, device=a.device) if bias_dtype is not None else None
+    ws = torch.empty(colsum_workspace(n, c) if db is not None else 0, dtype=torch.uint8, device=a.device)
+    _check(lib().pkm_swiglu_bwd(_ptr(dz), _ptr(a), _ptr(h), DT[a.dtype], n, c, _ptr(da), _ptr(dh), _ptr(db),
+                                DT[bias_dtype] if bias_dtype is not None else 0, _ptr(ws) if ws.numel() else None,
+                                ws.numel(), _stream(a.device)), "pkm_swiglu_bwd")
+    return da, dh, db
+
+
+def colsum(x: torch.Tensor, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """Column sums of a [n, c] tensor (fixed order)."""
+    x = x.contiguous()
+    _need_cuda(x)
+    n, c = x.shape
+    out = torch.empty(c, dtype=out_dtype or x.dtype, device=x.device)
+    ws = torch.empty(colsum_workspace(n, c), dtype=torch.uint8, device=x.device)
+    _check(lib().pkm_colsum(_ptr(x), DT[x.dtype], n, c, _ptr(out), DT[out.dtype], _ptr(ws), ws.numel(),
+                            _stream(x.device)), "pkm_colsum")
+    return out

@@ -15,42 +15,9 @@
 // accurate when the mean is large against the spread.
 #include <algorithm>
 
-#include "common.cuh"
+#include "rows.cuh"
 
 namespace pkm {
-
-constexpr int kNormThreads = 256;  // 8 warps
-constexpr int kNormChan = 8;       // channels per thread (one 16-byte vector of bf16)
-
-template <typename T>
-struct NormIO;
-template <>
-struct NormIO<float> {
-  __device__ static __forceinline__ void load(const float* p, float (&v)[kNormChan]) {
-    const float4 a = *reinterpret_cast<const float4*>(p);
-    const float4 b = *reinterpret_cast<const float4*>(p + 4);
-    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-  }
-  __device__ static __forceinline__ void store(float* p, const float (&v)[kNormChan]) {
-    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
-    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
-  }
-};
-template <>
-struct NormIO<__nv_bfloat16> {
-  __device__ static __forceinline__ void load(const __nv_bfloat16* p, float (&v)[kNormChan]) {
-    VecTraits<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(p), v);
-  }
-  __device__ static __forceinline__ void store(__nv_bfloat16* p, const float (&v)[kNormChan]) {
-    st_run(p, PKM_DT_BF16, 0, v, kNormChan);
-  }
-};
-
-// Row range of row block rb of nb over n rows.
-__device__ __forceinline__ void row_range(int64_t n, int rb, int nb, int64_t& r0, int64_t& r1) {
-  r0 = n * rb / nb;
-  r1 = n * (rb + 1) / nb;
-}
 
 // Column partial sums of two per-element quantities over a row block:
 //   mode 0 (forward statistics):  a = x - x[0], b = a * a
@@ -71,7 +38,7 @@ __global__ void __launch_bounds__(kNormThreads) norm_reduce_kernel(const T* __re
   for (int i = 0; i < kNormChan; ++i) sa[i] = sb[i] = ref[i] = 0.f;
   if (live) {
     if (MODE == 0) {
-      NormIO<T>::load(x + c0, ref);  // shift: row 0
+      RowIO<T>::load(x + c0, ref);  // shift: row 0
     } else {
 #pragma unroll
       for (int i = 0; i < kNormChan; ++i) ref[i] = mean[c0 + i];
@@ -79,7 +46,7 @@ __global__ void __launch_bounds__(kNormThreads) norm_reduce_kernel(const T* __re
   #pragma unroll 4
   for (int64_t r = r0 + warp; r < r1; r += kNormThreads / 32) {
       float v[kNormChan];
-      NormIO<T>::load(x + r * c + c0, v);
+      RowIO<T>::load(x + r * c + c0, v);
       if (MODE == 0) {
 #pragma unroll
         for (int i = 0; i < kNormChan; ++i) {
@@ -89,7 +56,7 @@ __global__ void __launch_bounds__(kNormThreads) norm_reduce_kernel(const T* __re
         }
       } else {
         float g[kNormChan];
-        NormIO<T>::load(dy + r * c + c0, g);
+        RowIO<T>::load(dy + r * c + c0, g);
 #pragma unroll
         for (int i = 0; i < kNormChan; ++i) {
           sa[i] += g[i];
@@ -177,10 +144,10 @@ __global__ void __launch_bounds__(kNormThreads) norm_apply_kernel(const T* __res
 #pragma unroll 4
   for (int64_t r = r0 + warp; r < r1; r += kNormThreads / 32) {
     float v[kNormChan];
-    NormIO<T>::load(x + r * c + c0, v);
+    RowIO<T>::load(x + r * c + c0, v);
 #pragma unroll
     for (int k = 0; k < kNormChan; ++k) v[k] = fmaf(v[k] - mu[k], sc[k], bi[k]);
-    NormIO<T>::store(out + r * c + c0, v);
+    RowIO<T>::store(out + r * c + c0, v);
   }
 }
 
@@ -228,25 +195,17 @@ __global__ void __launch_bounds__(kNormThreads) norm_bwd_apply_kernel(const T* _
 #pragma unroll 4
   for (int64_t r = r0 + warp; r < r1; r += kNormThreads / 32) {
     float g[kNormChan], v[kNormChan];
-    NormIO<T>::load(dy + r * c + c0, g);
-    NormIO<T>::load(x + r * c + c0, v);
+    RowIO<T>::load(dy + r * c + c0, g);
+    RowIO<T>::load(x + r * c + c0, v);
 #pragma unroll
     for (int k = 0; k < kNormChan; ++k) v[k] = ka[k] * (g[k] - km[k]) - kb[k] * (v[k] - mu[k]);
-    NormIO<T>::store(dx + r * c + c0, v);
+    RowIO<T>::store(dx + r * c + c0, v);
   }
 }
 
 // ---------------------------------------------------------------------------
 // host
 // ---------------------------------------------------------------------------
-static int norm_row_blocks(int64_t n, int64_t c) {
-  const int64_t tiles = (c + 32 * kNormChan - 1) / (32 * kNormChan);
-  // about 4 blocks per SM over the whole grid, at least 8 rows per warp
-  int64_t nb = std::max<int64_t>(1, (int64_t)num_sms() * 4 / std::max<int64_t>(tiles, 1));
-  nb = std::min<int64_t>(nb, std::max<int64_t>(1, n / 64));
-  return (int)std::min<int64_t>(nb, 4096);
-}
-
 static int norm_check(const void* x, int x_dtype, int64_t n, int64_t c) {
   if (x_dtype != PKM_DT_F32 && x_dtype != PKM_DT_BF16) return fail(PKM_ERR_UNSUPPORTED, "x must be f32 or bf16");
   if (n <= 0 || c <= 0) return fail(PKM_ERR_INVALID_ARG, "need n > 0 and c > 0");
@@ -258,7 +217,7 @@ static int norm_check(const void* x, int x_dtype, int64_t n, int64_t c) {
 template <typename T>
 static void launch_apply(const void* x, const float* mean, const float* rstd, const void* w, const void* b, int p_dtype,
                          int64_t n, int64_t c, void* out, cudaStream_t st) {
-  const dim3 grid((unsigned)((c + 32 * kNormChan - 1) / (32 * kNormChan)), (unsigned)norm_row_blocks(n, c));
+  const dim3 grid((unsigned)((c + 32 * kNormChan - 1) / (32 * kNormChan)), (unsigned)row_blocks(n, c));
   norm_apply_kernel<T><<<grid, kNormThreads, 0, st>>>(static_cast<const T*>(x), mean, rstd, w, b, p_dtype, n, c,
                                                       static_cast<T*>(out));
 }
@@ -269,7 +228,7 @@ using namespace pkm;
 
 extern "C" int pkm_batchnorm_workspace(int64_t n, int64_t c, size_t* bytes) {
   if (!bytes || n <= 0 || c <= 0) return fail(PKM_ERR_INVALID_ARG, "bad size");
-  const int nb = norm_row_blocks(n, c);
+  const int nb = row_blocks(n, c);
   *bytes = (((size_t)nb * (size_t)c * sizeof(float2) + 255) & ~(size_t)255) + (size_t)c * sizeof(float4);
   return PKM_OK;
 }
@@ -290,7 +249,7 @@ extern "C" int pkm_batchnorm_fwd(const void* x, int x_dtype, int64_t n, int64_t 
   size_t need = 0;
   pkm_batchnorm_workspace(n, c, &need);
   if (training && (!workspace || workspace_bytes < need)) return fail(PKM_ERR_WORKSPACE, "batchnorm workspace too small");
-  const int nb = norm_row_blocks(n, c);
+  const int nb = row_blocks(n, c);
   const unsigned fin_blocks = (unsigned)((c + 255) / 256);
   if (training) {
     float2* part = static_cast<float2*>(workspace);
@@ -327,7 +286,7 @@ extern "C" int pkm_batchnorm_bwd(const void* dy, const void* x, int x_dtype, int
   pkm_batchnorm_workspace(n, c, &need);
   if (!workspace || workspace_bytes < need) return fail(PKM_ERR_WORKSPACE, "batchnorm workspace too small");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int nb = norm_row_blocks(n, c);
+  const int nb = row_blocks(n, c);
   float2* part = static_cast<float2*>(workspace);
   float4* coef = reinterpret_cast<float4*>(static_cast<char*>(workspace) + (((size_t)nb * c * sizeof(float2) + 255) & ~(size_t)255));
   const dim3 grid((unsigned)((c + 32 * kNormChan - 1) / (32 * kNormChan)), (unsigned)nb);

@@ -14,10 +14,12 @@ runs on the sm_100a kernels:
   sub-score grid (``pkm_score_grad_dense``) followed by two GEMMs per
   (head, half) for the query and key gradients.
 
-The query projection, the SwiLU gate and the value projection are ordinary
-``nn.Linear`` modules as in the reference; the query batch norm keeps
-``nn.BatchNorm1d``'s parameters and buffers and runs on the library's
-batch-normalisation kernels (``QueryBatchNorm``).
+The query projection, the SwiLU projection and the value projection keep
+their ``nn.Linear`` modules and run as cuBLAS GEMMs; the SwiGLU gate between
+them and the bias gradients run on the library's kernels
+(``SwiGLUProjection``), and the query batch norm keeps ``nn.BatchNorm1d``'s
+parameters and buffers and runs on the library's batch-normalisation
+kernels (``QueryBatchNorm``).
 """
 from __future__ import annotations
 
@@ -143,6 +145,35 @@ class ProductKeyLookup(torch.autograd.Function):
         psw = ctx.saved_tensors[3]
         dq, dk = _score_backward(ctx, d_psw.contiguous(), psw)
         return dq, dk, None, None
+
+
+class SwiGLUProjection(torch.autograd.Function):
+    """``value_proj(a * silu(swilu_projection(x)))`` of ``HashingMemory.forward``
+    (``pkm/memory.py:226-229``): the two projections are cuBLAS GEMMs; the
+    gate runs as one pass each way (``pkm_swiglu_fwd`` / ``pkm_swiglu_bwd``,
+    the latter also summing the gate projection's bias gradient) and the
+    output projection's bias gradient as one column-sum pass."""
+
+    @staticmethod
+    def forward(ctx, a, x, ws, bs, wv, bv):
+        h = F.linear(x, ws, bs)
+        z = _native.swiglu_fwd(a, h)
+        ctx.save_for_backward(a, x, h, z, ws, wv)
+        ctx.bias_dtypes = (None if bs is None else bs.dtype, None if bv is None else bv.dtype)
+        return F.linear(z, wv, bv)
+
+    @staticmethod
+    def backward(ctx, dy):
+        a, x, h, z, ws, wv = ctx.saved_tensors
+        need_a, need_x, need_ws, need_bs, need_wv, need_bv = ctx.needs_input_grad
+        dy = dy.contiguous()
+        dbv = _native.colsum(dy, ctx.bias_dtypes[1]) if need_bv else None
+        dwv = dy.t().mm(z) if need_wv else None
+        dz = dy.mm(wv)
+        da, dh, dbs = _native.swiglu_bwd(dz, a, h, need_da=need_a, bias_dtype=ctx.bias_dtypes[0] if need_bs else None)
+        dws = dh.t().mm(x) if need_ws else None
+        dx = dh.mm(ws) if need_x else None
+        return da, dx, dws, dbs, dwv, dbv
 
 
 # ---------------------------------------------------------------------------
@@ -297,7 +328,8 @@ class HashingMemory(nn.Module):
         if self.v_proj and not self.swilu_proj:
             output = self.value_proj(output)
         if self.swilu_proj:
-            output = self.value_proj(output * F.silu(self.swilu_projection(input)))
+            output = SwiGLUProjection.apply(output, input, self.swilu_projection.weight, self.swilu_projection.bias,
+                                            self.value_proj.weight, self.value_proj.bias)
         output = F.dropout(output, p=self.value_dropout, training=self.training)
         if self.gating:
             output = F.sigmoid(self.gating(input)) * output

@@ -21,7 +21,8 @@ def install_cpu_kernels(set_attr=setattr):
     import fake_native
     from modelos_b200 import _native
     from modelos_b200.pkm import colwise_embedding_bag, xformer_embeddingbag
-    for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense"):
+    for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense", "swiglu_fwd",
+                 "swiglu_bwd", "colsum"):
         set_attr(_native, name, getattr(fake_native, name))
 
     def bag(indices, weight, per_sample_weights, mode="sum", bw_algo="reverse_indices"):

@@ -101,6 +101,23 @@ def fw_update_bwd(d_new, d_scaled, scaled, counts, scale, lr, weight_decay, grad
     return (dv if need_values else None), (dg if need_grad else None)
 
 
+def swiglu_fwd(a, h):
+    return a * torch.nn.functional.silu(h)
+
+
+def swiglu_bwd(dz, a, h, need_da=True, bias_dtype=None):
+    s = torch.nn.functional.silu(h)
+    sig = torch.sigmoid(h)
+    da = dz * s if need_da else None
+    dh = dz * a * sig * (1 + h * (1 - sig))
+    db = dh.sum(0).to(bias_dtype) if bias_dtype is not None else None
+    return da, dh, db
+
+
+def colsum(x, out_dtype=None):
+    return x.sum(0).to(out_dtype or x.dtype)
+
+
 def read_device_errors(dev=None, reset=True):
     return 0
 
@@ -113,6 +130,7 @@ def install(monkeypatch):
     """Route ``modelos_b200._native`` calls to this module for one test."""
     from modelos_b200 import _native
     for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense",
-                 "fw_update", "fw_update_bwd", "read_device_errors", "check_device_errors"):
+                 "fw_update", "fw_update_bwd", "swiglu_fwd", "swiglu_bwd", "colsum", "read_device_errors",
+                 "check_device_errors"):
         monkeypatch.setattr(_native, name, globals()[name])
     return np
