@@ -84,18 +84,16 @@ __global__ void __launch_bounds__(kNormThreads) norm_reduce_kernel(const T* __re
 
 // Forward finalise: mean, 1/sqrt(var + eps) (biased variance), the running
 // statistics update (unbiased variance), per channel.
-__global__ void norm_fwd_finalize_kernel(const float2* __restrict__ part, int nb, const void* x, int x_dtype,
-                                         int64_t n, int64_t c, double eps, double momentum, void* running_mean,
-                                         void* running_var, int r_dtype, float* __restrict__ save_mean,
-                                         float* __restrict__ save_rstd) {
-  const int64_t ch = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (ch >= c) return;
-  double sa = 0.0, sb = 0.0;
-  for (int rb = 0; rb < nb; ++rb) {
-    const float2 p = part[(int64_t)rb * c + ch];
-    sa += p.x;
-    sb += p.y;
-  }
+__global__ void __launch_bounds__(256) norm_fwd_finalize_kernel(const float2* __restrict__ part, int nb, const void* x,
+                                                                int x_dtype, int64_t n, int64_t c, double eps,
+                                                                double momentum, void* running_mean,
+                                                                void* running_var, int r_dtype,
+                                                                float* __restrict__ save_mean,
+                                                                float* __restrict__ save_rstd) {
+  const Sum2 r = colsum_fixed(nullptr, part, nb, c);
+  const int64_t ch = (int64_t)blockIdx.x * 32 + (threadIdx.x & 31);
+  if (threadIdx.x >= 32 || ch >= c) return;
+  const double sa = r.a, sb = r.b;
   const double shift = ld_f(x, x_dtype, ch);
   const double dm = sa / (double)n;
   const double var = std::max(0.0, sb / (double)n - dm * dm);
@@ -154,17 +152,14 @@ __global__ void __launch_bounds__(kNormThreads) norm_apply_kernel(const T* __res
 // Backward finalise: dbias = sum dy, dweight = rstd * sum dy (x - mean), and
 // the coefficients of dx = a (dy - m) - b (x - mean):
 //   a = w rstd, m = sum dy / n, b = a rstd^2 sum dy (x - mean) / n.
-__global__ void norm_bwd_finalize_kernel(const float2* __restrict__ part, int nb, int64_t n, int64_t c,
-                                         const float* __restrict__ rstd, const void* weight, int p_dtype,
-                                         void* dweight, void* dbias, float4* __restrict__ coef) {
-  const int64_t ch = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (ch >= c) return;
-  double sa = 0.0, sb = 0.0;
-  for (int rb = 0; rb < nb; ++rb) {
-    const float2 p = part[(int64_t)rb * c + ch];
-    sa += p.x;
-    sb += p.y;
-  }
+__global__ void __launch_bounds__(256) norm_bwd_finalize_kernel(const float2* __restrict__ part, int nb, int64_t n,
+                                                                int64_t c, const float* __restrict__ rstd,
+                                                                const void* weight, int p_dtype, void* dweight,
+                                                                void* dbias, float4* __restrict__ coef) {
+  const Sum2 r = colsum_fixed(nullptr, part, nb, c);
+  const int64_t ch = (int64_t)blockIdx.x * 32 + (threadIdx.x & 31);
+  if (threadIdx.x >= 32 || ch >= c) return;
+  const double sa = r.a, sb = r.b;
   const double rs = rstd[ch];
   const double w = weight ? ld_f(weight, p_dtype, ch) : 1.0;
   if (dbias) st_f(dbias, p_dtype, ch, (float)sa);
@@ -260,7 +255,7 @@ extern "C" int pkm_batchnorm_fwd(const void* x, int x_dtype, int64_t n, int64_t 
     else
       norm_reduce_kernel<__nv_bfloat16, 0><<<grid, kNormThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), nullptr,
                                                                           nullptr, n, c, part);
-    norm_fwd_finalize_kernel<<<fin_blocks, 256, 0, st>>>(part, nb, x, x_dtype, n, c, eps, momentum, running_mean,
+    norm_fwd_finalize_kernel<<<(unsigned)((c + 31) / 32), 256, 0, st>>>(part, nb, x, x_dtype, n, c, eps, momentum, running_mean,
                                                          running_var, r_dtype, save_mean, save_rstd);
   } else {
     norm_eval_stats_kernel<<<fin_blocks, 256, 0, st>>>(running_mean, running_var, r_dtype, c, eps, save_mean,
@@ -296,7 +291,7 @@ extern "C" int pkm_batchnorm_bwd(const void* dy, const void* x, int x_dtype, int
   else
     norm_reduce_kernel<__nv_bfloat16, 1><<<grid, kNormThreads, 0, st>>>(
         static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(dy), save_mean, n, c, part);
-  norm_bwd_finalize_kernel<<<(unsigned)((c + 255) / 256), 256, 0, st>>>(part, nb, n, c, save_rstd, weight, p_dtype,
+  norm_bwd_finalize_kernel<<<(unsigned)((c + 31) / 32), 256, 0, st>>>(part, nb, n, c, save_rstd, weight, p_dtype,
                                                                         dweight, dbias, coef);
   if (dx) {
     if (x_dtype == PKM_DT_F32)

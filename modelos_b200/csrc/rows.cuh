@@ -55,6 +55,44 @@ inline int row_blocks(int64_t n, int64_t c) {
   return (int)std::min<int64_t>(nb, 4096);
 }
 
+// Fixed-order sum of the per-row-block partials part[rb][ch] (rb < nb) for
+// the 32 channels of this block (blockDim 256, grid ceil(c / 32)): warp w
+// adds blocks w, w+8, w+16, ... in order (fp64), then warp 0 adds the eight
+// warp sums in warp order.  Valid in warp 0 (lane = channel in the group);
+// every thread of the block must call it.
+struct Sum2 {
+  double a, b;
+};
+__device__ __forceinline__ Sum2 colsum_fixed(const float* part, const float2* part2, int nb, int64_t c) {
+  __shared__ double sa[8][32], sb[8][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t ch = (int64_t)blockIdx.x * 32 + lane;
+  double a = 0.0, b = 0.0;
+  if (ch < c) {
+    for (int rb = warp; rb < nb; rb += 8) {
+      if (part2) {
+        const float2 v = part2[(int64_t)rb * c + ch];
+        a += v.x;
+        b += v.y;
+      } else {
+        a += part[(int64_t)rb * c + ch];
+      }
+    }
+  }
+  sa[warp][lane] = a;
+  sb[warp][lane] = b;
+  __syncthreads();
+  Sum2 r{0.0, 0.0};
+  if (warp == 0) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      r.a += sa[w][lane];
+      r.b += sb[w][lane];
+    }
+  }
+  return r;
+}
+
 inline dim3 row_grid(int64_t n, int64_t c) {
   return dim3((unsigned)((c + 32 * kNormChan - 1) / (32 * kNormChan)), (unsigned)row_blocks(n, c));
 }

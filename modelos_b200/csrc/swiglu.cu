@@ -125,12 +125,11 @@ __global__ void __launch_bounds__(kNormThreads) colsum_kernel(const T* __restric
 }
 
 // out[c] = sum over row blocks of part (fixed order, fp64), as dtype.
-__global__ void colsum_finalize_kernel(const float* __restrict__ part, int nb, int64_t c, void* out, int out_dtype) {
-  const int64_t ch = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (ch >= c) return;
-  double s = 0.0;
-  for (int rb = 0; rb < nb; ++rb) s += part[(int64_t)rb * c + ch];
-  st_f(out, out_dtype, ch, (float)s);
+__global__ void __launch_bounds__(256) colsum_finalize_kernel(const float* __restrict__ part, int nb, int64_t c,
+                                                              void* out, int out_dtype) {
+  const Sum2 r = colsum_fixed(part, nullptr, nb, c);
+  const int64_t ch = (int64_t)blockIdx.x * 32 + (threadIdx.x & 31);
+  if (threadIdx.x < 32 && ch < c) st_f(out, out_dtype, ch, (float)r.a);
 }
 
 static int rows_check(int dtype, int64_t n, int64_t c, std::initializer_list<const void*> ptrs) {
@@ -202,7 +201,7 @@ extern "C" int pkm_swiglu_bwd(const void* dz, const void* a, const void* h, int 
         static_cast<const __nv_bfloat16*>(dz), static_cast<const __nv_bfloat16*>(a),
         static_cast<const __nv_bfloat16*>(h), n, c, static_cast<__nv_bfloat16*>(da), static_cast<__nv_bfloat16*>(dh),
         part);
-  if (dbias) colsum_finalize_kernel<<<(unsigned)((c + 255) / 256), 256, 0, st>>>(part, (int)grid.y, c, dbias, bias_dtype);
+  if (dbias) colsum_finalize_kernel<<<(unsigned)((c + 31) / 32), 256, 0, st>>>(part, (int)grid.y, c, dbias, bias_dtype);
   return check_cuda("pkm_swiglu_bwd");
 }
 
@@ -226,6 +225,6 @@ extern "C" int pkm_colsum(const void* x, int dtype, int64_t n, int64_t c, void* 
     colsum_kernel<float><<<grid, kNormThreads, 0, st>>>(static_cast<const float*>(x), n, c, part);
   else
     colsum_kernel<__nv_bfloat16><<<grid, kNormThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, c, part);
-  colsum_finalize_kernel<<<(unsigned)((c + 255) / 256), 256, 0, st>>>(part, (int)grid.y, c, out, out_dtype);
+  colsum_finalize_kernel<<<(unsigned)((c + 31) / 32), 256, 0, st>>>(part, (int)grid.y, c, out, out_dtype);
   return check_cuda("pkm_colsum");
 }
