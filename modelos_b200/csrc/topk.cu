@@ -196,6 +196,90 @@ __device__ __forceinline__ void stage1_select(const uint32_t (&key)[EPL], int kn
   warp_sort_desc(okey, oidx, dummy);
 }
 
+// Number of true halves in the sum (mod 2^32) of at most 8 bf16x2 compare
+// masks (0xffff per true half): the low half holds -lo mod 2^16, the high
+// half -hi mod 2^16 after the low half's borrow is removed.
+__device__ __forceinline__ int mask_count(uint32_t s) {
+  const uint32_t lo = (0u - s) & 0xffffu;
+  const uint32_t rest = s - lo * 0xffffu;
+  return (int)(lo + (((0u - rest) >> 16) & 0xffffu));
+}
+__device__ __forceinline__ __nv_bfloat162 bf2(uint32_t w) { return *reinterpret_cast<__nv_bfloat162*>(&w); }
+__device__ __forceinline__ uint32_t unkey16_bits(uint32_t k) { return (k & 0x8000u) ? (k & 0x7fffu) : (~k & 0xffffu); }
+
+// Stage 1 for bf16 rows held as raw pairs (lane l: elements l*EPL ..
+// l*EPL+EPL-1, word k = elements 2k and 2k+1): the same selection as
+// stage1_select, with every count taken by packed bf16x2 comparisons
+// (two elements per instruction, -0 equal to +0 as in the key order).
+template <int EPL>
+__device__ __forceinline__ void stage1_select_bf16(const uint32_t (&w)[EPL / 2], int knn, uint32_t* s_key,
+                                                   uint32_t* s_idx, uint32_t& okey, uint32_t& oidx) {
+  constexpr int NW = EPL / 2;
+  static_assert(NW <= 8, "mask_count takes at most 8 masks");
+  const int lane = threadIdx.x & 31;
+  __nv_bfloat162 m2 = bf2(w[0]);
+#pragma unroll
+  for (int k = 1; k < NW; ++k) m2 = __hmax2(m2, bf2(w[k]));
+  const uint32_t mw = *reinterpret_cast<uint32_t*>(&m2);
+  const uint32_t lmax = max(key16(mw & 0xffffu), key16(mw >> 16));
+  const uint32_t lo = __reduce_min_sync(0xffffffffu, lmax), hi = __reduce_max_sync(0xffffffffu, lmax);
+  uint32_t T = lo;
+  if (lo != hi) {
+    const int top = 31 - __clz(lo ^ hi);
+    T = lo & ~((2u << top) - 1u);
+#pragma unroll 1
+    for (int bit = top; bit >= 0; --bit) {
+      const uint32_t cand = T | (1u << bit);
+      const uint32_t cb = unkey16_bits(cand);
+      const __nv_bfloat162 c2 = bf2(cb | (cb << 16));
+      uint32_t acc = 0;
+#pragma unroll
+      for (int k = 0; k < NW; ++k) acc += __hge2_mask(bf2(w[k]), c2);
+      if (__reduce_add_sync(0xffffffffu, mask_count(acc)) >= knn) T = cand;
+    }
+  }
+  const uint32_t tb = unkey16_bits(T);
+  const __nv_bfloat162 t2 = bf2(tb | (tb << 16));
+  uint32_t gtm[NW], eqm[NW];
+  uint32_t gacc = 0, eacc = 0;
+#pragma unroll
+  for (int k = 0; k < NW; ++k) {
+    gtm[k] = __hgt2_mask(bf2(w[k]), t2);
+    eqm[k] = __heq2_mask(bf2(w[k]), t2);
+    gacc += gtm[k];
+    eacc += eqm[k];
+  }
+  const int need_eq = knn - __reduce_add_sync(0xffffffffu, mask_count(gacc));
+  // lower lanes hold lower indices: equal keys are taken in lane order
+  int eqr = warp_excl_prefix(mask_count(eacc));
+  uint32_t selmask = 0;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const uint32_t sh = (e & 1) ? 31 : 15;
+    bool sel = (gtm[e >> 1] >> sh) & 1u;
+    if ((eqm[e >> 1] >> sh) & 1u) {
+      sel = eqr < need_eq;
+      ++eqr;
+    }
+    if (sel) selmask |= 1u << e;
+  }
+  int pos = warp_excl_prefix(__popc(selmask));
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    if (selmask & (1u << e)) {
+      s_key[pos] = key16((e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xffffu));
+      s_idx[pos] = lane * EPL + e;
+      ++pos;
+    }
+  }
+  __syncwarp();
+  okey = lane < knn ? s_key[lane] : 0u;
+  oidx = lane < knn ? s_idx[lane] : 0xffffffffu;
+  __syncwarp();
+  float dummy = 0.f;
+  warp_sort_desc(okey, oidx, dummy);
+}
+
 // Exact stage 2 by a k-way merge of the knn sorted rows s1[i] + s2[.] (one
 // row per lane, equal sums in ascending slot order).  Used for rows where
 // pairs equal to the knn-th sum lie outside the candidate set.
@@ -258,7 +342,7 @@ constexpr int kTopkWarps = 8;
 constexpr int kPairCap = 128;  // candidate pairs for knn <= 32 (119 at knn = 32)
 
 template <typename T, int EPL>
-__global__ void __launch_bounds__(kTopkWarps * 32) product_topk_kernel(const T* __restrict__ scores, int64_t rows,
+__global__ void __launch_bounds__(kTopkWarps * 32, 3) product_topk_kernel(const T* __restrict__ scores, int64_t rows,
                                                                         int n, int knn,
                                                                         int64_t* __restrict__ out_idx,
                                                                         T* __restrict__ out_scores,
@@ -276,6 +360,8 @@ __global__ void __launch_bounds__(kTopkWarps * 32) product_topk_kernel(const T* 
   constexpr int KB = ScoreT<T>::KEYBITS;
   constexpr int PV = ScoreT<T>::PER_VEC;
   constexpr int NV = (EPL % PV == 0) ? EPL / PV : 0;  // 16-byte loads per lane and half
+  // bf16 rows of 8 or 16 scores per lane take the packed-pair stage 1
+  constexpr bool kPackedBf16 = sizeof(T) == 2 && (EPL == 8 || EPL == 16);
   const bool full = n == 32 * EPL;
 
   // candidate pairs (i, j) with (i+1)(j+1) <= knn, packed i | j << 8
@@ -297,6 +383,31 @@ __global__ void __launch_bounds__(kTopkWarps * 32) product_topk_kernel(const T* 
     for (int p = 0; p < 2; ++p) {
       const T* row = scores + (r * 2 + p) * (int64_t)n;
       uint32_t key[EPL];
+      uint32_t ok, oi;
+      if constexpr (kPackedBf16) {
+        if (full && vec_ok) {
+        // bf16 rows compared as packed pairs
+        uint32_t w[EPL / 2];
+        const uint4* vp = reinterpret_cast<const uint4*>(row + (int64_t)lane * EPL);
+#pragma unroll
+        for (int v = 0; v < EPL / 8; ++v) {
+          const uint4 q = __ldg(vp + v);
+          w[4 * v] = q.x;
+          w[4 * v + 1] = q.y;
+          w[4 * v + 2] = q.z;
+          w[4 * v + 3] = q.w;
+        }
+        stage1_select_bf16<EPL>(w, knn, s_key, s_idx, ok, oi);
+        if (p == 0) {
+          k1 = ok;
+          i1 = oi;
+        } else {
+          k2 = ok;
+          i2 = oi;
+        }
+        continue;
+        }
+      }
       if (NV > 0 && full && vec_ok) {
         const uint4* vp = reinterpret_cast<const uint4*>(row + (int64_t)lane * EPL);
 #pragma unroll
@@ -308,7 +419,6 @@ __global__ void __launch_bounds__(kTopkWarps * 32) product_topk_kernel(const T* 
           key[e] = m < n ? ScoreT<T>::key_at(row, m) : 0u;
         }
       }
-      uint32_t ok, oi;
       stage1_select<T, EPL>(key, knn, s_key, s_idx, ok, oi);
       if (p == 0) {
         k1 = ok;
