@@ -232,6 +232,32 @@ PKM_API int pkm_grad_shard_reduce(const void* recv, int dtype, int64_t num_rows,
                                   void* stream);
 
 /*
+ * Ragged entry lists, for tables sharded by rows over ranks (each owner
+ * serves the entries that other ranks route to it):
+ * pkm_segment_sum: out[s] = sum over entries e in [seg_offsets[s],
+ *   seg_offsets[s+1]) of entry_w[e] * rows[entry_row[e]] (fp32, entry order);
+ *   the forward of an embedding bag whose bags have different sizes.
+ *   Workspace: pkm_segment_sum_workspace(n_segs) bytes, 256-byte aligned.
+ * pkm_bag_bwd_ragged: pkm_bag_bwd where entry e's upstream gradient is row
+ *   src_of[e] of grad_rows [n_src, dim] (instead of bag e / bag_size);
+ *   row_idx [n_entries] are the table rows.  Workspace:
+ *   pkm_bag_bwd_workspace(n_entries, 1, num_rows, dim).
+ * Replace the shard-local parts of the row-sharded embedding bag (the
+ * reference's bag, pkm/xformer_embeddingbag.py:97-138 and :331-386, with the
+ * table split over ranks).
+ */
+PKM_API int pkm_segment_sum_workspace(int64_t n_segs, size_t* bytes);
+PKM_API int pkm_segment_sum(const void* rows, int row_dtype, int64_t num_rows, int64_t dim, const int32_t* entry_row,
+                            const float* entry_w, int64_t n_entries, const int64_t* seg_offsets, int64_t n_segs,
+                            void* out, int out_dtype, void* workspace, size_t workspace_bytes, uint32_t* dev_err,
+                            void* stream);
+PKM_API int pkm_bag_bwd_ragged(const int64_t* row_idx, const int32_t* src_of, const void* psw, int psw_dtype,
+                               const void* weight, int weight_dtype, const void* grad_rows, int64_t n_entries,
+                               int64_t n_src, int64_t num_rows, int64_t dim, void* grad_weight,
+                               int grad_weight_dtype, void* grad_psw, int grad_psw_dtype, int32_t* row_counts,
+                               void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream);
+
+/*
  * In-switch all-reduce of a table gradient over NVLink SHARP (NVLS): every
  * rank's gradient [num_rows, dim] sits in one symmetric buffer whose
  * multicast address is mc_src; the owner of rows [rank*shard_rows, ...)

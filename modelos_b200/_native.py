@@ -43,6 +43,10 @@ _SIGS = {
     "pkm_bag_bwd_sharded": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _I, _I64, _I, _P, _I, _P, _P,
                              ctypes.c_size_t, _P, _P], _I),
     "pkm_grad_shard_reduce": ([_P, _I, _I64, _I64, _I, _I, _I64, _P, ctypes.c_float, _I, _P], _I),
+    "pkm_segment_sum_workspace": ([_I64, ctypes.POINTER(ctypes.c_size_t)], _I),
+    "pkm_segment_sum": ([_P, _I, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _I, _P, ctypes.c_size_t, _P, _P], _I),
+    "pkm_bag_bwd_ragged": ([_P, _P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _I, _P, _P,
+                            ctypes.c_size_t, _P, _P], _I),
     "pkm_grad_multimem_allreduce": ([_P, _P, _I, _I64, _I64, _I, _I, _I64, ctypes.c_float, _I, _P], _I),
     "pkm_colsum_workspace": ([_I64, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
     "pkm_swiglu_fwd": ([_P, _P, _I, _I64, _I64, _P, _P], _I),
@@ -557,3 +561,49 @@ def colsum(x: torch.Tensor, out_dtype: Optional[torch.dtype] = None) -> torch.Te
     _check(lib().pkm_colsum(_ptr(x), DT[x.dtype], n, c, _ptr(out), DT[out.dtype], _ptr(ws), ws.numel(),
                             _stream(x.device)), "pkm_colsum")
     return out
+
+
+# ---------------------------------------------------------------------------
+# ragged entry lists (row-sharded tables)
+# ---------------------------------------------------------------------------
+def segment_sum(rows: torch.Tensor, entry_row: torch.Tensor, entry_w: torch.Tensor, seg_offsets: torch.Tensor,
+                out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """``out[s] = sum_{e in segment s} entry_w[e] * rows[entry_row[e]]``."""
+    assert rows.dim() == 2 and rows.is_contiguous()
+    entry_row = entry_row.to(torch.int32).contiguous()
+    entry_w = entry_w.to(torch.float32).contiguous()
+    seg_offsets = seg_offsets.to(torch.int64).contiguous()
+    _need_cuda(rows, entry_row, entry_w, seg_offsets)
+    K, D = rows.shape
+    n_segs = seg_offsets.numel() - 1
+    out = torch.empty((n_segs, D), dtype=out_dtype or rows.dtype, device=rows.device)
+    nb = ctypes.c_size_t(0)
+    _check(lib().pkm_segment_sum_workspace(n_segs, ctypes.byref(nb)), "pkm_segment_sum_workspace")
+    ws = torch.empty(max(int(nb.value), 1), dtype=torch.uint8, device=rows.device)
+    _check(lib().pkm_segment_sum(_ptr(rows), DT[rows.dtype], K, D, _ptr(entry_row), _ptr(entry_w), entry_row.numel(),
+                                 _ptr(seg_offsets), n_segs, _ptr(out), DT[out.dtype], _ptr(ws), ws.numel(),
+                                 _ptr(err_word(rows.device)), _stream(rows.device)), "pkm_segment_sum")
+    return out
+
+
+def bag_bwd_ragged(row_idx: torch.Tensor, src_of: torch.Tensor, psw: Optional[torch.Tensor], weight: torch.Tensor,
+                   grad_rows: torch.Tensor, need_dpsw: bool = True):
+    """K4 over a ragged entry list: ``(dW [K, D], dpsw [E] or None)``."""
+    row_idx = row_idx.to(torch.int64).contiguous()
+    src_of = src_of.to(torch.int32).contiguous()
+    grad_rows = grad_rows.to(weight.dtype).contiguous()
+    _need_cuda(row_idx, src_of, psw, weight, grad_rows)
+    E = row_idx.numel()
+    K, D = weight.shape
+    dW = torch.empty((K, D), dtype=weight.dtype, device=weight.device)
+    if psw is not None:
+        psw = psw.contiguous()
+    dpsw = torch.empty_like(psw) if (need_dpsw and psw is not None) else None
+    ws_bytes = bag_bwd_workspace(E, 1, K, D)
+    ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=weight.device)
+    _check(lib().pkm_bag_bwd_ragged(_ptr(row_idx), _ptr(src_of), _ptr(psw), DT[psw.dtype] if psw is not None else 0,
+                                    _ptr(weight), DT[weight.dtype], _ptr(grad_rows), E, grad_rows.shape[0], K, D,
+                                    _ptr(dW), DT[dW.dtype], _ptr(dpsw), DT[dpsw.dtype] if dpsw is not None else 0,
+                                    None, _ptr(ws), ws_bytes, _ptr(err_word(weight.device)),
+                                    _stream(weight.device)), "pkm_bag_bwd_ragged")
+    return dW, dpsw

@@ -491,7 +491,7 @@ static int bag_bwd_impl(const int64_t* indices, const void* psw, int psw_dtype, 
                         int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size, int64_t num_rows,
                         int64_t dim, const GradDest& dest, int grad_weight_dtype, void* grad_psw,
                         int grad_psw_dtype, int32_t* row_counts, void* workspace, size_t workspace_bytes,
-                        uint32_t* dev_err, void* stream) {
+                        uint32_t* dev_err, void* stream, const int32_t* src_of = nullptr, int64_t n_src = 0) {
   int rc = check_bag_common(indices, n_bags, bag_size, num_rows, dim, weight_dtype);
   if (rc) return rc;
   if (!valid_dtype(grad_weight_dtype) || (psw && !valid_dtype(psw_dtype)) ||
@@ -596,6 +596,8 @@ static int bag_bwd_impl(const int64_t* indices, const void* psw, int psw_dtype, 
     a.out_dtype = grad_weight_dtype;
     a.partials = partials;
     a.err = dev_err;
+    a.src_of = src_of;
+    a.n_src = n_src;
     a.shard_rows = dest.shard_rows;
     a.shard_rank = dest.rank;
     for (int i = 0; i < kMaxShards; ++i) a.shard_base[i] = dest.base[i];
@@ -750,4 +752,82 @@ extern "C" int pkm_grad_multimem_allreduce(const void* mc_src, void* mc_dst, int
       static_cast<const char*>(mc_src), static_cast<char*>(mc_dst), r0 * row_vecs, n_vecs, dtype == PKM_DT_BF16,
       scale);
   return check_cuda("pkm_grad_multimem_allreduce");
+}
+
+// ---------------------------------------------------------------------------
+// ragged entry lists (row-sharded tables)
+// ---------------------------------------------------------------------------
+__global__ void seg_items_kernel(const int64_t* __restrict__ offs, int64_t n_segs, int4* __restrict__ desc,
+                                 int32_t* n_items, uint32_t* err) {
+  for (int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; s < n_segs; s += (int64_t)gridDim.x * blockDim.x) {
+    int64_t b = offs[s], e = offs[s + 1];
+    if (b < 0 || e < b) {  // malformed offsets: an empty segment, reported
+      raise_err(err, PKM_DEVERR_INDEX);
+      b = e = 0;
+    }
+    desc[s] = make_int4((int)s, (int)b, (int)e, -1);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *n_items = (int32_t)n_segs;
+}
+
+extern "C" int pkm_segment_sum_workspace(int64_t n_segs, size_t* bytes) {
+  if (!bytes || n_segs < 0) return fail(PKM_ERR_INVALID_ARG, "bad size");
+  *bytes = (size_t)n_segs * sizeof(int4) + 256;
+  return PKM_OK;
+}
+
+extern "C" int pkm_segment_sum(const void* rows, int row_dtype, int64_t num_rows, int64_t dim, const int32_t* entry_row,
+                               const float* entry_w, int64_t n_entries, const int64_t* seg_offsets, int64_t n_segs,
+                               void* out, int out_dtype, void* workspace, size_t workspace_bytes, uint32_t* dev_err,
+                               void* stream) {
+  if (!valid_dtype(row_dtype) || !valid_dtype(out_dtype)) return fail(PKM_ERR_INVALID_ARG, "bad dtype");
+  if (num_rows < 0 || dim <= 0 || n_entries < 0 || n_segs < 0) return fail(PKM_ERR_INVALID_ARG, "bad size");
+  if (n_entries >= (int64_t(1) << 31) || num_rows >= (int64_t(1) << 31) || n_segs >= (int64_t(1) << 31))
+    return fail(PKM_ERR_UNSUPPORTED, "sizes must stay below 2^31");
+  const int64_t rb = dim * dtype_size(row_dtype);
+  if (rb % 16 != 0 || rb > 4096) return fail(PKM_ERR_UNSUPPORTED, "row bytes must be a multiple of 16, at most 4096");
+  if (n_segs == 0) return PKM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!out || !seg_offsets) return fail(PKM_ERR_INVALID_ARG, "NULL pointer");
+  if (n_entries == 0 || num_rows == 0) {
+    cudaMemsetAsync(out, 0, (size_t)(n_segs * dim * dtype_size(out_dtype)), st);
+    return check_cuda("pkm_segment_sum memset");
+  }
+  if (!rows || !aligned16(rows) || !entry_row || !entry_w) return fail(PKM_ERR_INVALID_ARG, "NULL or unaligned input");
+  size_t need = 0;
+  pkm_segment_sum_workspace(n_segs, &need);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(PKM_ERR_WORKSPACE, "workspace too small or not 256-byte aligned");
+  int4* desc = static_cast<int4*>(workspace);
+  int32_t* n_items = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + (size_t)n_segs * sizeof(int4));
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((n_segs + 255) / 256, (int64_t)num_sms() * 8));
+  seg_items_kernel<<<(unsigned)blocks, 256, 0, st>>>(seg_offsets, n_segs, desc, n_items, dev_err);
+  GatherArgs a{};
+  a.rows = static_cast<const char*>(rows);
+  a.row_bytes = rb;
+  a.dim = dim;
+  a.num_rows = num_rows;  // entry rows are checked against the table
+  a.occ = entry_row;
+  a.occ_w = entry_w;
+  a.L = 1;
+  a.n_items_dev = n_items;
+  a.item_desc = desc;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  a.err = dev_err;
+  return gather_launch(row_dtype, true, false, a, n_segs, st);
+}
+
+extern "C" int pkm_bag_bwd_ragged(const int64_t* row_idx, const int32_t* src_of, const void* psw, int psw_dtype,
+                                  const void* weight, int weight_dtype, const void* grad_rows, int64_t n_entries,
+                                  int64_t n_src, int64_t num_rows, int64_t dim, void* grad_weight,
+                                  int grad_weight_dtype, void* grad_psw, int grad_psw_dtype, int32_t* row_counts,
+                                  void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream) {
+  if (n_entries > 0 && !src_of) return fail(PKM_ERR_INVALID_ARG, "src_of is NULL");
+  if (n_src < 0) return fail(PKM_ERR_INVALID_ARG, "bad size");
+  GradDest dest{};
+  dest.out = grad_weight;
+  return bag_bwd_impl(row_idx, psw, psw_dtype, weight, weight_dtype, grad_rows, n_entries, 1, num_rows, dim, dest,
+                      grad_weight_dtype, grad_psw, grad_psw_dtype, row_counts, workspace, workspace_bytes, dev_err,
+                      stream, src_of, n_src);
 }

@@ -37,6 +37,8 @@ struct GatherArgs {
   const void* w;        // bag mode: per-sample weights, nullable (= 1)
   int w_dtype;
   const int32_t* occ;   // seg mode: occurrence ids sorted by row
+  const int32_t* src_of;  // seg mode, optional: source row of each occurrence (else occurrence / L)
+  int64_t n_src;          // with src_of: number of source rows
   const float* occ_w;   // seg mode: their weights (fp32)
   int64_t L;            // bag size
   // items

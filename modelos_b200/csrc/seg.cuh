@@ -147,7 +147,16 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const __grid_con
     int32_t bag = 0;
     if (e < NE) {
       if ((uint32_t)occ < n_occ) {
-        bag = (int32_t)((uint32_t)occ / L);
+        if (a.src_of) {
+          bag = a.src_of[occ];
+          if ((uint64_t)(uint32_t)bag >= (uint64_t)a.n_src) {
+            raise_err(a.err, PKM_DEVERR_INDEX);
+            bag = 0;
+            w = 0.f;
+          }
+        } else {
+          bag = (int32_t)((uint32_t)occ / L);
+        }
       } else {
         raise_err(a.err, PKM_DEVERR_INDEX);
         occ = 0;

@@ -71,3 +71,57 @@ def run(rank: int, world: int, port: int, out_dir: str, dtype_name: str, mode: s
         del ex, red
     finally:
         dist.destroy_process_group()
+
+
+def sharded_inputs(rank: int, dtype, dev):
+    import torch
+    K, D, B, L = 4096, 256, 512, 32
+    g = torch.Generator().manual_seed(11)
+    table = (torch.randn(K, D, generator=g) * 0.1).to(dtype)
+    g = torch.Generator().manual_seed(200 + rank)
+    idx = torch.randint(0, K, (B, L), generator=g)
+    psw = torch.softmax(torch.randn(B, L, generator=g), -1).to(dtype)
+    d_out = torch.randn(B, D, generator=g).to(dtype)
+    return table.to(dev), idx.to(dev), psw.to(dev), d_out.to(dev)
+
+
+def run_sharded(rank: int, world: int, port: int, out_dir: str, dtype_name: str):
+    """Row-sharded bag on NCCL against the dense kernels over the full table."""
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from modelos_b200 import _native
+        from modelos_b200.sharded import RowShardedEmbeddingBag
+        dtype = getattr(torch, dtype_name)
+        table, idx, psw, d_out = sharded_inputs(rank, dtype, dev)
+        m = RowShardedEmbeddingBag(table.shape[0], table.shape[1], dtype=dtype, device=dev)
+        m.load_full(table)
+        p = psw.clone().requires_grad_()
+        out = m(idx, p)
+        out.backward(d_out)
+        torch.cuda.synchronize()
+        # dense references: this rank's bags, and every rank's bags for dW
+        ref_out = _native.bag_fwd(idx, table, psw)
+        _, ref_dpsw, _ = _native.bag_bwd(idx, table, psw, d_out)
+        all_idx, all_psw, all_d = [], [], []
+        for r in range(world):
+            _, i_r, p_r, d_r = sharded_inputs(r, dtype, dev)
+            all_idx.append(i_r)
+            all_psw.append(p_r)
+            all_d.append(d_r)
+        ref_dW, _, _ = _native.bag_bwd(torch.cat(all_idx), table, torch.cat(all_psw), torch.cat(all_d))
+        S = m.shard_rows
+        torch.save({"out": out.detach().cpu(), "ref_out": ref_out.cpu(), "dpsw": p.grad.cpu(),
+                    "ref_dpsw": ref_dpsw.cpu(), "dW": m.weight.grad.cpu(),
+                    "ref_dW": ref_dW[rank * S:(rank + 1) * S].cpu()},
+                   os.path.join(out_dir, f"shard{rank}.pt"))
+        _native.check_device_errors(dev)
+    finally:
+        dist.destroy_process_group()

@@ -22,7 +22,7 @@ def install_cpu_kernels(set_attr=setattr):
     from modelos_b200 import _native
     from modelos_b200.pkm import colwise_embedding_bag, xformer_embeddingbag
     for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense", "swiglu_fwd",
-                 "swiglu_bwd", "colsum"):
+                 "swiglu_bwd", "colsum", "segment_sum", "bag_bwd_ragged"):
         set_attr(_native, name, getattr(fake_native, name))
 
     def bag(indices, weight, per_sample_weights, mode="sum", bw_algo="reverse_indices"):
@@ -68,5 +68,45 @@ def run(rank: int, world: int, port: int, out_dir: str, mode: str):
         (y ** 2).sum().backward()
         red.finish()
         torch.save({n: p.grad for n, p in m.named_parameters()}, os.path.join(out_dir, f"rank{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+SHARD_K, SHARD_D, SHARD_B, SHARD_L = 50, 16, 5, 7
+
+
+def sharded_case(rank: int):
+    """Table, this rank's bags and upstream gradient (seeded; the full table is
+    the same on every rank)."""
+    import torch
+    g = torch.Generator().manual_seed(7)
+    table = torch.randn(SHARD_K, SHARD_D, generator=g)
+    g = torch.Generator().manual_seed(100 + rank)
+    idx = torch.randint(0, SHARD_K, (SHARD_B, SHARD_L), generator=g)
+    idx[0, :3] = 0  # a repeated row inside one bag
+    psw = torch.rand(SHARD_B, SHARD_L, generator=g)
+    d_out = torch.randn(SHARD_B, SHARD_D, generator=g)
+    return table, idx, psw, d_out
+
+
+def run_sharded(rank: int, world: int, port: int, out_dir: str):
+    """One rank of the row-sharded bag on gloo with the CPU stand-in kernels."""
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        install_cpu_kernels()
+        from modelos_b200.sharded import RowShardedEmbeddingBag
+        table, idx, psw, d_out = sharded_case(rank)
+        m = RowShardedEmbeddingBag(SHARD_K, SHARD_D)
+        m.load_full(table)
+        p = psw.clone().requires_grad_()
+        out = m(idx, p)
+        out.backward(d_out)
+        torch.save({"out": out.detach(), "dpsw": p.grad, "dW": m.weight.grad, "rows": m.shard_rows},
+                   os.path.join(out_dir, f"shard{rank}.pt"))
     finally:
         dist.destroy_process_group()

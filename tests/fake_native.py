@@ -118,6 +118,22 @@ def colsum(x, out_dtype=None):
     return x.sum(0).to(out_dtype or x.dtype)
 
 
+def segment_sum(rows, entry_row, entry_w, seg_offsets, out_dtype=None):
+    n_segs = seg_offsets.numel() - 1
+    seg = torch.repeat_interleave(torch.arange(n_segs), (seg_offsets[1:] - seg_offsets[:-1]).long())
+    out = torch.zeros((n_segs, rows.shape[1]), dtype=torch.float32)
+    out.index_add_(0, seg, rows[entry_row.long()].float() * entry_w.float()[:, None])
+    return out.to(out_dtype or rows.dtype)
+
+
+def bag_bwd_ragged(row_idx, src_of, psw, weight, grad_rows, need_dpsw=True):
+    g = grad_rows.float()[src_of.long()]
+    dW = torch.zeros(weight.shape, dtype=torch.float32)
+    dW.index_add_(0, row_idx.long(), g * psw.float()[:, None])
+    dpsw = (g * weight.float()[row_idx.long()]).sum(1).to(psw.dtype) if need_dpsw else None
+    return dW.to(weight.dtype), dpsw
+
+
 def read_device_errors(dev=None, reset=True):
     return 0
 
@@ -130,7 +146,8 @@ def install(monkeypatch):
     """Route ``modelos_b200._native`` calls to this module for one test."""
     from modelos_b200 import _native
     for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense",
-                 "fw_update", "fw_update_bwd", "swiglu_fwd", "swiglu_bwd", "colsum", "read_device_errors",
+                 "fw_update", "fw_update_bwd", "swiglu_fwd", "swiglu_bwd", "colsum", "segment_sum",
+                 "bag_bwd_ragged", "read_device_errors",
                  "check_device_errors"):
         monkeypatch.setattr(_native, name, globals()[name])
     return np

@@ -60,3 +60,36 @@ def test_dead_rank_fails_fast(tmp_path):
     codes = _spawn(2, "fail", tmp_path)
     assert codes[1] != 0
     assert codes[0] != 0  # the surviving rank errors out (connection closed or timeout)
+
+
+def test_row_sharded_bag_matches_dense(tmp_path):
+    """Row-sharded table (gloo, 2 ranks, CPU stand-in kernels): outputs, weight
+    gradients and each owner's table-gradient rows equal the dense bag over
+    the full table with all ranks' bags."""
+    import dist_worker
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=dist_worker.run_sharded, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert [p.exitcode for p in procs] == [0, 0]
+    dW_full = torch.zeros(dist_worker.SHARD_K, dist_worker.SHARD_D)
+    for r in range(2):
+        table, idx, psw, d_out = dist_worker.sharded_case(r)
+        got = torch.load(os.path.join(tmp_path, f"shard{r}.pt"))
+        ref = (table[idx] * psw[..., None]).sum(1)
+        assert torch.allclose(got["out"], ref, atol=1e-5, rtol=1e-5)
+        ref_dpsw = (table[idx] * d_out[:, None, :]).sum(-1)
+        assert torch.allclose(got["dpsw"], ref_dpsw, atol=1e-5, rtol=1e-5)
+        dW_full.index_add_(0, idx.reshape(-1), (d_out[:, None, :] * psw[..., None]).reshape(-1, dist_worker.SHARD_D))
+    for r in range(2):
+        got = torch.load(os.path.join(tmp_path, f"shard{r}.pt"))
+        S = got["rows"]
+        rows = dW_full[r * S:(r + 1) * S]
+        assert torch.allclose(got["dW"][: rows.shape[0]], rows, atol=1e-5, rtol=1e-5)

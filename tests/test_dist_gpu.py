@@ -57,3 +57,40 @@ def test_sharded_table_grad_two_ranks(tmp_path, dtype_name, mode):
         else:
             assert torch.equal(d["got"], d["ref"])
         assert torch.equal(d["got_keys"], d["ref_keys"])
+
+
+@pytest.mark.parametrize("dtype_name,tol", [("float32", 1e-5), ("bfloat16", 2e-2)])
+def test_row_sharded_bag_two_ranks(tmp_path, dtype_name, tol):
+    """Row-sharded table on two GPUs (NCCL all-to-all routing, ragged bag
+    kernels) against the dense bag kernels over the full table: outputs and
+    per-sample gradients of each rank's bags, and each owner's table rows of
+    the gradient over every rank's bags (those bit for bit: the same rows
+    are summed in the same order)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    sys.path.insert(0, HERE)
+    import dist_gpu_worker
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=dist_gpu_worker.run_sharded, args=(r, 2, port, str(tmp_path), dtype_name))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert [p.exitcode for p in procs] == [0, 0]
+
+    def rel(a, b):
+        a, b = a.double(), b.double()
+        return ((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()
+
+    for r in range(2):
+        d = torch.load(os.path.join(tmp_path, f"shard{r}.pt"))
+        assert rel(d["out"], d["ref_out"]) < tol
+        assert rel(d["dpsw"], d["ref_dpsw"]) < tol
+        assert torch.equal(d["dW"][: d["ref_dW"].shape[0]], d["ref_dW"])
