@@ -1,22 +1,21 @@
-// Row-gather engine shared by the embedding-bag forward (K3), its
-// double-backward (K5) and the sorted-segment backward (K4).
+// Row-gather engine of the embedding-bag forward (K3) and its
+// double-backward (K5); the backward's segment pass (K4) is in seg.cuh.
 //
-// One warp owns a contiguous range of "items" (bags, or chunks of a row's
-// sorted occurrence list).  The items' entries form one contiguous stream;
-// each entry names a source row, a weight and a position for an optional
-// per-entry dot product.  Source rows stream through a per-warp ring of
-// shared-memory slots: lane 0 issues one cp.async.bulk per row, `slots`
-// entries ahead of the consumer, and each slot's mbarrier flips when the
-// bytes land.  The whole warp then accumulates weight * row into fp32
-// registers (lane l owns 16-byte vectors l, l+32, ...; pairs of elements are
-// accumulated with the packed fma.rn.f32x2) in entry order, so every output
-// row is summed in a fixed, deterministic order, and reduces
+// One warp owns a contiguous range of bags.  The bags' entries form one
+// contiguous stream; each entry names a source row, a weight and a position
+// for an optional per-entry dot product.  Source rows stream through a
+// per-warp ring of shared-memory slots: lane 0 issues one cp.async.bulk per
+// row, `slots` entries ahead of the consumer, and each slot's mbarrier flips
+// when the bytes land.  The whole warp then accumulates weight * row into
+// fp32 registers (lane l owns 16-byte vectors l, l+32, ...; pairs of
+// elements are accumulated with the packed fma.rn.f32x2) in entry order, so
+// every output row is summed in a fixed, deterministic order, and reduces
 // <row, dot_vector> across the warp when a dot output is requested.
 //
-// Entry metadata (row id, weight, dot position) and, in segment mode, item
-// descriptors are staged through 64-entry shared rings filled one 32-entry
-// page ahead from registers loaded another page earlier; the per-item dot
-// vector is loaded into registers one item ahead.
+// Entry metadata (row id, weight, dot position) is staged through a 64-entry
+// shared ring filled one 32-entry page ahead from registers loaded another
+// page earlier; the per-bag dot vector is loaded into registers one bag
+// ahead.
 #pragma once
 
 #include "common.cuh"
@@ -429,224 +428,6 @@ __global__ void __launch_bounds__(NW * 32, 1) gather_kernel(const GatherArgs a) 
     int ds = cs;
     uint32_t dp = cpar;
     for (int64_t r = e; r < E1 && r < e + P; ++r) {
-      if (!mbar_wait(&bars[ds], dp, nullptr)) break;
-      if (++ds == P) {
-        ds = 0;
-        dp ^= 1u;
-      }
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// segment pass of the backward (K4)
-// ---------------------------------------------------------------------------
-// One stream of row copies per warp: for every item that has entries, the
-// item's table row (the dot vector, when dots are requested) followed by the
-// upstream-gradient rows of its entries.  Lane 0 keeps the ring `slots`
-// stream positions ahead of the consumer, so the table row of an item is
-// fetched as far ahead as any entry row.  Items without entries (rows no index
-// points to) take no stream position and write a zero row.
-template <typename RowT, int VPL, bool DOT, int NW, bool FULL>
-__global__ void __launch_bounds__(NW * 32, 1) gather_seg_kernel(const GatherArgs a) {
-  constexpr int NP = Pairs<RowT>::NP;
-  constexpr int HDR = DOT ? 1 : 0;  // stream positions before an item's entries
-  extern __shared__ __align__(128) unsigned char smem[];
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int P = a.slots;
-  const int64_t RB = a.row_bytes;
-
-  unsigned char* wbase = smem + warp * a.warp_smem;
-  unsigned char* ring = wbase;
-  const int64_t ring_bytes = ((int64_t)P * RB + 127) & ~(int64_t)127;
-  int2* m_sp = reinterpret_cast<int2*>(wbase + ring_bytes);
-  float* m_w = reinterpret_cast<float*>(m_sp + kMetaRing);
-  int4* m_items = reinterpret_cast<int4*>(m_w + kMetaRing);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(m_items + kMetaRing);
-
-  const int64_t nw = (int64_t)gridDim.x * NW;
-  const int64_t gw = (int64_t)blockIdx.x * NW + warp;
-  const int64_t n_items = (int64_t)(*a.n_items_dev);
-  const int64_t i0 = n_items * gw / nw;
-  const int64_t i1 = n_items * (gw + 1) / nw;
-  if (i0 >= i1) return;  // warp-uniform; no block-wide barrier follows
-  const int64_t ni = i1 - i0;
-  const int64_t E0 = a.item_desc[i0].y;
-  const int64_t E1 = a.item_desc[i1 - 1].z;
-
-  if (lane == 0) {
-    for (int s = 0; s < P; ++s) mbar_init(&bars[s], 1);
-    fence_barrier_init();
-    fence_proxy_async_smem();
-  }
-  {
-    GatherPrefetch p0 = gather_prefetch<G_SEG>(a, E0 + lane, E1);
-    GatherPrefetch p1 = gather_prefetch<G_SEG>(a, E0 + 32 + lane, E1);
-    gather_commit<G_SEG>(a, p0, E0 + lane, E1, m_sp, m_w, lane);
-    gather_commit<G_SEG>(a, p1, E0 + 32 + lane, E1, m_sp, m_w, 32 + lane);
-  }
-  GatherPrefetch pf = gather_prefetch<G_SEG>(a, E0 + 64 + lane, E1);
-  m_items[lane] = lane < ni ? a.item_desc[i0 + lane] : make_int4(0, 0, 0, -1);
-  m_items[32 + lane] = 32 + lane < ni ? a.item_desc[i0 + 32 + lane] : make_int4(0, 0, 0, -1);
-  int4 ipf = (64 + lane < ni) ? a.item_desc[i0 + 64 + lane] : make_int4(0, 0, 0, -1);
-  __syncwarp();
-
-  // producer state (used by lane 0)
-  int64_t pj = 0;                                 // item of the next position to issue
-  int pe = 0;                                     // position within that item
-  int64_t up = 0;                                 // next stream position to issue
-  int pslot = 0;                                  // its ring slot
-  int64_t uc = 0;                                 // next stream position to consume
-  int64_t item_vis = ni < 64 ? ni : (int64_t)64;  // items whose descriptors are in the ring
-  auto produce = [&]() {
-    while (up < uc + P && pj < item_vis) {
-      const int4 d = m_items[pj & (kMetaRing - 1)];
-      const int m = d.z - d.y;
-      if (m == 0) {
-        ++pj;
-        pe = 0;
-        continue;
-      }
-      const char* src;
-      if (DOT && pe == 0) {
-        src = a.dotvec + (int64_t)d.x * RB;
-      } else {
-        const int64_t eidx = (int64_t)d.y + (pe - HDR);
-        src = a.rows + (int64_t)m_sp[(eidx - E0) & (kMetaRing - 1)].x * RB;
-      }
-      mbar_arrive_expect_tx(&bars[pslot], (uint32_t)RB);
-      bulk_g2s(ring + (int64_t)pslot * RB, src, (uint32_t)RB, &bars[pslot]);
-      ++up;
-      if (++pslot == P) pslot = 0;
-      if (++pe == m + HDR) {
-        ++pj;
-        pe = 0;
-      }
-    }
-  };
-  if (lane == 0) produce();
-
-  int cslot = 0;
-  uint32_t cpar = 0;
-  int64_t rel = 0;  // entries consumed, relative to E0
-  bool failed = false;
-  auto advance = [&]() {
-    ++uc;
-    if (++cslot == P) {
-      cslot = 0;
-      cpar ^= 1u;
-    }
-  };
-  for (int64_t j = 0; j < ni && !failed; ++j) {
-    const int4 d = m_items[j & (kMetaRing - 1)];
-    const int m = d.z - d.y;
-    uint64_t acc[VPL][NP];
-#pragma unroll
-    for (int v = 0; v < VPL; ++v)
-#pragma unroll
-      for (int t = 0; t < NP; ++t) acc[v][t] = 0ull;
-    if (m > 0) {
-      uint64_t dv[VPL][NP];
-      if (DOT) {
-        if (!mbar_wait(&bars[cslot], cpar, a.err)) {
-          failed = true;
-          break;
-        }
-        const unsigned char* row = ring + (int64_t)cslot * RB;
-#pragma unroll
-        for (int v = 0; v < VPL; ++v) {
-          const int64_t off = (int64_t)(v * 32 + lane) * 16;
-          const uint4 raw = (FULL || off < RB) ? *reinterpret_cast<const uint4*>(row + off) : make_uint4(0, 0, 0, 0);
-          Pairs<RowT>::unpack(raw, dv[v]);
-        }
-        __syncwarp();
-        advance();
-        if (lane == 0) produce();
-      }
-      for (int q = 0; q < m; ++q) {
-        const int mi = (int)(rel & (kMetaRing - 1));
-        const int2 sp = m_sp[mi];
-        const float w = m_w[mi];
-        if (!mbar_wait(&bars[cslot], cpar, a.err)) {
-          failed = true;
-          break;
-        }
-        const unsigned char* slot = ring + (int64_t)cslot * RB;
-        const uint64_t w2 = pack2(__float_as_uint(w), __float_as_uint(w));
-        uint64_t dsum[VPL];  // one partial dot per vector: short dependency chains
-#pragma unroll
-        for (int v = 0; v < VPL; ++v) {
-          dsum[v] = 0ull;
-          const int64_t off = (int64_t)(v * 32 + lane) * 16;
-          if (FULL || off < RB) {
-            uint64_t f[NP];
-            Pairs<RowT>::unpack(*reinterpret_cast<const uint4*>(slot + off), f);
-#pragma unroll
-            for (int t = 0; t < NP; ++t) {
-              ffma2(acc[v][t], w2, f[t]);
-              if (DOT) ffma2(dsum[v], dv[v][t], f[t]);
-            }
-          }
-        }
-        if (DOT && a.dotout != nullptr) {
-          float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-          for (int v = 0; v < VPL; ++v) {
-            float x0, x1;
-            unpack2(dsum[v], x0, x1);
-            d0 += x0;
-            d1 += x1;
-          }
-          const float dt = warp_sum(d0 + d1);
-          if (lane == 0) st_f(a.dotout, a.dotout_dtype, sp.y, dt);
-        }
-        __syncwarp();
-        advance();
-        if ((rel & 31) == 31) {
-          // entry page rel/32 is consumed: its half now receives page rel/32 + 2
-          const int64_t page = rel >> 5;
-          const int64_t e2 = E0 + (page + 2) * 32 + lane;
-          gather_commit<G_SEG>(a, pf, e2, E1, m_sp, m_w, (int)((e2 - E0) & (kMetaRing - 1)));
-          pf = gather_prefetch<G_SEG>(a, E0 + (page + 3) * 32 + lane, E1);
-          __syncwarp();
-        }
-        ++rel;
-        if (lane == 0) produce();
-      }
-      if (failed) break;
-    }
-    // write the item's row (zeros for an item without entries)
-#pragma unroll
-    for (int v = 0; v < VPL; ++v) {
-      const int64_t c = (int64_t)(v * 32 + lane);
-      if (FULL || c * 16 < RB) {
-        float o[2 * NP];
-#pragma unroll
-        for (int t = 0; t < NP; ++t) unpack2(acc[v][t], o[2 * t], o[2 * t + 1]);
-        const int64_t e0 = c * (2 * NP);
-        if (d.w >= 0)
-          st_run(a.partials, PKM_DT_F32, (int64_t)d.w * a.dim + e0, o, 2 * NP);
-        else
-          st_run(a.out, a.out_dtype, (int64_t)d.x * a.dim + e0, o, 2 * NP);
-      }
-    }
-    if ((j & 31) == 31) {
-      // item page j/32 is done: its half receives page j/32 + 2
-      const int64_t ip = j >> 5;
-      m_items[((ip + 2) * 32 + lane) & (kMetaRing - 1)] = ipf;
-      ipf = make_int4(0, 0, 0, -1);
-      if ((ip + 3) * 32 + lane < ni) ipf = a.item_desc[i0 + (ip + 3) * 32 + lane];
-      item_vis = ni < (ip + 3) * 32 ? ni : (ip + 3) * 32;  // pages ip+1 and ip+2
-      __syncwarp();
-      if (lane == 0) produce();
-    }
-  }
-  if (failed) {
-    // drain copies that may still be in flight before the warp exits
-    int ds = cslot;
-    uint32_t dp = cpar;
-    for (int64_t r = uc; r < up; ++r) {
       if (!mbar_wait(&bars[ds], dp, nullptr)) break;
       if (++ds == P) {
         ds = 0;
