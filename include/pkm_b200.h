@@ -232,6 +232,25 @@ PKM_API int pkm_grad_shard_reduce(const void* recv, int dtype, int64_t num_rows,
                                   void* stream);
 
 /*
+ * pkm_bag_bwd in phases on one workspace: pkm_bag_bwd_sort runs the keys,
+ * scan, radix sort and chunk descriptors (and zeroes grad_psw of invalid
+ * indices, fills row_counts); pkm_bag_bwd_rows then runs the segment pass
+ * and the partial-row sums for the table rows [row_begin, row_end) only,
+ * writing those rows of grad_weight and grad_psw of their occurrences.  Each
+ * row range once, after the sort; together they equal pkm_bag_bwd.  Lets a
+ * caller start exchanging finished rows while later rows are computed.
+ */
+PKM_API int pkm_bag_bwd_sort(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                             int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                             int64_t num_rows, int64_t dim, void* grad_psw, int grad_psw_dtype, int32_t* row_counts,
+                             void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream);
+PKM_API int pkm_bag_bwd_rows(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                             int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                             int64_t num_rows, int64_t dim, int64_t row_begin, int64_t row_end, void* grad_weight,
+                             int grad_weight_dtype, void* grad_psw, int grad_psw_dtype, void* workspace,
+                             size_t workspace_bytes, uint32_t* dev_err, void* stream);
+
+/*
  * Ragged entry lists, for tables sharded by rows over ranks (each owner
  * serves the entries that other ranks route to it):
  * pkm_segment_sum: out[s] = sum over entries e in [seg_offsets[s],
@@ -264,14 +283,16 @@ PKM_API int pkm_bag_bwd_ragged(const int64_t* row_idx, const int32_t* src_of, co
  * reads each 16-byte vector of them with multimem.ld_reduce (the switch
  * returns the sum over ranks; bf16 accumulated in fp32) and stores it, times
  * `scale`, with multimem.st at the same offset of mc_dst (the multicast
- * address of the gradient buffers), which writes every rank's copy.  Called
- * by every rank for its own shard, between two barriers (after every rank's
- * gradient is written, before any rank reads the result).  Replaces the
- * data-parallel all-reduce of values.weight.grad.
+ * address of the gradient buffers), which writes every rank's copy.  Only the
+ * rows of its shard inside [row_begin, row_end) (row_end < 0: all), so the
+ * table can be exchanged in row ranges.  Called by every rank for its own
+ * shard, between two barriers (after every rank's rows of the range are
+ * written, before any rank reads the result).  Replaces the data-parallel
+ * all-reduce of values.weight.grad.
  */
 PKM_API int pkm_grad_multimem_allreduce(const void* mc_src, void* mc_dst, int dtype, int64_t num_rows,
-                                        int64_t dim, int world, int rank, int64_t shard_rows, float scale,
-                                        int max_blocks, void* stream);
+                                        int64_t dim, int world, int rank, int64_t shard_rows, int64_t row_begin,
+                                        int64_t row_end, float scale, int max_blocks, void* stream);
 
 /*
  * SwiGLU gate of the memory output (pkm/memory.py:226-229: output *

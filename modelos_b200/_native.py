@@ -47,7 +47,12 @@ _SIGS = {
     "pkm_segment_sum": ([_P, _I, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _I, _P, ctypes.c_size_t, _P, _P], _I),
     "pkm_bag_bwd_ragged": ([_P, _P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _I, _P, _P,
                             ctypes.c_size_t, _P, _P], _I),
-    "pkm_grad_multimem_allreduce": ([_P, _P, _I, _I64, _I64, _I, _I, _I64, ctypes.c_float, _I, _P], _I),
+    "pkm_grad_multimem_allreduce": ([_P, _P, _I, _I64, _I64, _I, _I, _I64, _I64, _I64, ctypes.c_float, _I, _P],
+                                    _I),
+    "pkm_bag_bwd_sort": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _P, ctypes.c_size_t, _P, _P],
+                         _I),
+    "pkm_bag_bwd_rows": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I, _P, _I, _P,
+                          ctypes.c_size_t, _P, _P], _I),
     "pkm_colsum_workspace": ([_I64, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
     "pkm_swiglu_fwd": ([_P, _P, _I, _I64, _I64, _P, _P], _I),
     "pkm_swiglu_bwd": ([_P, _P, _P, _I, _I64, _I64, _P, _P, _P, _I, _P, ctypes.c_size_t, _P], _I),
@@ -326,11 +331,50 @@ def grad_shard_reduce(recv: torch.Tensor, num_rows: int, rank: int, shard_rows: 
 
 
 def grad_multimem_allreduce(mc_src: int, mc_dst: int, dtype: torch.dtype, num_rows: int, dim: int, world: int,
-                            rank: int, shard_rows: int, device: torch.device, scale: float = 1.0, max_blocks: int = 0):
-    """In-switch all-reduce of this rank's shard (multicast addresses)."""
+                            rank: int, shard_rows: int, device: torch.device, scale: float = 1.0, max_blocks: int = 0,
+                            row_begin: int = 0, row_end: int = -1):
+    """In-switch all-reduce of this rank's shard rows in [row_begin, row_end)."""
     _check(lib().pkm_grad_multimem_allreduce(ctypes.c_void_p(mc_src), ctypes.c_void_p(mc_dst), DT[dtype], num_rows,
-                                             dim, world, rank, shard_rows, float(scale), int(max_blocks),
-                                             _stream(device)), "pkm_grad_multimem_allreduce")
+                                             dim, world, rank, shard_rows, row_begin, row_end, float(scale),
+                                             int(max_blocks), _stream(device)), "pkm_grad_multimem_allreduce")
+
+
+class BagBwdPhases:
+    """``bag_bwd`` split into the sort and row-range segment passes on one
+    workspace: ``sort()`` once, then ``rows(r0, r1, out)`` for each range."""
+
+    def __init__(self, indices: torch.Tensor, weight: torch.Tensor, psw: Optional[torch.Tensor],
+                 grad_out: torch.Tensor, need_dpsw: bool = True):
+        assert indices.dim() == 2 and indices.dtype == torch.long and indices.is_contiguous()
+        assert grad_out.dim() == 2 and grad_out.shape[0] == indices.shape[0] and grad_out.is_contiguous()
+        assert weight.dim() == 2 and weight.is_contiguous() and grad_out.dtype == weight.dtype
+        _need_cuda(indices, grad_out, weight, psw)
+        self.indices, self.weight, self.psw, self.grad_out = indices, weight, psw, grad_out
+        self.B, self.L = indices.shape
+        self.K, self.D = weight.shape
+        dev = weight.device
+        self.dpsw = torch.empty_like(psw) if (need_dpsw and psw is not None) else None
+        self.ws_bytes = bag_bwd_workspace(self.B, self.L, self.K, self.D)
+        self.ws = torch.empty((max(self.ws_bytes, 1),), dtype=torch.uint8, device=dev)
+
+    def _common(self):
+        p = self.psw
+        return (_ptr(self.indices), _ptr(p), DT[p.dtype] if p is not None else 0, _ptr(self.weight),
+                DT[self.weight.dtype], _ptr(self.grad_out), self.B, self.L, self.K, self.D)
+
+    def sort(self):
+        d = self.dpsw
+        _check(lib().pkm_bag_bwd_sort(*self._common(), _ptr(d), DT[d.dtype] if d is not None else 0, None,
+                                      _ptr(self.ws), self.ws_bytes, _ptr(err_word(self.weight.device)),
+                                      _stream(self.weight.device)), "pkm_bag_bwd_sort")
+
+    def rows(self, r0: int, r1: int, out: torch.Tensor):
+        assert out.shape == (self.K, self.D) and out.is_contiguous() and out.dtype == self.weight.dtype
+        d = self.dpsw
+        _check(lib().pkm_bag_bwd_rows(*self._common(), r0, r1, _ptr(out), DT[out.dtype], _ptr(d),
+                                      DT[d.dtype] if d is not None else 0, _ptr(self.ws), self.ws_bytes,
+                                      _ptr(err_word(self.weight.device)), _stream(self.weight.device)),
+               "pkm_bag_bwd_rows")
 
 
 def bag_bwd2(indices: torch.Tensor, a: Optional[torch.Tensor], gbar: torch.Tensor,

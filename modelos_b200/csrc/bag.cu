@@ -181,11 +181,12 @@ struct GradDest {
 };
 
 // Rows split over several chunks: sum the chunk partials in chunk order.
-__global__ void reduce_partials_kernel(const I4* __restrict__ offs, int64_t K, const float* __restrict__ partials,
-                                       int64_t D, const __grid_constant__ GradDest dest, int out_dtype) {
+__global__ void reduce_partials_kernel(const I4* __restrict__ offs, int64_t k0, int64_t k1,
+                                       const float* __restrict__ partials, int64_t D,
+                                       const __grid_constant__ GradDest dest, int out_dtype) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t k = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); k < K; k += warps) {
+  for (int64_t k = k0 + (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); k < k1; k += warps) {
     const I4 o = offs[k];
     const int items = offs[k + 1].y - o.y;
     if (items <= 1) continue;
@@ -487,11 +488,62 @@ extern "C" int pkm_bag_bwd_workspace(int64_t n_bags, int64_t bag_size, int64_t n
   return PKM_OK;
 }
 
+// Segment pass (+ per-sample dots) and the partial-row sums for the table
+// rows [row_begin, row_end) of a sorted workspace.
+static int bag_bwd_rows(const void* grad_out, const void* weight, int weight_dtype, int64_t n_bags,
+                        int64_t bag_size, int64_t K, int64_t D, const GradDest& dest, int grad_weight_dtype,
+                        void* grad_psw, int grad_psw_dtype, const int32_t* sorted, const float* w_sorted,
+                        const int4* desc, const int32_t* n_items, const I4* offs, float* partials, uint32_t* dev_err,
+                        const int32_t* src_of, int64_t n_src, int64_t row_begin, int64_t row_end, cudaStream_t st) {
+  if (row_end <= row_begin) return PKM_OK;
+  const int64_t M = n_bags * bag_size;
+  GatherArgs a{};
+  a.rows = static_cast<const char*>(grad_out);
+  a.row_bytes = D * dtype_size(weight_dtype);
+  a.dim = D;
+  a.num_rows = n_bags;
+  a.occ = sorted;
+  a.occ_w = w_sorted;
+  a.L = bag_size;
+  a.n_items_dev = n_items;
+  a.item_desc = desc;
+  a.dotvec = static_cast<const char*>(weight);
+  a.dotout = grad_psw;
+  a.dotout_dtype = grad_psw_dtype;
+  a.out = dest.out;
+  a.out_dtype = grad_weight_dtype;
+  a.partials = partials;
+  a.err = dev_err;
+  a.src_of = src_of;
+  a.n_src = n_src;
+  a.row_lo = row_begin;
+  a.row_hi = row_end;
+  a.shard_rows = dest.shard_rows;
+  a.shard_rank = dest.rank;
+  for (int i = 0; i < kMaxShards; ++i) a.shard_base[i] = dest.base[i];
+  const int64_t items_upper = K + (M + kChunk - 1) / kChunk + 1;
+  int rc = gather_launch(weight_dtype, true, grad_psw != nullptr, a, items_upper, st);
+  if (rc) return rc;
+  // rows that were split over several chunks
+  const int64_t nk = row_end - row_begin;
+  int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((nk + 7) / 8, (int64_t)num_sms() * 8));
+  reduce_partials_kernel<<<(unsigned)blocks, 256, 0, st>>>(offs, row_begin, row_end, partials, D, dest,
+                                                           grad_weight_dtype);
+  return check_cuda("pkm_bag_bwd");
+}
+
+// Phases of the bag backward: the sort (keys, scan, radix sort, chunk
+// descriptors) and the segment pass over a range of table rows, which can be
+// run as separate calls on the same workspace (the rows in any number of
+// ranges, each once, after the sort).
+enum { kBwdAll = 0, kBwdSort = 1, kBwdRows = 2 };
+
 static int bag_bwd_impl(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
                         int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size, int64_t num_rows,
                         int64_t dim, const GradDest& dest, int grad_weight_dtype, void* grad_psw,
                         int grad_psw_dtype, int32_t* row_counts, void* workspace, size_t workspace_bytes,
-                        uint32_t* dev_err, void* stream, const int32_t* src_of = nullptr, int64_t n_src = 0) {
+                        uint32_t* dev_err, void* stream, const int32_t* src_of = nullptr, int64_t n_src = 0,
+                        int phase = kBwdAll, int64_t row_begin = 0, int64_t row_end = -1) {
   int rc = check_bag_common(indices, n_bags, bag_size, num_rows, dim, weight_dtype);
   if (rc) return rc;
   if (!valid_dtype(grad_weight_dtype) || (psw && !valid_dtype(psw_dtype)) ||
@@ -509,6 +561,20 @@ static int bag_bwd_impl(const int64_t* indices, const void* psw, int psw_dtype, 
   if (grad_psw && (weight == nullptr || !aligned16(weight)))
     return fail(PKM_ERR_INVALID_ARG, "weight NULL or not 16-byte aligned");
   const BwdLayout L = bwd_layout(M, K, D);
+  if (row_end < 0) row_end = K;
+  if (row_begin < 0 || row_begin > row_end || row_end > K) return fail(PKM_ERR_INVALID_ARG, "bad row range");
+  if (phase != kBwdAll && dest.shard_rows > 0) return fail(PKM_ERR_UNSUPPORTED, "phased backward writes locally");
+  if ((M == 0 || K == 0) && phase != kBwdAll) {
+    if (phase == kBwdRows && row_end > row_begin)
+      cudaMemsetAsync(static_cast<char*>(dest.out) + row_begin * D * dtype_size(grad_weight_dtype), 0,
+                      (size_t)((row_end - row_begin) * D * dtype_size(grad_weight_dtype)), st);
+    if (phase == kBwdSort) {
+      if (row_counts && K > 0) cudaMemsetAsync(row_counts, 0, sizeof(int32_t) * K, st);
+      if (grad_psw && M > 0) cudaMemsetAsync(grad_psw, 0, (size_t)(M * dtype_size(grad_psw_dtype)), st);
+      if (M > 0 && dev_err) cudaMemsetAsync(dev_err, PKM_DEVERR_INDEX, 1, st);
+    }
+    return check_cuda("pkm_bag_bwd memset");
+  }
   if (M == 0 || K == 0) {
     if (K > 0 && dest.shard_rows > 0) {
       const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((K * D / 8 + 255) / 256, (int64_t)num_sms() * 8));
@@ -541,6 +607,13 @@ static int bag_bwd_impl(const int64_t* indices, const void* psw, int psw_dtype, 
   float* partials = reinterpret_cast<float*>(ws + L.partials);
 
   const int nsm = num_sms();
+  const int sort_passes = (bits_for(K) + 7) / 8;
+  if (phase == kBwdRows) {
+    int32_t* sorted = sort_passes & 1 ? vals_a : vals_b;  // where the last radix pass wrote the values
+    return bag_bwd_rows(grad_out, weight, weight_dtype, n_bags, bag_size, K, D, dest, grad_weight_dtype, grad_psw,
+                        grad_psw_dtype, sorted, w_sorted, desc, n_items, offs, partials, dev_err, src_of, n_src,
+                        row_begin, row_end, st);
+  }
   // 1. row keys + counts
   cudaMemsetAsync(counts, 0, sizeof(int32_t) * (K + 1), st);
   {
@@ -578,37 +651,10 @@ static int bag_bwd_impl(const int64_t* indices, const void* psw, int psw_dtype, 
     }
     rc = check_cuda("pkm_bag_bwd prologue");
     if (rc) return rc;
-    // 5. segment sums (+ per-sample gradient dots)
-    GatherArgs a{};
-    a.rows = static_cast<const char*>(grad_out);
-    a.row_bytes = D * dtype_size(weight_dtype);
-    a.dim = D;
-    a.num_rows = n_bags;
-    a.occ = vin;
-    a.occ_w = w_sorted;
-    a.L = bag_size;
-    a.n_items_dev = n_items;
-    a.item_desc = desc;
-    a.dotvec = static_cast<const char*>(weight);
-    a.dotout = grad_psw;
-    a.dotout_dtype = grad_psw_dtype;
-    a.out = dest.out;
-    a.out_dtype = grad_weight_dtype;
-    a.partials = partials;
-    a.err = dev_err;
-    a.src_of = src_of;
-    a.n_src = n_src;
-    a.shard_rows = dest.shard_rows;
-    a.shard_rank = dest.rank;
-    for (int i = 0; i < kMaxShards; ++i) a.shard_base[i] = dest.base[i];
-    const int64_t items_upper = K + (M + kChunk - 1) / kChunk + 1;
-    rc = gather_launch(weight_dtype, true, grad_psw != nullptr, a, items_upper, st);
-    if (rc) return rc;
-  }
-  // 6. rows that were split over several chunks
-  {
-    int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((K + 7) / 8, (int64_t)nsm * 8));
-    reduce_partials_kernel<<<(unsigned)blocks, 256, 0, st>>>(offs, K, partials, D, dest, grad_weight_dtype);
+    if (phase == kBwdSort) return PKM_OK;
+    return bag_bwd_rows(grad_out, weight, weight_dtype, n_bags, bag_size, K, D, dest, grad_weight_dtype, grad_psw,
+                        grad_psw_dtype, vin, w_sorted, desc, n_items, offs, partials, dev_err, src_of, n_src,
+                        row_begin, row_end, st);
   }
   return check_cuda("pkm_bag_bwd");
 }
@@ -733,16 +779,18 @@ extern "C" int pkm_bag_bwd_noalloc(const int64_t* indices, const void* psw, int 
 }
 
 extern "C" int pkm_grad_multimem_allreduce(const void* mc_src, void* mc_dst, int dtype, int64_t num_rows, int64_t dim,
-                                           int world, int rank, int64_t shard_rows, float scale, int max_blocks,
-                                           void* stream) {
+                                           int world, int rank, int64_t shard_rows, int64_t row_begin,
+                                           int64_t row_end, float scale, int max_blocks, void* stream) {
   if (dtype != PKM_DT_F32 && dtype != PKM_DT_BF16) return fail(PKM_ERR_UNSUPPORTED, "dtype must be f32 or bf16");
   if (world < 1 || rank < 0 || rank >= world) return fail(PKM_ERR_INVALID_ARG, "bad world / rank");
   if (shard_rows <= 0 || shard_rows * world < num_rows || dim <= 0) return fail(PKM_ERR_INVALID_ARG, "bad size");
   if ((dim * dtype_size(dtype)) % 16 != 0) return fail(PKM_ERR_UNSUPPORTED, "row bytes must be a multiple of 16");
   if (!mc_src || !mc_dst || !aligned16(mc_src) || !aligned16(mc_dst))
     return fail(PKM_ERR_INVALID_ARG, "multicast addresses NULL or not 16-byte aligned");
-  const int64_t r0 = (int64_t)rank * shard_rows;
-  const int64_t rows = std::min<int64_t>(shard_rows, num_rows - r0);
+  if (row_end < 0) row_end = num_rows;
+  const int64_t r0 = std::max<int64_t>((int64_t)rank * shard_rows, row_begin);
+  const int64_t r1 = std::min<int64_t>(std::min<int64_t>((int64_t)(rank + 1) * shard_rows, num_rows), row_end);
+  const int64_t rows = r1 - r0;
   if (rows <= 0) return PKM_OK;
   const int64_t row_vecs = dim * dtype_size(dtype) / 16;
   const int64_t n_vecs = rows * row_vecs;
@@ -830,4 +878,28 @@ extern "C" int pkm_bag_bwd_ragged(const int64_t* row_idx, const int32_t* src_of,
   return bag_bwd_impl(row_idx, psw, psw_dtype, weight, weight_dtype, grad_rows, n_entries, 1, num_rows, dim, dest,
                       grad_weight_dtype, grad_psw, grad_psw_dtype, row_counts, workspace, workspace_bytes, dev_err,
                       stream, src_of, n_src);
+}
+
+extern "C" int pkm_bag_bwd_sort(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                                int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                                int64_t num_rows, int64_t dim, void* grad_psw, int grad_psw_dtype,
+                                int32_t* row_counts, void* workspace, size_t workspace_bytes, uint32_t* dev_err,
+                                void* stream) {
+  GradDest dest{};
+  dest.out = reinterpret_cast<void*>(uintptr_t(1));  // not written by this phase
+  return bag_bwd_impl(indices, psw, psw_dtype, weight, weight_dtype, grad_out, n_bags, bag_size, num_rows, dim, dest,
+                      weight_dtype, grad_psw, grad_psw_dtype, row_counts, workspace, workspace_bytes, dev_err, stream,
+                      nullptr, 0, kBwdSort);
+}
+
+extern "C" int pkm_bag_bwd_rows(const int64_t* indices, const void* psw, int psw_dtype, const void* weight,
+                                int weight_dtype, const void* grad_out, int64_t n_bags, int64_t bag_size,
+                                int64_t num_rows, int64_t dim, int64_t row_begin, int64_t row_end, void* grad_weight,
+                                int grad_weight_dtype, void* grad_psw, int grad_psw_dtype, void* workspace,
+                                size_t workspace_bytes, uint32_t* dev_err, void* stream) {
+  GradDest dest{};
+  dest.out = grad_weight;
+  return bag_bwd_impl(indices, psw, psw_dtype, weight, weight_dtype, grad_out, n_bags, bag_size, num_rows, dim, dest,
+                      grad_weight_dtype, grad_psw, grad_psw_dtype, nullptr, workspace, workspace_bytes, dev_err,
+                      stream, nullptr, 0, kBwdRows, row_begin, row_end);
 }

@@ -38,6 +38,7 @@ struct GatherArgs {
   const int32_t* occ;   // seg mode: occurrence ids sorted by row
   const int32_t* src_of;  // seg mode, optional: source row of each occurrence (else occurrence / L)
   int64_t n_src;          // with src_of: number of source rows
+  int64_t row_lo, row_hi;  // seg mode: only the items of table rows [row_lo, row_hi) (row_hi <= row_lo: all)
   const float* occ_w;   // seg mode: their weights (fp32)
   int64_t L;            // bag size
   // items

@@ -121,9 +121,27 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const __grid_con
 
   const int64_t nw = (int64_t)gridDim.x * NW;
   const int64_t gw = (int64_t)blockIdx.x * NW + warp;
-  const int64_t n_items = (int64_t)(*a.n_items_dev);
-  const int64_t i0 = n_items * gw / nw;
-  const int64_t i1 = n_items * (gw + 1) / nw;
+  int64_t it_lo = 0, it_hi = (int64_t)(*a.n_items_dev);
+  if (a.row_hi > a.row_lo) {
+    // the items (sorted by row) of rows [row_lo, row_hi): two lower bounds
+    auto lower = [&](int64_t row) {
+      int64_t lo = 0, hi = it_hi;
+      while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if ((int64_t)a.item_desc[mid].x < row)
+          lo = mid + 1;
+        else
+          hi = mid;
+      }
+      return lo;
+    };
+    const int64_t b = lower(a.row_lo), e = lower(a.row_hi);
+    it_lo = b;
+    it_hi = e;
+  }
+  const int64_t n_items = it_hi - it_lo;
+  const int64_t i0 = it_lo + n_items * gw / nw;
+  const int64_t i1 = it_lo + n_items * (gw + 1) / nw;
   if (i0 >= i1) return;  // warp-uniform; the block has no barrier
   const int ni = (int)(i1 - i0);
   const int64_t E0 = a.item_desc[i0].y;

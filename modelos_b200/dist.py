@@ -53,7 +53,7 @@ class ShardedTableGrad:
     """
 
     def __init__(self, weight: torch.nn.Parameter, group: Optional[dist.ProcessGroup] = None,
-                 average: bool = False, max_blocks: Optional[int] = None, mode: str = "auto"):
+                 average: bool = False, max_blocks: Optional[int] = None, mode: str = "auto", chunks: int = 2):
         import torch.distributed._symmetric_memory as symm_mem
 
         if mode not in ("auto", "nvls", "p2p"):
@@ -97,6 +97,9 @@ class ShardedTableGrad:
         if max_blocks is None:  # grid cap of the side-stream kernel (measured best per mode / size)
             max_blocks = 64 if (self.mode == "nvls" or self.world <= 2) else 148
         self.max_blocks = max_blocks
+        # in-switch mode: the bag backward's rows are computed and exchanged in
+        # `chunks` row ranges, the exchange of one beside the pass of the next
+        self.chunks = max(1, int(chunks))
         self.side = torch.cuda.Stream(dev)
         self.flag = torch.zeros(1, device=dev)
         self.done = None
@@ -118,22 +121,29 @@ class ShardedTableGrad:
         the table gradient is complete after ``wait()``."""
         from . import _native
 
+        main = torch.cuda.current_stream(weight.device)
         if self.mode == "nvls":
-            _, dpsw, _ = _native.bag_bwd(indices, weight, psw, grad_out, need_dpsw=need_dpsw,
-                                         out=self.local[: self.K])
+            ph = _native.BagBwdPhases(indices, weight, psw, grad_out, need_dpsw=need_dpsw)
+            ph.sort()
+            bounds = [self.K * c // self.chunks for c in range(self.chunks + 1)]
+            for r0, r1 in zip(bounds[:-1], bounds[1:]):
+                ph.rows(r0, r1, self.local[: self.K])
+                self.side.wait_stream(main)
+                with torch.cuda.stream(self.side):
+                    dist.all_reduce(self.flag, group=self.group)  # every rank's rows [r0, r1) are written
+                    _native.grad_multimem_allreduce(self.mc_local, self.mc_full, weight.dtype, self.K, self.D,
+                                                    self.world, self.rank, self.shard_rows, weight.device,
+                                                    self.scale, self.max_blocks, r0, r1)
+            dpsw = ph.dpsw
         else:
             dpsw = _native.bag_bwd_sharded(indices, weight, psw, grad_out, self.recv_ptrs, self.rank,
                                            self.shard_rows, need_dpsw=need_dpsw)
-        self.side.wait_stream(torch.cuda.current_stream(weight.device))
-        with torch.cuda.stream(self.side):
-            dist.all_reduce(self.flag, group=self.group)  # every rank's rows are written
-            if self.mode == "nvls":
-                _native.grad_multimem_allreduce(self.mc_local, self.mc_full, weight.dtype, self.K, self.D,
-                                                self.world, self.rank, self.shard_rows, weight.device, self.scale,
-                                                self.max_blocks)
-            else:
+            self.side.wait_stream(main)
+            with torch.cuda.stream(self.side):
+                dist.all_reduce(self.flag, group=self.group)  # every rank's rows are in the receive buffers
                 _native.grad_shard_reduce(self.recv, self.K, self.rank, self.shard_rows, self.full_ptrs,
                                           self.scale, self.max_blocks)
+        with torch.cuda.stream(self.side):
             dist.all_reduce(self.flag, group=self.group)  # every shard is in every rank's gradient
             self.done = torch.cuda.Event()
             self.done.record(self.side)

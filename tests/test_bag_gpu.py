@@ -183,3 +183,25 @@ def test_config1_full_size_properties():
     lhs = dW.double().sum(0)
     rhs = (psw_d.double().sum(1)[:, None] * g_d.double()).sum(0)
     assert (lhs - rhs).abs().max().item() <= 2e-2 * rhs.abs().max().item() + 1e-2
+
+
+def test_phased_backward_equals_one_call():
+    """pkm_bag_bwd_sort + pkm_bag_bwd_rows over row ranges == pkm_bag_bwd, bit for bit."""
+    from modelos_b200 import _native
+    g = torch.Generator(device=DEV).manual_seed(9)
+    B, L, K, D = 700, 64, 3000, 256
+    idx = torch.randint(0, K, (B, L), generator=g, device=DEV)
+    idx[:40, :] = 17  # a hot row split over several chunks
+    psw = torch.rand(B, L, generator=g, device=DEV).bfloat16()
+    W = torch.randn(K, D, generator=g, device=DEV).bfloat16()
+    go = torch.randn(B, D, generator=g, device=DEV).bfloat16()
+    dW, dpsw, _ = _native.bag_bwd(idx, W, psw, go)
+    ph = _native.BagBwdPhases(idx, W, psw, go)
+    ph.sort()
+    out = torch.full_like(W, float("nan"))
+    for r0, r1 in ((0, 17), (17, 18), (18, 1500), (1500, K)):
+        ph.rows(r0, r1, out)
+    torch.cuda.synchronize()
+    assert torch.equal(out, dW)
+    assert torch.equal(ph.dpsw, dpsw)
+    _native.check_device_errors()
