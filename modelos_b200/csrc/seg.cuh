@@ -325,10 +325,9 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const __grid_con
       const uint32_t slot = ring_lane + cslot * rb;
       const float w = m_w[e & (kMetaRing - 1)];
       const uint64_t w2 = pack2(__float_as_uint(w), __float_as_uint(w));
-      uint64_t ds[VPL];
+      uint64_t ds[2] = {0ull, 0ull};  // dot accumulators of the even and the odd vectors
 #pragma unroll
       for (int v = 0; v < VPL; ++v) {
-        ds[v] = 0ull;
         if (FULL || (v * 32 + lane) * 16 < rb) {
           uint4 raw;
           asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -339,7 +338,7 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const __grid_con
 #pragma unroll
           for (int t = 0; t < NP; ++t) {
             ffma2(acc[v][t], w2, f[t]);
-            if (DOT) ffma2(ds[v], dv[v][t], f[t]);
+            if (DOT) ffma2(ds[v & 1], dv[v][t], f[t]);
           }
         }
       }
@@ -358,15 +357,11 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const __grid_con
       }
       cslot = cslot + 1 == DEPTH ? 0 : cslot + 1;
       if (DOT) {
-        float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-        for (int v = 0; v < VPL; ++v) {
-          float x0, x1;
-          unpack2(ds[v], x0, x1);
-          d0 += x0;
-          d1 += x1;
-        }
-        m_dot[e & 31][lane] = d0 + d1;
+        uint64_t d2;
+        asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d2) : "l"(ds[0]), "l"(ds[1]));
+        float x0, x1;
+        unpack2(d2, x0, x1);
+        m_dot[e & 31][lane] = x0 + x1;
       }
     }
     if ((e & 31) == 0 || e == NE) {
