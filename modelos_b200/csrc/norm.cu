@@ -43,32 +43,24 @@ __global__ void __launch_bounds__(kNormThreads) norm_reduce_kernel(const T* __re
 #pragma unroll
       for (int i = 0; i < kNormChan; ++i) ref[i] = mean[c0 + i];
     }
-    // four rows of loads in flight per thread, rows summed in order
-    constexpr int64_t kStep = kNormThreads / 32;
-    for (int64_t r = r0 + warp; r < r1; r += 4 * kStep) {
-      float v[4][kNormChan], g[4][kNormChan];
+  #pragma unroll 4
+  for (int64_t r = r0 + warp; r < r1; r += kNormThreads / 32) {
+      float v[kNormChan];
+      RowIO<T>::load(x + r * c + c0, v);
+      if (MODE == 0) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t rr = r + u * kStep;
-        if (rr < r1) {
-          RowIO<T>::load(x + rr * c + c0, v[u]);
-          if (MODE == 1) RowIO<T>::load(dy + rr * c + c0, g[u]);
+        for (int i = 0; i < kNormChan; ++i) {
+          const float d = v[i] - ref[i];
+          sa[i] += d;
+          sb[i] = fmaf(d, d, sb[i]);
         }
-      }
+      } else {
+        float g[kNormChan];
+        RowIO<T>::load(dy + r * c + c0, g);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (r + u * kStep < r1) {
-#pragma unroll
-          for (int i = 0; i < kNormChan; ++i) {
-            if (MODE == 0) {
-              const float d = v[u][i] - ref[i];
-              sa[i] += d;
-              sb[i] = fmaf(d, d, sb[i]);
-            } else {
-              sa[i] += g[u][i];
-              sb[i] = fmaf(g[u][i], v[u][i] - ref[i], sb[i]);
-            }
-          }
+        for (int i = 0; i < kNormChan; ++i) {
+          sa[i] += g[i];
+          sb[i] = fmaf(g[i], v[i] - ref[i], sb[i]);
         }
       }
     }
@@ -202,24 +194,14 @@ __global__ void __launch_bounds__(kNormThreads) norm_bwd_apply_kernel(const T* _
     km[k] = q.y;
     kb[k] = q.z;
   }
-  constexpr int64_t kStep = kNormThreads / 32;
-  for (int64_t r = r0 + warp; r < r1; r += 4 * kStep) {
-    float g[4][kNormChan], v[4][kNormChan];
+#pragma unroll 4
+  for (int64_t r = r0 + warp; r < r1; r += kNormThreads / 32) {
+    float g[kNormChan], v[kNormChan];
+    RowIO<T>::load(dy + r * c + c0, g);
+    RowIO<T>::load(x + r * c + c0, v);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (r + u * kStep < r1) {
-        RowIO<T>::load(dy + (r + u * kStep) * c + c0, g[u]);
-        RowIO<T>::load(x + (r + u * kStep) * c + c0, v[u]);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (r + u * kStep < r1) {
-#pragma unroll
-        for (int k = 0; k < kNormChan; ++k) v[u][k] = ka[k] * (g[u][k] - km[k]) - kb[k] * (v[u][k] - mu[k]);
-        RowIO<T>::store(dx + (r + u * kStep) * c + c0, v[u]);
-      }
-    }
+    for (int k = 0; k < kNormChan; ++k) v[k] = ka[k] * (g[k] - km[k]) - kb[k] * (v[k] - mu[k]);
+    RowIO<T>::store(dx + r * c + c0, v);
   }
 }
 

@@ -28,25 +28,14 @@ template <typename T>
 __global__ void __launch_bounds__(kNormThreads) swiglu_fwd_kernel(const T* __restrict__ a, const T* __restrict__ h,
                                                                  int64_t n, int64_t c, T* __restrict__ z) {
   const int64_t total = n * (c / kNormChan);
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  // four vectors of loads in flight per thread
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += 4 * stride) {
-    float av[4][kNormChan], hv[4][kNormChan];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t off = i * kNormChan;
+    float av[kNormChan], hv[kNormChan];
+    RowIO<T>::load(a + off, av);
+    RowIO<T>::load(h + off, hv);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (i + u * stride < total) {
-        RowIO<T>::load(a + (i + u * stride) * kNormChan, av[u]);
-        RowIO<T>::load(h + (i + u * stride) * kNormChan, hv[u]);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (i + u * stride < total) {
-#pragma unroll
-        for (int k = 0; k < kNormChan; ++k) av[u][k] = rnd_t<T>(av[u][k] * rnd_t<T>(silu_f(hv[u][k])));
-        RowIO<T>::store(z + (i + u * stride) * kNormChan, av[u]);
-      }
-    }
+    for (int k = 0; k < kNormChan; ++k) av[k] = rnd_t<T>(av[k] * rnd_t<T>(silu_f(hv[k])));
+    RowIO<T>::store(z + off, av);
   }
 }
 
@@ -66,38 +55,25 @@ __global__ void __launch_bounds__(kNormThreads) swiglu_bwd_kernel(const T* __res
   if (c0 < c) {
     int64_t r0, r1;
     row_range(n, blockIdx.y, gridDim.y, r0, r1);
-    // two rows of loads in flight per thread, rows summed in order
-    constexpr int64_t kStep = kNormThreads / 32;
-    for (int64_t r = r0 + warp; r < r1; r += 2 * kStep) {
-      float g[2][kNormChan], av[2][kNormChan], hv[2][kNormChan];
+#pragma unroll 2
+    for (int64_t r = r0 + warp; r < r1; r += kNormThreads / 32) {
+      const int64_t off = r * c + c0;
+      float g[kNormChan], av[kNormChan], hv[kNormChan];
+      RowIO<T>::load(dz + off, g);
+      RowIO<T>::load(a + off, av);
+      RowIO<T>::load(h + off, hv);
+      float o1[kNormChan], o2[kNormChan];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        if (r + u * kStep < r1) {
-          const int64_t off = (r + u * kStep) * c + c0;
-          RowIO<T>::load(dz + off, g[u]);
-          RowIO<T>::load(a + off, av[u]);
-          RowIO<T>::load(h + off, hv[u]);
-        }
+      for (int k = 0; k < kNormChan; ++k) {
+        const float sig = 1.f / (1.f + expf(-hv[k]));
+        const float s = rnd_t<T>(silu_f(hv[k]));  // silu(h) as the forward rounded it
+        const float ds = rnd_t<T>(g[k] * av[k]);
+        o1[k] = rnd_t<T>(g[k] * s);
+        o2[k] = rnd_t<T>(ds * sig * (1.f + hv[k] * (1.f - sig)));
+        sum[k] += o2[k];
       }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        if (r + u * kStep < r1) {
-          const int64_t off = (r + u * kStep) * c + c0;
-          float o1[kNormChan], o2[kNormChan];
-#pragma unroll
-          for (int k = 0; k < kNormChan; ++k) {
-            const float e = expf(-hv[u][k]);
-            const float sig = 1.f / (1.f + e);
-            const float s = rnd_t<T>(hv[u][k] / (1.f + e));  // silu(h) as the forward rounded it
-            const float ds = rnd_t<T>(g[u][k] * av[u][k]);
-            o1[k] = rnd_t<T>(g[u][k] * s);
-            o2[k] = rnd_t<T>(ds * sig * (1.f + hv[u][k] * (1.f - sig)));
-            sum[k] += o2[k];
-          }
-          if (da) RowIO<T>::store(da + off, o1);
-          RowIO<T>::store(dh + off, o2);
-        }
-      }
+      if (da) RowIO<T>::store(da + off, o1);
+      RowIO<T>::store(dh + off, o2);
     }
   }
   if (part == nullptr) return;  // grid-uniform
@@ -127,18 +103,12 @@ __global__ void __launch_bounds__(kNormThreads) colsum_kernel(const T* __restric
   if (c0 < c) {
     int64_t r0, r1;
     row_range(n, blockIdx.y, gridDim.y, r0, r1);
-    constexpr int64_t kStep = kNormThreads / 32;
-    for (int64_t r = r0 + warp; r < r1; r += 4 * kStep) {
-      float v[4][kNormChan];
+#pragma unroll 4
+    for (int64_t r = r0 + warp; r < r1; r += kNormThreads / 32) {
+      float v[kNormChan];
+      RowIO<T>::load(x + r * c + c0, v);
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (r + u * kStep < r1) RowIO<T>::load(x + (r + u * kStep) * c + c0, v[u]);
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (r + u * kStep < r1) {
-#pragma unroll
-          for (int k = 0; k < kNormChan; ++k) sum[k] += v[u][k];
-        }
+      for (int k = 0; k < kNormChan; ++k) sum[k] += v[k];
     }
   }
 #pragma unroll
