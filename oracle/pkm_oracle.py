@@ -48,6 +48,13 @@ __all__ = [
     "bincount",
     "fw_value_update",
     "marginal_entropy",
+    "batchnorm_train",
+    "batchnorm_bwd",
+    "batchnorm_eval",
+    "swiglu",
+    "swiglu_bwd",
+    "segment_sum",
+    "bag_bwd_ragged",
 ]
 
 
@@ -286,17 +293,118 @@ def bincount(indices, K: int) -> np.ndarray:
     return np.bincount(np.asarray(indices, dtype=np.int64).reshape(-1), minlength=K)
 
 
-def fw_value_update(p, g, counts, scale, lr, wd):
-    """Fast-weight value update of ``update_fw`` (``fwpkm/fwpkm.py:333-365``).
+def fw_value_update(p, g, counts, scale, lr, wd, clip: bool = False):
+    """Fast-weight value update of ``update_fw`` (``fwpkm/fwpkm.py:333-365``)
+    and ``update_fw_param`` (``:266-272``).
 
-    ``g' = g * scale / max(count, 1)``; ``p' = p - lr * (g' + wd * p)``,
+    ``g' = g * scale / max(count, 1)``; ``u = clamp(g', -1, 1)`` when
+    ``clip`` (``grad_clip``), else ``g'``; ``p' = p - lr * (u + wd * p)``,
     float64.  Returns (p', g').
     """
     p = np.asarray(p, dtype=np.float64)
     g = np.asarray(g, dtype=np.float64)
     c = np.maximum(np.asarray(counts, dtype=np.float64), 1.0)
     gs = g * scale / c[:, None]
-    return p - lr * (gs + wd * p), gs
+    u = np.clip(gs, -1.0, 1.0) if clip else gs
+    return p - lr * (u + wd * p), gs
+
+
+# --------------------------------------------------------------------------
+# query batch norm (pkm/memory.py:308-309: nn.BatchNorm1d(heads * k_dim,
+# eps=1e-6, momentum=0.1) on the [n, c] query projection)
+# --------------------------------------------------------------------------
+def batchnorm_train(x, weight, bias, running_mean, running_var, momentum: float, eps: float):
+    """Training forward in float64: batch mean and biased variance normalise,
+    the running statistics move by ``momentum`` with the unbiased variance.
+    Returns (out, mean, rstd, new_running_mean, new_running_var)."""
+    x = np.asarray(x, dtype=np.float64)
+    n = x.shape[0]
+    mean = x.mean(axis=0)
+    var = ((x - mean) ** 2).mean(axis=0)
+    rstd = 1.0 / np.sqrt(var + eps)
+    out = (x - mean) * rstd
+    if weight is not None:
+        out = out * np.asarray(weight, dtype=np.float64)
+    if bias is not None:
+        out = out + np.asarray(bias, dtype=np.float64)
+    unbiased = var * n / max(n - 1, 1)
+    rm = (1 - momentum) * np.asarray(running_mean, dtype=np.float64) + momentum * mean
+    rv = (1 - momentum) * np.asarray(running_var, dtype=np.float64) + momentum * unbiased
+    return out, mean, rstd, rm, rv
+
+
+def batchnorm_bwd(dy, x, mean, rstd, weight):
+    """Training backward in float64: (dx, dweight, dbias)."""
+    dy = np.asarray(dy, dtype=np.float64)
+    x = np.asarray(x, dtype=np.float64)
+    n = x.shape[0]
+    xhat = (x - mean) * rstd
+    w = np.ones_like(mean) if weight is None else np.asarray(weight, dtype=np.float64)
+    db = dy.sum(axis=0)
+    dw = (dy * xhat).sum(axis=0)
+    dx = w * rstd * (dy - db / n - xhat * dw / n)
+    return dx, dw, db
+
+
+def batchnorm_eval(x, weight, bias, running_mean, running_var, eps: float):
+    """Evaluation forward in float64 with the running statistics."""
+    x = np.asarray(x, dtype=np.float64)
+    out = (x - running_mean) / np.sqrt(np.asarray(running_var, dtype=np.float64) + eps)
+    if weight is not None:
+        out = out * weight
+    if bias is not None:
+        out = out + bias
+    return out
+
+
+# --------------------------------------------------------------------------
+# SwiGLU gate of the memory output (pkm/memory.py:226-229:
+# value_proj(output * F.silu(swilu_projection(input))))
+# --------------------------------------------------------------------------
+def swiglu(a, h):
+    """``a * silu(h)``, silu(h) = h / (1 + exp(-h)), float64."""
+    a = np.asarray(a, dtype=np.float64)
+    h = np.asarray(h, dtype=np.float64)
+    return a * h / (1.0 + np.exp(-h))
+
+
+def swiglu_bwd(dz, a, h):
+    """(da, dh) of ``swiglu``: da = dz * silu(h), dh = dz * a * silu'(h),
+    silu'(h) = sig * (1 + h * (1 - sig)), float64."""
+    dz = np.asarray(dz, dtype=np.float64)
+    a = np.asarray(a, dtype=np.float64)
+    h = np.asarray(h, dtype=np.float64)
+    sig = 1.0 / (1.0 + np.exp(-h))
+    return dz * h * sig, dz * a * sig * (1.0 + h * (1.0 - sig))
+
+
+# --------------------------------------------------------------------------
+# ragged bags (one rank's shard of a row-sharded table)
+# --------------------------------------------------------------------------
+def segment_sum(rows, entry_row, entry_w, offsets):
+    """``out[s] = sum_{e in [offsets[s], offsets[s+1])} w[e] * rows[row[e]]``:
+    the bag forward (``pkm/xformer_embeddingbag.py:97-138``) over bags of
+    different sizes, float64."""
+    rows = np.asarray(rows, dtype=np.float64)
+    offsets = np.asarray(offsets, dtype=np.int64)
+    out = np.zeros((len(offsets) - 1, rows.shape[1]))
+    for s in range(len(offsets) - 1):
+        e0, e1 = offsets[s], offsets[s + 1]
+        if e1 > e0:
+            out[s] = (np.asarray(entry_w[e0:e1], dtype=np.float64)[:, None] * rows[entry_row[e0:e1]]).sum(0)
+    return out
+
+
+def bag_bwd_ragged(row_idx, src_of, psw, weight, grad_rows):
+    """The bag backward (``pkm/xformer_embeddingbag.py:331-386``) where entry e
+    reads upstream row ``src_of[e]``: (dW, dpsw), float64."""
+    weight = np.asarray(weight, dtype=np.float64)
+    g = np.asarray(grad_rows, dtype=np.float64)[np.asarray(src_of)]
+    w = np.asarray(psw, dtype=np.float64)
+    dW = np.zeros_like(weight)
+    np.add.at(dW, np.asarray(row_idx), g * w[:, None])
+    dpsw = (g * weight[np.asarray(row_idx)]).sum(1)
+    return dW, dpsw
 
 
 def marginal_entropy(M, topk: int, eps: float = 1e-8) -> float:

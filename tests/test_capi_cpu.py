@@ -68,3 +68,40 @@ def test_cpu_tensors_are_rejected():
     w = torch.zeros(4, 16)
     with pytest.raises(RuntimeError, match="CUDA"):
         _native.bag_fwd(idx, w, None)
+
+
+def test_new_entry_points_reject_bad_arguments():
+    """Argument checks of the batch-norm, SwiGLU, column-sum, fused-update,
+    ragged, phased and exchange entry points come before any device work."""
+    L = _native.lib()
+    fake = ctypes.c_void_p(256)
+    c_d = ctypes.c_double
+    # batch norm: unsupported dtype, channels not a multiple of 8
+    assert L.pkm_batchnorm_fwd(fake, 7, 4, 16, None, None, 0, None, None, 0, 1, c_d(0.1), c_d(1e-6), fake, fake,
+                               fake, None, 0, None) == 2
+    assert L.pkm_batchnorm_fwd(fake, 0, 4, 12, None, None, 0, None, None, 0, 1, c_d(0.1), c_d(1e-6), fake, fake,
+                               fake, None, 0, None) == 2
+    assert L.pkm_batchnorm_bwd(fake, fake, 1, 0, 16, fake, fake, None, 0, fake, None, None, None, 0, None) == 1
+    # SwiGLU and column sums
+    assert L.pkm_swiglu_fwd(fake, fake, 1, 4, 12, fake, None) == 2
+    assert L.pkm_colsum(fake, 1, -1, 16, fake, 1, None, 0, None) == 1
+    # fused fast-weight update: bad dtype, negative rows
+    assert L.pkm_fw_update(fake, fake, 2, 4, 16, None, 0, c_d(1), c_d(0.1), c_d(0), 1, fake, None, fake, None,
+                           None) == 2
+    assert L.pkm_fw_update(fake, fake, 0, -4, 16, None, 0, c_d(1), c_d(0.1), c_d(0), 1, fake, None, fake, None,
+                           None) == 1
+    # ragged segment sum: negative sizes
+    assert L.pkm_segment_sum(fake, 0, 10, 16, fake, fake, -1, fake, 2, fake, 0, None, 0, None, None) == 1
+    # phased backward: row range outside the table
+    assert L.pkm_bag_bwd_rows(fake, fake, 0, fake, 0, fake, 4, 2, 10, 16, 5, 11, fake, 0, None, 0, fake, 1 << 20,
+                              None, None) == 1
+    # exchange: world above one NVLink domain, shard rows not covering the table
+    ptrs = (ctypes.c_void_p * 9)(*([fake] * 9))
+    assert L.pkm_grad_shard_reduce(fake, 1, 100, 16, 9, 0, 12, ptrs, ctypes.c_float(1.0), 0, None) == 1
+    assert L.pkm_grad_shard_reduce(fake, 1, 100, 16, 2, 0, 12, ptrs, ctypes.c_float(1.0), 0, None) == 1
+    assert L.pkm_grad_multimem_allreduce(fake, fake, 1, 100, 16, 2, 3, 50, 0, -1, ctypes.c_float(1.0), 0,
+                                         None) == 1
+    # zero-size work is a no-op without a device
+    assert L.pkm_segment_sum(None, 0, 10, 16, None, None, 0, None, 0, None, 0, None, 0, None, None) == 0
+    assert L.pkm_fw_update(None, None, 0, 0, 16, None, 0, c_d(1), c_d(0.1), c_d(0), 1, None, None, None, None,
+                           None) == 0
