@@ -205,3 +205,28 @@ def test_phased_backward_equals_one_call():
     assert torch.equal(out, dW)
     assert torch.equal(ph.dpsw, dpsw)
     _native.check_device_errors()
+
+
+def test_ragged_kernels_against_oracle():
+    """pkm_segment_sum and pkm_bag_bwd_ragged (the shard-local kernels of the
+    row-sharded table) against the oracle; empty segments included."""
+    from modelos_b200 import _native
+    g = torch.Generator().manual_seed(12)
+    K, D = 500, 128
+    sizes = torch.randint(0, 40, (300,), generator=g)
+    sizes[5] = 0
+    offsets = torch.cat([torch.zeros(1, dtype=torch.long), torch.cumsum(sizes, 0)])
+    E = int(offsets[-1])
+    rows = torch.randint(0, K, (E,), generator=g)
+    w = torch.rand(E, generator=g)
+    W = torch.randn(K, D, generator=g)
+    out = _native.segment_sum(W.to(DEV), rows.to(DEV), w.to(DEV), offsets.to(DEV))
+    ref = po.segment_sum(W.numpy(), rows.numpy(), w.numpy(), offsets.numpy())
+    assert rel_err(out.cpu().numpy(), ref) < 1e-5
+    src = torch.repeat_interleave(torch.arange(len(sizes)), sizes)
+    gr = torch.randn(len(sizes), D, generator=g)
+    dW, dpsw = _native.bag_bwd_ragged(rows.to(DEV), src.to(DEV), w.to(DEV), W.to(DEV), gr.to(DEV))
+    rdW, rdpsw = po.bag_bwd_ragged(rows.numpy(), src.numpy(), w.numpy(), W.numpy(), gr.numpy())
+    assert rel_err(dW.cpu().numpy(), rdW) < 1e-5
+    assert rel_err(dpsw.cpu().numpy(), rdpsw) < 1e-5
+    _native.check_device_errors()

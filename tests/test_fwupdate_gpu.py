@@ -55,3 +55,17 @@ def test_backward_matches_autograd(clip):
     ((rn * w1).sum() + (rs * w2).sum()).backward()
     for a, b in ((v.grad, vr.grad), (gr.grad, grr.grad)):
         assert ((a - b).abs().max() / b.abs().max()).item() < 1e-6
+
+
+def test_against_oracle():
+    from modelos_b200 import _native
+    from oracle import pkm_oracle as po
+    g = torch.Generator().manual_seed(3)
+    K, D = 1000, 64
+    values = torch.randn(K, D, generator=g)
+    grad = torch.randn(K, D, generator=g) * 1e-6
+    indices = torch.randint(0, K, (64, 4, 8), generator=g)
+    new, scaled, counts = _native.fw_update(values.to(DEV), grad.to(DEV), indices.to(DEV), 65536, 0.1, 0.02, True)
+    rnew, rs = po.fw_value_update(values.numpy(), grad.numpy(), counts.cpu().numpy(), 65536, 0.1, 0.02, clip=True)
+    assert ((new.cpu().double() - torch.from_numpy(rnew)).abs().max() / torch.from_numpy(rnew).abs().max()) < 1e-6
+    assert ((scaled.cpu().double() - torch.from_numpy(rs)).abs().max() / torch.from_numpy(rs).abs().max()) < 1e-6

@@ -103,3 +103,27 @@ def test_deterministic():
         ours.weight.grad = None
     for a, b in zip(*outs):
         assert torch.equal(a, b)
+
+
+def test_against_oracle():
+    """fp32 kernels against the oracle's float64 restatement."""
+    import numpy as np
+
+    from modelos_b200 import _native
+    from oracle import pkm_oracle as po
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(2000, 64, generator=g) * 3 + 2
+    w = torch.rand(64, generator=g) + 0.5
+    b = torch.randn(64, generator=g)
+    rm, rv = torch.zeros(64), torch.ones(64)
+    dy = torch.randn(2000, 64, generator=g)
+    xd, wd, bd, rmd, rvd = (t.to(DEV) for t in (x, w, b, rm, rv))
+    out, mean, rstd = _native.batchnorm_fwd(xd, wd, bd, rmd, rvd, True, 0.1, 1e-6)
+    ro, rmean, rrstd, rrm, rrv = po.batchnorm_train(x.numpy(), w.numpy(), b.numpy(), rm.numpy(), rv.numpy(), 0.1,
+                                                    1e-6)
+    assert rel(out.cpu(), torch.from_numpy(ro)) < 1e-5
+    assert rel(rmd.cpu(), torch.from_numpy(rrm)) < 1e-5 and rel(rvd.cpu(), torch.from_numpy(rrv)) < 1e-5
+    dx, dw, db = _native.batchnorm_bwd(dy.to(DEV), xd, mean, rstd, wd)
+    rdx, rdw, rdb = po.batchnorm_bwd(dy.numpy(), x.numpy(), rmean, rrstd, w.numpy())
+    for a, r in ((dx, rdx), (dw, rdw), (db, rdb)):
+        assert rel(a.cpu(), torch.from_numpy(np.asarray(r))) < 1e-5

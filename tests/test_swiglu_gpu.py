@@ -52,3 +52,19 @@ def test_colsum_deterministic_and_exact_order_free():
     assert rel(s1, x.float().sum(0)) < 2e-2
     f = torch.randn(1000, 64, generator=g, device=DEV)
     assert rel(_native.colsum(f), f.double().sum(0)) < 1e-6
+
+
+def test_gate_against_oracle():
+    from modelos_b200 import _native
+    from oracle import pkm_oracle as po
+    g = torch.Generator().manual_seed(2)
+    a = torch.randn(333, 64, generator=g)
+    h = torch.randn(333, 64, generator=g) * 3
+    dz = torch.randn(333, 64, generator=g)
+    z = _native.swiglu_fwd(a.to(DEV), h.to(DEV))
+    assert rel(z.cpu(), torch.from_numpy(po.swiglu(a.numpy(), h.numpy()))) < 1e-5
+    da, dh, db = _native.swiglu_bwd(dz.to(DEV), a.to(DEV), h.to(DEV), bias_dtype=torch.float32)
+    rda, rdh = po.swiglu_bwd(dz.numpy(), a.numpy(), h.numpy())
+    assert rel(da.cpu(), torch.from_numpy(rda)) < 1e-5
+    assert rel(dh.cpu(), torch.from_numpy(rdh)) < 1e-5
+    assert rel(db.cpu(), torch.from_numpy(rdh.sum(0))) < 1e-5
