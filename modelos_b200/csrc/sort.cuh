@@ -165,9 +165,15 @@ void scan_exclusive(Load ld, int64_t n, T* out, T* block_sums, cudaStream_t st) 
 // rounds of 32, so (warp, round, lane) order is item order, and equal digits
 // keep their order through __match_any_sync ranks.
 // ---------------------------------------------------------------------------
-constexpr int kSortThreads = 256;
+#ifndef PKM_SORT_THREADS
+#define PKM_SORT_THREADS 256
+#endif
+#ifndef PKM_SORT_IPT
+#define PKM_SORT_IPT 8  // items per thread: 2048-item tiles (measured 50 us faster per c2 backward than 4096)
+#endif
+constexpr int kSortThreads = PKM_SORT_THREADS;
 constexpr int kSortWarps = kSortThreads / 32;
-constexpr int kSortIpt = 16;
+constexpr int kSortIpt = PKM_SORT_IPT;
 constexpr int kSortTile = kSortThreads * kSortIpt;
 constexpr int kRadix = 256;
 
