@@ -181,21 +181,31 @@ struct GradDest {
 };
 
 // Rows split over several chunks: sum the chunk partials in chunk order.
+// A warp checks 32 rows at once and sums only the split ones (rare: a row
+// needs more than one chunk of occurrences).
 __global__ void reduce_partials_kernel(const I4* __restrict__ offs, int64_t k0, int64_t k1,
                                        const float* __restrict__ partials, int64_t D,
                                        const __grid_constant__ GradDest dest, int out_dtype) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t k = k0 + (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); k < k1; k += warps) {
-    const I4 o = offs[k];
-    const int items = offs[k + 1].y - o.y;
-    if (items <= 1) continue;
-    const float* base = partials + (int64_t)o.z * D;
-    void* row = dest.row(k, D, out_dtype);
-    for (int64_t e = lane; e < D; e += 32) {
-      float s = 0.f;
-      for (int j = 0; j < items; ++j) s += base[(int64_t)j * D + e];
-      st_f(row, out_dtype, e, s);
+  for (int64_t g = k0 + ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; g < k1;
+       g += warps * 32) {
+    const int64_t mine = g + lane;
+    bool split = false;
+    if (mine < k1) split = offs[mine + 1].y - offs[mine].y > 1;
+    unsigned todo = __ballot_sync(0xffffffffu, split);
+    while (todo) {
+      const int64_t k = g + __ffs(todo) - 1;
+      todo &= todo - 1;
+      const I4 o = offs[k];
+      const int items = offs[k + 1].y - o.y;
+      const float* base = partials + (int64_t)o.z * D;
+      void* row = dest.row(k, D, out_dtype);
+      for (int64_t e = lane; e < D; e += 32) {
+        float s = 0.f;
+        for (int j = 0; j < items; ++j) s += base[(int64_t)j * D + e];
+        st_f(row, out_dtype, e, s);
+      }
     }
   }
   if (dest.shard_rows > 0) __threadfence_system();
@@ -526,7 +536,7 @@ static int bag_bwd_rows(const void* grad_out, const void* weight, int weight_dty
   if (rc) return rc;
   // rows that were split over several chunks
   const int64_t nk = row_end - row_begin;
-  int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((nk + 7) / 8, (int64_t)num_sms() * 8));
+  int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((nk + 255) / 256, (int64_t)num_sms() * 8));
   reduce_partials_kernel<<<(unsigned)blocks, 256, 0, st>>>(offs, row_begin, row_end, partials, D, dest,
                                                            grad_weight_dtype);
   return check_cuda("pkm_bag_bwd");
