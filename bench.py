@@ -1,4 +1,4 @@
-"""Benchmark: PKM layer forward + backward tokens/s.
+"""Benchmark: PKM layer forward + backward tokens/s (the headline benchmark's config 2).
 
 One step = forward + backward of ``HashingMemory`` at the config-2 shape
 (x [8, 2048, 1024] bf16, heads 4, knn 32, k_dim 512, n_keys 512 -> 262144

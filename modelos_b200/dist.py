@@ -4,7 +4,7 @@ Tokens are independent in the memory lookup, so the layer shards over the
 batch: every rank holds the full (replicated) value table and runs its own
 tokens, and the gradients are summed across ranks.  The value table's
 gradient is the large one (``[n_keys^2, v_dim]``, 512 MiB in bf16 at
-BASELINE config 2); ``ShardedTableGrad`` fuses its exchange into the bag
+benchmark config 2); ``ShardedTableGrad`` fuses its exchange into the bag
 backward (rows stored to their owners over NVLink while the segment pass
 computes, owner-side reduction and all-gather beside the rest of the
 backward).  ``GradReducer`` all-reduces every other gradient from its

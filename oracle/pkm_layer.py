@@ -1,6 +1,6 @@
 """numpy restatement of one ``HashingMemory`` training step (forward + backward).
 
-TEST INFRASTRUCTURE / CPU BASELINE ONLY: used by ``bench.py`` for the timed
+TEST INFRASTRUCTURE / CPU REFERENCE TIMING ONLY: used by ``bench.py`` for the timed
 CPU baseline (``cpu_baseline`` and ``--impl reference``), never by the
 product package.  It follows ``HashingMemory.forward`` (``pkm/memory.py:190-248``)
 and the autograd of each step, with BLAS matmuls for the dense parts and the

@@ -13,10 +13,10 @@ import math
 import numpy as np
 import torch
 
-# BASELINE config 0 (``pkm/memory.py:41-68`` argument names).
+# Benchmark config 0 (``pkm/memory.py:41-68`` argument names).
 CONFIG0 = dict(input_dim=512, output_dim=512, mem_k_dim=256, mem_v_dim=512, mem_heads=4,
                mem_knn=32, mem_n_keys=128)
-# BASELINE config 2 geometry (bf16, query BatchNorm).
+# Benchmark config 2 geometry (bf16, query BatchNorm).
 CONFIG2 = dict(input_dim=1024, output_dim=1024, mem_k_dim=512, mem_v_dim=1024, mem_heads=4,
                mem_knn=32, mem_n_keys=512, mem_query_batchnorm=True, mem_query_rmsnorm=False)
 
@@ -35,7 +35,7 @@ def pkm_state(cfg: dict, seed: int = 0) -> dict:
     Init follows ``HashingMemory.reset_parameters`` (``pkm/memory.py:169-188``)
     for keys (U(+-1/sqrt(k_dim))), values (N(0, v_dim^-1/2)) and the SwiLU /
     value projections (N(0, output_dim^-1/2)); the query Linear and all biases
-    keep nn.Linear's default U(+-1/sqrt(fan_in)), as BASELINE config 0 states.
+    keep nn.Linear's default U(+-1/sqrt(fan_in)), as benchmark config 0 states.
     """
     g = torch.Generator().manual_seed(seed)
     C = cfg["input_dim"]
@@ -71,7 +71,7 @@ def pkm_input(shape, seed: int = 0) -> torch.Tensor:
 
 def embbag_case(B: int, L: int, K: int, D: int, seed: int = 0, heads: int = 1,
                 w_std: float = 0.03):
-    """Embedding-bag inputs in the style of BASELINE config 1.
+    """Embedding-bag inputs in the style of benchmark config 1.
 
     Indices uniform in [0, K) with replacement, per-bag weights the softmax of
     N(0,1) logits normalised per head (``heads`` groups of L/heads), table

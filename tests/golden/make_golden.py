@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this folder from the reference itself.
 
 Run in a container that has the reference tree (read-only) at
-``$MODELOS_REF`` (default ``/root/reference``)::
+``$MODELOS_REF`` (default: a ``reference`` folder beside this repository)::
 
     python tests/golden/make_golden.py
 
@@ -29,7 +29,8 @@ import torch  # noqa: E402
 
 import cases  # noqa: E402
 
-REF = os.environ.get("MODELOS_REF", "/root/reference")
+REF = os.environ.get("MODELOS_REF",
+                     os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))), "reference"))
 
 
 def _import_ref():

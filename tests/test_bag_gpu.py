@@ -150,7 +150,7 @@ def test_out_of_range_indices_are_skipped_and_flagged():
 
 
 def test_config1_full_size_properties():
-    """BASELINE config 1 at full size (16384 bags x 128, 262144 x 1024 bf16):
+    """Benchmark config 1 at full size (16384 bags x 128, 262144 x 1024 bf16):
     sampled bags and rows against the oracle plus checksum identities."""
     from modelos_b200 import _native
     B, L, K, D = 16384, 128, 262144, 1024

@@ -38,7 +38,7 @@ def _call_noalloc(L, idx, psw, W, g, gw, gp, counts, err, dt):
 def test_noalloc_backward_matches_workspace_backward(dtype, tol):
     from modelos_b200 import _native
     L = _native.lib()
-    # BASELINE config-0 bag geometry: 256 bags x 128, 16384 x 512 table
+    # benchmark config-0 bag geometry: 256 bags x 128, 16384 x 512 table
     idx, psw, W, g = cases.embbag_case(256, 128, 16384, 512, seed=9, heads=4)
     idx, psw, W, g = idx.to(DEV), psw.to(DEV, dtype), W.to(DEV, dtype), g.to(DEV, dtype)
     idx[0, :64] = 7  # one row with a long segment
