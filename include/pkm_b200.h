@@ -251,6 +251,43 @@ PKM_API int pkm_bag_bwd_rows(const int64_t* indices, const void* psw, int psw_dt
                              size_t workspace_bytes, uint32_t* dev_err, void* stream);
 
 /*
+ * Routing around the all-to-all of the row-sharded embedding bag (the
+ * reference's bag, pkm/xformer_embeddingbag.py:97-138 and :331-386, with
+ * the table split by rows: rank o owns rows [o*shard_rows, (o+1)*shard_rows)).
+ * pkm_route_pack: owner = indices[e] / shard_rows for the n = n_bags *
+ *   bag_size occurrences; a stable partition by owner.  Writes, per packed
+ *   position p: order[p] (the occurrence), local_row[p] (its row inside the
+ *   owner's shard), weight[p] (psw as fp32, 1 when psw is NULL), bag[p]
+ *   (occurrence / bag_size); send_counts[o] (int64 [world]) = entries for
+ *   owner o.  Indices outside [0, world*shard_rows) set PKM_DEVERR_INDEX, are
+ *   not counted and sort after the last owner.  world <= 255.
+ * pkm_route_segments: entries grouped by group_counts (device int64
+ *   [groups]) with bags ascending inside each group (true of a pack's output
+ *   and of what the all-to-all delivers); one segment per run of equal bag
+ *   inside a group.  Writes seg_of[e], seg_start[s] (int64, with
+ *   seg_start[n_seg] = n: the offsets pkm_segment_sum takes), seg_bag[s] and
+ *   seg_counts[g] (int64 [groups]).  Arrays sized for n entries / n segments.
+ * pkm_route_combine: out[b] (n_bags x dim, out_dtype) = the partial rows
+ *   [n_seg, dim] of bag b's segments (at most one per group; segments grouped
+ *   by seg_counts) summed in group order in fp32 from zero, rounded once;
+ *   bags without segments are zero.
+ * Workspaces: the *_workspace sizes, 256-byte aligned.
+ */
+PKM_API int pkm_route_pack_workspace(int64_t n, size_t* bytes);
+PKM_API int pkm_route_pack(const int64_t* indices, const void* psw, int psw_dtype, int64_t n_bags, int64_t bag_size,
+                           int64_t shard_rows, int world, int64_t* send_counts, int32_t* order, int32_t* local_row,
+                           float* weight, int32_t* bag, void* workspace, size_t workspace_bytes, uint32_t* dev_err,
+                           void* stream);
+PKM_API int pkm_route_segments_workspace(int64_t n, size_t* bytes);
+PKM_API int pkm_route_segments(const int32_t* bag, int64_t n, const int64_t* group_counts, int groups,
+                               int32_t* seg_of, int64_t* seg_start, int32_t* seg_bag, int64_t* seg_counts,
+                               void* workspace, size_t workspace_bytes, void* stream);
+PKM_API int pkm_route_combine_workspace(int groups, int64_t n_bags, size_t* bytes);
+PKM_API int pkm_route_combine(const void* partial, int dtype, int64_t n_seg, int64_t dim, const int32_t* seg_bag,
+                              const int64_t* seg_counts, int groups, int64_t n_bags, void* out, int out_dtype,
+                              void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream);
+
+/*
  * Ragged entry lists, for tables sharded by rows over ranks (each owner
  * serves the entries that other ranks route to it):
  * pkm_segment_sum: out[s] = sum over entries e in [seg_offsets[s],
@@ -313,6 +350,28 @@ PKM_API int pkm_swiglu_bwd(const void* dz, const void* a, const void* h, int dty
                            void* stream);
 PKM_API int pkm_colsum(const void* x, int dtype, int64_t n, int64_t c, void* out, int out_dtype, void* workspace,
                        size_t workspace_bytes, void* stream);
+
+/*
+ * Addressing statistics of a batch of slot indices, on the device, replacing
+ * Qwen3PKMDecoderLayer.compute_addr_stats (modeling_qwen3pkm.py:447-471)
+ * without its .item() synchronisations.  With counts = bincount(indices)
+ * over [0, rows), writes four doubles to the device array out:
+ *   out[0] = sum of counts[k] over slots with counts[k] > 1  (collided)
+ *   out[1] = number of slots with counts[k] > 0              (covered)
+ *   out[2] = KL(counts / n_indices || uniform over rows), with the
+ *            probabilities clamped to [eps, 1 - eps] inside the logs and
+ *            zero-probability terms dropped, as torch.distributions does
+ *   out[3] = number of indices counted (n_indices unless some were outside
+ *            [0, rows), which also sets PKM_DEVERR_INDEX)
+ * so collision_ratio = out[0] / (n_indices + 1e-6) and coverage_ratio =
+ * out[1] / rows.  n_indices must be positive (the reference's Categorical
+ * rejects an empty histogram).  The workspace (pkm_addr_stats_workspace
+ * bytes, 256-byte aligned) holds the int32 bins and per-block partials; the
+ * reduction order is fixed, so results are bit-reproducible.
+ */
+PKM_API int pkm_addr_stats_workspace(int64_t rows, size_t* bytes);
+PKM_API int pkm_addr_stats(const int64_t* indices, int64_t n_indices, int64_t rows, double* out, void* workspace,
+                           size_t workspace_bytes, uint32_t* dev_err, void* stream);
 
 /*
  * Fused FwPKM value update: one SGD step of the fast-weight inner loop on the

@@ -61,6 +61,14 @@ _SIGS = {
                        _P, _P, _P, _P, _P], _I),
     "pkm_fw_update_bwd": ([_P, _P, _P, _P, _I, _I64, _I64, ctypes.c_double, ctypes.c_double, ctypes.c_double, _I,
                            _P, _P, _P], _I),
+    "pkm_route_pack_workspace": ([_I64, ctypes.POINTER(ctypes.c_size_t)], _I),
+    "pkm_route_pack": ([_P, _P, _I, _I64, _I64, _I64, _I, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P], _I),
+    "pkm_route_segments_workspace": ([_I64, ctypes.POINTER(ctypes.c_size_t)], _I),
+    "pkm_route_segments": ([_P, _I64, _P, _I, _P, _P, _P, _P, _P, ctypes.c_size_t, _P], _I),
+    "pkm_route_combine_workspace": ([_I, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
+    "pkm_route_combine": ([_P, _I, _I64, _I64, _P, _P, _I, _I64, _P, _I, _P, ctypes.c_size_t, _P, _P], _I),
+    "pkm_addr_stats_workspace": ([_I64, ctypes.POINTER(ctypes.c_size_t)], _I),
+    "pkm_addr_stats": ([_P, _I64, _I64, _P, _P, ctypes.c_size_t, _P, _P], _I),
     "pkm_batchnorm_workspace": ([_I64, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
     "pkm_batchnorm_fwd": ([_P, _I, _I64, _I64, _P, _P, _I, _P, _P, _I, _I, ctypes.c_double, ctypes.c_double,
                            _P, _P, _P, _P, ctypes.c_size_t, _P], _I),
@@ -651,3 +659,99 @@ def bag_bwd_ragged(row_idx: torch.Tensor, src_of: torch.Tensor, psw: Optional[to
                                     None, _ptr(ws), ws_bytes, _ptr(err_word(weight.device)),
                                     _stream(weight.device)), "pkm_bag_bwd_ragged")
     return dW, dpsw
+
+
+# ---------------------------------------------------------------------------
+# row-sharded routing
+# ---------------------------------------------------------------------------
+def _ws_query(fn, *args) -> int:
+    nb = ctypes.c_size_t(0)
+    _check(getattr(lib(), fn)(*args, ctypes.byref(nb)), fn)
+    return int(nb.value)
+
+
+def route_pack(indices: torch.Tensor, psw: Optional[torch.Tensor], shard_rows: int, world: int):
+    """Stable partition of the occurrences of ``indices [B, L]`` by owner
+    rank: ``(send_counts int64 [world], order, local_row, bag int32 [n],
+    weight fp32 [n])``, all on the device."""
+    assert indices.dim() == 2 and indices.dtype == torch.long
+    indices = indices.contiguous()
+    if psw is not None:
+        assert psw.shape == indices.shape
+        psw = psw.contiguous()
+    _need_cuda(indices, psw)
+    B, L = indices.shape
+    n = B * L
+    dev = indices.device
+    send = torch.empty(world, dtype=torch.int64, device=dev)
+    order = torch.empty(n, dtype=torch.int32, device=dev)
+    local_row = torch.empty(n, dtype=torch.int32, device=dev)
+    bag = torch.empty(n, dtype=torch.int32, device=dev)
+    weight = torch.empty(n, dtype=torch.float32, device=dev)
+    ws = torch.empty(max(_ws_query("pkm_route_pack_workspace", n), 1), dtype=torch.uint8, device=dev)
+    _check(lib().pkm_route_pack(_ptr(indices), _ptr(psw), DT[psw.dtype] if psw is not None else 0, B, L,
+                                int(shard_rows), int(world), _ptr(send), _ptr(order), _ptr(local_row),
+                                _ptr(weight), _ptr(bag), _ptr(ws), ws.numel(), _ptr(err_word(dev)), _stream(dev)),
+           "pkm_route_pack")
+    return send, order, local_row, bag, weight
+
+
+def route_segments(bag: torch.Tensor, group_counts: torch.Tensor, groups: int):
+    """Runs of equal bag inside each group: ``(seg_of int32 [n], seg_start
+    int64 [n + 1], seg_bag int32 [n], seg_counts int64 [groups])``; only the
+    first ``seg_counts.sum()`` segments (and ``+ 1`` starts) are meaningful."""
+    bag = bag.to(torch.int32).contiguous()
+    group_counts = group_counts.to(torch.int64).contiguous()
+    _need_cuda(bag, group_counts)
+    n = bag.numel()
+    dev = bag.device
+    seg_of = torch.empty(n, dtype=torch.int32, device=dev)
+    seg_start = torch.empty(n + 1, dtype=torch.int64, device=dev)
+    seg_bag = torch.empty(n, dtype=torch.int32, device=dev)
+    seg_counts = torch.empty(groups, dtype=torch.int64, device=dev)
+    ws = torch.empty(max(_ws_query("pkm_route_segments_workspace", n), 1), dtype=torch.uint8, device=dev)
+    _check(lib().pkm_route_segments(_ptr(bag), n, _ptr(group_counts), int(groups), _ptr(seg_of), _ptr(seg_start),
+                                    _ptr(seg_bag), _ptr(seg_counts), _ptr(ws), ws.numel(), _stream(dev)),
+           "pkm_route_segments")
+    return seg_of, seg_start, seg_bag, seg_counts
+
+
+def route_combine(partial: torch.Tensor, seg_bag: torch.Tensor, seg_counts: torch.Tensor, groups: int,
+                  n_bags: int, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """``out [n_bags, D]``: each bag's partial rows summed in group order."""
+    assert partial.dim() == 2
+    partial = partial.contiguous()
+    seg_bag = seg_bag.to(torch.int32).contiguous()
+    seg_counts = seg_counts.to(torch.int64).contiguous()
+    _need_cuda(partial, seg_bag, seg_counts)
+    n_seg, D = partial.shape
+    dev = partial.device
+    out = torch.empty((n_bags, D), dtype=out_dtype or partial.dtype, device=dev)
+    ws = torch.empty(max(_ws_query("pkm_route_combine_workspace", int(groups), int(n_bags)), 1), dtype=torch.uint8,
+                     device=dev)
+    _check(lib().pkm_route_combine(_ptr(partial), DT[partial.dtype], n_seg, D, _ptr(seg_bag), _ptr(seg_counts),
+                                   int(groups), int(n_bags), _ptr(out), DT[out.dtype], _ptr(ws), ws.numel(),
+                                   _ptr(err_word(dev)), _stream(dev)), "pkm_route_combine")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# addressing statistics
+# ---------------------------------------------------------------------------
+def addr_stats(indices: torch.Tensor, rows: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """float64 device tensor ``[collided, covered, kl, counted]`` of the slot
+    histogram of ``indices`` over ``[0, rows)``; stream-ordered, no sync."""
+    idx = indices.reshape(-1).contiguous()
+    assert idx.dtype == torch.long
+    _need_cuda(idx)
+    if idx.numel() == 0:
+        raise ValueError("addressing statistics of an empty index set are undefined")
+    need = ctypes.c_size_t()
+    _check(lib().pkm_addr_stats_workspace(int(rows), ctypes.byref(need)), "pkm_addr_stats_workspace")
+    ws = torch.empty(need.value, dtype=torch.uint8, device=idx.device)
+    if out is None:
+        out = torch.empty(4, dtype=torch.float64, device=idx.device)
+    assert out.dtype == torch.float64 and out.numel() >= 4 and out.is_contiguous()
+    _check(lib().pkm_addr_stats(_ptr(idx), idx.numel(), int(rows), _ptr(out), _ptr(ws), ws.numel(),
+                                _ptr(err_word(idx.device)), _stream(idx.device)), "pkm_addr_stats")
+    return out

@@ -20,22 +20,9 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "count.cuh"
 
 namespace pkm {
-
-// Per-row occurrence counts (int32; the caller zeroes them).  Indices outside
-// [0, rows) are reported and skipped.
-__global__ void fw_count_kernel(const int64_t* __restrict__ idx, int64_t n, int64_t rows, int32_t* __restrict__ counts,
-                                uint32_t* err) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t k = idx[i];
-    if (k < 0 || k >= rows) {
-      raise_err(err, PKM_DEVERR_INDEX);
-      continue;
-    }
-    atomicAdd(&counts[k], 1);
-  }
-}
 
 template <typename T>
 struct FwIO;
@@ -175,7 +162,7 @@ extern "C" int pkm_fw_update(const void* values, const void* grad, int dtype, in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaMemsetAsync(counts, 0, sizeof(int32_t) * rows, st);
   if (n_indices > 0)
-    fw_count_kernel<<<fw_blocks(n_indices), 256, 0, st>>>(indices, n_indices, rows, counts, dev_err);
+    slot_count_kernel<<<fw_blocks(n_indices), 256, 0, st>>>(indices, n_indices, rows, counts, dev_err);
   const FwScalars s = fw_scalars(dtype, scale, lr, weight_decay, grad_clip);
   const int64_t total = rows * dim * dtype_size(dtype) / 16;
   if (dtype == PKM_DT_F32)

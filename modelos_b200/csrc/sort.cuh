@@ -1,8 +1,11 @@
-// Device-wide exclusive scan and a stable LSD radix sort of (row, occurrence)
+// Device-wide exclusive scan and a stable LSD radix sort of (key, occurrence)
 // pairs.  Both are written for the bag backward (K4): the scan turns per-row
 // occurrence counts into segment offsets, and the sort orders occurrence ids
 // by row with ties kept in ascending occurrence order, which is what makes
-// the segment sums of K4 deterministic.
+// the segment sums of K4 deterministic.  The row-sharded routing uses one
+// pass of the same sort (the owner rank as the digit) and the scan.  The
+// non-template kernels have internal linkage so that several translation
+// units can include this header.
 #pragma once
 
 #include "common.cuh"
@@ -177,7 +180,7 @@ constexpr int kSortIpt = PKM_SORT_IPT;
 constexpr int kSortTile = kSortThreads * kSortIpt;
 constexpr int kRadix = 256;
 
-__global__ void __launch_bounds__(kSortThreads) radix_upsweep_kernel(const uint32_t* keys, int64_t n, int shift,
+static __global__ void __launch_bounds__(kSortThreads) radix_upsweep_kernel(const uint32_t* keys, int64_t n, int shift,
                                                                      int* hist, int64_t tiles) {
   __shared__ int cnt[kRadix];
   for (int i = threadIdx.x; i < kRadix; i += kSortThreads) cnt[i] = 0;
@@ -194,7 +197,7 @@ __global__ void __launch_bounds__(kSortThreads) radix_upsweep_kernel(const uint3
 // vals_in == nullptr: the values are the item positions (first pass).
 // keys_out == nullptr: keys are not written (last pass).
 // w != nullptr: also writes w_out[pos] = float(w[value]) (last pass).
-__global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
+static __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
     const uint32_t* keys_in, const int32_t* vals_in, int64_t n, int shift, const int* hist_scan,
     int64_t tiles, uint32_t* keys_out, int32_t* vals_out, const void* w, int w_dtype, float* w_out) {
   __shared__ int wcnt[kSortWarps][kRadix];

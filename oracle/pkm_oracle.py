@@ -55,6 +55,7 @@ __all__ = [
     "swiglu_bwd",
     "segment_sum",
     "bag_bwd_ragged",
+    "addr_stats",
 ]
 
 
@@ -417,3 +418,26 @@ def marginal_entropy(M, topk: int, eps: float = 1e-8) -> float:
     P = e / e.sum(axis=1, keepdims=True)
     Pbar = P.mean(axis=0)
     return float(-(Pbar * np.log(Pbar + eps)).sum())
+
+
+def addr_stats(indices, K: int) -> dict:
+    """``compute_addr_stats`` (``modeling_qwen3pkm.py:454-463``), float64.
+
+    The histogram's KL divergence from the uniform distribution follows
+    torch.distributions' categorical KL: ``sum p*(log c(p) - log c(q))`` over
+    the slots with ``p > 0``, ``c`` clamping to ``[eps, 1 - eps]`` with
+    ``eps`` the fp32 machine epsilon (the probabilities are fp32 there).
+    """
+    idx = np.asarray(indices, dtype=np.int64).reshape(-1)
+    c = np.bincount(idx, minlength=K).astype(np.int64)
+    S = int(c.sum())
+    eps = float(np.finfo(np.float32).eps)
+    p = c / S
+    lq = np.log(np.clip(1.0 / K, eps, 1 - eps))
+    nz = c > 0
+    kld = float((p[nz] * (np.log(np.clip(p[nz], eps, 1 - eps)) - lq)).sum())
+    return {
+        "collision_ratio": int(c[c > 1].sum()) / (idx.size + 1e-6),
+        "coverage_ratio": int(nz.sum()) / K,
+        "kld": kld,
+    }

@@ -101,3 +101,41 @@ def checksum(t: torch.Tensor) -> np.ndarray:
     a = t.detach().double().reshape(-1)
     w = torch.arange(a.numel(), dtype=torch.float64) / max(1, a.numel())
     return np.array([a.sum().item(), a.abs().sum().item(), (a * w).sum().item()])
+
+
+# Addressing-statistics cases: name -> (slots K, generator).  ``c4_chunk`` is
+# one FwPKM chunk of benchmark config 4 (8 x 512 tokens, 4 heads x top-32
+# over 512^2 slots); ``clamped`` has a total count above 1/eps(fp32), so both
+# of torch's probability clamps act (the lone slot's p < eps, the hot
+# slot's p > 1 - eps).
+ADDR_CASES = ("c4_chunk", "hot", "single_slot", "permutation", "tiny", "clamped")
+
+
+def addr_case(name: str, seed: int = 0):
+    """``(indices int64, K, addr_loss [n] fp32)`` of one addressing case."""
+    g = torch.Generator().manual_seed(40_000 + seed)
+    if name == "c4_chunk":
+        K = 512 * 512
+        idx = torch.randint(0, K, (4096, 128), generator=g)
+    elif name == "hot":
+        K = 4096
+        idx = torch.randint(0, K, (20000,), generator=g)
+        hot = torch.rand(20000, generator=g) < 0.6
+        idx[hot] = torch.randint(0, 8, (int(hot.sum()),), generator=g) * 37
+    elif name == "single_slot":
+        K = 64
+        idx = torch.full((1000,), 5, dtype=torch.long)
+    elif name == "permutation":
+        K = 1024
+        idx = torch.randperm(K, generator=g)
+    elif name == "tiny":
+        K = 16
+        idx = torch.tensor([2, 2, 9], dtype=torch.long)
+    elif name == "clamped":
+        K = 64
+        idx = torch.zeros(9_000_000, dtype=torch.long)
+        idx[4_500_000] = 1
+    else:
+        raise KeyError(name)
+    loss = torch.rand((max(1, idx.shape[0]),), generator=g)
+    return idx, K, loss

@@ -85,17 +85,23 @@ def sharded_inputs(rank: int, dtype, dev):
     return table.to(dev), idx.to(dev), psw.to(dev), d_out.to(dev)
 
 
-def run_sharded(rank: int, world: int, port: int, out_dir: str, dtype_name: str):
-    """Row-sharded bag on NCCL against the dense kernels over the full table."""
+def run_sharded(rank: int, world: int, port: int, out_dir: str, dtype_name: str, backend: str = "nccl"):
+    """Row-sharded bag against the dense kernels over the full table: NCCL
+    with one GPU per rank, or gloo with every rank on GPU 0 (the collectives
+    then move host copies; no kernel of one rank waits on another)."""
     import torch
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    torch.cuda.set_device(rank)
-    dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
-                            device_id=dev)
+    gpu = rank if backend == "nccl" else 0
+    torch.cuda.set_device(gpu)
+    dev = torch.device("cuda", gpu)
+    if backend == "nccl":
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+    else:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         from modelos_b200 import _native
         from modelos_b200.sharded import RowShardedEmbeddingBag

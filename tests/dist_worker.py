@@ -22,7 +22,8 @@ def install_cpu_kernels(set_attr=setattr):
     from modelos_b200 import _native
     from modelos_b200.pkm import colwise_embedding_bag, xformer_embeddingbag
     for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense", "swiglu_fwd",
-                 "swiglu_bwd", "colsum", "segment_sum", "bag_bwd_ragged"):
+                 "swiglu_bwd", "colsum", "segment_sum", "bag_bwd_ragged", "route_pack", "route_segments",
+                 "route_combine", "read_device_errors"):
         set_attr(_native, name, getattr(fake_native, name))
 
     def bag(indices, weight, per_sample_weights, mode="sum", bw_algo="reverse_indices"):
@@ -89,8 +90,10 @@ def sharded_case(rank: int):
     return table, idx, psw, d_out
 
 
-def run_sharded(rank: int, world: int, port: int, out_dir: str):
-    """One rank of the row-sharded bag on gloo with the CPU stand-in kernels."""
+def run_sharded(rank: int, world: int, port: int, out_dir: str, bad_rank=None):
+    """One rank of the row-sharded bag on gloo with the CPU stand-in kernels;
+    with ``bad_rank``, that rank's first index lies outside the table and
+    every rank records the IndexError it raised."""
     import torch
     import torch.distributed as dist
 
@@ -104,6 +107,16 @@ def run_sharded(rank: int, world: int, port: int, out_dir: str):
         m = RowShardedEmbeddingBag(SHARD_K, SHARD_D)
         m.load_full(table)
         p = psw.clone().requires_grad_()
+        if bad_rank is not None:
+            if rank == bad_rank:
+                idx[0, 0] = SHARD_K + 3
+            try:
+                m(idx, p)
+                msg = None
+            except IndexError as e:
+                msg = str(e)
+            torch.save({"raised": msg}, os.path.join(out_dir, f"bad{rank}.pt"))
+            return
         out = m(idx, p)
         out.backward(d_out)
         torch.save({"out": out.detach(), "dpsw": p.grad, "dW": m.weight.grad, "rows": m.shard_rows},

@@ -134,6 +134,49 @@ def bag_bwd_ragged(row_idx, src_of, psw, weight, grad_rows, need_dpsw=True):
     return dW.to(weight.dtype), dpsw
 
 
+def route_pack(indices, psw, shard_rows, world):
+    B, L = indices.shape
+    flat = indices.reshape(-1)
+    owner = torch.div(flat, shard_rows, rounding_mode="floor")
+    ok = (flat >= 0) & (owner < world)
+    key = torch.where(ok, owner, torch.full_like(owner, world))
+    order = torch.argsort(key, stable=True)
+    send = torch.bincount(key, minlength=world + 1)[:world]
+    local_row = torch.where(ok[order], flat[order] - key[order] * shard_rows, torch.zeros_like(flat)).to(torch.int32)
+    bag = torch.div(order, L, rounding_mode="floor").to(torch.int32)
+    weight = psw.reshape(-1)[order].float() if psw is not None else torch.ones(flat.numel())
+    return send, order.to(torch.int32), local_row, bag, weight
+
+
+def route_segments(bag, group_counts, groups):
+    n = bag.numel()
+    grp = torch.repeat_interleave(torch.arange(groups), group_counts.long().cpu())
+    grp = torch.cat([grp, torch.full((max(0, n - grp.numel()),), groups, dtype=grp.dtype)])[:n]
+    start = torch.ones(n, dtype=torch.bool)
+    if n > 1:
+        start[1:] = (bag[1:] != bag[:-1]) | (grp[1:] != grp[:-1])
+    seg_of = (torch.cumsum(start.to(torch.int32), 0) - 1).to(torch.int32)
+    first = torch.nonzero(start).reshape(-1)
+    n_seg = first.numel()
+    seg_start = torch.zeros(n + 1, dtype=torch.int64)
+    seg_start[:n_seg] = first
+    seg_start[n_seg] = n
+    seg_bag = torch.zeros(n, dtype=torch.int32)
+    seg_bag[:n_seg] = bag[first].to(torch.int32)
+    seg_counts = torch.bincount(grp[first], minlength=groups + 1)[:groups]
+    return seg_of, seg_start, seg_bag, seg_counts
+
+
+def route_combine(partial, seg_bag, seg_counts, groups, n_bags, out_dtype=None):
+    out = torch.zeros((n_bags, partial.shape[1]), dtype=torch.float32)
+    pos = 0
+    for g in range(groups):  # group order: the summation order
+        c = int(seg_counts[g])
+        out.index_add_(0, seg_bag[pos:pos + c].long(), partial[pos:pos + c].float())
+        pos += c
+    return out.to(out_dtype or partial.dtype)
+
+
 def read_device_errors(dev=None, reset=True):
     return 0
 
@@ -147,7 +190,7 @@ def install(monkeypatch):
     from modelos_b200 import _native
     for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense",
                  "fw_update", "fw_update_bwd", "swiglu_fwd", "swiglu_bwd", "colsum", "segment_sum",
-                 "bag_bwd_ragged", "read_device_errors",
+                 "bag_bwd_ragged", "route_pack", "route_segments", "route_combine", "read_device_errors",
                  "check_device_errors"):
         monkeypatch.setattr(_native, name, globals()[name])
     return np

@@ -218,6 +218,26 @@ def gen_fwpkm(fw, name, score_type, seed=0):
     print("wrote", name)
 
 
+def gen_addr_stats(name):
+    """``compute_addr_stats`` of the reference's decoder layer
+    (``modeling_qwen3pkm.py:447-471``) on ``cases.addr_case`` inputs; the
+    method only reads ``config.fwpkm_n_subkeys`` and ``config.fwpkm_addr_loss``."""
+    import refmodel
+    model = refmodel.load("refmodel_golden", ours=False)
+    out = {}
+    for cname in cases.ADDR_CASES:
+        idx, K, loss = cases.addr_case(cname)
+        n = int(round(K ** 0.5))
+        assert n * n == K
+        stub = types.SimpleNamespace(config=types.SimpleNamespace(fwpkm_n_subkeys=n, fwpkm_addr_loss="me"))
+        st = model.Qwen3PKMDecoderLayer.compute_addr_stats(stub, idx, loss)
+        out[cname + "_idx_checksum"] = cases.checksum(idx)
+        out[cname + "_stats"] = np.array([st["collision_ratio"], st["coverage_ratio"], st["kld"],
+                                          st["addressing_loss/me"]], dtype=np.float64)
+    np.savez_compressed(os.path.join(HERE, name), **out)
+    print("wrote", name)
+
+
 def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     mem, xeb, fw, gw, leg = _import_ref()
@@ -230,7 +250,15 @@ def main():
     c2 = dict(cases.CONFIG2)
     c2.update(mem_n_keys=64)  # same layer, smaller table so the fixture stays small
     gen_pkm(mem, c2, "c2_small_bf16.npz", (2, 32, 1024), torch.bfloat16)
+    gen_addr_stats("addr_stats.npz")
 
 
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 1:  # regenerate named fixtures only, e.g. ``addr_stats``
+        for arg in sys.argv[1:]:
+            if arg == "addr_stats":
+                gen_addr_stats("addr_stats.npz")
+            else:
+                raise SystemExit(f"unknown fixture {arg}")
+    else:
+        main()

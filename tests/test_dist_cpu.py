@@ -93,3 +93,25 @@ def test_row_sharded_bag_matches_dense(tmp_path):
         S = got["rows"]
         rows = dW_full[r * S:(r + 1) * S]
         assert torch.allclose(got["dW"][: rows.shape[0]], rows, atol=1e-5, rtol=1e-5)
+
+
+def test_row_sharded_bad_index_raises_on_every_rank(tmp_path):
+    """An index outside the table on one rank: every rank raises IndexError
+    at the same step (the validity of each sender's indices travels with
+    the counts), so no rank is left waiting in a collective."""
+    import dist_worker
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=dist_worker.run_sharded, args=(r, 2, port, str(tmp_path), 1)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert [p.exitcode for p in procs] == [0, 0]
+    msgs = [torch.load(os.path.join(tmp_path, f"bad{r}.pt"))["raised"] for r in range(2)]
+    assert msgs[1] == "row index outside the sharded table"
+    assert msgs[0] is not None and "rank(s) [1]" in msgs[0]

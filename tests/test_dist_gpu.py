@@ -1,9 +1,14 @@
-"""Fused data-parallel exchanges of the value-table gradient on two GPUs
+"""Multi-rank GPU paths.
+
+Fused data-parallel exchanges of the value-table gradient on two GPUs
 (NVLink stores to the row owners, and the in-switch multimem all-reduce):
 the table gradient equals the NCCL all-reduce of the ranks' local
 gradients, bit for bit at two ranks (one addition per element, rounded
 once) in fp32 and for the NVLink-store exchange in bf16, and within one
-bf16 ulp for the in-switch reduction in bf16."""
+bf16 ulp for the in-switch reduction in bf16.
+
+Row-sharded table: on two GPUs over NCCL, and with 2 or 3 ranks sharing
+GPU 0 over gloo (runs on a one-GPU machine)."""
 from __future__ import annotations
 
 import os
@@ -59,6 +64,44 @@ def test_sharded_table_grad_two_ranks(tmp_path, dtype_name, mode):
         assert torch.equal(d["got_keys"], d["ref_keys"])
 
 
+def _run_row_sharded(tmp_path, dtype_name, tol, world, backend):
+    import torch.multiprocessing as mp
+    sys.path.insert(0, HERE)
+    import dist_gpu_worker
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=dist_gpu_worker.run_sharded, args=(r, world, port, str(tmp_path), dtype_name, backend))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert [p.exitcode for p in procs] == [0] * world
+
+    def rel(a, b):
+        a, b = a.double(), b.double()
+        return ((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()
+
+    for r in range(world):
+        d = torch.load(os.path.join(tmp_path, f"shard{r}.pt"))
+        assert rel(d["out"], d["ref_out"]) < tol
+        assert rel(d["dpsw"], d["ref_dpsw"]) < tol
+        assert torch.equal(d["dW"][: d["ref_dW"].shape[0]], d["ref_dW"])
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("dtype_name,tol", [("float32", 1e-5), ("bfloat16", 2e-2)])
+def test_row_sharded_bag_ranks_on_one_gpu(tmp_path, dtype_name, tol, world):
+    """The row-sharded table with every rank on GPU 0 over gloo: the routing
+    kernels (pack, segments, combine) and the ragged bag kernels for 2 and 3
+    owners, against the dense kernels over the full table."""
+    _run_row_sharded(tmp_path, dtype_name, tol, world, "gloo")
+
+
 @pytest.mark.parametrize("dtype_name,tol", [("float32", 1e-5), ("bfloat16", 2e-2)])
 def test_row_sharded_bag_two_ranks(tmp_path, dtype_name, tol):
     """Row-sharded table on two GPUs (NCCL all-to-all routing, ragged bag
@@ -68,29 +111,4 @@ def test_row_sharded_bag_two_ranks(tmp_path, dtype_name, tol):
     are summed in the same order)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    import torch.multiprocessing as mp
-    sys.path.insert(0, HERE)
-    import dist_gpu_worker
-    ctx = mp.get_context("spawn")
-    port = _free_port()
-    procs = [ctx.Process(target=dist_gpu_worker.run_sharded, args=(r, 2, port, str(tmp_path), dtype_name))
-             for r in range(2)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=240)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
-            p.join()
-    assert [p.exitcode for p in procs] == [0, 0]
-
-    def rel(a, b):
-        a, b = a.double(), b.double()
-        return ((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()
-
-    for r in range(2):
-        d = torch.load(os.path.join(tmp_path, f"shard{r}.pt"))
-        assert rel(d["out"], d["ref_out"]) < tol
-        assert rel(d["dpsw"], d["ref_dpsw"]) < tol
-        assert torch.equal(d["dW"][: d["ref_dW"].shape[0]], d["ref_dW"])
+    _run_row_sharded(tmp_path, dtype_name, tol, 2, "nccl")

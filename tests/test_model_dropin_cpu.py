@@ -11,59 +11,16 @@ small model from the same seed, and require identical state dicts: same
 keys, shapes, dtypes and values.  The forward needs a GPU and the reference
 tree together, so it is not run here.
 
-Only this container holds the reference tree; without it the tests skip.
-``configuration_qwen3pkm.py`` does not parse as shipped (an unterminated
-string at ``:99``); it is loaded from its text with that string closed, in
-memory, without touching the file.
+Without the reference tree (``tests/refmodel.py`` finds it) the tests skip.
 """
 from __future__ import annotations
-
-import importlib
-import os
-import sys
-import types
 
 import pytest
 import torch
 
-REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.environ.get("MODELOS_REF", os.path.join(os.path.dirname(REPO), "reference"))
+import refmodel
 
-pytestmark = pytest.mark.skipif(not os.path.isfile(os.path.join(REF, "modeling_qwen3pkm.py")),
-                                reason="reference tree not present")
-
-
-def _config_module(pkg: str):
-    path = os.path.join(REF, "configuration_qwen3pkm.py")
-    with open(path) as f:
-        src = f.read()
-    broken = "\"fwpkm_value_src='hidden' \n"
-    if broken in src:
-        src = src.replace(broken, "\"fwpkm_value_src='hidden'\"\n")
-    mod = types.ModuleType(pkg + ".configuration_qwen3pkm")
-    mod.__package__ = pkg
-    mod.__file__ = path
-    sys.modules[mod.__name__] = mod
-    exec(compile(src, path, "exec"), mod.__dict__)
-    return mod
-
-
-def _load(pkg: str, ours: bool):
-    """Import ``modeling_qwen3pkm`` as ``pkg.modeling_qwen3pkm``; with
-    ``ours`` its ``.pkm`` / ``.fwpkm`` imports resolve to this package."""
-    if pkg + ".modeling_qwen3pkm" in sys.modules:
-        return sys.modules[pkg + ".modeling_qwen3pkm"]
-    root = types.ModuleType(pkg)
-    root.__path__ = [REF]
-    sys.modules[pkg] = root
-    _config_module(pkg)
-    if ours:
-        import modelos_b200.fwpkm.fwmlp
-        import modelos_b200.fwpkm.fwpkm
-        import modelos_b200.pkm.memory
-        for name in ("pkm", "pkm.memory", "fwpkm", "fwpkm.fwpkm", "fwpkm.fwmlp"):
-            sys.modules[f"{pkg}.{name}"] = importlib.import_module("modelos_b200." + name)
-    return importlib.import_module(pkg + ".modeling_qwen3pkm")
+pytestmark = pytest.mark.skipif(not refmodel.available(), reason="reference tree not present")
 
 
 def _tiny_config(cfg_cls, **over):
@@ -78,7 +35,7 @@ def _tiny_config(cfg_cls, **over):
 
 @pytest.fixture(scope="module")
 def models():
-    return _load("refmodel_refpkg", ours=False), _load("refmodel_b200pkg", ours=True)
+    return refmodel.load("refmodel_refpkg", ours=False), refmodel.load("refmodel_b200pkg", ours=True)
 
 
 @pytest.mark.parametrize("over", [

@@ -188,3 +188,18 @@ def test_numpy_layer_port_matches_reference_step(c0):
     assert rel_err(G["keys"], c0["keys_grad"]) < 1e-4
     assert rel_err(np.linalg.norm(G["values.weight"], axis=1), c0["values_grad_rownorm"]) < 1e-4
     assert rel_err(G["query_proj.query_mlps.0.bias"], c0["bq_grad"]) < 1e-4
+
+
+@pytest.mark.parametrize("name", cases.ADDR_CASES)
+def test_addr_stats_oracle_matches_reference(name):
+    """``compute_addr_stats`` of the reference's decoder layer: the two ratios
+    are integer counts over the same denominators (equal exactly); the KL is
+    fp32 in the reference and fp64 here."""
+    d = np.load(os.path.join(GOLD, "addr_stats.npz"))
+    idx, K, _ = cases.addr_case(name)
+    np.testing.assert_allclose(cases.checksum(idx), d[name + "_idx_checksum"], rtol=1e-12, atol=1e-9)
+    st = po.addr_stats(idx.numpy(), K)
+    ref = d[name + "_stats"]
+    assert st["collision_ratio"] == ref[0]
+    assert st["coverage_ratio"] == ref[1]
+    assert abs(st["kld"] - ref[2]) <= 1e-5 * max(1.0, abs(ref[2]))
