@@ -139,3 +139,33 @@ def addr_case(name: str, seed: int = 0):
         raise KeyError(name)
     loss = torch.rand((max(1, idx.shape[0]),), generator=g)
     return idx, K, loss
+
+
+# Token ranges of three successive ``forward_w_past`` calls over one
+# ``fwpkm_case`` (T = 16, chunk 8, lookahead 1): the first only queues, the
+# second updates once and queues the rest, the third updates again.
+STREAM_CALLS = ((0, 4), (4, 13), (13, 16))
+
+
+def run_stream(m, q, ref_v, d, rel_err, tol=1e-5):
+    """Drive ``m`` through ``STREAM_CALLS`` under ``no_grad`` (as generation
+    does) and compare every call with the fixture ``d``."""
+    B, T = q.shape[:2]
+    ids = torch.arange(B * T, device=q.device).view(B, T)
+    past = (None,) * 6
+    with torch.no_grad():
+        for c, (t0, t1) in enumerate(STREAM_CALLS):
+            res = m(q[:, t0:t1], ref_v[:, t0:t1], None, 8, past_key_values=past, token_ids=ids[:, t0:t1])
+            past = res["past_key_values"]
+            np.testing.assert_array_equal(res["indices"].cpu().numpy(), d[f"c{c}_indices"])
+            assert (res["losses"] is not None) == bool(d[f"c{c}_updated"]), c
+            pairs = [(res["output"], "output"), (res["scores"], "scores"), (past[0], "past_q"),
+                     (past[1], "past_hyp"), (past[2], "past_ref"), (m.keys, "keys"), (m.values, "values")]
+            if res["losses"] is not None:
+                pairs.append((res["losses"], "losses"))
+                got_addr = res["addr_loss"].item()
+                ref_addr = float(d[f"c{c}_addr_loss"])
+                assert abs(got_addr - ref_addr) <= tol * abs(ref_addr) + 1e-7, c
+            for got, key in pairs:
+                assert rel_err(got.detach().float().cpu().numpy(), d[f"c{c}_{key}"]) < tol, (c, key)
+            np.testing.assert_array_equal(past[5].cpu().numpy(), d[f"c{c}_past_ids"])

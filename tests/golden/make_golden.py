@@ -218,6 +218,43 @@ def gen_fwpkm(fw, name, score_type, seed=0):
     print("wrote", name)
 
 
+def gen_fwpkm_stream(fw, name, score_type, seed=1):
+    """``forward_w_past`` (``fwpkm/fwpkm.py:560-820``) over three successive
+    calls that carry the signal queue: the first only queues, the second
+    updates once and queues the rest, the third updates again.  Run under ``no_grad`` as in
+    generation, with token ids (the reference's queue pop indexes them when
+    ``lookahead > 0``)."""
+    torch.manual_seed(0)
+    m = fw.FastWeightProductKeyMemory(qk_score_type=score_type, **FW_KW).train()
+    keys, values, q, ref_v = cases.fwpkm_case(seed)
+    with torch.no_grad():
+        m.keys.copy_(keys)
+        m.values.copy_(values)
+    B, T = q.shape[:2]
+    ids = torch.arange(B * T).view(B, T)
+    past = (None,) * 6
+    out = {}
+    with torch.no_grad():
+        for c, (t0, t1) in enumerate(cases.STREAM_CALLS):
+            res = m(q[:, t0:t1], ref_v[:, t0:t1], None, 8, past_key_values=past, token_ids=ids[:, t0:t1])
+            past = res["past_key_values"]
+            out[f"c{c}_output"] = _np(res["output"])
+            out[f"c{c}_indices"] = res["indices"].numpy()
+            out[f"c{c}_scores"] = _np(res["scores"])
+            out[f"c{c}_updated"] = np.array(res["losses"] is not None)
+            if res["losses"] is not None:
+                out[f"c{c}_losses"] = _np(res["losses"])
+                out[f"c{c}_addr_loss"] = np.array(res["addr_loss"].item())
+            for k, t in zip(("q", "hyp", "ref"), past[:3]):
+                out[f"c{c}_past_{k}"] = _np(t)
+            out[f"c{c}_past_ids"] = past[5].numpy()
+            # copies: the module updates its parameters in place
+            out[f"c{c}_keys"] = _np(m.keys).copy()
+            out[f"c{c}_values"] = _np(m.values).copy()
+    np.savez_compressed(os.path.join(HERE, name), **out)
+    print("wrote", name)
+
+
 def gen_addr_stats(name):
     """``compute_addr_stats`` of the reference's decoder layer
     (``modeling_qwen3pkm.py:447-471``) on ``cases.addr_case`` inputs; the
@@ -251,6 +288,8 @@ def main():
     c2.update(mem_n_keys=64)  # same layer, smaller table so the fixture stays small
     gen_pkm(mem, c2, "c2_small_bf16.npz", (2, 32, 1024), torch.bfloat16)
     gen_addr_stats("addr_stats.npz")
+    gen_fwpkm_stream(fw, "fwpkm_stream_dot.npz", "dot_product")
+    gen_fwpkm_stream(fw, "fwpkm_stream_idw.npz", "idw")
 
 
 if __name__ == "__main__":
@@ -258,6 +297,10 @@ if __name__ == "__main__":
         for arg in sys.argv[1:]:
             if arg == "addr_stats":
                 gen_addr_stats("addr_stats.npz")
+            elif arg == "fwpkm_stream":
+                fw = _import_ref()[2]
+                gen_fwpkm_stream(fw, "fwpkm_stream_dot.npz", "dot_product")
+                gen_fwpkm_stream(fw, "fwpkm_stream_idw.npz", "idw")
             else:
                 raise SystemExit(f"unknown fixture {arg}")
     else:

@@ -76,6 +76,23 @@ def test_double_backward_wrapper_gradgradcheck():
     assert rel_err(d_a.cpu().numpy(), ref_a.cpu().numpy()) < 1e-6
 
 
+@pytest.mark.parametrize("score_type,fname", [("dot_product", "fwpkm_stream_dot.npz"),
+                                              ("idw", "fwpkm_stream_idw.npz")])
+def test_forward_w_past_matches_reference(score_type, fname):
+    """``forward_w_past`` (``fwpkm/fwpkm.py:560-820``) over three calls that
+    carry the signal queue (queue only; update then queue; update): outputs,
+    indices, losses, queues and fast weights after every call."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
+    d = np.load(os.path.join(GOLD, fname))
+    m = FastWeightProductKeyMemory(qk_score_type=score_type, **FW_KW).to(DEV).train()
+    keys, values, q, ref_v = cases.fwpkm_case(1)
+    with torch.no_grad():
+        m.keys.copy_(keys)
+        m.values.copy_(values)
+    cases.run_stream(m, q.to(DEV), ref_v.to(DEV), d, rel_err)
+
+
 def test_forward_w_past_streaming_runs_and_updates():
     """Streaming path (``fwpkm/fwpkm.py:560-820``): output of the first call
     equals the no-past read of the same weights; the queue carries lookahead."""

@@ -56,6 +56,21 @@ def test_fwpkm_chunk_loop_matches_reference(cpu_kernels, score_type, fname):
         assert rel_err(got.detach().numpy(), d[key]) < 1e-5, key
 
 
+@pytest.mark.parametrize("score_type,fname", [("dot_product", "fwpkm_stream_dot.npz"),
+                                              ("idw", "fwpkm_stream_idw.npz")])
+def test_fwpkm_streaming_matches_reference(cpu_kernels, score_type, fname):
+    """``forward_w_past`` over three calls carrying the signal queue: outputs,
+    losses, queues and fast weights after every call equal the reference's."""
+    from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
+    d = np.load(os.path.join(GOLD, fname))
+    m = FastWeightProductKeyMemory(qk_score_type=score_type, **FW_KW).train()
+    keys, values, q, ref_v = cases.fwpkm_case(1)
+    with torch.no_grad():
+        m.keys.copy_(keys)
+        m.values.copy_(values)
+    cases.run_stream(m, q, ref_v, d, rel_err)
+
+
 def test_fwpkm_without_addressing_loss_keeps_keys(cpu_kernels):
     from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
     m = FastWeightProductKeyMemory(addr_loss=None, **FW_KW).train()
