@@ -111,3 +111,47 @@ def test_forward_w_past_streaming_runs_and_updates():
     assert res2["losses"] is not None
     assert res2["past_key_values"][0].shape[1] == 1  # lookahead tail
     assert not torch.equal(m.values.detach().cpu(), values)
+
+
+def test_config4_full_size_properties():
+    """Benchmark config 4 at full size: k_dim 512, v_dim 1024, 4 heads x
+    top-32 over 512^2 fp32 fast-weight slots (idw scores, joint softmax,
+    addressing loss "me"), bf16 inputs [8, 4096] in chunks of 512 positions
+    (eight inner updates of 4096 tokens, create_graph), then the outer
+    backward.  Size-independent checks: indices in range, each token's
+    scores sum to 1, everything finite, and the first chunk's output equals
+    the bag (K3) of the initial fast weights with the returned indices and
+    scores."""
+    from modelos_b200 import _native
+    from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
+    torch.manual_seed(0)
+    B, T, CH, H, KNN, N_SUB = 8, 4096, 512, 4, 32, 512
+    m = FastWeightProductKeyMemory(mem_k_dim=512, mem_v_dim=1024, mem_heads=H, mem_topk=KNN, mem_n_subkeys=N_SUB,
+                                   learning_rate=0.1).to(DEV).train()
+    m.reset_parameters()
+    values0 = m.values.detach().clone()
+    g = torch.Generator(device=DEV).manual_seed(4)
+    q = torch.randn(B, T, H * 512, generator=g, device=DEV).bfloat16().requires_grad_()
+    ref_v = torch.randn(B, T, 1024, generator=g, device=DEV).bfloat16().requires_grad_()
+    res = m(q, ref_v, None, CH)
+    out = res["output"]
+    loss = (out.float() ** 2).sum() + res["addr_loss"]
+    loss.backward()
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    assert out.shape == (B, T, 1024) and out.dtype == torch.bfloat16
+    idx = res["indices"]
+    assert idx.shape == (B, T, H, KNN)
+    assert int(idx.min()) >= 0 and int(idx.max()) < N_SUB * N_SUB
+    ssum = res["scores"].float().reshape(B, T, -1).sum(-1)
+    assert (ssum - 1).abs().max().item() < 1e-5
+    for name, t in (("output", out), ("losses", res["losses"]), ("q.grad", q.grad), ("ref_v.grad", ref_v.grad),
+                    ("keys.grad", m.keys.grad), ("values.grad", m.values.grad), ("keys", m.keys),
+                    ("values", m.values)):
+        assert torch.isfinite(t.float()).all(), name
+    assert m.values.grad.abs().max().item() > 0 and q.grad.abs().max().item() > 0
+    c0_idx = idx[:, :CH].reshape(B * CH, H * KNN)
+    c0_w = res["scores"][:, :CH].reshape(B * CH, H * KNN).float()
+    ref0 = _native.bag_fwd(c0_idx.contiguous(), values0, c0_w.contiguous())
+    got0 = out.detach()[:, :CH].reshape(B * CH, -1).float()
+    assert rel_err(got0.cpu().numpy(), ref0.float().cpu().numpy()) < 2e-2
