@@ -9,6 +9,11 @@ fused NVLink exchange of ``modelos_b200.dist.ShardedTableGrad``, the others
 through NCCL.  Inputs are synthetic (seeded normal draws; there is no dataset).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--grad-exchange fused|nccl|owner] [--optimizer none|sgd]
+
+``--optimizer sgd`` adds an SGD step of every parameter to each timed step
+(a different metric, named in the line); with ``--grad-exchange owner`` the
+table's step is sharded by rows (``modelos_b200.dist.RowOwnerSGD``).
 
 Prints one JSON line on rank 0.  ``--impl reference`` times the CPU port of
 the reference's path (``oracle/pkm_layer.py``) on the host cores instead.
@@ -28,6 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "PKM layer tokens/s (fwd+bwd)"
+METRIC_SGD = "PKM layer tokens/s (fwd+bwd+SGD step)"
 UNIT = "tokens/s"
 B, T, C = 8, 2048, 1024
 CFG = dict(input_dim=1024, output_dim=1024, mem_k_dim=512, mem_v_dim=1024, mem_heads=4, mem_knn=32,
@@ -217,10 +223,18 @@ def run_ours(args, rank, world, local_rank):
     x = torch.randn((B, T, C), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
     x_host = x.cpu().pin_memory()
     reducer = None
+    owner = None
     exchange = "none"
     if world > 1:
-        from modelos_b200.dist import GradReducer, ShardedTableGrad
-        if args.grad_exchange == "fused":
+        from modelos_b200.dist import GradReducer, RowOwnerSGD, ShardedTableGrad
+        if args.grad_exchange == "owner":
+            # the table's gradient is reduce-scattered inside the bag backward;
+            # its owner applies SGD to its rows and stores them into every
+            # rank's table (the optimizer step below)
+            owner = RowOwnerSGD(m.values.weight, lr=args.lr)
+            reducer = GradReducer(params, sharded=[owner])
+            exchange = "owner sgd: segment-pass stores to row owners + owner SGD and all-gather of the updated rows"
+        elif args.grad_exchange == "fused":
             # the value-table gradient goes to its row owners over NVLink while
             # the bag backward computes it; owners reduce and all-gather beside
             # the rest of the backward
@@ -233,6 +247,11 @@ def run_ours(args, rank, world, local_rank):
             reducer = GradReducer(params, early=[m.values.weight])
             exchange = "nccl all-reduce from a post-accumulate hook"
 
+    opt = None
+    if args.optimizer == "sgd":
+        dense = [p for p in params if owner is None or p is not m.values.weight]
+        opt = torch.optim.SGD(dense, lr=args.lr, foreach=True)
+
     def step(xin):
         for p in params:
             p.grad = None
@@ -241,6 +260,10 @@ def run_ours(args, rank, world, local_rank):
         loss.backward()
         if reducer is not None:
             reducer.finish()
+        if opt is not None:
+            opt.step()
+        if owner is not None:
+            owner.step()
         return loss
 
     for _ in range(args.warmup):
@@ -345,10 +368,12 @@ def run_ours(args, rank, world, local_rank):
     roof["kernel"] = dom
     other = [k for k in rl if k != dom][0]
     line = {
-        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": METRIC if opt is None else METRIC_SGD, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded normal x, reset_parameters init)",
-        "config": dict(config_obj(world), grad_exchange=exchange),
+        "config": dict(config_obj(world), grad_exchange=exchange,
+                       **({} if opt is None else {"optimizer": f"sgd lr {args.lr} (foreach; table rows by owner "
+                                                                f"with --grad-exchange owner)"})),
         "e2e": {"value": round(B * T * world / (e2e_ms / 1000.0), 1), "unit": UNIT,
                 "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4,
                 "ms_per_step": round(e2e_ms, 4)},
@@ -370,9 +395,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--grad-exchange", default="fused", choices=["fused", "nccl"],
-                    help="data-parallel exchange of the value-table gradient (N > 1)")
+    ap.add_argument("--grad-exchange", default="fused", choices=["fused", "nccl", "owner"],
+                    help="data-parallel exchange of the value-table gradient (N > 1); owner: the table's "
+                         "optimizer sharded by rows (needs --optimizer sgd)")
+    ap.add_argument("--optimizer", default="none", choices=["none", "sgd"],
+                    help="add an SGD step of every parameter to each timed step")
+    ap.add_argument("--lr", type=float, default=1e-3)
     args = ap.parse_args()
+    if args.grad_exchange == "owner" and args.optimizer != "sgd":
+        ap.error("--grad-exchange owner updates the table in the optimizer step: add --optimizer sgd")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -232,6 +232,25 @@ PKM_API int pkm_grad_shard_reduce(const void* recv, int dtype, int64_t num_rows,
                                   void* stream);
 
 /*
+ * Row-owner optimizer step of a replicated table (reduce-scatter -> owner
+ * update -> all-gather of parameters): sums this rank's shard copies in
+ * `recv` like pkm_grad_shard_reduce, scales by `scale`, applies SGD
+ * without momentum to this rank's rows of the table,
+ *   d = g + weight_decay * p (rounded to the table dtype; skipped when 0),
+ *   p' = p - lr * d (one fused multiply-add, rounded once),
+ * the foreach update of torch.optim.SGD, and stores the new rows into rows
+ * [rank*shard_rows, ...) of every rank's table table_bases[d] (HOST array
+ * of world peer-writable addresses; table_bases[rank] is read first).
+ * Ordering as pkm_grad_shard_reduce: after every rank's
+ * pkm_bag_bwd_sharded, and readers of the table after every rank's call.
+ * Replaces the all-reduce of values.weight.grad plus every rank's full-table
+ * optimizer pass.  dtype f32 or bf16.
+ */
+PKM_API int pkm_grad_shard_sgd(const void* recv, int dtype, int64_t num_rows, int64_t dim, int world, int rank,
+                               int64_t shard_rows, void* const* table_bases, float lr, float weight_decay,
+                               float scale, int max_blocks, void* stream);
+
+/*
  * pkm_bag_bwd in phases on one workspace: pkm_bag_bwd_sort runs the keys,
  * scan, radix sort and chunk descriptors (and zeroes grad_psw of invalid
  * indices, fills row_counts); pkm_bag_bwd_rows then runs the segment pass

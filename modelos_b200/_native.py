@@ -43,6 +43,8 @@ _SIGS = {
     "pkm_bag_bwd_sharded": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _I, _I64, _I, _P, _I, _P, _P,
                              ctypes.c_size_t, _P, _P], _I),
     "pkm_grad_shard_reduce": ([_P, _I, _I64, _I64, _I, _I, _I64, _P, ctypes.c_float, _I, _P], _I),
+    "pkm_grad_shard_sgd": ([_P, _I, _I64, _I64, _I, _I, _I64, _P, ctypes.c_float, ctypes.c_float, ctypes.c_float, _I,
+                            _P], _I),
     "pkm_segment_sum_workspace": ([_I64, ctypes.POINTER(ctypes.c_size_t)], _I),
     "pkm_segment_sum": ([_P, _I, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _I, _P, ctypes.c_size_t, _P, _P], _I),
     "pkm_bag_bwd_ragged": ([_P, _P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _P, _I, _P, _P,
@@ -336,6 +338,20 @@ def grad_shard_reduce(recv: torch.Tensor, num_rows: int, rank: int, shard_rows: 
     _check(lib().pkm_grad_shard_reduce(_ptr(recv), DT[recv.dtype], num_rows, D, world, rank, shard_rows,
                                        _ptr_array(grad_bases), float(scale), int(max_blocks), _stream(recv.device)),
            "pkm_grad_shard_reduce")
+
+
+def grad_shard_sgd(recv: torch.Tensor, num_rows: int, rank: int, shard_rows: int, table_bases, lr: float,
+                   weight_decay: float = 0.0, scale: float = 1.0, max_blocks: int = 0):
+    """Sum this rank's received shard rows, apply SGD to this rank's rows of
+    the table and store them into every rank's table (``table_bases``:
+    device addresses, one per rank)."""
+    _need_cuda(recv)
+    world = len(table_bases)
+    assert recv.is_contiguous() and recv.shape[0] == world and recv.shape[1] == shard_rows
+    D = recv.shape[2]
+    _check(lib().pkm_grad_shard_sgd(_ptr(recv), DT[recv.dtype], num_rows, D, world, rank, shard_rows,
+                                    _ptr_array(table_bases), float(lr), float(weight_decay), float(scale),
+                                    int(max_blocks), _stream(recv.device)), "pkm_grad_shard_sgd")
 
 
 def grad_multimem_allreduce(mc_src: int, mc_dst: int, dtype: torch.dtype, num_rows: int, dim: int, world: int,

@@ -351,6 +351,94 @@ __global__ void __launch_bounds__(256) multimem_allreduce_kernel(const char* mc_
   __threadfence_system();
 }
 
+// Row-owner optimizer step (reduce-scatter -> owner update -> all-gather):
+// the owner sums the world copies of its shard's gradient rows exactly as
+// shard_reduce_kernel does, applies plain SGD to its rows of the table,
+//   d  = g + weight_decay * p        (rounded to the table dtype; skipped when 0)
+//   p' = p - lr * d                  (one fused multiply-add, rounded once)
+// which is torch.optim.SGD's foreach update without momentum, and stores the
+// new rows into row (rank * shard_rows + r) of every rank's table.
+__device__ __forceinline__ void unpack_vec(const uint4& a, float (&f)[8], bool bf16) {
+  if (bf16) {
+    VecTraits<__nv_bfloat16>::unpack(a, f);
+  } else {
+    f[0] = __uint_as_float(a.x), f[1] = __uint_as_float(a.y), f[2] = __uint_as_float(a.z),
+    f[3] = __uint_as_float(a.w);
+    f[4] = f[5] = f[6] = f[7] = 0.f;
+  }
+}
+__device__ __forceinline__ uint4 pack_vec(const float (&f)[8], bool bf16) {
+  if (bf16) {
+    uint4 r;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return r;
+  }
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+}
+
+__global__ void __launch_bounds__(256) shard_sgd_kernel(const uint4* __restrict__ recv, int64_t shard_vecs,
+                                                       int64_t n_vecs, int world, int rank, bool bf16, float scale,
+                                                       float lr, float wd, const __grid_constant__ GradDest dest) {
+  const int64_t n_chunks = (n_vecs + (int64_t)blockDim.x * kShardVec - 1) / ((int64_t)blockDim.x * kShardVec);
+  const int64_t base = (int64_t)rank * shard_vecs;  // this shard's first vector in a full table
+  const uint4* own = reinterpret_cast<const uint4*>(dest.base[rank]) + base;
+  const int n = bf16 ? 8 : 4;
+  for (int64_t chunk = blockIdx.x; chunk < n_chunks; chunk += gridDim.x) {
+    const int64_t v0 = (chunk * blockDim.x) * kShardVec + threadIdx.x;
+    uint4 acc[kShardVec], par[kShardVec];
+    bool live[kShardVec];
+#pragma unroll
+    for (int u = 0; u < kShardVec; ++u) {
+      const int64_t v = v0 + (int64_t)u * blockDim.x;
+      live[u] = v < n_vecs;
+      acc[u] = live[u] ? recv[v] : make_uint4(0, 0, 0, 0);
+      par[u] = live[u] ? own[v] : make_uint4(0, 0, 0, 0);
+    }
+    for (int s = 1; s < world; ++s) {
+      uint4 x[kShardVec];
+#pragma unroll
+      for (int u = 0; u < kShardVec; ++u) {
+        const int64_t v = v0 + (int64_t)u * blockDim.x;
+        x[u] = live[u] ? recv[(int64_t)s * shard_vecs + v] : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kShardVec; ++u) acc[u] = add_vec(acc[u], x[u], bf16);
+    }
+#pragma unroll
+    for (int u = 0; u < kShardVec; ++u) {
+      if (scale != 1.f) acc[u] = scale_vec(acc[u], scale, bf16);
+      float g[8], p[8];
+      unpack_vec(acc[u], g, bf16);
+      unpack_vec(par[u], p, bf16);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i >= n) break;
+        float d = g[i];
+        if (wd != 0.f) {
+          d = __fmaf_rn(wd, p[i], d);
+          if (bf16) d = __bfloat162float(__float2bfloat16_rn(d));
+        }
+        p[i] = __fmaf_rn(-lr, d, p[i]);
+      }
+      par[u] = pack_vec(p, bf16);
+    }
+    for (int d = 0; d < world; ++d) {
+      uint4* dst = reinterpret_cast<uint4*>(dest.base[d]) + base;
+#pragma unroll
+      for (int u = 0; u < kShardVec; ++u) {
+        const int64_t v = v0 + (int64_t)u * blockDim.x;
+        if (live[u]) dst[v] = par[u];
+      }
+    }
+  }
+  __threadfence_system();
+}
+
 constexpr int kChunk = 256;
 
 struct BwdLayout {
@@ -734,6 +822,28 @@ extern "C" int pkm_grad_shard_reduce(const void* recv, int dtype, int64_t num_ro
                                                         n_vecs, row_vecs, world, rank, dtype == PKM_DT_BF16, scale,
                                                         dest);
   return check_cuda("pkm_grad_shard_reduce");
+}
+
+extern "C" int pkm_grad_shard_sgd(const void* recv, int dtype, int64_t num_rows, int64_t dim, int world, int rank,
+                                  int64_t shard_rows, void* const* table_bases, float lr, float weight_decay,
+                                  float scale, int max_blocks, void* stream) {
+  if (dtype != PKM_DT_F32 && dtype != PKM_DT_BF16) return fail(PKM_ERR_UNSUPPORTED, "dtype must be f32 or bf16");
+  GradDest dest{};
+  int rc = shard_dest(dest, table_bases, world, rank, shard_rows, num_rows, dim, dtype);
+  if (rc) return rc;
+  if (!recv || !aligned16(recv)) return fail(PKM_ERR_INVALID_ARG, "recv NULL or not 16-byte aligned");
+  const int64_t rows = std::min<int64_t>(shard_rows, num_rows - (int64_t)rank * shard_rows);
+  if (rows <= 0) return PKM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t row_vecs = dim * dtype_size(dtype) / 16;
+  const int64_t n_vecs = rows * row_vecs;
+  const int64_t per_block = 256 * kShardVec;
+  int64_t blocks = (n_vecs + per_block - 1) / per_block;
+  if (max_blocks > 0) blocks = std::min<int64_t>(blocks, max_blocks);
+  shard_sgd_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const uint4*>(recv), shard_rows * row_vecs, n_vecs,
+                                                     world, rank, dtype == PKM_DT_BF16, scale, lr, weight_decay,
+                                                     dest);
+  return check_cuda("pkm_grad_shard_sgd");
 }
 
 // ---------------------------------------------------------------------------

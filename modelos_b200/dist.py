@@ -7,9 +7,11 @@ gradient is the large one (``[n_keys^2, v_dim]``, 512 MiB in bf16 at
 benchmark config 2); ``ShardedTableGrad`` fuses its exchange into the bag
 backward (rows stored to their owners over NVLink while the segment pass
 computes, owner-side reduction and all-gather beside the rest of the
-backward).  ``GradReducer`` all-reduces every other gradient from its
-post-accumulate hook as soon as it exists, and without a
-``ShardedTableGrad`` the table's too (plain NCCL).  BatchNorm statistics
+backward); ``RowOwnerSGD`` instead shards the table's optimizer by rows
+(reduce-scatter inside the bag backward, owner update, all-gather of the
+updated rows).  ``GradReducer`` all-reduces every other gradient from its
+post-accumulate hook as soon as it exists, and without either of them the
+table's too (plain NCCL).  BatchNorm statistics
 stay per rank, as the reference's ``nn.BatchNorm1d`` does under data
 parallelism.
 """
@@ -19,6 +21,20 @@ from typing import Iterable, List, Optional
 
 import torch
 import torch.distributed as dist
+
+
+def _symm_offset(h, t: torch.Tensor, rank: int) -> int:
+    """Byte offset of ``t`` inside its symmetric allocation (handle ``h``)."""
+    off = t.data_ptr() - int(h.buffer_ptrs[rank])
+    if off < 0 or off + t.numel() * t.element_size() > int(h.buffer_size):
+        raise RuntimeError("tensor lies outside its symmetric allocation")
+    return off
+
+
+def _symm_peers(h, t: torch.Tensor, rank: int, world: int) -> List[int]:
+    """Device addresses of ``t``'s counterpart on every rank."""
+    off = _symm_offset(h, t, rank)
+    return [int(h.buffer_ptrs[i]) + off for i in range(world)]
 
 
 class ShardedTableGrad:
@@ -107,14 +123,10 @@ class ShardedTableGrad:
         weight._pkm_grad_exchange = self
 
     def _offset(self, h, t) -> int:
-        off = t.data_ptr() - int(h.buffer_ptrs[self.rank])
-        if off < 0 or off + t.numel() * t.element_size() > int(h.buffer_size):
-            raise RuntimeError("tensor lies outside its symmetric allocation")
-        return off
+        return _symm_offset(h, t, self.rank)
 
     def _peers(self, h, t):
-        off = self._offset(h, t)
-        return [int(h.buffer_ptrs[i]) + off for i in range(self.world)]
+        return _symm_peers(h, t, self.rank, self.world)
 
     def backward(self, indices, weight, psw, grad_out, need_dpsw: bool):
         """Bag backward of one step: returns (table gradient, psw gradient);
@@ -166,6 +178,93 @@ class ShardedTableGrad:
             del self.weight._pkm_grad_exchange
 
 
+class RowOwnerSGD:
+    """SGD of a replicated value table with the optimizer sharded by rows:
+    reduce-scatter, row-owner update, all-gather of the parameters.
+
+    Rank ``o`` owns table rows ``[o*S, (o+1)*S)`` (``S = ceil(K / world)``).
+    The table itself is moved into symmetric memory (``weight.data`` becomes
+    a view of it) so that peers can write it.  In the backward the bag
+    kernel stores each finished row of this rank's gradient straight into
+    its owner's receive buffer (``pkm_bag_bwd_sharded``: the reduce-scatter
+    inside the compute) and returns no table gradient.  ``step()`` then, on
+    the current stream: a barrier; each owner sums the ``world`` copies of
+    its rows, applies ``p -= lr * (g + weight_decay * p)`` to its rows only
+    and stores them into every rank's table (``pkm_grad_shard_sgd``); a
+    second barrier.  Against an all-reduce of the table gradient followed by
+    every rank's optimizer pass over the whole table, the gradient is never
+    all-gathered and each rank's optimizer touches 1/world of the rows.
+
+    Use it in place of the table's entry in the dense optimizer and in
+    ``GradReducer`` (``sharded=[...]``); call ``step()`` after the backward
+    of every step, on every rank.
+    """
+
+    def __init__(self, weight: torch.nn.Parameter, lr: float, weight_decay: float = 0.0,
+                 group: Optional[dist.ProcessGroup] = None, average: bool = False, max_blocks: int = 0):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if self.world > 8:
+            raise ValueError("the fused exchange spans one NVLink domain (at most 8 ranks)")
+        K, D = weight.shape
+        self.K, self.D = K, D
+        self.shard_rows = -(-K // self.world)
+        dev = weight.device
+        rows = self.world * self.shard_rows
+        self.table = symm_mem.empty((rows, D), dtype=weight.dtype, device=dev)
+        h_table = symm_mem.rendezvous(self.table, self.group)
+        self.recv = symm_mem.empty((self.world, self.shard_rows, D), dtype=weight.dtype, device=dev)
+        h_recv = symm_mem.rendezvous(self.recv, self.group)
+        self._handles = [h_table, h_recv]
+        with torch.no_grad():
+            self.table[:K].copy_(weight.data)
+            self.table[K:].zero_()
+        weight.data = self.table[:K]
+        self.table_ptrs = _symm_peers(h_table, self.table, self.rank, self.world)
+        self.recv_ptrs = _symm_peers(h_recv, self.recv, self.rank, self.world)
+        self.lr, self.weight_decay = float(lr), float(weight_decay)
+        self.scale = 1.0 / self.world if average else 1.0
+        self.max_blocks = max_blocks
+        self.flag = torch.zeros(1, device=dev)
+        self.pending = False
+        self.weight = weight
+        weight._pkm_grad_exchange = self
+
+    def backward(self, indices, weight, psw, grad_out, need_dpsw: bool):
+        """Bag backward of one step: the table gradient goes to the row
+        owners (no local gradient is returned); returns (None, psw gradient)."""
+        from . import _native
+
+        dpsw = _native.bag_bwd_sharded(indices, weight, psw, grad_out, self.recv_ptrs, self.rank, self.shard_rows,
+                                       need_dpsw=need_dpsw)
+        self.pending = True
+        return None, dpsw
+
+    def wait(self):
+        """Nothing to wait for: the table gradient never materialises
+        (``GradReducer`` calls this for every sharded table)."""
+
+    def step(self):
+        """Owner update of this step's gradient, then every rank's table
+        holds every updated row.  Every rank must call it."""
+        from . import _native
+
+        if not self.pending:
+            raise RuntimeError("RowOwnerSGD.step() without a backward through the table")
+        dist.all_reduce(self.flag, group=self.group)  # every rank's rows are in the receive buffers
+        _native.grad_shard_sgd(self.recv, self.K, self.rank, self.shard_rows, self.table_ptrs, self.lr,
+                               self.weight_decay, self.scale, self.max_blocks)
+        dist.all_reduce(self.flag, group=self.group)  # every shard is in every rank's table
+        self.pending = False
+
+    def close(self):
+        if getattr(self.weight, "_pkm_grad_exchange", None) is self:
+            del self.weight._pkm_grad_exchange
+
+
 class GradReducer:
     """Sum gradients of ``params`` over ``group`` (``average`` divides by the
     world size).  A gradient of at least ``bucket_bytes`` starts its
@@ -179,7 +278,7 @@ class GradReducer:
 
     def __init__(self, params: Iterable[torch.nn.Parameter], early: Iterable[torch.nn.Parameter] = (),
                  group: Optional[dist.ProcessGroup] = None, average: bool = False,
-                 sharded: Iterable[ShardedTableGrad] = (), bucket_bytes: int = 1 << 20):
+                 sharded: Iterable = (), bucket_bytes: int = 1 << 20):
         self.group = group
         self.average = average
         self.sharded = list(sharded)

@@ -131,3 +131,55 @@ def run_sharded(rank: int, world: int, port: int, out_dir: str, dtype_name: str,
         _native.check_device_errors(dev)
     finally:
         dist.destroy_process_group()
+
+
+def run_owner(rank: int, world: int, port: int, out_dir: str, dtype_name: str):
+    """RowOwnerSGD (reduce-scatter in the bag backward, owner SGD, all-gather
+    of the rows) against NCCL all-reduce of the table gradient plus
+    torch.optim.SGD on every rank, over two steps."""
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from modelos_b200.dist import RowOwnerSGD
+        from modelos_b200.pkm.memory import HashingMemory
+
+        dtype = getattr(torch, dtype_name)
+        lr, wd = 0.05, 0.01
+
+        def make():
+            torch.manual_seed(0)
+            m = HashingMemory(**CFG)
+            m.reset_parameters()
+            return m.to(dev, dtype)
+
+        ref, m = make(), make()
+        owner = RowOwnerSGD(m.values.weight, lr=lr, weight_decay=wd)
+        opt = torch.optim.SGD([ref.values.weight], lr=lr, weight_decay=wd, foreach=True)
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        tables = []
+        for _ in range(2):
+            x = torch.randn((2, 300, CFG["input_dim"]), generator=g, device=dev).to(dtype)
+            for mod in (ref, m):
+                for p in mod.parameters():
+                    p.grad = None
+                y, _ = mod(x)
+                (y.float() ** 2).sum().backward()
+            dist.all_reduce(ref.values.weight.grad)
+            opt.step()
+            assert m.values.weight.grad is None
+            owner.step()
+            torch.cuda.synchronize()
+            tables.append((ref.values.weight.detach().cpu().clone(), m.values.weight.detach().cpu().clone()))
+        torch.save({"tables": tables, "aliased": m.values.weight.data_ptr() == owner.table.data_ptr()},
+                   os.path.join(out_dir, f"owner{rank}.pt"))
+        owner.close()
+        del owner
+    finally:
+        dist.destroy_process_group()
