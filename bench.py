@@ -400,7 +400,8 @@ def main():
                          "optimizer sharded by rows (needs --optimizer sgd)")
     ap.add_argument("--optimizer", default="none", choices=["none", "sgd"],
                     help="add an SGD step of every parameter to each timed step")
-    ap.add_argument("--lr", type=float, default=1e-3)
+    ap.add_argument("--lr", type=float, default=1e-6,
+                    help="SGD learning rate (the loss sums 16.7 M squares: larger rates diverge)")
     args = ap.parse_args()
     if args.grad_exchange == "owner" and args.optimizer != "sgd":
         ap.error("--grad-exchange owner updates the table in the optimizer step: add --optimizer sgd")

@@ -21,6 +21,9 @@
 // equal to T are taken in ascending slot order (slot = i1 * n + i2), as
 // many as the top knn has room for.  Nothing of the product is
 // materialised.
+//
+// Non-finite scores (a diverged model) keep every index a valid slot: NaN
+// ranks above +inf, as in torch.topk, in both stages.
 #include <algorithm>
 
 #include "common.cuh"
@@ -28,9 +31,12 @@
 namespace pkm {
 
 // Order-preserving integer key of a score (larger score -> larger key).
+// Every NaN takes the largest key (torch.topk ranks NaN above +inf), so a
+// present element never has key 0, the mark of an absent one.
 __device__ __forceinline__ uint32_t key32(float x) {
   if (x == 0.f) x = 0.f;  // -0 and +0 compare equal
   const uint32_t u = __float_as_uint(x);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0xffffffffu;
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 __device__ __forceinline__ float unkey32(uint32_t k) {
@@ -38,7 +44,16 @@ __device__ __forceinline__ float unkey32(uint32_t k) {
 }
 __device__ __forceinline__ uint32_t key16(uint32_t b) {
   if (b == 0x8000u) b = 0;
+  if ((b & 0x7fffu) > 0x7f80u) return 0xffffu;  // NaN
   return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
+}
+// When a row's stage-1 values hold both +inf and -inf, its pair sums are
+// formed with +-inf taken as +-FLT_MAX, so that no sum is inf - inf: the
+// sum's key then never increases along a sorted row or column (NaN operands
+// give NaN sums, the largest key), which the candidate pruning and the
+// bounded selection rely on.  Rows without that mix keep exact sums.
+__device__ __forceinline__ float sat_inf(float x) {
+  return fabsf(x) == INFINITY ? copysignf(3.402823466e38f, x) : x;
 }
 __device__ __forceinline__ float unkey16(uint32_t k) {
   const uint32_t b = (k & 0x8000u) ? (k & 0x7fffu) : (~k & 0xffffu);
@@ -219,8 +234,16 @@ __device__ __forceinline__ void stage1_select_bf16(const uint32_t (&w)[EPL / 2],
   const int lane = threadIdx.x & 31;
   __nv_bfloat162 m2 = bf2(w[0]);
 #pragma unroll
-  for (int k = 1; k < NW; ++k) m2 = __hmax2(m2, bf2(w[k]));
+  for (int k = 1; k < NW; ++k) m2 = __hmax2_nan(m2, bf2(w[k]));  // a NaN anywhere reaches the lane maximum
   const uint32_t mw = *reinterpret_cast<uint32_t*>(&m2);
+  if (__any_sync(0xffffffffu, (mw & 0x7fffu) > 0x7f80u || ((mw >> 16) & 0x7fffu) > 0x7f80u)) {
+    // packed comparisons never count a NaN: select on integer keys instead
+    uint32_t key[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) key[e] = key16((e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xffffu));
+    stage1_select<__nv_bfloat16, EPL>(key, knn, s_key, s_idx, okey, oidx);
+    return;
+  }
   const uint32_t lmax = max(key16(mw & 0xffffu), key16(mw >> 16));
   const uint32_t lo = __reduce_min_sync(0xffffffffu, lmax), hi = __reduce_max_sync(0xffffffffu, lmax);
   uint32_t T = lo;
@@ -429,8 +452,13 @@ __global__ void __launch_bounds__(kTopkWarps * 32, 3) product_topk_kernel(const 
       }
     }
     const bool live = lane < knn;
-    const float v1 = live ? ScoreT<T>::value(k1) : -INFINITY;
-    const float v2 = live ? ScoreT<T>::value(k2) : -INFINITY;
+    float v1 = live ? ScoreT<T>::value(k1) : -INFINITY;
+    float v2 = live ? ScoreT<T>::value(k2) : -INFINITY;
+    if (__any_sync(0xffffffffu, live && (v1 == INFINITY || v2 == INFINITY)) &&
+        __any_sync(0xffffffffu, live && (v1 == -INFINITY || v2 == -INFINITY)) && live) {
+      v1 = sat_inf(v1);  // +inf and -inf both present: keep every sum free of inf - inf
+      v2 = sat_inf(v2);
+    }
     if (sub1 && live) {
       sub1[r * knn + lane] = i1;
       sub2[r * knn + lane] = i2;
@@ -625,6 +653,8 @@ __global__ void __launch_bounds__(256) score_grad_dense_kernel(const int64_t* __
     if (psw) p = ld_f(psw, dt, r * knn + lane);
     slot = indices[r * knn + lane];
   }
+  // a slot outside [0, n^2) has no sub-keys to credit
+  const bool in_range = slot >= 0 && slot < (int64_t)n * n;
   float ds = g;
   if (psw) {
     const float dot = warp_sum(p * g);
@@ -636,9 +666,10 @@ __global__ void __launch_bounds__(256) score_grad_dense_kernel(const int64_t* __
   __syncwarp();
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
-    const int key = live ? (int)(half ? slot % n : slot / n) : n + lane;
+    const bool use = live && in_range;
+    const int key = use ? (int)(half ? slot % n : slot / n) : n + lane;
     const unsigned peers = __match_any_sync(0xffffffffu, key);
-    if (live && lane == __ffs(peers) - 1) {
+    if (use && lane == __ffs(peers) - 1) {
       float s = 0.f;
       unsigned mrem = peers;
       while (mrem) {

@@ -188,3 +188,64 @@ def test_score_grad_dense_matches_scatter_of_softmax_backward(dtype):
     tolr = 1e-6 if dtype == torch.float32 else 2e-2
     assert rel_err(dS.numpy(), ref.numpy()) < tolr
     assert (dS[ref == 0] == 0).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_product_topk_nonfinite_scores(dtype):
+    """Scores with NaN and +-inf (what a diverged model produces): every
+    index stays a distinct valid slot built from the stage-1 lists, NaN
+    ranks above everything (torch.topk's order), and finite rows are
+    unaffected."""
+    from modelos_b200 import _native
+    n, knn = 512, 32
+    g = torch.Generator().manual_seed(11)
+    s = torch.randn(64, 2, n, generator=g)
+    nan, inf = float("nan"), float("inf")
+    s[0] = nan                      # all NaN
+    s[1, 0, 7] = nan                # one NaN in half 0
+    s[2, 1, :300] = nan             # most of half 1 NaN
+    s[3, 0, 5] = inf
+    s[3, 1, 9] = -inf               # inf + (-inf) pairs
+    s[4, 0] = inf
+    s[4, 1] = -inf                  # every pair inf - inf
+    s[5, 0, 3] = -inf
+    s[5, 1, 4] = inf
+    s[6] = -inf
+    s[7, 0, ::2] = nan
+    s[7, 1, 1::3] = inf
+    s = s.to(dtype)
+    idx, top, psw, s1, s2 = _native.product_topk(s.to(DEV).contiguous(), knn, want_psw=True, want_sub=True)
+    idx, s1, s2 = idx.cpu(), s1.cpu(), s2.cpu()
+    assert ((idx >= 0) & (idx < n * n)).all()
+    assert ((s1 >= 0) & (s1 < n)).all() and ((s2 >= 0) & (s2 < n)).all()
+    for r in range(s.shape[0]):
+        assert idx[r].unique().numel() == knn, r
+        assert set((idx[r] // n).tolist()) <= set(s1[r].tolist()), r
+        assert set((idx[r] % n).tolist()) <= set(s2[r].tolist()), r
+    # a NaN sub-key is the best of its half, and every chosen slot uses it
+    assert s1[1, 0].item() == 7 and ((idx[1] // n) == 7).all()
+    # half 1 of row 2: the 32 lowest-index NaNs, in index order
+    assert s2[2].tolist() == list(range(knn))
+    ref = po.product_topk(s[8:].float().numpy(), knn, bf16=dtype == torch.bfloat16)
+    np.testing.assert_array_equal(idx[8:].numpy(), ref["indices"])
+
+
+def test_score_grad_dense_ignores_out_of_range_slots():
+    """A slot outside [0, n^2) credits no sub-key; the rest of the row is the
+    same as without it."""
+    from modelos_b200 import _native
+    g = torch.Generator().manual_seed(2)
+    R, knn, n = 64, 32, 128
+    idx = torch.stack([torch.randperm(n * n, generator=g)[:knn] for _ in range(R)])
+    dpsw = torch.randn(R, knn, generator=g)
+    full = _native.score_grad_dense(idx.to(DEV), None, dpsw.to(DEV), n).cpu()
+    bad = idx.clone()
+    bad[:, 3] = -1
+    bad[:, 7] = n * n + 5
+    d2 = dpsw.clone()
+    d2[:, 3] = 0
+    d2[:, 7] = 0
+    got = _native.score_grad_dense(bad.to(DEV), None, dpsw.to(DEV), n).cpu()
+    ref = _native.score_grad_dense(idx.to(DEV), None, d2.to(DEV), n).cpu()
+    assert torch.equal(got, ref)
+    assert not torch.equal(got, full)
