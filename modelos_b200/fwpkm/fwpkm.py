@@ -24,7 +24,6 @@ from __future__ import annotations
 import math
 from collections import OrderedDict, defaultdict
 from logging import getLogger
-from typing import Optional
 
 import torch
 from torch import nn

@@ -6,9 +6,7 @@ from __future__ import annotations
 
 import os
 import socket
-import sys
 
-import pytest
 import torch
 import torch.multiprocessing as mp
 
