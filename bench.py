@@ -1,22 +1,32 @@
-"""Benchmark: PKM layer forward + backward tokens/s (the headline benchmark's config 2).
+"""Benchmark: PKM layer forward + backward tokens/s (the headline benchmark's
+config 2), and the embedding bag's HBM GB/s (config 1).
 
-One step = forward + backward of ``HashingMemory`` at the config-2 shape
-(x [8, 2048, 1024] bf16, heads 4, knn 32, k_dim 512, n_keys 512 -> 262144
-slots, v_dim 1024, query BatchNorm) with loss ``sum(out**2)``; at N GPUs
-every rank runs that step on its own batch (weak scaling) and the gradients
-are summed over the ranks inside the step: the value table's through the
-fused NVLink exchange of ``modelos_b200.dist.ShardedTableGrad``, the others
-through NCCL.  Inputs are synthetic (seeded normal draws; there is no dataset).
+One step of the default workload (``--workload c2``) = forward + backward of
+``HashingMemory`` at the config-2 shape (x [8, 2048, 1024] bf16, heads 4,
+knn 32, k_dim 512, n_keys 512 -> 262144 slots, v_dim 1024, query BatchNorm)
+with loss ``sum(out**2)``; at N GPUs every rank runs that step on its own batch
+(weak scaling) and the gradients are summed over the ranks inside the step:
+the value table's through the fused NVLink exchange of
+``modelos_b200.dist.ShardedTableGrad``, the others through NCCL.  The same
+line carries ``emb_bag``: config 1 (bag forward + backward over a bf16
+[262144, 1024] table, 16384 bags of 128 uniform indices) measured in the
+same run.  ``--workload c1`` prints that measurement as its own line.
+Inputs are synthetic (seeded draws with the configs' distributions; there is
+no dataset).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--grad-exchange fused|nccl|owner] [--optimizer none|sgd]
+                    [--workload c2|c1] [--grad-exchange fused|nccl|owner]
+                    [--optimizer none|sgd]
 
 ``--optimizer sgd`` adds an SGD step of every parameter to each timed step
 (a different metric, named in the line); with ``--grad-exchange owner`` the
 table's step is sharded by rows (``modelos_b200.dist.RowOwnerSGD``).
 
-Prints one JSON line on rank 0.  ``--impl reference`` times the CPU port of
-the reference's path (``oracle/pkm_layer.py``) on the host cores instead.
+``--impl reference`` times the reference's CPU path on the host cores
+instead: ``oracle/ref_torch.py``, the reference's layer step on torch's CPU
+operators (bit-identical to the reference on the fixtures), in bf16 on a
+2048-token slice of the workload per step; for config 1, ``F.embedding_bag``
+forward + backward on 2048 of the 16384 bags.  Prints one JSON line on rank 0.
 """
 from __future__ import annotations
 
@@ -34,13 +44,23 @@ sys.path.insert(0, ROOT)
 
 METRIC = "PKM layer tokens/s (fwd+bwd)"
 METRIC_SGD = "PKM layer tokens/s (fwd+bwd+SGD step)"
+METRIC_C1 = "emb-bag fwd+bwd HBM GB/s (algorithmic bytes)"
 UNIT = "tokens/s"
 B, T, C = 8, 2048, 1024
 CFG = dict(input_dim=1024, output_dim=1024, mem_k_dim=512, mem_v_dim=1024, mem_heads=4, mem_knn=32,
            mem_n_keys=512, mem_query_batchnorm=True, mem_query_rmsnorm=False)
+# config 1: bags, bag size, table rows, row width
+C1_N, C1_L, C1_K, C1_D = 16384, 128, 262144, 1024
+REF_TOKENS = 2048   # tokens per reference-arm step (one sequence of the c2 batch)
+REF_BAGS = 2048     # bags per reference-arm step at config 1
 
 
-def config_obj(n):
+def config_obj(n, workload="c2"):
+    if workload == "c1":
+        return {"workload": "c1: embedding bag fwd+bwd, table bf16 [262144,1024] N(0,0.03), 16384 bags x 128 "
+                            "int64 indices uniform with replacement, fp32 per-head softmax weights, bf16 dOut",
+                "bags_per_rank_step": C1_N, "parallelism": f"replicas{n}" if n > 1 else "single",
+                "l2": "inputs larger than L2 (table 512 MiB, dense table gradient 512 MiB per step)"}
     return {"workload": "c2: HashingMemory fwd+bwd, x[8,2048,1024] bf16, H=4 knn=32 k_dim=512 "
                         "n_keys=512 (262144 slots) v_dim=1024, query BatchNorm, loss sum(out^2)",
             "tokens_per_rank_step": B * T, "global_batch": B * n, "seq_len": T,
@@ -48,108 +68,179 @@ def config_obj(n):
             "l2": "inputs larger than L2 (value table 512 MiB, dense value grad 512 MiB per step)"}
 
 
-# ---------------------------------------------------------------------------
-# CPU port (reference arm and cpu_baseline)
-# ---------------------------------------------------------------------------
-def cpu_port_rate(sample_tokens=256, steps=2, warmup=1):
-    import numpy as np
-
-    from oracle.pkm_layer import layer_step, make_params
-
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
-    except Exception:  # pragma: no cover
-        cores = os.cpu_count() or 1
-    P = make_params(CFG, 0)
-    rng = np.random.default_rng(1)
-    x = rng.standard_normal((1, sample_tokens, C), dtype=np.float32)
-    for _ in range(warmup):
-        layer_step(P, x, CFG["mem_heads"], CFG["mem_knn"], norm="bn")
-    ts = []
-    for _ in range(steps):
-        t0 = time.perf_counter()
-        layer_step(P, x, CFG["mem_heads"], CFG["mem_knn"], norm="bn")
-        ts.append(time.perf_counter() - t0)
-    t = statistics.median(ts)
-    cpu = ""
+def cpu_model() -> str:
     try:
         for line in open("/proc/cpuinfo"):
             if line.startswith("model name"):
-                cpu = line.split(":", 1)[1].strip()
-                break
+                return line.split(":", 1)[1].strip()
     except OSError:
         pass
-    return {"value": sample_tokens / t, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{sample_tokens} tokens of the c2 layer (fwd+bwd, fp32 numpy port of "
-                      f"oracle/pkm_layer.py, BLAS threads={cores}, host {os.cpu_count()} cpus {cpu}), "
-                      f"median of {steps} after {warmup} warm-up; s/step={t:.3f}"}
+    return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# the reference's CPU path (reference arm and cpu_baseline)
+# ---------------------------------------------------------------------------
+def _timed(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    return ts
+
+
+def ref_layer_rate(steps=5, warmup=2, tokens=REF_TOKENS):
+    """The reference's layer step (``oracle/ref_torch.py``: its torch CPU
+    operators in its order, bf16) on ``tokens`` tokens of the c2 workload."""
+    import torch
+
+    from oracle import ref_torch as rt
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    P = rt.make_params(CFG, 0, torch.bfloat16)
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn((1, tokens, C), generator=g).to(torch.bfloat16)
+    ts = _timed(lambda: rt.layer_step(P, x, CFG["mem_heads"], CFG["mem_knn"], CFG["mem_k_dim"], "bn"), steps, warmup)
+    t = statistics.median(ts)
+    cores = torch.get_num_threads()
+    return {"value": tokens / t, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{tokens} tokens of the c2 layer per step (fwd+bwd, bf16, the reference's torch CPU operators "
+                      f"via oracle/ref_torch.py, torch threads={cores}, host {os.cpu_count()} cpus {cpu_model()}), "
+                      f"median of {steps} after {warmup} warm-up; s/step median {t:.4f} mean "
+                      f"{statistics.mean(ts):.4f}",
+            "ms_per_step": 1000.0 * t, "steps": steps, "warmup": warmup, "tokens_per_step": tokens}
+
+
+def ref_bag_rate(steps=5, warmup=2, bags=REF_BAGS):
+    """Config 1 on the reference's CPU branch (``F.embedding_bag`` forward and
+    its autograd backward, ``pkm/xformer_embeddingbag.py:436-437``) over
+    ``bags`` of the 16384 bags, bf16 table and weights (PKM semantics)."""
+    import torch
+    import torch.nn.functional as F
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    W = (torch.randn((C1_K, C1_D), generator=g) * 0.03).to(torch.bfloat16).requires_grad_(True)
+    idx = torch.randint(0, C1_K, (bags, C1_L), generator=g)
+    psw = torch.softmax(torch.randn((bags, 4, C1_L // 4), generator=g), -1).reshape(bags, C1_L)
+    psw = psw.to(torch.bfloat16).requires_grad_(True)
+    dout = torch.randn((bags, C1_D), generator=g).to(torch.bfloat16)
+
+    def step():
+        W.grad = None
+        psw.grad = None
+        F.embedding_bag(idx, W, per_sample_weights=psw, mode="sum").backward(dout)
+
+    ts = _timed(step, steps, warmup)
+    t = statistics.median(ts)
+    fwd, bwd = bag_bytes(bags, C1_L, C1_D, C1_K, s_w=2)
+    cores = torch.get_num_threads()
+    return {"value": (fwd + bwd) / t / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{bags} of the {C1_N} config-1 bags per step (F.embedding_bag fwd + autograd bwd, bf16, "
+                      f"torch threads={cores}, host {os.cpu_count()} cpus {cpu_model()}), median of {steps} after "
+                      f"{warmup} warm-up; s/step {t:.4f}; algorithmic bytes of the sample (dense table gradient "
+                      f"counted in full)",
+            "ms_per_step": 1000.0 * t, "steps": steps, "warmup": warmup}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    cb = cpu_port_rate()
-    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT,
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * B * T / cb["value"], "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_obj(world),
-            "cpu_baseline": cb,
-            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    steps, warmup = max(args.steps, 1), max(args.warmup, 0)
+    if args.workload == "c1":
+        cb = ref_bag_rate(steps, warmup)
+        metric, unit = METRIC_C1, "GB/s"
+    else:
+        cb = ref_layer_rate(steps, warmup)
+        metric, unit = METRIC, UNIT
+    line = {"impl": "reference", "metric": metric, "value": round(cb["value"], 3), "unit": unit,
+            "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": round(cb["ms_per_step"], 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": config_obj(world, args.workload), "cpu_baseline": dict(cb),
+            "e2e": {"value": round(cb["value"], 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    line["cpu_baseline"]["value"] = line["value"]
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
-# clocks sampler
+# clocks: NVML sampled in a child process over the whole run, summarised over
+# the samples taken inside the timed region
 # ---------------------------------------------------------------------------
+_SAMPLER = r"""
+import sys, time
+import pynvml
+pynvml.nvmlInit()
+try:
+    h = pynvml.nvmlDeviceGetHandleByUUID(sys.argv[1])
+except Exception:
+    h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[2]))
+print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+period = float(sys.argv[3])
+while True:
+    t = time.time()
+    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+    try:
+        r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+    except Exception:
+        r = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+    print("%.6f %d %d" % (t, sm, r), flush=True)
+    time.sleep(period)
+"""
+_REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown"}
+
+
 class Clocks:
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, index):
-        self.index = index
+    def __init__(self, dev_index: int, period_s: float = 0.005):
+        self.dev_index = dev_index
+        self.period = period_s
         self.p = None
+        self.window = None
 
-    def __enter__(self):
+    def start(self):
+        import torch
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "100"],
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.dev_index).uuid)
+            self.p = subprocess.Popen([sys.executable, "-c", _SAMPLER, uuid, str(self.dev_index), str(self.period)],
                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.p = None
         return self
 
-    def __exit__(self, *a):
+    def mark(self, t0, t1):
+        self.window = (t0, t1)
+
+    def stop(self):
+        self.out = ""
         if self.p is not None:
             self.p.terminate()
             try:
-                self.out, _ = self.p.communicate(timeout=5)
+                self.out, _ = self.p.communicate(timeout=10)
             except Exception:
                 self.p.kill()
-                self.out = ""
-        else:
-            self.out = ""
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        mx, samples = None, []
         for line in (self.out or "").splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+            f = line.split()
+            if len(f) == 2 and f[0] == "max":
+                mx = float(f[1])
+            elif len(f) == 3:
+                samples.append((float(f[0]), float(f[1]), int(f[2])))
+        if not samples:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["unsampled"]}
+        t0, t1 = self.window or (samples[0][0], samples[-1][0])
+        inside = [s for s in samples if t0 <= s[0] <= t1]
+        scope = "timed region"
+        if len(inside) < 3:  # a region shorter than a few sampling periods: add the run around it
+            inside = [s for s in samples if t0 - 2.0 <= s[0] <= t1 + 0.1]
+            scope = "timed region and the 2 s of warm-up before it"
+        reasons = sorted({name for _, _, r in inside for bit, name in _REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(inside), "scope": scope, "source": "NVML, %.0f ms period" % (1000 * self.period)}
 
 
 # ---------------------------------------------------------------------------
@@ -179,20 +270,24 @@ def traffic_from_profiles():
 
 
 def bag_bytes(N, L, D, K, s_v=2, s_idx=8, s_w=2, s_out=2):
+    """Algorithmic bytes of one bag forward and one bag backward (the logical
+    bytes of the reference's kernels: every entry's table / upstream row read,
+    the indices and weights, every touched table row read once for the weight
+    gradient, the dense table gradient written in full)."""
     fwd = N * L * (D * s_v + s_idx + s_w) + N * D * s_out
     kt = K * (1.0 - math.exp(-N * L / K))
     bwd = N * L * (D * s_v + s_idx + s_w + s_w) + kt * D * s_v + K * D * s_v
     return fwd, bwd
 
 
-def count_launches(step, x):
+def count_launches(step, *a):
     """Kernels of libpkm_b200 launched by one step (profiled outside timing)."""
     import torch
     from torch.profiler import ProfilerActivity, profile
 
     try:
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            step(x)
+            step(*a)
             torch.cuda.synchronize()
         n = 0
         for ev in prof.events():
@@ -204,6 +299,139 @@ def count_launches(step, x):
         return None
 
 
+def _roof(nbytes, k_ms, hbm, src, traffic, launches):
+    if k_ms is None or not (k_ms > 0):
+        return None
+    ach = nbytes / (k_ms / 1000.0) / 1e9
+    r = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
+         "traffic": traffic, "kernel_ms": round(k_ms, 4), "algorithmic_bytes": int(nbytes),
+         "launches_timed": launches, "peak_source": src}
+    if traffic:
+        # DRAM bytes actually moved (ncu) over the live kernel time: where
+        # the algorithmic rate exceeds it, the difference is served by L2
+        r["dram_achieved"] = round(traffic / (k_ms / 1000.0) / 1e9, 1)
+        r["dram_frac"] = round(traffic / (k_ms / 1000.0) / 1e9 / hbm, 4)
+    return r
+
+
+def c1_inputs(dev, seed=0):
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    W = (torch.randn((C1_K, C1_D), generator=g, device=dev) * 0.03).to(torch.bfloat16)
+    idx = torch.randint(0, C1_K, (C1_N, C1_L), generator=g, device=dev)
+    psw = torch.softmax(torch.randn((C1_N, 4, C1_L // 4), generator=g, device=dev), -1).reshape(C1_N, C1_L)
+    dout = torch.randn((C1_N, C1_D), generator=g, device=dev).to(torch.bfloat16)
+    return W, idx, psw.contiguous(), dout
+
+
+def measure_c1(dev, steps, warmup):
+    """Config 1 on this library's kernels: one step = K3 (bag forward) + K4
+    (bag backward: dense table gradient and weight gradient), inputs resident,
+    device time by CUDA events.  Returns the timing and roofline fields."""
+    import torch
+
+    from modelos_b200 import _native
+    W, idx, psw, dout = c1_inputs(dev)
+    dW = torch.empty_like(W)
+    probe = _native.EventProbe(["pkm_bag_fwd", "pkm_bag_bwd"], min_rows=C1_K)
+
+    def step():
+        _native.bag_fwd(idx, W, psw)
+        _native.bag_bwd(idx, W, psw, dout, out=dW)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    _native.set_probe(probe)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    _native.set_probe(None)
+    _native.check_device_errors(dev)
+    ms = e0.elapsed_time(e1) / steps
+    fwd, bwd = bag_bytes(C1_N, C1_L, C1_D, C1_K, s_w=4)
+    hbm, src = peaks()
+    tr = traffic_from_profiles()
+    res = {"ms_per_step": round(ms, 4), "gbs": round((fwd + bwd) / (ms / 1000.0) / 1e9, 1),
+           "algorithmic_bytes_per_step": int(fwd + bwd), "peak": hbm, "peak_source": src,
+           "frac": round((fwd + bwd) / (ms / 1000.0) / 1e9 / hbm, 4),
+           "roofline_60pct_ms": round((fwd + bwd) / (0.6 * hbm * 1e9) * 1000.0, 4)}
+    for name, nb in (("pkm_bag_fwd", fwd), ("pkm_bag_bwd", bwd)):
+        res[name] = _roof(nb, probe.mean_ms(name), hbm, src, tr.get(f"{name}.c1"), probe.count(name))
+    return res, (W, idx, psw, dout, dW, step)
+
+
+def run_ours_c1(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from modelos_b200 import _native
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    clk = Clocks(local_rank).start()
+    res, (W, idx, psw, dout, dW, step) = measure_c1(dev, 1, args.warmup)  # warm-up run
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.time()
+    res, _ = measure_c1(dev, args.steps, 0)
+    clk.mark(t0, time.time())
+    t = torch.tensor([res["ms_per_step"]], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # end to end: each step copies its indices, weights and upstream gradient
+    # from pinned host memory and reads the weight gradient back
+    h_idx, h_psw, h_dout = idx.cpu().pin_memory(), psw.cpu().pin_memory(), dout.cpu().pin_memory()
+    h_dpsw = torch.empty(psw.shape, dtype=psw.dtype).pin_memory()
+    d_idx, d_psw, d_dout = torch.empty_like(idx), torch.empty_like(psw), torch.empty_like(dout)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    for _ in range(args.steps):
+        d_idx.copy_(h_idx, non_blocking=True)
+        d_psw.copy_(h_psw, non_blocking=True)
+        d_dout.copy_(h_dout, non_blocking=True)
+        _native.bag_fwd(d_idx, W, d_psw)
+        _, dpsw, _ = _native.bag_bwd(d_idx, W, d_psw, d_dout, out=dW)
+        h_dpsw.copy_(dpsw, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    e2e_ms = (time.perf_counter() - w0) * 1000.0 / args.steps
+    t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    launches = count_launches(step)
+    clk.stop()
+    if rank != 0:
+        return
+    nbytes = res["algorithmic_bytes_per_step"]
+    roof = res["pkm_bag_bwd"] if (res["pkm_bag_bwd"] or {}).get("kernel_ms", 0) >= \
+        (res["pkm_bag_fwd"] or {}).get("kernel_ms", 0) else res["pkm_bag_fwd"]
+    dom = "pkm_bag_bwd" if roof is res["pkm_bag_bwd"] else "pkm_bag_fwd"
+    line = {"metric": METRIC_C1, "value": round(nbytes * world / (ms / 1000.0) / 1e9, 1), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded: table N(0,0.03), uniform indices, softmax weights, N(0,1) dOut)",
+            "config": config_obj(world, "c1"),
+            "e2e": {"value": round(nbytes * world / (e2e_ms / 1000.0) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": idx.numel() * 8 + psw.numel() * 4 + dout.numel() * 2,
+                    "d2h_bytes_per_step": psw.numel() * 4, "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": None if launches is None else launches * args.steps,
+            "gpu_launches_per_step": launches,
+            "roofline": dict(roof, kernel=dom), "frac_of_step": res["frac"],
+            "roofline_60pct_ms": res["roofline_60pct_ms"], "kernels": {k: res[k] for k in ("pkm_bag_fwd",
+                                                                                         "pkm_bag_bwd")},
+            "clocks": clk.summary()}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = ref_bag_rate()
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -213,6 +441,7 @@ def run_ours(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    clk = Clocks(local_rank).start()
     torch.manual_seed(1234 + rank)
     m = HashingMemory(**CFG)
     torch.manual_seed(0)  # identical parameters on every rank
@@ -272,19 +501,21 @@ def run_ours(args, rank, world, local_rank):
     _native.check_device_errors(dev)
 
     # ---- timed region (device time, CUDA events), probes on the bag kernels
-    probe = _native.EventProbe(["pkm_bag_fwd", "pkm_bag_bwd"], min_rows=m.values.weight.shape[0])
+    names = ["pkm_bag_fwd", "pkm_bag_bwd", "pkm_bag_bwd_sort", "pkm_bag_bwd_rows"]
+    probe = _native.EventProbe(names, min_rows=m.values.weight.shape[0])
     _native.set_probe(probe)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    with Clocks(local_rank) as clk:
-        e0.record()
-        for _ in range(args.steps):
-            step(x)
-        e1.record()
-        torch.cuda.synchronize()
+    t0 = time.time()
+    e0.record()
+    for _ in range(args.steps):
+        step(x)
+    e1.record()
+    torch.cuda.synchronize()
+    clk.mark(t0, time.time())
     _native.set_probe(None)
     if world > 1:
         dist.barrier()
@@ -310,7 +541,7 @@ def run_ours(args, rank, world, local_rank):
     compute = torch.cuda.current_stream(dev)
     for ev in free:
         ev.record(compute)
-    t0 = time.perf_counter()
+    w0 = time.perf_counter()
 
     def h2d(b):
         copy_stream.wait_event(free[b])
@@ -332,7 +563,7 @@ def run_ours(args, rank, world, local_rank):
         pending = loss
     lv = pending.item()
     torch.cuda.synchronize()
-    e2e_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
+    e2e_ms = (time.perf_counter() - w0) * 1000.0 / args.steps
     t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -343,34 +574,39 @@ def run_ours(args, rank, world, local_rank):
     launches_per_step = count_launches(step, x)
     _native.check_device_errors(dev)
 
+    # config 1 in the same run (rank 0 of a single-GPU run: the replicated
+    # bag microbenchmark has no data-parallel form)
+    emb = None
+    if world == 1:
+        del bufs
+        emb, _ = measure_c1(dev, max(args.steps, 20), max(args.warmup, 3))
+    clk.stop()
+
     if rank != 0:
         return
     hbm, src = peaks()
     N, L, D, K = B * T, CFG["mem_heads"] * CFG["mem_knn"], CFG["mem_v_dim"], CFG["mem_n_keys"] ** 2
     fwd_b, bwd_b = bag_bytes(N, L, D, K)
     tr = traffic_from_profiles()
-    rl = {}
-    for name, nbytes in (("pkm_bag_fwd", fwd_b), ("pkm_bag_bwd", bwd_b)):
-        k_ms = probe.mean_ms(name)
-        ach = nbytes / (k_ms / 1000.0) / 1e9
-        traffic = tr.get(f"{name}.c2")
-        rl[name] = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-                    "frac": round(ach / hbm, 4), "traffic": traffic,
-                    "kernel_ms": round(k_ms, 4), "algorithmic_bytes": int(nbytes),
-                    "launches_timed": probe.count(name), "peak_source": src}
-        if traffic:
-            # DRAM bytes actually moved (ncu) over the live kernel time: where
-            # the algorithmic rate exceeds it, the difference is served by L2
-            rl[name]["dram_achieved"] = round(traffic / (k_ms / 1000.0) / 1e9, 1)
-            rl[name]["dram_frac"] = round(traffic / (k_ms / 1000.0) / 1e9 / hbm, 4)
-    dom = max(rl, key=lambda k: rl[k]["kernel_ms"])
-    roof = dict(rl[dom])
-    roof["kernel"] = dom
-    other = [k for k in rl if k != dom][0]
+    # the bag backward is one launch, or (in-switch exchange) a sort launch
+    # followed by row-range launches: time per backward = their sum per step
+    n_bwd = probe.count("pkm_bag_bwd") or probe.count("pkm_bag_bwd_sort")
+    bwd_ms = None
+    if n_bwd:
+        bwd_ms = (probe.total_ms("pkm_bag_bwd") + probe.total_ms("pkm_bag_bwd_sort")
+                  + probe.total_ms("pkm_bag_bwd_rows")) / n_bwd
+    rl = {"pkm_bag_fwd": _roof(fwd_b, probe.mean_ms("pkm_bag_fwd"), hbm, src, tr.get("pkm_bag_fwd.c2"),
+                               probe.count("pkm_bag_fwd")),
+          "pkm_bag_bwd": _roof(bwd_b, bwd_ms, hbm, src, tr.get("pkm_bag_bwd.c2"), n_bwd)}
+    if probe.count("pkm_bag_bwd_sort"):
+        rl["pkm_bag_bwd"]["phases"] = "pkm_bag_bwd_sort + pkm_bag_bwd_rows (row ranges beside the exchange)"
+    timed = {k: v for k, v in rl.items() if v is not None}
+    dom = max(timed, key=lambda k: timed[k]["kernel_ms"]) if timed else None
     line = {
-        "metric": METRIC if opt is None else METRIC_SGD, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded normal x, reset_parameters init)",
+        "metric": METRIC if opt is None else METRIC_SGD, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded normal x, reset_parameters init)",
         "config": dict(config_obj(world), grad_exchange=exchange,
                        **({} if opt is None else {"optimizer": f"sgd lr {args.lr} (foreach; table rows by owner "
                                                                 f"with --grad-exchange owner)"})),
@@ -379,12 +615,14 @@ def run_ours(args, rank, world, local_rank):
                 "ms_per_step": round(e2e_ms, 4)},
         "gpu_launches": None if launches_per_step is None else launches_per_step * args.steps,
         "gpu_launches_per_step": launches_per_step,
-        "roofline": roof,
-        "roofline_other": dict(rl[other], kernel=other),
+        "roofline": dict(rl[dom], kernel=dom) if dom else None,
+        "roofline_other": {k: v for k, v in rl.items() if k != dom},
         "clocks": clk.summary(),
     }
+    if emb is not None:
+        line["emb_bag"] = dict(emb, metric=METRIC_C1, config=config_obj(1, "c1")["workload"])
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_port_rate()
+        line["cpu_baseline"] = ref_layer_rate()
     print(json.dumps(line), flush=True)
 
 
@@ -394,6 +632,8 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c2", choices=["c2", "c1"],
+                    help="c2: the PKM layer (default); c1: the embedding bag alone")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--grad-exchange", default="fused", choices=["fused", "nccl", "owner"],
                     help="data-parallel exchange of the value-table gradient (N > 1); owner: the table's "
@@ -405,6 +645,8 @@ def main():
     args = ap.parse_args()
     if args.grad_exchange == "owner" and args.optimizer != "sgd":
         ap.error("--grad-exchange owner updates the table in the optimizer step: add --optimizer sgd")
+    if args.warmup < 3 and args.impl == "ours":
+        ap.error("--warmup must be at least 3")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -420,7 +662,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.workload == "c1":
+            run_ours_c1(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -104,9 +104,11 @@ PKM_API int pkm_bag_bwd(const int64_t* indices, const void* psw, int psw_dtype, 
  * pkm_bag_bwd, without the workspace: the scratch is a 16 MiB static device
  * array inside the library, held by every GPU that loads it until exit.
  * Sizes whose pkm_bag_bwd_workspace() exceeds 16 MiB return
- * PKM_ERR_UNSUPPORTED before any launch.  The first call on a device looks up
- * the array's device address (cudaGetSymbolAddress); make that first call
- * before any stream capture.  All calls share the one array, so calls that
+ * PKM_ERR_UNSUPPORTED before any launch.  Every call looks up the array's
+ * device address (cudaGetSymbolAddress, with the caller's device current), so
+ * the address stays right across a device or context reset; the first call on
+ * a device also loads the library's device code there, so make that first
+ * call before any stream capture.  All calls share the one array, so calls that
  * overlap on the GPU (other streams, other host threads) race; the kernels
  * clear what must start at zero on every call.
  */

@@ -150,11 +150,14 @@ class EventProbe:
         ev1.record()
         self.events[name].append((ev0, ev1))
 
-    def mean_ms(self, name: str) -> float:
+    def total_ms(self, name: str) -> float:
+        return sum(a.elapsed_time(b) for a, b in self.events.get(name, []))
+
+    def mean_ms(self, name: str) -> Optional[float]:
         ev = self.events.get(name, [])
         if not ev:
-            return float("nan")
-        return sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+            return None
+        return self.total_ms(name) / len(ev)
 
     def count(self, name: str) -> int:
         return len(self.events.get(name, []))
@@ -388,17 +391,22 @@ class BagBwdPhases:
 
     def sort(self):
         d = self.dpsw
-        _check(lib().pkm_bag_bwd_sort(*self._common(), _ptr(d), DT[d.dtype] if d is not None else 0, None,
-                                      _ptr(self.ws), self.ws_bytes, _ptr(err_word(self.weight.device)),
-                                      _stream(self.weight.device)), "pkm_bag_bwd_sort")
+        ev = _pstart("pkm_bag_bwd_sort", self.K)
+        rc = lib().pkm_bag_bwd_sort(*self._common(), _ptr(d), DT[d.dtype] if d is not None else 0, None,
+                                    _ptr(self.ws), self.ws_bytes, _ptr(err_word(self.weight.device)),
+                                    _stream(self.weight.device))
+        _pstop("pkm_bag_bwd_sort", ev)
+        _check(rc, "pkm_bag_bwd_sort")
 
     def rows(self, r0: int, r1: int, out: torch.Tensor):
         assert out.shape == (self.K, self.D) and out.is_contiguous() and out.dtype == self.weight.dtype
         d = self.dpsw
-        _check(lib().pkm_bag_bwd_rows(*self._common(), r0, r1, _ptr(out), DT[out.dtype], _ptr(d),
-                                      DT[d.dtype] if d is not None else 0, _ptr(self.ws), self.ws_bytes,
-                                      _ptr(err_word(self.weight.device)), _stream(self.weight.device)),
-               "pkm_bag_bwd_rows")
+        ev = _pstart("pkm_bag_bwd_rows", self.K)
+        rc = lib().pkm_bag_bwd_rows(*self._common(), r0, r1, _ptr(out), DT[out.dtype], _ptr(d),
+                                    DT[d.dtype] if d is not None else 0, _ptr(self.ws), self.ws_bytes,
+                                    _ptr(err_word(self.weight.device)), _stream(self.weight.device))
+        _pstop("pkm_bag_bwd_rows", ev)
+        _check(rc, "pkm_bag_bwd_rows")
 
 
 def bag_bwd2(indices: torch.Tensor, a: Optional[torch.Tensor], gbar: torch.Tensor,

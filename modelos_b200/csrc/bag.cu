@@ -2,7 +2,6 @@
 // (K4) and the double-backward of the weight gradient (K5), with their C ABI
 // entry points.
 #include <algorithm>
-#include <mutex>
 #include <string>
 
 #include "gather.cuh"
@@ -857,23 +856,17 @@ extern "C" int pkm_grad_shard_sgd(const void* recv, int dtype, int64_t num_rows,
 namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {nullptr};
-
-// Device address of the scratch array on the current device, looked up once
-// per device (the host-side symbol is only a stand-in, never a device address).
+// Device address of the scratch array on the current device (the host-side
+// symbol is only a stand-in, never a device address).  It is looked up on
+// every call, with the caller's device current: after the first call on a
+// device (which loads the library's device code there) the lookup is cheap,
+// and an address cached across calls would go stale if the caller reset the
+// device or its primary context in between.
 int noalloc_scratch(void** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return check_cuda("cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(PKM_ERR_UNSUPPORTED, "device ordinal above 63");
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess)
-      return check_cuda("cudaGetSymbolAddress(g_noalloc_scratch)");
-    g_noalloc_ptr[dev] = p;
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess)
+    return check_cuda("cudaGetSymbolAddress(g_noalloc_scratch)");
+  *out = p;
   return PKM_OK;
 }
 }  // namespace

@@ -1,5 +1,6 @@
 // Library-level entry points: version, status strings, last-error detail,
 // and the host helpers shared by the kernel files.
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -23,17 +24,21 @@ int check_cuda(const char* what) {
   return PKM_ERR_CUDA;
 }
 
+// SM count of the current device, cached per device ordinal; host threads
+// may call into the library at the same time, so the entries are atomics
+// (two threads that miss together both store the same value).
 int num_sms() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (cache[dev] == 0) {
-    int v = 0;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
     cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev] = v > 0 ? v : 1;
+    v = v > 0 ? v : 1;
+    cache[dev].store(v, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return v;
 }
 
 }  // namespace pkm

@@ -96,6 +96,69 @@ def fwpkm_case(seed: int = 0, B=2, T=16, heads=2, k_dim=16, v_dim=32, n_sub=16, 
     return keys, values, q, ref_v
 
 
+# Benchmark config 4 geometry (FwPKM): k_dim 512, v_dim 1024, 4 heads x top-32
+# over 512^2 fp32 fast-weight slots; the module's other defaults (idw,
+# softmax, addressing loss "me", lookahead 1, fp32 fast weights).
+FW_C4 = dict(mem_k_dim=512, mem_v_dim=1024, mem_heads=4, mem_topk=32, mem_n_subkeys=512, learning_rate=0.1)
+# A config-4 slice small enough for the reference on CPU: one sequence of
+# 512 positions in two chunks of 256 (two inner updates).
+FW_C4_T, FW_C4_CHUNK = 512, 256
+
+
+def fwpkm_c4_case(seed: int = 0, T: int = FW_C4_T):
+    """Config-4-geometry FwPKM inputs: keys U(+-1/sqrt(k_dim)) and values
+    N(0, v_dim^-1/2) as ``reset_parameters`` (``fwpkm/fwpkm.py:91-96``);
+    q [1, T, H*k_dim] and ref_v [1, T, v_dim] N(0,1), rounded to bf16 (the
+    config's input dtype) and kept in fp32, the dtype the fast-weight path
+    computes in (``fp32_fw``, ``fwpkm/fwpkm.py:406-409``)."""
+    kw = FW_C4
+    H, kd, D, n = kw["mem_heads"], kw["mem_k_dim"], kw["mem_v_dim"], kw["mem_n_subkeys"]
+    g = torch.Generator().manual_seed(31_000 + seed)
+    keys = _u(g, (2 * H * n, kd // 2), 1 / math.sqrt(kd))
+    values = _n(g, (n * n, D), D ** -0.5)
+    q = torch.randn((1, T, H * kd), generator=g).bfloat16().float()
+    ref_v = torch.randn((1, T, D), generator=g).bfloat16().float()
+    return keys, values, q, ref_v
+
+
+SUMMARY_SAMPLE = 64
+
+
+def summarize(t: torch.Tensor, rows_idx=None, nsample: int = SUMMARY_SAMPLE, seed: int = 0,
+              nonzero_rows: bool = False) -> dict:
+    """Size-independent fingerprint of a 2-D (or flattened-to-2-D) tensor.
+
+    Per row, in float64 on the tensor's device: the L2 norm and the product
+    with one fixed random vector; plus ``nsample`` full rows.  The generator
+    picks the rows (among the nonzero rows when ``nonzero_rows``: sparse
+    gradients) and stores their indices; a checker passes those indices back
+    as ``rows_idx``.  Comparing the three parts normwise bounds every row's
+    size and direction and samples its elements.
+    """
+    t2 = t.detach().reshape(t.shape[0], -1).double()
+    cols = t2.shape[1]
+    r = torch.randn(cols, generator=torch.Generator().manual_seed(77_000), dtype=torch.float64).to(t2.device)
+    out = {"rownorm": t2.norm(dim=1).cpu().numpy(), "proj": (t2 @ r).cpu().numpy()}
+    if rows_idx is None:
+        g = np.random.default_rng(seed)
+        pool = np.arange(t2.shape[0])
+        if nonzero_rows:
+            pool = torch.nonzero(t2.abs().amax(dim=1) > 0).flatten().cpu().numpy()
+        rows_idx = np.sort(g.choice(pool, size=min(nsample, len(pool)), replace=False))
+    out["rows_idx"] = np.asarray(rows_idx, dtype=np.int64)
+    out["rows"] = t2[torch.from_numpy(out["rows_idx"]).to(t2.device)].cpu().numpy()
+    return out
+
+
+def bf16_bits(t: torch.Tensor) -> np.ndarray:
+    """bf16 tensor -> uint16 bit patterns (half the bytes of a float32 copy)."""
+    return t.detach().to(torch.bfloat16).cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def from_bf16_bits(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)
+
+
 def checksum(t: torch.Tensor) -> np.ndarray:
     """(sum, sum|x|, sum x*i) in float64: a cheap fingerprint of a tensor."""
     a = t.detach().double().reshape(-1)

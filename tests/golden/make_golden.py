@@ -255,6 +255,114 @@ def gen_fwpkm_stream(fw, name, score_type, seed=1):
     print("wrote", name)
 
 
+def _put_summary(out, prefix, t, nonzero_rows=False, f32=False):
+    s = cases.summarize(t, nonzero_rows=nonzero_rows)
+    for k, v in s.items():
+        if f32 and k in ("rownorm", "proj"):
+            v = v.astype(np.float32)
+        out[f"{prefix}_{k}"] = v
+
+
+C2_FULL_TOKENS = 2048   # one 2048-position sequence of the config-2 batch
+C2_FULL_GI_TOKENS = 512  # tokens whose query is stored for the selection check
+
+
+def gen_c2_full(mem, name, seed=0):
+    """Config 2 at full table geometry (n_keys 512 -> 262144 slots of 1024
+    bf16, k_dim 512, 4 heads x top-32, query BatchNorm) on one 2048-token
+    sequence: the reference's bf16 layer forward + backward on CPU
+    (``pkm/memory.py:190-248``, bag through ``F.embedding_bag``).
+
+    Stored: the reference's indices (the selection the checker pins), loss,
+    fingerprints (``cases.summarize``) of the output and of every gradient,
+    and, for the first 512 tokens, the reference's bf16 query with its
+    ``get_indices`` scores and indices (the selection check on one query)."""
+    cfg = cases.CONFIG2
+    torch.manual_seed(0)
+    m = mem.HashingMemory(**cfg)
+    st = cases.pkm_state(cfg, seed)
+    m.load_state_dict(st)
+    m = m.to(torch.bfloat16).train()
+    x = cases.pkm_input((1, C2_FULL_TOKENS, cfg["input_dim"]), seed).to(torch.bfloat16).requires_grad_(True)
+    out = {"param_checksums": np.stack([cases.checksum(st[k]) for k in sorted(st)]),
+           "x_checksum": cases.checksum(x)}
+    with torch.no_grad():
+        q = m.query_proj(x.view(-1, cfg["input_dim"])[:C2_FULL_GI_TOKENS])
+        s, i = m.get_indices(q, cfg["mem_knn"])
+    m.query_proj.norm.reset_running_stats()  # the slice above updated them
+    out["gi_query"] = cases.bf16_bits(q)
+    out["gi_scores"] = _np(s)
+    out["gi_indices"] = i.numpy().astype(np.int32)
+    y, idx = m(x)
+    loss = (y.float() ** 2).sum()
+    loss.backward()
+    out["indices"] = idx.numpy().astype(np.int32)
+    out["loss"] = np.array(loss.item())
+    _put_summary(out, "out", y.view(C2_FULL_TOKENS, -1).float())
+    _put_summary(out, "x_grad", x.grad.view(C2_FULL_TOKENS, -1).float())
+    out["keys_grad"] = cases.bf16_bits(m.keys.grad)
+    _put_summary(out, "values_grad", m.values.weight.grad.float(), nonzero_rows=True, f32=True)
+    _put_summary(out, "wq_grad", m.query_proj.query_mlps[0].weight.grad.float())
+    out["bq_grad"] = _np(m.query_proj.query_mlps[0].bias.grad)
+    out["bn_w_grad"] = _np(m.query_proj.norm.weight.grad)
+    out["bn_b_grad"] = _np(m.query_proj.norm.bias.grad)
+    out["bn_running_mean"] = _np(m.query_proj.norm.running_mean)
+    out["bn_running_var"] = _np(m.query_proj.norm.running_var)
+    _put_summary(out, "wv_grad", m.value_proj.weight.grad.float())
+    out["bv_grad"] = _np(m.value_proj.bias.grad)
+    _put_summary(out, "ws_grad", m.swilu_projection.weight.grad.float())
+    out["bs_grad"] = _np(m.swilu_projection.bias.grad)
+    np.savez_compressed(os.path.join(HERE, name), **out)
+    print("wrote", name)
+
+
+def gen_fwpkm_c4(fw, name, score_type, seed=0):
+    """``forward_wo_past`` (``fwpkm/fwpkm.py:395-558``) at config-4 geometry
+    (``cases.FW_C4``: 262144 slots of 1024 fp32 values) on a 512-position
+    sequence in two chunks of 256, then the outer backward of
+    ``sum(out^2) + addr_loss`` through the double backward.  Stored: indices,
+    scores, per-token losses, the addressing loss, grad norms, the output,
+    and fingerprints of the final fast weights (the values as their change)
+    and of every outer gradient."""
+    torch.manual_seed(0)
+    m = fw.FastWeightProductKeyMemory(qk_score_type=score_type, **cases.FW_C4).train()
+    keys, values, q, ref_v = cases.fwpkm_c4_case(seed)
+    with torch.no_grad():
+        m.keys.copy_(keys)
+        m.values.copy_(values)
+        # the first chunk's selection on the initial keys (raw scores)
+        H, kd = cases.FW_C4["mem_heads"], cases.FW_C4["mem_k_dim"]
+        q0 = q[0, :cases.FW_C4_CHUNK].reshape(-1, H, kd)
+        s0, i0, _, _, _, _ = m.get_indices(q0, m.keys.float())
+    q = q.clone().requires_grad_(True)
+    ref_v = ref_v.clone().requires_grad_(True)
+    res = m(q, ref_v, None, cases.FW_C4_CHUNK)
+    loss = (res["output"] ** 2).sum() + res["addr_loss"]
+    loss.backward()
+    T = q.shape[1]
+    out = {
+        "keys_checksum": cases.checksum(keys), "values_checksum": cases.checksum(values),
+        "q_checksum": cases.checksum(q), "ref_v_checksum": cases.checksum(ref_v),
+        "gi0_scores": _np(s0).reshape(-1, cases.FW_C4["mem_topk"]),
+        "gi0_indices": i0.numpy().astype(np.int32).reshape(-1, cases.FW_C4["mem_topk"]),
+        "indices": res["indices"].numpy().astype(np.int32),
+        "scores": _np(res["scores"]),
+        "losses": _np(res["losses"]),
+        "addr_loss": np.array(res["addr_loss"].item()),
+        "grad_norms": np.array([g.item() for g in res["grad_norms"]]),
+        "output": _np(res["output"]),
+        "loss": np.array(loss.item()),
+    }
+    _put_summary(out, "final_keys", m.keys.detach())
+    _put_summary(out, "values_delta", m.values.detach() - values, nonzero_rows=True, f32=True)
+    _put_summary(out, "q_grad", q.grad.view(T, -1))
+    _put_summary(out, "ref_v_grad", ref_v.grad.view(T, -1))
+    _put_summary(out, "keys_grad", m.keys.grad)
+    _put_summary(out, "values_grad", m.values.grad, nonzero_rows=True, f32=True)
+    np.savez_compressed(os.path.join(HERE, name), **out)
+    print("wrote", name)
+
+
 def gen_addr_stats(name):
     """``compute_addr_stats`` of the reference's decoder layer
     (``modeling_qwen3pkm.py:447-471``) on ``cases.addr_case`` inputs; the
@@ -290,6 +398,9 @@ def main():
     gen_addr_stats("addr_stats.npz")
     gen_fwpkm_stream(fw, "fwpkm_stream_dot.npz", "dot_product")
     gen_fwpkm_stream(fw, "fwpkm_stream_idw.npz", "idw")
+    gen_c2_full(mem, "c2_full_bf16.npz")
+    gen_fwpkm_c4(fw, "fwpkm_c4_dot.npz", "dot_product")
+    gen_fwpkm_c4(fw, "fwpkm_c4_idw.npz", "idw")
 
 
 if __name__ == "__main__":
@@ -297,6 +408,12 @@ if __name__ == "__main__":
         for arg in sys.argv[1:]:
             if arg == "addr_stats":
                 gen_addr_stats("addr_stats.npz")
+            elif arg == "c2_full":
+                gen_c2_full(_import_ref()[0], "c2_full_bf16.npz")
+            elif arg == "fwpkm_c4":
+                fw = _import_ref()[2]
+                gen_fwpkm_c4(fw, "fwpkm_c4_dot.npz", "dot_product")
+                gen_fwpkm_c4(fw, "fwpkm_c4_idw.npz", "idw")
             elif arg == "fwpkm_stream":
                 fw = _import_ref()[2]
                 gen_fwpkm_stream(fw, "fwpkm_stream_dot.npz", "dot_product")

@@ -103,3 +103,67 @@ def test_product_path_refuses_cpu_tensors():
     from modelos_b200.pkm.xformer_embeddingbag import xformers_embedding_bag
     with pytest.raises(RuntimeError, match="CUDA"):
         xformers_embedding_bag(torch.zeros(2, 3, dtype=torch.long), torch.zeros(4, 16), torch.ones(2, 3))
+
+
+# ---------------------------------------------------------------------------
+# benchmarked geometries with the selection pinned to the reference's
+# (``tests/pinned.py``); the kernels are the CPU stand-ins
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("score_type,fname", [("dot_product", "fwpkm_c4_dot.npz"), ("idw", "fwpkm_c4_idw.npz")])
+def test_fwpkm_config4_geometry_pinned_matches_reference(cpu_kernels, monkeypatch, score_type, fname):
+    from pinned import check_summary, pin_fwpkm_selection
+
+    from modelos_b200 import _native
+    from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
+    d = np.load(os.path.join(GOLD, fname))
+    calls = pin_fwpkm_selection(monkeypatch, _native, torch.from_numpy(d["indices"].astype(np.int64)),
+                                cases.FW_C4_CHUNK)
+    m = FastWeightProductKeyMemory(qk_score_type=score_type, **cases.FW_C4).train()
+    keys, values, q, ref_v = cases.fwpkm_c4_case(0)
+    with torch.no_grad():
+        m.keys.copy_(keys)
+        m.values.copy_(values)
+    q.requires_grad_(True)
+    ref_v.requires_grad_(True)
+    res = m(q, ref_v, None, cases.FW_C4_CHUNK)
+    ((res["output"] ** 2).sum() + res["addr_loss"]).backward()
+    assert calls[0] == 2
+    T = q.shape[1]
+    assert rel_err(res["output"].detach().numpy(), d["output"]) < 1e-5
+    assert rel_err(res["losses"].numpy(), d["losses"]) < 1e-5
+    for t, key in ((m.keys.detach(), "final_keys"), (m.values.detach() - values, "values_delta"),
+                   (q.grad.view(T, -1), "q_grad"), (ref_v.grad.view(T, -1), "ref_v_grad"),
+                   (m.keys.grad, "keys_grad"), (m.values.grad, "values_grad")):
+        check_summary(t, d, key, 1e-5)
+
+
+def test_hashing_memory_config2_geometry_pinned_matches_reference(cpu_kernels, monkeypatch):
+    """The bf16 layer at config-2 geometry on one 2048-token sequence (the
+    query batch norm is torch's on CPU here; on the GPU it is the library's)."""
+    import torch.nn.functional as F
+    from pinned import check_summary, pin_pkm_selection
+
+    from modelos_b200 import _native
+    from modelos_b200.pkm import memory as mem
+    d = np.load(os.path.join(GOLD, "c2_full_bf16.npz"))
+
+    def torch_bn(self, x):
+        return F.batch_norm(x, self.running_mean, self.running_var, self.weight, self.bias, True, self.momentum,
+                            self.eps)
+
+    monkeypatch.setattr(mem.QueryBatchNorm, "forward", torch_bn)
+    pin_pkm_selection(monkeypatch, _native, torch.from_numpy(d["indices"].astype(np.int64)).view(-1, 32))
+    m = mem.HashingMemory(**cases.CONFIG2)
+    m.load_state_dict(cases.pkm_state(cases.CONFIG2, 0))
+    m = m.bfloat16().train()
+    x = cases.pkm_input((1, 2048, 1024), 0).bfloat16().requires_grad_(True)
+    y, _ = m(x)
+    loss = (y.float() ** 2).sum()
+    loss.backward()
+    assert abs(loss.item() - float(d["loss"])) <= 2e-2 * abs(float(d["loss"]))
+    check_summary(y.view(2048, -1).float(), d, "out", 2e-2)
+    check_summary(x.grad.view(2048, -1).float(), d, "x_grad", 2e-2)
+    check_summary(m.values.weight.grad.float(), d, "values_grad", 2e-2)
+    check_summary(m.query_proj.query_mlps[0].weight.grad.float(), d, "wq_grad", 2e-2)
+    kg = cases.from_bf16_bits(d["keys_grad"]).float().numpy()
+    assert rel_err(m.keys.grad.float().numpy(), kg) < 2e-2

@@ -203,3 +203,64 @@ def test_addr_stats_oracle_matches_reference(name):
     assert st["collision_ratio"] == ref[0]
     assert st["coverage_ratio"] == ref[1]
     assert abs(st["kld"] - ref[2]) <= 1e-5 * max(1.0, abs(ref[2]))
+
+
+def test_c2_full_geometry_selection_tie_aware():
+    """Config-2 geometry (262144 slots, bf16) on the reference's own query:
+    the oracle's selection agrees with the reference's ``get_indices`` up to
+    near-ties (bf16 score lists tie at the top-k boundary)."""
+    d = np.load(os.path.join(GOLD, "c2_full_bf16.npz"))
+    g = torch.Generator().manual_seed(0)
+    cfg = cases.CONFIG2
+    H, n, kd = cfg["mem_heads"], cfg["mem_n_keys"], cfg["mem_k_dim"]
+    # the keys are the first draw of ``cases.pkm_state`` (no need to draw the table)
+    keys = cases._u(g, (2 * H * n, kd // 2), 1 / np.sqrt(kd)).bfloat16().float().numpy()
+    q = cases.from_bf16_bits(d["gi_query"]).float().numpy()
+    res = po.pkm_get_indices(q, keys, H, 32, bf16=True)
+    bound = 4 * 2.0 ** -8 * np.maximum(np.abs(d["gi_scores"]).max(axis=1), 1e-3)
+    n_exact, n_tie, _ = compare_topk(res["scores"], res["indices"], d["gi_scores"],
+                                     d["gi_indices"].astype(np.int64), res["all_scores"], bound=bound, bf16=True)
+    # exact bf16 ties inside the lists are ordered differently on the two
+    # sides (lowest index first here), so rows pass through the near-tie rule
+    assert n_exact + n_tie == q.shape[0]
+
+
+@pytest.mark.parametrize("mode,fname", [("dot", "fwpkm_c4_dot.npz"), ("idw", "fwpkm_c4_idw.npz")])
+def test_c4_geometry_first_chunk_selection_tie_aware(mode, fname):
+    """Config-4 geometry, first chunk on the initial keys: the oracle's fp32
+    selection agrees with the reference's up to near-ties (the idw scores of
+    512 sub-keys pack into exact fp32 ties, ordered by torch's partial sort
+    on the reference's side and by the lowest index here)."""
+    d = np.load(os.path.join(GOLD, fname))
+    keys, values, q, ref_v = cases.fwpkm_c4_case(0)
+    np.testing.assert_allclose(cases.checksum(keys), d["keys_checksum"], rtol=1e-12)
+    H, kd, knn = 4, 512, 32
+    q0 = q[0, :cases.FW_C4_CHUNK].reshape(-1, kd).numpy()
+    res = po.pkm_get_indices(q0, keys.numpy(), H, knn, mode=mode)
+    bound = 8 * np.spacing(np.abs(d["gi0_scores"]).max(axis=1).astype(np.float32)).astype(np.float64)
+    n_exact, n_tie, _ = compare_topk(res["scores"], res["indices"], d["gi0_scores"],
+                                     d["gi0_indices"].astype(np.int64), res["all_scores"], bound=bound)
+    assert n_exact + n_tie == q0.shape[0] and n_exact > 0
+
+
+def test_torch_restatement_equals_reference_at_config2_geometry():
+    """``oracle/ref_torch.py`` (the timed reference arm of ``bench.py``) runs
+    the reference's CPU operators in the reference's order: at config-2
+    geometry its indices, loss, output and key gradient equal the
+    reference's bit for bit, and the value-table gradient's fingerprint to
+    the fixture's float32 storage."""
+    from oracle import ref_torch as rt
+    d = np.load(os.path.join(GOLD, "c2_full_bf16.npz"))
+    P = rt.params_from_state(cases.pkm_state(cases.CONFIG2, 0), torch.bfloat16)
+    x = cases.pkm_input((1, 2048, 1024), 0).bfloat16()
+    out, slots, loss = rt.layer_step(P, x, 4, 32, 512, "bn")
+    np.testing.assert_array_equal(slots.numpy(), d["indices"])
+    assert loss.item() == float(d["loss"])
+    s = cases.summarize(out.view(2048, -1).float(), rows_idx=d["out_rows_idx"])
+    for part in ("rownorm", "proj", "rows"):
+        np.testing.assert_array_equal(s[part], d["out_" + part])
+    np.testing.assert_array_equal(cases.bf16_bits(P["keys"].grad), d["keys_grad"])
+    s = cases.summarize(P["values"].grad.float(), rows_idx=d["values_grad_rows_idx"])
+    np.testing.assert_array_equal(s["rows"], d["values_grad_rows"])
+    assert rel_err(s["rownorm"], d["values_grad_rownorm"]) < 1e-7
+    np.testing.assert_array_equal(P["bq"].grad.float().numpy(), d["bq_grad"])

@@ -228,6 +228,32 @@ def test_product_topk_nonfinite_scores(dtype):
     assert s2[2].tolist() == list(range(knn))
     ref = po.product_topk(s[8:].float().numpy(), knn, bf16=dtype == torch.bfloat16)
     np.testing.assert_array_equal(idx[8:].numpy(), ref["indices"])
+    # rows with NaN but no -inf follow torch.topk's order (NaN above every
+    # number, +inf next), ties to the lowest index: both stages exactly
+    bf16 = dtype == torch.bfloat16
+    sf = s.float().numpy()
+    for r in (1, 2, 7):
+        lists = [_nan_first_topk(sf[r, p], np.arange(n), knn) for p in (0, 1)]
+        assert s1[r].tolist() == lists[0].tolist() and s2[r].tolist() == lists[1].tolist(), r
+        i1, i2 = np.meshgrid(lists[0], lists[1], indexing="ij")
+        sums = (sf[r, 0][i1] + sf[r, 1][i2]).astype(np.float32).reshape(-1)
+        if bf16:
+            sums = po.bf16_round(sums)
+        want = _nan_first_topk(sums, (i1 * n + i2).reshape(-1), knn)
+        assert idx[r].tolist() == want.tolist(), r
+    # every pair inf - inf (row 4): the reference's sums are NaN; here the
+    # pairs are summed as FLT_MAX - FLT_MAX = 0, so all tie and the lowest
+    # slots win (a documented departure in scores and order)
+    assert idx[4].tolist() == list(range(knn))
+    assert (top[4].float().cpu() == 0).all()
+
+
+def _nan_first_topk(vals: np.ndarray, ids: np.ndarray, k: int) -> np.ndarray:
+    """Ids of the k best values: NaN first, then descending, ties by lowest id."""
+    nan = np.isnan(vals)
+    v = np.where(nan, 0.0, vals.astype(np.float64))
+    order = np.lexsort((ids, -v, -nan.astype(np.int64)))
+    return ids[order[:k]]
 
 
 def test_score_grad_dense_ignores_out_of_range_slots():
