@@ -196,6 +196,22 @@ PKM_API int pkm_score_grad_dense(const int64_t* indices, const void* psw, const 
                                  int64_t rows, int64_t knn, int64_t n_keys, void* d_scores, void* stream);
 
 /*
+ * Score transform of the fast-weight memory over rows of `width` scores (one
+ * token's H*knn top-k scores, jointly over the heads).  Replaces
+ * FastWeightProductKeyMemory.score_transform (fwpkm/fwpkm.py:105-115):
+ *   x = scores / temperature;  mode 0: out = softmax(x) over the row,
+ *   mode 1: out = silu(x),  mode 2: out = relu(x);
+ * fp32 arithmetic, out in the scores' dtype.  width <= 512.
+ * The backward writes d_scores = d(out)/d(scores)^T grad_out; it reads `out`
+ * for the softmax and `scores` for silu / relu (the other may be NULL).
+ */
+PKM_API int pkm_score_transform_fwd(const void* scores, int dtype, int64_t rows, int64_t width,
+                                    double temperature, int mode, void* out, void* stream);
+PKM_API int pkm_score_transform_bwd(const void* scores, const void* out, const void* grad_out, int dtype,
+                                    int64_t rows, int64_t width, double temperature, int mode, void* grad_scores,
+                                    void* stream);
+
+/*
  * Data-parallel bag backward: K4 fused with the reduce-scatter of the table
  * gradient over NVLink.  Rank o owns table rows [o*shard_rows,
  * (o+1)*shard_rows) and holds a receive buffer [world][shard_rows][dim] (dtype

@@ -40,6 +40,8 @@ _SIGS = {
     "pkm_product_topk": ([_P, _I, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P], _I),
     "pkm_score_bwd_prep": ([_P, _P, _P, _I, _I64, _I64, _I64, _I64, _P, _P, _P], _I),
     "pkm_score_grad_dense": ([_P, _P, _P, _I, _I64, _I64, _I64, _P, _P], _I),
+    "pkm_score_transform_fwd": ([_P, _I, _I64, _I64, ctypes.c_double, _I, _P, _P], _I),
+    "pkm_score_transform_bwd": ([_P, _P, _P, _I, _I64, _I64, ctypes.c_double, _I, _P, _P], _I),
     "pkm_bag_bwd_sharded": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _I, _I64, _I, _P, _I, _P, _P,
                              ctypes.c_size_t, _P, _P], _I),
     "pkm_grad_shard_reduce": ([_P, _I, _I64, _I64, _I, _I, _I64, _P, ctypes.c_float, _I, _P], _I),
@@ -502,6 +504,40 @@ def score_grad_dense(indices: torch.Tensor, psw: Optional[torch.Tensor], dpsw: t
                                     _ptr(out), _stream(dpsw.device))
     _check(rc, "pkm_score_grad_dense")
     return out
+
+
+TRANSFORM_MODES = {"softmax": 0, "silu": 1, "relu": 2}
+
+
+def score_transform_fwd(scores: torch.Tensor, temperature: float, mode: str = "softmax") -> torch.Tensor:
+    """``score_transform`` of FwPKM on [rows, width] scores: softmax / silu /
+    relu of ``scores / temperature`` over each row, in the scores' dtype."""
+    assert scores.dim() == 2 and scores.is_contiguous()
+    _need_cuda(scores)
+    out = torch.empty_like(scores)
+    rc = lib().pkm_score_transform_fwd(_ptr(scores), DT[scores.dtype], scores.shape[0], scores.shape[1],
+                                       float(temperature), TRANSFORM_MODES[mode], _ptr(out),
+                                       _stream(scores.device))
+    _check(rc, "pkm_score_transform_fwd")
+    return out
+
+
+def score_transform_bwd(scores: Optional[torch.Tensor], out: Optional[torch.Tensor], grad_out: torch.Tensor,
+                        temperature: float, mode: str = "softmax") -> torch.Tensor:
+    """Gradient of ``score_transform_fwd`` w.r.t. the scores."""
+    grad_out = grad_out.contiguous()
+    assert grad_out.dim() == 2
+    ref = out if mode == "softmax" else scores
+    assert ref is not None and ref.shape == grad_out.shape and ref.is_contiguous()
+    if ref.dtype != grad_out.dtype:
+        grad_out = grad_out.to(ref.dtype)
+    _need_cuda(grad_out, ref)
+    ds = torch.empty_like(grad_out)
+    rc = lib().pkm_score_transform_bwd(_ptr(scores), _ptr(out), _ptr(grad_out), DT[grad_out.dtype],
+                                       grad_out.shape[0], grad_out.shape[1], float(temperature),
+                                       TRANSFORM_MODES[mode], _ptr(ds), _stream(grad_out.device))
+    _check(rc, "pkm_score_transform_bwd")
+    return ds
 
 
 # ---------------------------------------------------------------------------

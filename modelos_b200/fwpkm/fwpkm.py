@@ -119,6 +119,30 @@ class IdwScore(torch.autograd.Function):
         return (-grad / (1e-3 + dist.pow(2))) * (2 * dist)
 
 
+class ScoreTransform(torch.autograd.Function):
+    """``score_transform`` (``fwpkm/fwpkm.py:105-115``) on the library's
+    kernel: softmax / silu / relu of ``scores / temperature`` over each row
+    of ``[tokens, H*knn]`` (jointly over the heads), in the scores' dtype.
+    The outer backward needs this transform's first derivative only (the
+    inner updates differentiate the bag, not the weights' normalisation), so
+    the backward is one kernel and is not itself differentiable."""
+
+    @staticmethod
+    def forward(ctx, scores, temperature, mode):
+        s = scores.contiguous()
+        y = _native.score_transform_fwd(s, temperature, mode)
+        ctx.save_for_backward(s if mode != "softmax" else None, y if mode == "softmax" else None)
+        ctx.args = (temperature, mode)
+        return y
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, dy):
+        s, y = ctx.saved_tensors
+        temperature, mode = ctx.args
+        return _native.score_transform_bwd(s, y, dy, temperature, mode), None, None
+
+
 class FusedValueUpdate(torch.autograd.Function):
     """Value branch of ``update_fw`` (``fwpkm/fwpkm.py:274-367``) as one
     kernel pass: ``scaled = grad * scale / max(bincount(indices), 1)``,
@@ -208,14 +232,11 @@ class FastWeightProductKeyMemory(nn.Module):
         return out
 
     def score_transform(self, scores):
-        scores = scores / self.score_temperature
-        if self.score_nonlinear == "softmax":
-            return F.softmax(scores, dim=-1).type_as(scores)
-        if self.score_nonlinear == "silu":
-            return F.silu(scores).type_as(scores)
-        if self.score_nonlinear == "relu":
-            return F.relu(scores).type_as(scores)
-        raise NotImplementedError(f"Non-linear {self.score_nonlinear} not implemented for scores.")
+        """Normalise each row of ``scores`` [tokens, H*knn] (``fwpkm/fwpkm.py:105-115``)."""
+        if self.score_nonlinear not in ("softmax", "silu", "relu"):
+            raise NotImplementedError(f"Non-linear {self.score_nonlinear} not implemented for scores.")
+        rows = scores.reshape(-1, scores.shape[-1])
+        return ScoreTransform.apply(rows, float(self.score_temperature), self.score_nonlinear).view(scores.shape)
 
     def compute_marginal_entropy(self, M, epsilon=1e-8):
         """Entropy of the batch-mean of a top-k-thresholded softmax of M [N, K]."""

@@ -177,6 +177,27 @@ def route_combine(partial, seg_bag, seg_counts, groups, n_bags, out_dtype=None):
     return out.to(out_dtype or partial.dtype)
 
 
+def score_transform_fwd(scores, temperature, mode="softmax"):
+    x = scores / temperature
+    if mode == "softmax":
+        return torch.softmax(x, dim=-1).type_as(scores)
+    return (torch.nn.functional.silu(x) if mode == "silu" else torch.relu(x)).type_as(scores)
+
+
+def score_transform_bwd(scores, out, grad_out, temperature, mode="softmax"):
+    g = grad_out.to(out.dtype if mode == "softmax" else scores.dtype)
+    if mode == "softmax":
+        d = out * (g - (g * out).sum(-1, keepdim=True))
+    else:
+        x = scores / temperature
+        if mode == "silu":
+            s = torch.sigmoid(x)
+            d = g * s * (1 + x * (1 - s))
+        else:
+            d = g * (x > 0).to(g.dtype)
+    return d / temperature
+
+
 def read_device_errors(dev=None, reset=True):
     return 0
 
@@ -190,7 +211,8 @@ def install(monkeypatch):
     from modelos_b200 import _native
     for name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense",
                  "fw_update", "fw_update_bwd", "swiglu_fwd", "swiglu_bwd", "colsum", "segment_sum",
-                 "bag_bwd_ragged", "route_pack", "route_segments", "route_combine", "read_device_errors",
+                 "bag_bwd_ragged", "route_pack", "route_segments", "route_combine", "score_transform_fwd",
+                 "score_transform_bwd", "read_device_errors",
                  "check_device_errors"):
         monkeypatch.setattr(_native, name, globals()[name])
     return np

@@ -105,3 +105,17 @@ def test_new_entry_points_reject_bad_arguments():
     assert L.pkm_segment_sum(None, 0, 10, 16, None, None, 0, None, 0, None, 0, None, 0, None, None) == 0
     assert L.pkm_fw_update(None, None, 0, 0, 16, None, 0, c_d(1), c_d(0.1), c_d(0), 1, None, None, None, None,
                            None) == 0
+
+
+def test_score_transform_rejects_bad_arguments():
+    """The FwPKM score transform checks width, mode, temperature and dtype
+    before any device work."""
+    L = _native.lib()
+    fake = ctypes.c_void_p(256)
+    c_d = ctypes.c_double
+    assert L.pkm_score_transform_fwd(fake, 0, 4, 513, c_d(1.0), 0, fake, None) == 2   # wider than 512
+    assert L.pkm_score_transform_fwd(fake, 0, 4, 128, c_d(1.0), 3, fake, None) == 1   # unknown mode
+    assert L.pkm_score_transform_fwd(fake, 0, 4, 128, c_d(0.0), 0, fake, None) == 1   # temperature 0
+    assert L.pkm_score_transform_fwd(fake, 9, 4, 128, c_d(1.0), 0, fake, None) == 1   # dtype
+    assert L.pkm_score_transform_bwd(fake, None, fake, 0, 4, 128, c_d(1.0), 0, fake, None) == 1  # softmax needs out
+    assert L.pkm_score_transform_fwd(None, 0, 0, 128, c_d(1.0), 0, None, None) == 0   # empty

@@ -68,8 +68,14 @@ def test_config2_full_geometry_selection(c2):
     s_all = _native.subkey_scores(q, keys, 4)
     s_np = s_all.float().cpu().numpy()
     ref_s = po.subkey_scores(q.float().cpu().numpy(), keys.float().cpu().numpy(), 4, bf16=True)
-    ulp = np.spacing(np.abs(ref_s).astype(np.float32)) * 2.0 ** 16  # bf16 ulp of each score
-    assert (np.abs(s_np - ref_s) <= ulp).all(), float((np.abs(s_np - ref_s) / ulp).max())
+    # the tensor cores sum in another order than the sequential fp32 sum: the
+    # fp32 results differ by a few ulps of the partial sums, so after rounding
+    # a score differs by at most one bf16 ulp of itself, or (near zero, where
+    # the sum cancels) by a few fp32 ulps of the row's scale
+    ulp = np.spacing(np.abs(ref_s).astype(np.float32)) * 2.0 ** 16
+    scale = np.abs(ref_s).max(axis=-1, keepdims=True) * 2.0 ** -20
+    err = np.abs(s_np - ref_s)
+    assert (err <= ulp + scale).all(), float((err / (ulp + scale)).max())
     idx, top, _, _, _ = _native.product_topk(s_all, 32)
     o = po.product_topk(s_np, 32, bf16=True)
     np.testing.assert_array_equal(idx.cpu().numpy(), o["indices"])
@@ -102,7 +108,7 @@ def test_config2_full_geometry_layer_matches_reference(c2, monkeypatch):
     torch.cuda.synchronize()
     _native.check_device_errors()
     assert len(calls) == 1
-    np.testing.assert_array_equal(idx.view(2048, -1).cpu().numpy(), d["indices"])
+    np.testing.assert_array_equal(idx.view(d["indices"].shape).cpu().numpy(), d["indices"])
     assert abs(loss.item() - float(d["loss"])) <= BF16_TOL * abs(float(d["loss"]))
     check_summary(y.view(2048, -1).float(), d, "out", BF16_TOL)
     check_summary(x.grad.view(2048, -1).float(), d, "x_grad", BF16_TOL)
