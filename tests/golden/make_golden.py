@@ -336,6 +336,18 @@ def gen_fwpkm_c4(fw, name, score_type, seed=0):
         s0, i0, _, _, _, _ = m.get_indices(q0, m.keys.float())
     q = q.clone().requires_grad_(True)
     ref_v = ref_v.clone().requires_grad_(True)
+    # the inner gradients' norms in float64 as well: torch's fp32 norm on CPU
+    # (what the reference's ``grad_norms`` holds) is 0.2 % low on these
+    # 268M-element gradients, while a device reduction in fp32 is not
+    norms64 = []
+    update_fw = m.update_fw
+
+    def recording_update_fw(*a, **kw):
+        new, grads = update_fw(*a, **kw)
+        norms64.append([torch.linalg.vector_norm(g.detach(), dtype=torch.float64).item() for g in grads])
+        return new, grads
+
+    m.update_fw = recording_update_fw
     res = m(q, ref_v, None, cases.FW_C4_CHUNK)
     loss = (res["output"] ** 2).sum() + res["addr_loss"]
     loss.backward()
@@ -350,6 +362,7 @@ def gen_fwpkm_c4(fw, name, score_type, seed=0):
         "losses": _np(res["losses"]),
         "addr_loss": np.array(res["addr_loss"].item()),
         "grad_norms": np.array([g.item() for g in res["grad_norms"]]),
+        "grad_norms_f64": np.array(norms64).mean(axis=0),
         "output": _np(res["output"]),
         "loss": np.array(loss.item()),
     }

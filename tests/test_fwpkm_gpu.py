@@ -191,5 +191,5 @@ def test_score_transform_matches_torch(mode, dtype, width, temp):
     (dr,) = torch.autograd.grad(yr, r, dy.float())
     tol = 1e-5 if dtype == torch.float32 else 2e-2
     assert y.dtype == dtype
-    assert rel_err(y.float().cpu().numpy(), yr.detach().numpy()) < tol
+    assert rel_err(y.detach().float().cpu().numpy(), yr.detach().numpy()) < tol
     assert rel_err(dx.float().cpu().numpy(), dr.numpy()) < tol

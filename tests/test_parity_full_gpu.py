@@ -190,7 +190,9 @@ def test_config4_geometry_matches_reference(score_type, fname, monkeypatch):
     assert rel_err(res["scores"].detach().cpu().numpy(), d["scores"]) < tol
     assert rel_err(res["losses"].cpu().numpy(), d["losses"]) < tol
     assert abs(res["addr_loss"].item() - float(d["addr_loss"])) <= tol * abs(float(d["addr_loss"]))
-    assert rel_err(np.array([g.item() for g in res["grad_norms"]]), d["grad_norms"]) < tol
+    # the inner gradients' norms: against their float64 values on the
+    # reference's side (its own fp32 CPU reduction is 0.2 % low at this size)
+    assert rel_err(np.array([g.item() for g in res["grad_norms"]]), d["grad_norms_f64"]) < tol
     assert abs(loss.item() - float(d["loss"])) <= tol * abs(float(d["loss"]))
     check_summary(m.keys.detach(), d, "final_keys", tol)
     check_summary(m.values.detach() - values.to(DEV), d, "values_delta", tol)
