@@ -205,6 +205,61 @@ PKM_API int pkm_score_grad_dense(const int64_t* indices, const void* psw, const 
  * The backward writes d_scores = d(out)/d(scores)^T grad_out; it reads `out`
  * for the softmax and `scores` for silu / relu (the other may be NULL).
  */
+/*
+ * Dense bf16 GEMM on the tensor cores (fp32 accumulate):
+ *   C[b][m, n] = sum_k A[b][m, k] * B[b][n, k] + bias[n]      (b < batch)
+ * Replaces the nn.Linear / matmul calls of the layer: the query projection
+ * (pkm/memory.py:317-349), the SwiLU and value projections (:143-149,
+ * 226-229) with their data and weight gradients, and the dense scoring
+ * backward (:267-268).  A is a row-major bf16 matrix [a_rows, a_cols] with
+ * row pitch lda elements, read K-major (A[m, k] at row m, column k) or
+ * MN-major (A[m, k] at row k, column m); B likewise with n in place of m.
+ * Batch b reads A shifted by (a_batch_x columns, a_batch_y rows), B by
+ * (b_batch_x, b_batch_y), and writes C + b * c_batch_stride (row pitch ldc).
+ * bias may be NULL.  C is bf16 or fp32.  K must be a multiple of 64 unless
+ * it spans the operands' whole K extent (then the tail reads zeros); N a
+ * multiple of 8, the column batch offsets multiples of 8, bases and row
+ * pitches 16-byte aligned.  When the output tiles cannot fill the GPU the K
+ * range is split and summed in a fixed order; pkm_gemm_workspace gives the
+ * bytes of fp32 partials that needs (0 otherwise), the caller provides them.
+ */
+PKM_API int pkm_gemm_workspace(int64_t batch, int64_t M, int64_t N, int64_t K, size_t* bytes);
+PKM_API int pkm_gemm_bf16(const void* A, int a_mn_major, int64_t a_rows, int64_t a_cols, int64_t lda,
+                          const void* B, int b_mn_major, int64_t b_rows, int64_t b_cols, int64_t ldb,
+                          int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_batch_x, int64_t a_batch_y,
+                          int64_t b_batch_x, int64_t b_batch_y, const void* bias, int bias_dtype, void* C,
+                          int c_dtype, int64_t ldc, int64_t c_batch_stride, void* workspace,
+                          size_t workspace_bytes, uint32_t* dev_err, void* stream);
+/*
+ * The SwiLU-gated value projection's GEMMs with the gate in their epilogue
+ * (pkm/memory.py:226-229, value_proj(output * silu(swilu_projection(input)))):
+ *   forward:  h = x @ ws^T + bs  and  z = a * silu(h)     (one GEMM, M x N)
+ *   backward: dz = dy @ wv,  da = dz * silu(h),  dh = dz * a * silu'(h)
+ * x [M, K] (pitch ldx), ws [N, K], a / h / z / da / dh [M, N] (pitch ld),
+ * dy [M, K] (pitch ldy), wv [K, N] (pitch ldw); all bf16, every intermediate
+ * rounded to bf16 where torch's eager ops round it (the same values as
+ * pkm_gemm_bf16 followed by pkm_swiglu_fwd / pkm_swiglu_bwd).  bs may be
+ * NULL; da may be NULL.  The bias gradient of ws is the column sum of dh
+ * (pkm_colsum).  Constraints as pkm_gemm_bf16; no workspace.
+ */
+PKM_API int pkm_gemm_swiglu_fwd(const void* x, int64_t ldx, const void* ws, const void* bs, int bias_dtype,
+                                const void* a, int64_t M, int64_t N, int64_t K, void* h, void* z, int64_t ld,
+                                uint32_t* dev_err, void* stream);
+PKM_API int pkm_gemm_swiglu_bwd(const void* dy, int64_t ldy, const void* wv, int64_t ldw, const void* a,
+                                const void* h, int64_t M, int64_t N, int64_t K, void* dh, void* da, int64_t ld,
+                                uint32_t* dev_err, void* stream);
+
+/*
+ * Test hook, no counterpart in the reference: the number of polls each
+ * pipeline wait of pkm_gemm_bf16 may take before it gives up, sets
+ * PKM_DEVERR_TIMEOUT in the error word and returns (a negative value
+ * restores the default, 2^24; 0 gives up without polling).  Copies and MMAs
+ * already in flight are still awaited with the default limit and TMEM is
+ * released, so a short limit only ends the kernel early; its output is then
+ * undefined.  Read by later launches.
+ */
+PKM_API int pkm_debug_set_wait_limit(int64_t polls);
+
 PKM_API int pkm_score_transform_fwd(const void* scores, int dtype, int64_t rows, int64_t width,
                                     double temperature, int mode, void* out, void* stream);
 PKM_API int pkm_score_transform_bwd(const void* scores, const void* out, const void* grad_out, int dtype,

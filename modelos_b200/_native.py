@@ -41,6 +41,12 @@ _SIGS = {
     "pkm_score_bwd_prep": ([_P, _P, _P, _I, _I64, _I64, _I64, _I64, _P, _P, _P], _I),
     "pkm_score_grad_dense": ([_P, _P, _P, _I, _I64, _I64, _I64, _P, _P], _I),
     "pkm_score_transform_fwd": ([_P, _I, _I64, _I64, ctypes.c_double, _I, _P, _P], _I),
+    "pkm_gemm_workspace": ([_I64, _I64, _I64, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
+    "pkm_gemm_bf16": ([_P, _I, _I64, _I64, _I64, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                       _I64, _I64, _P, _I, _P, _I, _I64, _I64, _P, ctypes.c_size_t, _P, _P], _I),
+    "pkm_debug_set_wait_limit": ([_I64], _I),
+    "pkm_gemm_swiglu_fwd": ([_P, _I64, _P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P], _I),
+    "pkm_gemm_swiglu_bwd": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P], _I),
     "pkm_score_transform_bwd": ([_P, _P, _P, _I, _I64, _I64, ctypes.c_double, _I, _P, _P], _I),
     "pkm_bag_bwd_sharded": ([_P, _P, _I, _P, _I, _P, _I64, _I64, _I64, _I64, _P, _I, _I, _I64, _I, _P, _I, _P, _P,
                              ctypes.c_size_t, _P, _P], _I),
@@ -504,6 +510,95 @@ def score_grad_dense(indices: torch.Tensor, psw: Optional[torch.Tensor], dpsw: t
                                     _ptr(out), _stream(dpsw.device))
     _check(rc, "pkm_score_grad_dense")
     return out
+
+
+# ---------------------------------------------------------------------------
+# dense GEMM on the tensor cores
+# ---------------------------------------------------------------------------
+def gemm_workspace(batch: int, M: int, N: int, K: int) -> int:
+    n = ctypes.c_size_t(0)
+    _check(lib().pkm_gemm_workspace(batch, M, N, K, ctypes.byref(n)), "pkm_gemm_workspace")
+    return int(n.value)
+
+
+def _mat(t: torch.Tensor):
+    """(rows, cols, row pitch) of a 2-D row-major view (unit column stride)."""
+    assert t.dim() == 2 and t.stride(1) == 1 and t.dtype == torch.bfloat16, "GEMM operands: 2-D bf16, unit column stride"
+    return t.shape[0], t.shape[1], t.stride(0)
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, bias=None,
+         out: Optional[torch.Tensor] = None, out_dtype=torch.bfloat16, batch: int = 1, M: Optional[int] = None,
+         N: Optional[int] = None, K: Optional[int] = None, a_batch=(0, 0), b_batch=(0, 0),
+         c_batch_stride: int = 0) -> torch.Tensor:
+    """``C[m, n] = sum_k A[m, k] B[n, k] (+ bias[n])`` on the tensor cores.
+
+    ``a`` is read K-major (``a[m, k]``) or, with ``a_mn``, MN-major
+    (``a[k, m]``); ``b`` likewise (``b[n, k]`` or ``b[k, n]``).  So
+    ``x @ w.T`` is ``gemm(x, w)``, ``dy @ w`` is ``gemm(dy, w, b_mn=True)``
+    and ``dy.T @ x`` is ``gemm(dy, x, a_mn=True, b_mn=True)``.  For a batch
+    of GEMMs, ``a_batch`` / ``b_batch`` are the (column, row) shifts of one
+    batch's operand region and ``c_batch_stride`` its output offset; ``out``
+    must then be given, as must M, N, K."""
+    ar, ac, lda = _mat(a)
+    br, bc, ldb = _mat(b)
+    _need_cuda(a, b, bias, out)
+    if M is None:
+        M = ac if a_mn else ar
+    if K is None:
+        K = ar if a_mn else ac
+    if N is None:
+        N = bc if b_mn else br
+    if out is None:
+        assert batch == 1
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    assert out.stride(-1) == 1
+    ldc = out.stride(-2) if out.dim() >= 2 else N
+    ws_bytes = gemm_workspace(batch, M, N, K)
+    ws = torch.empty((max(ws_bytes, 16) // 4,), dtype=torch.float32, device=a.device) if ws_bytes else None
+    rc = lib().pkm_gemm_bf16(_ptr(a), int(a_mn), ar, ac, lda, _ptr(b), int(b_mn), br, bc, ldb, batch, M, N, K,
+                             a_batch[0], a_batch[1], b_batch[0], b_batch[1], _ptr(bias),
+                             DT[bias.dtype] if bias is not None else 0, _ptr(out), DT[out.dtype], ldc,
+                             c_batch_stride, _ptr(ws), ws_bytes, _ptr(err_word(a.device)), _stream(a.device))
+    _check(rc, "pkm_gemm_bf16")
+    return out
+
+
+def gemm_swiglu_fwd(x: torch.Tensor, ws: torch.Tensor, bs: Optional[torch.Tensor], a: torch.Tensor):
+    """``h = x @ ws.T + bs`` and ``z = a * silu(h)`` in one tensor-core GEMM:
+    returns (h, z)."""
+    M, K = x.shape
+    N = ws.shape[0]
+    assert ws.shape == (N, K) and a.shape == (M, N)
+    x, ws, a = x.contiguous(), ws.contiguous(), a.contiguous()
+    _need_cuda(x, ws, bs, a)
+    h = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    z = torch.empty_like(h)
+    rc = lib().pkm_gemm_swiglu_fwd(_ptr(x), K, _ptr(ws), _ptr(bs), DT[bs.dtype] if bs is not None else 0, _ptr(a),
+                                   M, N, K, _ptr(h), _ptr(z), N, _ptr(err_word(x.device)), _stream(x.device))
+    _check(rc, "pkm_gemm_swiglu_fwd")
+    return h, z
+
+
+def gemm_swiglu_bwd(dy: torch.Tensor, wv: torch.Tensor, a: torch.Tensor, h: torch.Tensor, need_da: bool = True):
+    """``dz = dy @ wv`` with the gate's backward in the epilogue: returns (da|None, dh)."""
+    M, K = dy.shape
+    N = wv.shape[1]
+    assert wv.shape == (K, N) and a.shape == (M, N) and h.shape == (M, N)
+    dy, wv, a, h = dy.contiguous(), wv.contiguous(), a.contiguous(), h.contiguous()
+    _need_cuda(dy, wv, a, h)
+    dh = torch.empty((M, N), dtype=torch.bfloat16, device=dy.device)
+    da = torch.empty_like(dh) if need_da else None
+    rc = lib().pkm_gemm_swiglu_bwd(_ptr(dy), K, _ptr(wv), N, _ptr(a), _ptr(h), M, N, K, _ptr(dh), _ptr(da), N,
+                                   _ptr(err_word(dy.device)), _stream(dy.device))
+    _check(rc, "pkm_gemm_swiglu_bwd")
+    return da, dh
+
+
+def set_wait_limit(polls: int):
+    """Test hook: the pipeline wait limit of the GEMM kernel (negative: the
+    default; 0: every wait gives up at once)."""
+    _check(lib().pkm_debug_set_wait_limit(int(polls)), "pkm_debug_set_wait_limit")
 
 
 TRANSFORM_MODES = {"softmax": 0, "silu": 1, "relu": 2}

@@ -11,15 +11,20 @@ runs on the sm_100a kernels:
   (token, head) (K2, ``pkm_product_topk``),
 * the weighted bag over the value table (K3/K4 via ``xFormerEmbeddingBag``),
 * and, in the backward, the softmax gradient scattered onto the dense
-  sub-score grid (``pkm_score_grad_dense``) followed by two GEMMs per
-  (head, half) for the query and key gradients.
+  sub-score grid (``pkm_score_grad_dense``) followed by two batched GEMMs
+  over the (head, half) groups for the query and key gradients.
 
 The query projection, the SwiLU projection and the value projection keep
-their ``nn.Linear`` modules and run as cuBLAS GEMMs; the SwiGLU gate between
-them and the bias gradients run on the library's kernels
-(``SwiGLUProjection``), and the query batch norm keeps ``nn.BatchNorm1d``'s
-parameters and buffers and runs on the library's batch-normalisation
-kernels (``QueryBatchNorm``).
+their ``nn.Linear`` modules (same parameters) and run, with their data and
+weight gradients, on the library's tensor-core GEMM in bf16
+(``pkm_gemm_bf16``: either operand K-major or MN-major, so no gradient
+transposes a tensor); the SwiGLU gate between them and the bias gradients
+run on the library's kernels (``SwiGLUProjection``), and the query batch
+norm keeps ``nn.BatchNorm1d``'s parameters and buffers and runs on the
+library's batch-normalisation kernels (``QueryBatchNorm``).  The scoring
+backward's two GEMMs per (head, half) are one batched call each.  fp32
+layers (the CPU-runnable parity configuration) use torch's fp32 GEMMs for
+these dense products.
 """
 from __future__ import annotations
 
@@ -91,6 +96,22 @@ def _score_backward(ctx, d_scores, psw):
     N = R // H
     dS = _native.score_grad_dense(idx, psw, d_scores.to(query.dtype), n).view(N, H * 2, n)
     dq = dk = None
+    G = H * 2
+    if _tc(query, keys) and half % 8 == 0 and n % 8 == 0 and (n % 64 == 0 or G == 1):
+        # batched GEMMs over the H*2 (head, half) groups on the tensor cores,
+        # each group's operands addressed by coordinate offsets (no copies)
+        dS2 = dS.view(N, G * n)
+        if ctx.needs_input_grad[0]:
+            dq = torch.empty((N, G * half), dtype=query.dtype, device=query.device)
+            _native.gemm(dS2, keys.view(G * n, half), b_mn=True, batch=G, M=N, N=half, K=n, a_batch=(n, 0),
+                         b_batch=(0, n), out=dq, c_batch_stride=half)
+            dq = dq.view(R, kd)
+        if ctx.needs_input_grad[1]:
+            dk = torch.empty((G * n, half), dtype=keys.dtype, device=keys.device)
+            _native.gemm(dS2, query.view(N, G * half), a_mn=True, b_mn=True, batch=G, M=n, N=half, K=N,
+                         a_batch=(n, 0), b_batch=(half, 0), out=dk, c_batch_stride=n * half)
+            dk = dk.view(keys.shape)
+        return dq, dk
     if ctx.needs_input_grad[0]:
         # one strided batched GEMM over the H*2 (head, half) blocks, written
         # straight into the token-major [N, H, 2, half] layout of the query
@@ -147,41 +168,79 @@ class ProductKeyLookup(torch.autograd.Function):
         return dq, dk, None, None
 
 
+# ---------------------------------------------------------------------------
+# dense projections: bf16 on the library's tensor-core GEMM (pkm_gemm_bf16),
+# other dtypes (the fp32 parity configuration) on torch's GEMMs
+# ---------------------------------------------------------------------------
+def _tc(*ts) -> bool:
+    return all(t.dtype == torch.bfloat16 and t.is_cuda for t in ts)
+
+
+def linear(x, w, b=None):
+    """``x @ w.T + b`` (``F.linear``)."""
+    if _tc(x, w) and w.shape[0] % 8 == 0:
+        return _native.gemm(x.contiguous(), w.contiguous(), bias=b)
+    return F.linear(x, w, b)
+
+
+def matmul_nn(dy, w):
+    """``dy @ w`` (the data gradient of ``linear``)."""
+    if _tc(dy, w) and w.shape[1] % 8 == 0:
+        return _native.gemm(dy.contiguous(), w.contiguous(), b_mn=True)
+    return dy.mm(w)
+
+
+def matmul_tn(dy, x, out_dtype=None):
+    """``dy.T @ x`` (the weight gradient of ``linear``)."""
+    if _tc(dy, x) and x.shape[1] % 8 == 0:
+        return _native.gemm(dy.contiguous(), x.contiguous(), a_mn=True, b_mn=True, out_dtype=out_dtype or x.dtype)
+    return dy.t().mm(x)
+
+
 class LinearColsumBias(torch.autograd.Function):
-    """``F.linear(x, w, b)`` whose backward reduces the bias gradient with the
-    library's column-sum kernel (torch's reduction is several times slower
-    on [16384, 2048] activations); the GEMMs stay cuBLAS."""
+    """``F.linear(x, w, b)`` on the library's GEMM (bf16), with the bias
+    gradient reduced by the library's column-sum kernel."""
 
     @staticmethod
     def forward(ctx, x, w, b):
         ctx.save_for_backward(x, w)
-        ctx.b_dtype = b.dtype
-        return F.linear(x, w, b)
+        ctx.b_dtype = None if b is None else b.dtype
+        return linear(x, w, b)
 
     @staticmethod
     def backward(ctx, dy):
         x, w = ctx.saved_tensors
         dy = dy.contiguous()
-        dx = dy.mm(w) if ctx.needs_input_grad[0] else None
-        dw = dy.t().mm(x) if ctx.needs_input_grad[1] else None
-        db = _native.colsum(dy, ctx.b_dtype) if ctx.needs_input_grad[2] else None
+        dx = matmul_nn(dy, w) if ctx.needs_input_grad[0] else None
+        dw = matmul_tn(dy, x, w.dtype) if ctx.needs_input_grad[1] else None
+        db = _native.colsum(dy, ctx.b_dtype) if ctx.b_dtype is not None and ctx.needs_input_grad[2] else None
         return dx, dw, db
 
 
 class SwiGLUProjection(torch.autograd.Function):
     """``value_proj(a * silu(swilu_projection(x)))`` of ``HashingMemory.forward``
-    (``pkm/memory.py:226-229``): the two projections are cuBLAS GEMMs; the
-    gate runs as one pass each way (``pkm_swiglu_fwd`` / ``pkm_swiglu_bwd``,
-    the latter also summing the gate projection's bias gradient) and the
-    output projection's bias gradient as one column-sum pass."""
+    (``pkm/memory.py:226-229``): both projections and their gradients on the
+    library's GEMM (bf16), the gate in the epilogues of the gate projection's
+    GEMM (forward: h and z) and of the value projection's data-gradient GEMM
+    (backward: da and dh); the bias gradients are column sums.  Other
+    dtypes run the gate as one pass each way (``pkm_swiglu_fwd`` /
+    ``pkm_swiglu_bwd``)."""
+
+    @staticmethod
+    def _fused(a, x, ws, wv):
+        # the gate rides in the GEMM epilogues (bf16, N a multiple of 8)
+        return _tc(a, x, ws, wv) and ws.shape[0] % 8 == 0 and a.shape == (x.shape[0], ws.shape[0])
 
     @staticmethod
     def forward(ctx, a, x, ws, bs, wv, bv):
-        h = F.linear(x, ws, bs)
-        z = _native.swiglu_fwd(a, h)
+        if SwiGLUProjection._fused(a, x, ws, wv):
+            h, z = _native.gemm_swiglu_fwd(x, ws, bs, a)
+        else:
+            h = linear(x, ws, bs)
+            z = _native.swiglu_fwd(a, h)
         ctx.save_for_backward(a, x, h, z, ws, wv)
         ctx.bias_dtypes = (None if bs is None else bs.dtype, None if bv is None else bv.dtype)
-        return F.linear(z, wv, bv)
+        return linear(z, wv, bv)
 
     @staticmethod
     def backward(ctx, dy):
@@ -189,11 +248,16 @@ class SwiGLUProjection(torch.autograd.Function):
         need_a, need_x, need_ws, need_bs, need_wv, need_bv = ctx.needs_input_grad
         dy = dy.contiguous()
         dbv = _native.colsum(dy, ctx.bias_dtypes[1]) if need_bv else None
-        dwv = dy.t().mm(z) if need_wv else None
-        dz = dy.mm(wv)
-        da, dh, dbs = _native.swiglu_bwd(dz, a, h, need_da=need_a, bias_dtype=ctx.bias_dtypes[0] if need_bs else None)
-        dws = dh.t().mm(x) if need_ws else None
-        dx = dh.mm(ws) if need_x else None
+        dwv = matmul_tn(dy, z, wv.dtype) if need_wv else None
+        if SwiGLUProjection._fused(a, x, ws, wv):
+            da, dh = _native.gemm_swiglu_bwd(dy, wv, a, h, need_da=need_a)
+            dbs = _native.colsum(dh, ctx.bias_dtypes[0]) if need_bs and ctx.bias_dtypes[0] is not None else None
+        else:
+            dz = matmul_nn(dy, wv)
+            da, dh, dbs = _native.swiglu_bwd(dz, a, h, need_da=need_a,
+                                             bias_dtype=ctx.bias_dtypes[0] if need_bs else None)
+        dws = matmul_tn(dh, x, ws.dtype) if need_ws else None
+        dx = matmul_nn(dh, ws) if need_x else None
         return da, dx, dws, dbs, dwv, dbv
 
 
@@ -457,8 +521,8 @@ class QueryMLP(nn.Module):
         input = input.contiguous().view(-1, self.input_dim) if input.dim() > 2 else input
         bs = len(input)
         mlp = self.query_mlps
-        if len(mlp) == 1 and isinstance(mlp[0], nn.Linear) and mlp[0].bias is not None:
-            # single projection: its bias gradient is the library's column sum
+        if len(mlp) == 1 and isinstance(mlp[0], nn.Linear):
+            # single projection: the library's GEMM, bias gradient by column sum
             query = LinearColsumBias.apply(input, mlp[0].weight, mlp[0].bias)
         else:
             query = mlp(input)
