@@ -231,6 +231,21 @@ PKM_API int pkm_gemm_bf16(const void* A, int a_mn_major, int64_t a_rows, int64_t
                           int c_dtype, int64_t ldc, int64_t c_batch_stride, void* workspace,
                           size_t workspace_bytes, uint32_t* dev_err, void* stream);
 /*
+ * fp32 GEMM on the CUDA cores, same operand views and batching as
+ * pkm_gemm_bf16 (no bias, fp32 C, any K, no workspace):
+ *   C[b][m, n] = sum_k A[b][m, k] * B[b][n, k]
+ * Replaces the fp32 einsum / cdist gradients of the fast-weight memory's
+ * sub-key scores (fwpkm/fwpkm.py:853-869: dS @ K and dS^T @ Q per (head, half)
+ * group) and their second derivatives.  Elements outside the operands' row
+ * and column extents read as 0.
+ */
+PKM_API int pkm_gemm_f32(const float* A, int a_mn_major, int64_t a_rows, int64_t a_cols, int64_t lda,
+                         const float* B, int b_mn_major, int64_t b_rows, int64_t b_cols, int64_t ldb,
+                         int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_batch_x, int64_t a_batch_y,
+                         int64_t b_batch_x, int64_t b_batch_y, float* C, int64_t ldc, int64_t c_batch_stride,
+                         void* stream);
+
+/*
  * The SwiLU-gated value projection's GEMMs with the gate in their epilogue
  * (pkm/memory.py:226-229, value_proj(output * silu(swilu_projection(input)))):
  *   forward:  h = x @ ws^T + bs  and  z = a * silu(h)     (one GEMM, M x N)

@@ -45,6 +45,8 @@ _SIGS = {
     "pkm_gemm_bf16": ([_P, _I, _I64, _I64, _I64, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                        _I64, _I64, _P, _I, _P, _I, _I64, _I64, _P, ctypes.c_size_t, _P, _P], _I),
     "pkm_debug_set_wait_limit": ([_I64], _I),
+    "pkm_gemm_f32": ([_P, _I, _I64, _I64, _I64, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                      _I64, _I64, _P, _I64, _I64, _P], _I),
     "pkm_gemm_swiglu_fwd": ([_P, _I64, _P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P], _I),
     "pkm_gemm_swiglu_bwd": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P], _I),
     "pkm_score_transform_bwd": ([_P, _P, _P, _I, _I64, _I64, ctypes.c_double, _I, _P, _P], _I),
@@ -561,6 +563,30 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
                              DT[bias.dtype] if bias is not None else 0, _ptr(out), DT[out.dtype], ldc,
                              c_batch_stride, _ptr(ws), ws_bytes, _ptr(err_word(a.device)), _stream(a.device))
     _check(rc, "pkm_gemm_bf16")
+    return out
+
+
+def gemm_f32(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False,
+             out: Optional[torch.Tensor] = None, batch: int = 1, M: Optional[int] = None, N: Optional[int] = None,
+             K: Optional[int] = None, a_batch=(0, 0), b_batch=(0, 0), c_batch_stride: int = 0) -> torch.Tensor:
+    """fp32 ``C[m, n] = sum_k A[m, k] B[n, k]`` on the CUDA cores; the same
+    operand views and batching as ``gemm``."""
+    for t in (a, b):
+        assert t.dim() == 2 and t.stride(1) == 1 and t.dtype == torch.float32, "fp32 GEMM operands: 2-D, unit stride"
+    _need_cuda(a, b, out)
+    ar, ac, lda = a.shape[0], a.shape[1], a.stride(0)
+    br, bc, ldb = b.shape[0], b.shape[1], b.stride(0)
+    M = M if M is not None else (ac if a_mn else ar)
+    K = K if K is not None else (ar if a_mn else ac)
+    N = N if N is not None else (bc if b_mn else br)
+    if out is None:
+        assert batch == 1
+        out = torch.empty((M, N), dtype=torch.float32, device=a.device)
+    assert out.dtype == torch.float32 and out.stride(-1) == 1
+    rc = lib().pkm_gemm_f32(_ptr(a), int(a_mn), ar, ac, lda, _ptr(b), int(b_mn), br, bc, ldb, batch, M, N, K,
+                            a_batch[0], a_batch[1], b_batch[0], b_batch[1], _ptr(out), out.stride(-2), c_batch_stride,
+                            _stream(a.device))
+    _check(rc, "pkm_gemm_f32")
     return out
 
 

@@ -12,9 +12,11 @@ loss back-propagates through every update (``forward_wo_past``, ``:395-558``).
 Kernel mapping:
 
 * sub-key scores, dot or idw (K1, ``pkm_subkey_scores``; idw is built from
-  the distance mode), bit-exact in fp32; their backward is written with
-  differentiable tensor ops so second derivatives exist for the inner
-  updates, and reads the same saved tensors as the reference's autograd;
+  the distance mode), bit-exact in fp32; their backward's grouped products
+  run on the library's fp32 GEMM (``pkm_gemm_f32``) inside an autograd node
+  that is differentiable once more (second derivatives for the inner
+  updates), reading the same saved tensors as the reference's autograd;
+* the score transform (joint softmax over H*knn, ``pkm_score_transform``);
 * dual / cartesian top-k (K2, ``pkm_product_topk``), ties to the lowest index;
 * the bag forward, its sorted-segment backward and the double-backward
   (K3 / K4 / K5, through ``xformer_embeddingbag_grad_wrapper``).
@@ -41,13 +43,93 @@ def l2norm(x: torch.FloatTensor, dim: int = -1, eps: float = 1e-6):
     return x * inv_norm
 
 
+def _group_mm(dS, q, k, H, want_dq=True, want_dk=True):
+    """Per (head, half) group g: ``dS_g @ K_g`` and ``dS_g^T @ Q_g``, for
+    sub-key scores ``S_g = Q_g @ K_g^T`` (``fwpkm/fwpkm.py:861``).  dS [R, 2, n]
+    (row = token*H + head), q [R, k_dim], k [2*H*n, k_dim/2]; the groups are
+    addressed as column / row offsets of the 2-D views, no copies.  fp32 on
+    the library's fp32 GEMM; other dtypes as the einsums."""
+    R, kd = q.shape
+    half, G = kd // 2, 2 * H
+    T = R // H
+    n = k.shape[0] // G
+    if not (dS.dtype == q.dtype == k.dtype == torch.float32 and dS.is_cuda):
+        d = dS.view(T, H, 2, n)
+        dq = torch.einsum("thpn,hpnd->thpd", d, k.view(H, 2, n, half)).reshape(R, kd) if want_dq else None
+        dk = torch.einsum("thpn,thpd->hpnd", d, q.view(T, H, 2, half)).reshape(k.shape) if want_dk else None
+        return dq, dk
+    dS2 = dS.contiguous().view(T, G * n)
+    q2 = q.contiguous().view(T, G * half)
+    k2 = k.contiguous().view(G * n, half)
+    dq = dk = None
+    if want_dq:
+        dq = torch.empty((T, G * half), dtype=q.dtype, device=q.device)
+        _native.gemm_f32(dS2, k2, b_mn=True, batch=G, M=T, N=half, K=n, a_batch=(n, 0), b_batch=(0, n), out=dq,
+                         c_batch_stride=half)
+        dq = dq.view(R, kd)
+    if want_dk:
+        dk = torch.empty((G * n, half), dtype=k.dtype, device=k.device)
+        _native.gemm_f32(dS2, q2, a_mn=True, b_mn=True, batch=G, M=n, N=half, K=T, a_batch=(n, 0),
+                         b_batch=(half, 0), out=dk, c_batch_stride=n * half)
+        dk = dk.view(k.shape)
+    return dq, dk
+
+
+def _group_scores(a, k, H):
+    """``S_g = A_g @ K_g^T`` per (head, half) group for a query-shaped a
+    [R, k_dim] and key-shaped k: [R, 2, n] (the scoring product itself, as a
+    GEMM; used for second derivatives)."""
+    R, kd = a.shape
+    half, G = kd // 2, 2 * H
+    T = R // H
+    n = k.shape[0] // G
+    if not (a.dtype == k.dtype == torch.float32 and a.is_cuda):
+        return torch.einsum("thpd,hpnd->thpn", a.view(T, H, 2, half), k.view(H, 2, n, half)).reshape(R, 2, n)
+    out = torch.empty((T, G * n), dtype=a.dtype, device=a.device)
+    _native.gemm_f32(a.contiguous().view(T, G * half), k.contiguous().view(G * n, half), batch=G, M=T, N=n, K=half,
+                     a_batch=(half, 0), b_batch=(0, n), out=out, c_batch_stride=n)
+    return out.view(R, 2, n)
+
+
+class GroupMM(torch.autograd.Function):
+    """``(dS_g @ K_g, dS_g^T @ Q_g)`` over the (head, half) groups: the
+    gradients of the sub-key products, differentiable once more in
+    (dS, q, k) for the inner updates' ``create_graph`` (the outer backward
+    takes the second derivative through them)."""
+
+    @staticmethod
+    def forward(ctx, dS, q, k, H):
+        ctx.save_for_backward(dS, q, k)
+        ctx.H = H
+        dq, dk = _group_mm(dS, q, k, H)
+        return dq, dk
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, g_dq, g_dk):
+        dS, q, k = ctx.saved_tensors
+        H = ctx.H
+        d_dS = d_q = d_k = None
+        # dq = dS @ K:  d(dS) += g_dq @ K^T,  dK += dS^T @ g_dq
+        # dk = dS^T @ Q: d(dS) += Q @ g_dk^T,  dQ += dS @ g_dk
+        if g_dq is not None:
+            d_dS = _group_scores(g_dq.contiguous(), k, H)
+            _, d_k = _group_mm(dS, g_dq.contiguous(), k, H, want_dq=False)
+        if g_dk is not None:
+            t = _group_scores(q, g_dk.contiguous(), H)
+            d_dS = t if d_dS is None else d_dS + t
+            d_q, _ = _group_mm(dS, q, g_dk.contiguous(), H, want_dk=False)
+        return d_dS, d_q, d_k, None
+
+
 class SubkeyScores(torch.autograd.Function):
     """Dot-product sub-key scores ``[R, 2, n]`` of queries ``[R, k_dim]``
     (``fwpkm/fwpkm.py:861``).
 
-    Forward: the sequential-sum kernel.  Backward: two einsums on the saved
-    query and keys, like the reference's einsum backward, and itself
-    differentiable (the inner updates take gradients with
+    Forward: the sequential-sum kernel.  Backward: the grouped products
+    ``dS @ K`` and ``dS^T @ Q`` on the saved query and keys (as the
+    reference's einsum backward reads them), through ``GroupMM`` so that
+    they are differentiable again (the inner updates take gradients with
     ``create_graph=True``)."""
 
     @staticmethod
@@ -60,14 +142,8 @@ class SubkeyScores(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dS):
         q, k = ctx.saved_tensors
-        H = ctx.heads
-        R, kd = q.shape
-        half = kd // 2
-        n = k.shape[0] // (2 * H)
-        d = dS.view(R // H, H, 2, n)
-        dq = torch.einsum("thpn,hpnd->thpd", d, k.view(H, 2, n, half))
-        dk = torch.einsum("thpn,thpd->hpnd", d, q.view(R // H, H, 2, half))
-        return dq.reshape(R, kd), dk.reshape(k.shape), None
+        dq, dk = GroupMM.apply(dS.contiguous(), q, k, ctx.heads)
+        return dq, dk, None
 
 
 class SubkeyDist(torch.autograd.Function):
@@ -94,11 +170,13 @@ class SubkeyDist(torch.autograd.Function):
         R, kd = q.shape
         half = kd // 2
         n = k.shape[0] // (2 * H)
-        ratio = (grad / dist).view(R // H, H, 2, n)
+        ratio = grad / dist
+        rk, rq = GroupMM.apply(ratio.contiguous(), q, k, H)  # ratio @ K, ratio^T @ Q per group
+        r4 = ratio.view(R // H, H, 2, n)
         qv = q.view(R // H, H, 2, half)
         kv = k.view(H, 2, n, half)
-        dq = qv * ratio.sum(-1, keepdim=True) - torch.einsum("thpn,hpnd->thpd", ratio, kv)
-        dk = kv * ratio.sum(0).unsqueeze(-1) - torch.einsum("thpn,thpd->hpnd", ratio, qv)
+        dq = qv * r4.sum(-1, keepdim=True) - rk.view(R // H, H, 2, half)
+        dk = kv * r4.sum(0).unsqueeze(-1) - rq.view(H, 2, n, half)
         return dq.reshape(R, kd), dk.reshape(k.shape), None
 
 

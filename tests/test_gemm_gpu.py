@@ -152,3 +152,55 @@ def test_fused_swiglu_gemms_equal_unfused_kernels():
     sig = torch.sigmoid(hr)
     assert rel_err(da, dzr * F.silu(hr)) < 2e-2
     assert rel_err(dh, dzr * a.float() * sig * (1 + hr * (1 - sig))) < 2e-2
+
+
+F32_CASES = [
+    # M, N, K, a_mn, b_mn
+    (300, 200, 100, False, False),
+    (256, 256, 4096, True, True),
+    (1000, 136, 512, False, True),
+    (7, 5, 3, True, False),
+]
+
+
+@pytest.mark.parametrize("M,N,K,a_mn,b_mn", F32_CASES)
+def test_gemm_f32_matches_torch(M, N, K, a_mn, b_mn):
+    """The fp32 CUDA-core GEMM (``pkm_gemm_f32``) vs torch fp32 (no TF32)."""
+    from modelos_b200 import _native
+    torch.backends.cuda.matmul.allow_tf32 = False
+    g = torch.Generator().manual_seed(M * 7 + K)
+    a = torch.randn((K, M) if a_mn else (M, K), generator=g).to(DEV)
+    b = torch.randn((K, N) if b_mn else (N, K), generator=g).to(DEV)
+    c = _native.gemm_f32(a, b, a_mn=a_mn, b_mn=b_mn)
+    ref = (a.T if a_mn else a).double() @ (b.T if b_mn else b).double().T
+    assert rel_err(c, ref) < 1e-5
+
+
+def test_group_mm_second_derivatives_match_einsum():
+    """The fast-weight memory's sub-key scores (``SubkeyScores``: sequential
+    fp32 kernel forward, ``GroupMM`` backward on the fp32 GEMM) give the
+    same first and second derivatives as the reference's einsum formulation
+    (``fwpkm/fwpkm.py:861``) evaluated in float64."""
+    from modelos_b200.fwpkm.fwpkm import SubkeyScores
+    g = torch.Generator().manual_seed(5)
+    T, H, n, kd = 96, 4, 64, 128
+    q0 = torch.randn(T * H, kd, generator=g)
+    k0 = torch.randn(2 * H * n, kd // 2, generator=g) * 0.1
+    W = torch.randn(T * H, 2, n, generator=g)
+    U = torch.randn(T * H, kd, generator=g)
+    V = torch.randn(2 * H * n, kd // 2, generator=g)
+
+    def run(q, k, scores_fn):
+        s = scores_fn(q, k)
+        gq, gk = torch.autograd.grad((s * W.to(s)).sum(), (q, k), create_graph=True)
+        loss2 = (gq * U.to(gq)).sum() + (gk * V.to(gk)).sum() + (s ** 2).sum()
+        return [t.double().cpu() for t in (gq, gk, *torch.autograd.grad(loss2, (q, k)))]
+
+    def einsum_scores(q, k):
+        return torch.einsum("thpd,hpnd->thpn", q.view(T, H, 2, kd // 2), k.view(H, 2, n, kd // 2)).reshape(-1, 2, n)
+
+    got = run(q0.to(DEV).requires_grad_(True), k0.to(DEV).requires_grad_(True),
+              lambda q, k: SubkeyScores.apply(q, k, H))
+    ref = run(q0.double().requires_grad_(True), k0.double().requires_grad_(True), einsum_scores)
+    for a_, b_ in zip(got, ref):
+        assert rel_err(a_, b_) < 1e-5
