@@ -129,7 +129,7 @@ def test_fused_swiglu_gemms_equal_unfused_kernels():
 
     from modelos_b200 import _native
     g = torch.Generator().manual_seed(11)
-    M, C, V = 1000, 1024, 1024
+    M, C, V = 4096, 1024, 1024  # enough tiles that neither GEMM splits K (same summation order)
     x = torch.randn(M, C, generator=g).to(torch.bfloat16).to(DEV)
     a = (torch.randn(M, V, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
     ws = (torch.randn(V, C, generator=g) * C ** -0.5).to(torch.bfloat16).to(DEV)
