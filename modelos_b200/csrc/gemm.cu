@@ -18,8 +18,10 @@
 //   warp 1    MMA issuer: tcgen05.mma kind::f16 128x256x16 into one of two
 //             256-column TMEM accumulators; tcgen05.commit frees each stage
 //             and hands a finished accumulator to the epilogue;
-//   warps 2-5 epilogue: tcgen05.ld, one output row per thread, bias add,
-//             rounding and 16-byte stores (or fp32 partials).
+//   warps 2-9 epilogue: two warps per TMEM lane quarter, 128 of the 256
+//             columns each; tcgen05.ld of the next 32 columns in flight
+//             while the current ones get their bias, rounding and 16-byte
+//             stores (or fp32 partials), one output row per thread.
 // When the tiles alone cannot fill the SMs (weight gradients, K = tokens),
 // the K range is split over several CTAs that write fp32 partials; a second
 // kernel sums them in split order (deterministic) and applies the epilogue.
@@ -36,7 +38,8 @@ constexpr int GM_BM = 128, GM_BN = 256, GM_BK = 64, GM_STAGES = 4;
 constexpr int GM_A_BYTES = GM_BM * GM_BK * 2;  // 16 KiB
 constexpr int GM_B_BYTES = GM_BN * GM_BK * 2;  // 32 KiB
 constexpr int GM_STAGE = GM_A_BYTES + GM_B_BYTES;
-constexpr int GM_THREADS = 192;
+constexpr int GM_EPI_WARPS = 8;  // two per TMEM lane quarter, 128 columns each
+constexpr int GM_THREADS = 64 + GM_EPI_WARPS * 32;
 constexpr int GM_SMEM = GM_STAGES * GM_STAGE + 1024 + 256;
 constexpr int GM_MN_BOX = 64;                   // MN-major tiles arrive as 64-wide boxes
 constexpr int GM_MN_BOX_BYTES = GM_MN_BOX * GM_BK * 2;  // 8 KiB
@@ -139,6 +142,28 @@ __device__ __forceinline__ float gm_bias(const GemmArgs& a, int n) {
   return ld_f(a.bias, a.bias_dtype, n);
 }
 
+// bias[n0 .. n0+31] (0 past N or without a bias), 16-byte loads where whole
+__device__ __forceinline__ void gm_bias32(const GemmArgs& a, int n0, float* f) {
+  if (!a.bias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = 0.f;
+    return;
+  }
+  const bool whole = n0 + 32 <= a.N;
+  if (whole && a.bias_dtype == PKM_DT_BF16 && (reinterpret_cast<uintptr_t>(a.bias) & 15u) == 0) {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.bias) + n0);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) VecTraits<__nv_bfloat16>::unpack(__ldg(p + v), f + 8 * v);
+  } else if (whole && a.bias_dtype == PKM_DT_F32 && (reinterpret_cast<uintptr_t>(a.bias) & 15u) == 0) {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const float*>(a.bias) + n0);
+#pragma unroll
+    for (int v = 0; v < 8; ++v) VecTraits<float>::unpack(__ldg(p + v), f + 4 * v);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = n0 + j < a.N ? ld_f(a.bias, a.bias_dtype, n0 + j) : 0.f;
+  }
+}
+
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                      const GemmArgs a) {
@@ -161,7 +186,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
+      mbar_init(&tempty[i], GM_EPI_WARPS * 32);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -257,7 +282,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       mbar_wait(drain, 0, nullptr);
     }
   } else {
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;       // which 128 of the tile's 256 columns
+    constexpr int HC = GM_BN / 2 / 32;      // 32-column chunks per warp
     const int row = q * 32 + lane;
     int li = 0;
     for (int64_t unit = blockIdx.x; unit < a.units; unit += gridDim.x, ++li) {
@@ -267,43 +294,51 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       int b, mt, nt, s;
       gm_decode(a, unit, b, mt, nt, s);
       const int m = mt * GM_BM + row;
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * GM_BN);
-#pragma unroll 1
-      for (int c = 0; c < GM_BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
-        tmem_ld_wait();
-        const int n0 = nt * GM_BN + c * 32;
-        if (m >= a.M || n0 >= a.N) continue;
-        if (a.splits > 1) {
-          float* dst = a.ws + (((int64_t)s * a.batch + b) * a.M + m) * (int64_t)a.N + n0;
+      const uint32_t tbase =
+          tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * GM_BN + half * (GM_BN / 2));
+      // two register buffers: the load of chunk c + 1 is in flight while
+      // chunk c is converted and stored (tcgen05.wait::ld waits for all)
+      uint32_t r[2][32];
+      tmem_ld_32x32b_x32(tbase, r[0]);
+      tmem_ld_wait();
 #pragma unroll
-          for (int v = 0; v < 8; ++v)
-            if (n0 + v * 4 + 4 <= a.N)
-              reinterpret_cast<float4*>(dst)[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                                              __uint_as_float(r[4 * v + 2]),
-                                                              __uint_as_float(r[4 * v + 3]));
-          continue;
-        }
-        float f[32];
+      for (int c = 0; c < HC; ++c) {
+        if (c + 1 < HC) tmem_ld_32x32b_x32(tbase + (uint32_t)((c + 1) * 32), r[(c + 1) & 1]);
+        const uint32_t* rc = r[c & 1];
+        const int n0 = nt * GM_BN + half * (GM_BN / 2) + c * 32;
+        if (m < a.M && n0 < a.N) {
+          if (a.splits > 1) {
+            float* dst = a.ws + (((int64_t)s * a.batch + b) * a.M + m) * (int64_t)a.N + n0;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]) + gm_bias(a, min(n0 + j, a.N - 1));
-        const int64_t e0 = b * a.c_bs + (int64_t)m * a.ldc + n0;
-        if (a.epi) {
-          const int64_t x0 = (int64_t)m * a.ld_aux + n0;
+            for (int v = 0; v < 8; ++v)
+              if (n0 + v * 4 + 4 <= a.N)
+                reinterpret_cast<float4*>(dst)[v] =
+                    make_float4(__uint_as_float(rc[4 * v]), __uint_as_float(rc[4 * v + 1]),
+                                __uint_as_float(rc[4 * v + 2]), __uint_as_float(rc[4 * v + 3]));
+          } else {
+            float f[32];
+            gm_bias32(a, n0, f);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            if (n0 + v * 8 + 8 > a.N) continue;
-            float o[8], o2[8];
-            gm_gate8(a, x0 + v * 8, f + v * 8, o, o2);
-            st_run(a.c, PKM_DT_BF16, e0 + v * 8, o, 8);
-            if (a.aux_out) st_run(a.aux_out, PKM_DT_BF16, x0 + v * 8, o2, 8);
+            for (int j = 0; j < 32; ++j) f[j] += __uint_as_float(rc[j]);
+            const int64_t e0 = b * a.c_bs + (int64_t)m * a.ldc + n0;
+            if (a.epi) {
+              const int64_t x0 = (int64_t)m * a.ld_aux + n0;
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                if (n0 + v * 8 + 8 > a.N) continue;
+                float o[8], o2[8];
+                gm_gate8(a, x0 + v * 8, f + v * 8, o, o2);
+                st_run(a.c, PKM_DT_BF16, e0 + v * 8, o, 8);
+                if (a.aux_out) st_run(a.aux_out, PKM_DT_BF16, x0 + v * 8, o2, 8);
+              }
+            } else {
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                if (n0 + v * 8 + 8 <= a.N) st_run(a.c, a.c_dtype, e0 + v * 8, f + v * 8, 8);
+            }
           }
-          continue;
         }
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          if (n0 + v * 8 + 8 <= a.N) st_run(a.c, a.c_dtype, e0 + v * 8, f + v * 8, 8);
+        tmem_ld_wait();
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
