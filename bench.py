@@ -51,11 +51,23 @@ CFG = dict(input_dim=1024, output_dim=1024, mem_k_dim=512, mem_v_dim=1024, mem_h
            mem_n_keys=512, mem_query_batchnorm=True, mem_query_rmsnorm=False)
 # config 1: bags, bag size, table rows, row width
 C1_N, C1_L, C1_K, C1_D = 16384, 128, 262144, 1024
+# config 4: FwPKM on [8, 4096, 1024] in chunks of 512 (fp32 fast weights)
+C4_B, C4_T, C4_CHUNK = 8, 4096, 512
+C4_FW = dict(mem_k_dim=512, mem_v_dim=1024, mem_heads=4, mem_topk=32, mem_n_subkeys=512, learning_rate=0.1)
+METRIC_C4 = "FwPKM layer tokens/s (fwd+bwd)"
 REF_TOKENS = 2048   # tokens per reference-arm step (one sequence of the c2 batch)
 REF_BAGS = 2048     # bags per reference-arm step at config 1
 
 
 def config_obj(n, workload="c2"):
+    if workload == "c4":
+        return {"workload": "c4: FastWeightProductKeyMemory fwd (8 chunks of 512 positions, inner SGD update "
+                            "lr 0.1 with create_graph) + outer bwd, x[8,4096,1024] bf16 -> q = Linear(1024->2048), "
+                            "ref_v = Linear(1024->1024), k_dim 512, 4 heads x top-32 over 512^2 fp32 fast-weight "
+                            "slots of 1024, idw scores, joint softmax, addressing loss me, loss sum(out^2)",
+                "tokens_per_rank_step": C4_B * C4_T, "global_batch": C4_B * n, "seq_len": C4_T,
+                "parallelism": "single" if n == 1 else f"dp{n}",
+                "l2": "inputs larger than L2 (fp32 fast-weight table 1 GiB, updated per chunk)"}
     if workload == "c1":
         return {"workload": "c1: embedding bag fwd+bwd, table bf16 [262144,1024] N(0,0.03), 16384 bags x 128 "
                             "int64 indices uniform with replacement, fp32 per-head softmax weights, bf16 dOut",
@@ -146,6 +158,41 @@ def ref_bag_rate(steps=5, warmup=2, bags=REF_BAGS):
             "ms_per_step": 1000.0 * t, "steps": steps, "warmup": warmup}
 
 
+REF_C4_TOKENS = 512  # positions of one sequence per reference-arm step at config 4 (one chunk)
+
+
+def ref_fw_rate(steps=3, warmup=1, tokens=REF_C4_TOKENS):
+    """Config 4 on the reference's CPU path (``oracle/ref_torch.fw_step``: the
+    fast-weight layer's torch CPU operators in its order, fp32 fast weights)
+    on one sequence of ``tokens`` positions (one chunk of 512) per step."""
+    import torch
+
+    from oracle import ref_torch as rt
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    P = rt.fw_make_params(C4_FW, 0)
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn((1, tokens, 2048), generator=g).to(torch.bfloat16)
+    v = torch.randn((1, tokens, 1024), generator=g).to(torch.bfloat16)
+    keys0, values0 = P["keys"].detach().clone(), P["values"].detach().clone()
+
+    def step():
+        with torch.no_grad():
+            P["keys"].copy_(keys0)
+            P["values"].copy_(values0)
+        rt.fw_step(P, q, v, C4_FW, C4_CHUNK, "idw")
+
+    ts = _timed(step, steps, warmup)
+    t = statistics.median(ts)
+    cores = torch.get_num_threads()
+    return {"value": tokens / t, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{tokens} positions (one chunk of {C4_CHUNK}) of the c4 layer per step (fwd with inner "
+                      f"update + outer bwd, fp32 fast weights, the reference's torch CPU operators via "
+                      f"oracle/ref_torch.py, torch threads={cores}, host {os.cpu_count()} cpus {cpu_model()}), "
+                      f"median of {steps} after {warmup} warm-up; s/step {t:.3f}",
+            "ms_per_step": 1000.0 * t, "steps": steps, "warmup": warmup, "tokens_per_step": tokens}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -153,6 +200,11 @@ def run_reference(args, rank, world):
     if args.workload == "c1":
         cb = ref_bag_rate(steps, warmup)
         metric, unit = METRIC_C1, "GB/s"
+    elif args.workload == "c4":
+        # a step of the CPU path takes seconds: at most 3 after 1 warm-up
+        steps, warmup = min(steps, 3), min(warmup, 1)
+        cb = ref_fw_rate(steps, warmup)
+        metric, unit = METRIC_C4, UNIT
     else:
         cb = ref_layer_rate(steps, warmup)
         metric, unit = METRIC, UNIT
@@ -238,6 +290,8 @@ class Clocks:
         if len(inside) < 3:  # a region shorter than a few sampling periods: add the run around it
             inside = [s for s in samples if t0 - 2.0 <= s[0] <= t1 + 0.1]
             scope = "timed region and the 2 s of warm-up before it"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["unsampled"], "samples": 0}
         reasons = sorted({name for _, _, r in inside for bit, name in _REASONS.items() if r & bit})
         return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": mx, "reasons": reasons,
                 "samples": len(inside), "scope": scope, "source": "NVML, %.0f ms period" % (1000 * self.period)}
@@ -429,6 +483,86 @@ def run_ours_c1(args, rank, world, local_rank):
             "clocks": clk.summary()}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = ref_bag_rate()
+    print(json.dumps(line), flush=True)
+
+
+def run_ours_c4(args, rank, world, local_rank):
+    """Config 4 on one GPU: the fast-weight memory's chunked forward with its
+    inner updates, then the outer backward through them."""
+    import torch
+
+    from modelos_b200 import _native
+    from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
+    from modelos_b200.pkm.memory import linear
+
+    if world > 1:
+        raise SystemExit("--workload c4 runs on one GPU")
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    clk = Clocks(local_rank).start()
+    torch.manual_seed(0)
+    m = FastWeightProductKeyMemory(**C4_FW).to(dev).train()
+    m.reset_parameters()
+    wq = torch.nn.Linear(1024, 2048).to(dev, torch.bfloat16)
+    wv = torch.nn.Linear(1024, 1024).to(dev, torch.bfloat16)
+    keys0, values0 = m.keys.detach().clone(), m.values.detach().clone()
+    g = torch.Generator(device=dev).manual_seed(1000)
+    x = torch.randn((C4_B, C4_T, 1024), generator=g, device=dev).to(torch.bfloat16)
+    x_host = x.cpu().pin_memory()
+
+    def step(xin):
+        # every step starts from the same fast weights (the layer writes the
+        # final ones back into its parameters)
+        with torch.no_grad():
+            m.keys.copy_(keys0)
+            m.values.copy_(values0)
+        for p in list(m.parameters()) + list(wq.parameters()) + list(wv.parameters()):
+            p.grad = None
+        xf = xin.view(-1, 1024)
+        q = linear(xf, wq.weight, wq.bias).view(C4_B, C4_T, -1)
+        ref_v = linear(xf, wv.weight, wv.bias).view(C4_B, C4_T, -1)
+        res = m(q, ref_v, None, C4_CHUNK)
+        loss = (res["output"].float() ** 2).sum()
+        loss.backward()
+        return loss
+
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+    _native.check_device_errors(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record()
+    for _ in range(args.steps):
+        step(x)
+    e1.record()
+    torch.cuda.synchronize()
+    clk.mark(t0, time.time())
+    ms = e0.elapsed_time(e1) / args.steps
+    d_x = torch.empty_like(x)
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    for _ in range(args.steps):
+        d_x.copy_(x_host, non_blocking=True)
+        lv = step(d_x).item()
+    e2e_ms = (time.perf_counter() - w0) * 1000.0 / args.steps
+    assert math.isfinite(lv)
+    launches = count_launches(step, x)
+    _native.check_device_errors(dev)
+    clk.stop()
+    tokens = C4_B * C4_T
+    line = {"metric": METRIC_C4, "value": round(tokens / (ms / 1000.0), 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 inputs, fp32 fast weights",
+            "data": "synthetic (seeded normal x, reset_parameters init, default nn.Linear projections)",
+            "config": config_obj(world, "c4"),
+            "e2e": {"value": round(tokens / (e2e_ms / 1000.0), 1), "unit": UNIT,
+                    "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4,
+                    "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": None if launches is None else launches * args.steps, "gpu_launches_per_step": launches,
+            "clocks": clk.summary()}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = ref_fw_rate()
     print(json.dumps(line), flush=True)
 
 
@@ -632,8 +766,8 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2", "c1"],
-                    help="c2: the PKM layer (default); c1: the embedding bag alone")
+    ap.add_argument("--workload", default="c2", choices=["c2", "c1", "c4"],
+                    help="c2: the PKM layer (default); c1: the embedding bag alone; c4: the fast-weight memory")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--grad-exchange", default="fused", choices=["fused", "nccl", "owner"],
                     help="data-parallel exchange of the value-table gradient (N > 1); owner: the table's "
@@ -664,6 +798,8 @@ def main():
     try:
         if args.workload == "c1":
             run_ours_c1(args, rank, world, local_rank)
+        elif args.workload == "c4":
+            run_ours_c4(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

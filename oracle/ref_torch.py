@@ -126,3 +126,146 @@ def layer_step(P: dict, x: torch.Tensor, heads: int, knn: int, k_dim: int, norm:
     loss = (out.float() ** 2).sum()
     loss.backward()
     return out, slots, loss
+
+
+# ---------------------------------------------------------------------------
+# the fast-weight memory (fwpkm/fwpkm.py) on the same CPU operators
+# ---------------------------------------------------------------------------
+class _BagGradWrap(torch.autograd.Function):
+    """The weight gradient of the fast-weight bag, exposed so the outer
+    backward can differentiate it (fwpkm/xformer_embeddingbag_grad_wrapper.py
+    :13-74): forward passes the first-order gradient through; backward is the
+    bag's VJP, gathered rows weighted and dotted."""
+
+    @staticmethod
+    def forward(ctx, idx, psw, g, grad_weight):
+        ctx.save_for_backward(idx, psw, g)
+        return grad_weight
+
+    @staticmethod
+    def backward(ctx, g_bar):
+        idx, a, g = ctx.saved_tensors
+        B, L = idx.shape
+        rows = g_bar.index_select(0, idx.reshape(-1)).view(B, L, -1)
+        return None, (rows * g.unsqueeze(1)).sum(dim=-1), (a.unsqueeze(-1) * rows).sum(dim=1), None
+
+
+class _FwBag(torch.autograd.Function):
+    """``out[b] = sum_j psw[b,j] W[idx[b,j]]`` as the fast-weight memory runs it
+    on CPU (fwpkm/xformer_embeddingbag_grad_wrapper.py:83-155): gather and
+    weighted sum forward; the first-order backward of
+    fwpkm/xformer_embeddingbag_legacy.py:147-167 wrapped for double backward."""
+
+    @staticmethod
+    def forward(ctx, W, idx, psw):
+        B, L = idx.shape
+        rows = W.index_select(0, idx.reshape(-1)).view(B, L, -1)
+        ctx.save_for_backward(W, idx, psw)
+        return (rows * psw.unsqueeze(-1)).sum(dim=1)
+
+    @staticmethod
+    def backward(ctx, g):
+        W, idx, psw = ctx.saved_tensors
+        B, L = idx.shape
+        K, D = W.shape
+        with torch.no_grad():
+            rows = W.index_select(0, idx.reshape(-1)).view(B, L, D)
+            d_psw = (rows.float() * g.unsqueeze(1).float()).sum(-1).to(psw.dtype)
+            contrib = g.unsqueeze(1).float() * psw.unsqueeze(-1).float()
+            dW = torch.zeros(K, D, dtype=torch.float32)
+            dW.index_add_(0, idx.reshape(-1), contrib.reshape(-1, D))
+            dW = dW.to(W.dtype)
+        return _BagGradWrap.apply(idx, psw, g, dW), None, d_psw
+
+
+def fw_make_params(cfg: dict, seed: int = 0) -> dict:
+    """Fast weights drawn like ``reset_parameters`` (fwpkm/fwpkm.py:91-96), fp32 leaves."""
+    g = torch.Generator().manual_seed(seed)
+    H, kd, D, n = cfg["mem_heads"], cfg["mem_k_dim"], cfg["mem_v_dim"], cfg["mem_n_subkeys"]
+    keys = (torch.rand((2 * H * n, kd // 2), generator=g) * 2 - 1) / math.sqrt(kd)
+    values = torch.randn((n * n, D), generator=g) * D ** -0.5
+    return {"keys": keys.requires_grad_(True), "values": values.requires_grad_(True)}
+
+
+def _fw_scores(q, k, mode):
+    if mode == "dot_product":
+        return torch.einsum("bhd,hnd->bhn", q, k)
+    d = torch.cdist(q.permute(1, 0, 2), k, p=2, compute_mode="use_mm_for_euclid_dist").permute(1, 0, 2)
+    return -torch.log(1e-3 + d.pow(2))
+
+
+def _fw_marginal_entropy(M, topk, eps=1e-8):
+    kth = torch.topk(M, topk, dim=1)[0][:, -1].unsqueeze(1)
+    M = torch.where(M >= kth, M, torch.full_like(M, float("-inf"))).float()
+    P_bar = torch.mean(F.softmax(M, dim=1), dim=0)
+    return -torch.sum(P_bar * torch.log(P_bar + eps))
+
+
+def fw_forward(P: dict, q: torch.Tensor, ref_v: torch.Tensor, cfg: dict, chunk: int, mode: str = "idw"):
+    """``forward_wo_past`` (fwpkm/fwpkm.py:395-558) with the module defaults
+    (lookahead 1, softmax at temperature 1, SGD without weight decay, MSE
+    memorisation loss on the values only, addressing loss "me" of weight 1,
+    fp32 fast weights): returns (output [B, T, D], indices, addr_loss).  As
+    in the reference, the first chunk's fast weights are the parameters
+    themselves and the final weights are copied into them at the end."""
+    H, kd, topk, n = cfg["mem_heads"], cfg["mem_k_dim"], cfg["mem_topk"], cfg["mem_n_subkeys"]
+    lr = cfg.get("learning_rate", 1.0)
+    in_dtype = q.dtype
+    q, ref_v = q.float(), ref_v.float()
+    B, T = q.shape[:2]
+    half = kd // 2
+    outs, idxs, addr = [], [], []
+    fw = {"keys": P["keys"].float(), "values": P["values"].float()}
+    with torch.enable_grad():
+        for c0 in range(0, T, chunk):
+            c1 = min(c0 + chunk, T)
+            cT = c1 - c0
+            cq = q[:, c0:c1].contiguous().view(B * cT, H, kd)
+            cref = ref_v[:, c0:c1].contiguous()
+            kv = fw["keys"].view(H, 2, -1, half)
+            s1 = _fw_scores(cq[:, :, :half], kv[:, 0], mode)
+            s2 = _fw_scores(cq[:, :, half:], kv[:, 1], mode)
+            t1, i1 = s1.topk(topk, dim=2, largest=True)
+            t2, i2 = s2.topk(topk, dim=2, largest=True)
+            BT = B * cT
+            pair_s = (t1.view(BT, H, topk, 1).expand(BT, H, topk, topk)
+                      + t2.view(BT, H, 1, topk).expand(BT, H, topk, topk)).view(BT, H, topk ** 2)
+            pair_i = (i1.view(BT, H, topk, 1).expand(BT, H, topk, topk) * n
+                      + i2.view(BT, H, 1, topk).expand(BT, H, topk, topk)).view(BT, H, topk ** 2)
+            top, best = torch.topk(pair_s, k=topk, dim=2, largest=True, sorted=True)
+            slots = pair_i.gather(2, best).contiguous()
+            w = F.softmax(top.contiguous().view(BT, H * topk) / 1.0, dim=-1).type_as(top)
+            hyp = _FwBag.apply(fw["values"], slots.view(BT, H * topk), w).view(B, cT, -1)
+            outs.append(hyp)
+            idxs.append(slots.view(B, cT, -1))
+            mem = F.mse_loss(hyp[:, :-1].contiguous().view(-1, hyp.size(-1)),
+                             cref[:, 1:].contiguous().view(-1, hyp.size(-1)), reduction="none").mean(dim=-1)
+            a_loss = 1.0 * (-1.0 * _fw_marginal_entropy(s1.contiguous().view(-1, n), topk)
+                            + -1.0 * _fw_marginal_entropy(s2.contiguous().view(-1, n), topk))
+            params = (fw["keys"], fw["values"])
+            g_addr = torch.autograd.grad(a_loss, params, create_graph=True, allow_unused=True)
+            (g_mem,) = torch.autograd.grad(mem.mean() * 0.5, fw["values"], create_graph=True)
+            g_v = g_mem * (B * cT * cfg["mem_v_dim"] * topk * H)
+            cnt = torch.bincount(slots.view(-1), minlength=n * n).to(g_v.dtype)
+            cnt[cnt == 0] = 1.0
+            g_v = g_v / cnt.unsqueeze(-1)
+            fw = {"keys": fw["keys"] - lr * (g_addr[0] + 0.0 * fw["keys"]),
+                  "values": fw["values"] - lr * (g_v + 0.0 * fw["values"])}
+            addr.append(a_loss.detach())
+    with torch.no_grad():
+        P["keys"].data.copy_(fw["keys"].data)
+        P["values"].data.copy_(fw["values"].data)
+    out = torch.cat(outs, dim=1).to(in_dtype)
+    return out, torch.cat(idxs, dim=1), torch.stack(addr).mean()
+
+
+def fw_step(P: dict, q: torch.Tensor, ref_v: torch.Tensor, cfg: dict, chunk: int, mode: str = "idw"):
+    """One training step of the fast-weight layer: forward, loss
+    ``sum(out^2)``, outer backward into the leaves' and inputs' ``.grad``."""
+    for t in list(P.values()) + [q, ref_v]:
+        if t.requires_grad:
+            t.grad = None
+    out, idx, addr = fw_forward(P, q, ref_v, cfg, chunk, mode)
+    loss = (out.float() ** 2).sum()
+    loss.backward()
+    return out, idx, loss

@@ -264,3 +264,26 @@ def test_torch_restatement_equals_reference_at_config2_geometry():
     np.testing.assert_array_equal(s["rows"], d["values_grad_rows"])
     assert rel_err(s["rownorm"], d["values_grad_rownorm"]) < 1e-7
     np.testing.assert_array_equal(P["bq"].grad.float().numpy(), d["bq_grad"])
+
+
+def test_torch_restatement_of_the_fast_weight_layer_equals_reference():
+    """``oracle/ref_torch.fw_forward`` (the config-4 reference arm of
+    ``bench.py``) runs the fast-weight memory's CPU operators in the
+    reference's order: at config-4 geometry (idw) its indices, output, loss
+    and outer gradients equal the reference's bit for bit."""
+    from oracle import ref_torch as rt
+    d = np.load(os.path.join(GOLD, "fwpkm_c4_idw.npz"))
+    keys, values, q, ref_v = cases.fwpkm_c4_case(0)
+    P = {"keys": keys.clone().requires_grad_(True), "values": values.clone().requires_grad_(True)}
+    q.requires_grad_(True)
+    ref_v.requires_grad_(True)
+    out, idx, addr = rt.fw_forward(P, q, ref_v, cases.FW_C4, cases.FW_C4_CHUNK, "idw")
+    loss = (out ** 2).sum() + addr
+    loss.backward()
+    np.testing.assert_array_equal(idx.numpy().reshape(d["indices"].shape), d["indices"])
+    np.testing.assert_array_equal(out.detach().numpy(), d["output"])
+    assert loss.item() == float(d["loss"])
+    for t, key in ((q.grad.view(q.shape[1], -1), "q_grad"), (P["values"].grad, "values_grad"),
+                   (P["keys"].grad, "keys_grad")):
+        s = cases.summarize(t, rows_idx=d[key + "_rows_idx"])
+        np.testing.assert_array_equal(s["rows"], d[key + "_rows"])
