@@ -55,11 +55,21 @@ C1_N, C1_L, C1_K, C1_D = 16384, 128, 262144, 1024
 C4_B, C4_T, C4_CHUNK = 8, 4096, 512
 C4_FW = dict(mem_k_dim=512, mem_v_dim=1024, mem_heads=4, mem_topk=32, mem_n_subkeys=512, learning_rate=0.1)
 METRIC_C4 = "FwPKM layer tokens/s (fwd+bwd)"
+METRIC_C3 = "Qwen3-PKM train tokens/s (fwd+bwd)"
+C3_B, C3_T, C3_DECODE = 8, 2048, 256
 REF_TOKENS = 2048   # tokens per reference-arm step (one sequence of the c2 batch)
 REF_BAGS = 2048     # bags per reference-arm step at config 1
 
 
 def config_obj(n, workload="c2"):
+    if workload == "c3":
+        return {"workload": "c3: Qwen3-0.6B-shaped decoder (hidden 1024, 28 layers, 16/8 heads, head_dim 128, "
+                            "FFN 3072, vocab 151936, RoPE 1e6, tied embeddings) with HashingMemory (config-2 "
+                            "geometry, query RMSNorm) in place of the MLP at layers 6, 12, 18; bf16 random init; "
+                            "training step = fwd + bwd of the next-token loss on [8, 2048] uniform token ids; "
+                            "prefill = [8, 2048] with KV cache; decode = 256 greedy tokens per sequence",
+                "tokens_per_rank_step": C3_B * C3_T, "global_batch": C3_B * n, "seq_len": C3_T,
+                "parallelism": "single", "l2": "inputs larger than L2 (PKM tables 3 x 512 MiB, logits 5 GB)"}
     if workload == "c4":
         return {"workload": "c4: FastWeightProductKeyMemory fwd (8 chunks of 512 positions, inner SGD update "
                             "lr 0.1 with create_graph) + outer bwd, x[8,4096,1024] bf16 -> q = Linear(1024->2048), "
@@ -197,6 +207,11 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     steps, warmup = max(args.steps, 1), max(args.warmup, 0)
+    if args.workload == "c3":
+        print(json.dumps({"impl": "reference", "unavailable": "config 3 runs the reference's model file "
+                          "(modeling_qwen3pkm.py), which is not on the benchmark machine; the PKM layer it "
+                          "calls is the default workload (c2)", "metric": METRIC_C3}), flush=True)
+        return
     if args.workload == "c1":
         cb = ref_bag_rate(steps, warmup)
         metric, unit = METRIC_C1, "GB/s"
@@ -566,6 +581,97 @@ def run_ours_c4(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_ours_c3(args, rank, world, local_rank):
+    """Config 3 on one GPU: the model's training step (forward + backward),
+    then a prefill and a decode loop in evaluation mode."""
+    import torch
+
+    from modelos_b200 import _native
+    from modelos_b200.qwen3pkm import build_qwen3_pkm
+
+    if world > 1:
+        raise SystemExit("--workload c3 runs on one GPU")
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    clk = Clocks(local_rank).start()
+    model = build_qwen3_pkm(device=dev, dtype=torch.bfloat16).train()
+    g = torch.Generator(device=dev).manual_seed(0)
+    ids = torch.randint(0, model.config.vocab_size, (C3_B, C3_T), generator=g, device=dev)
+    ids_host = ids.cpu().pin_memory()
+    params = [p for p in model.parameters()]
+
+    def step(x):
+        for p in params:
+            p.grad = None
+        out = model(input_ids=x, labels=x, use_cache=False)
+        out.loss.backward()
+        return out.loss
+
+    for _ in range(args.warmup):
+        step(ids)
+    torch.cuda.synchronize()
+    _native.check_device_errors(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record()
+    for _ in range(args.steps):
+        step(ids)
+    e1.record()
+    torch.cuda.synchronize()
+    clk.mark(t0, time.time())
+    ms = e0.elapsed_time(e1) / args.steps
+    d_ids = torch.empty_like(ids)
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    for _ in range(args.steps):
+        d_ids.copy_(ids_host, non_blocking=True)
+        lv = step(d_ids).item()
+    e2e_ms = (time.perf_counter() - w0) * 1000.0 / args.steps
+    assert math.isfinite(lv)
+    launches = count_launches(step, ids)
+    for p in params:
+        p.grad = None
+
+    # prefill and decode (evaluation mode, KV cache)
+    model.eval()
+    with torch.no_grad():
+        for _ in range(2):
+            model(input_ids=ids, use_cache=True)
+        torch.cuda.synchronize()
+        e0.record()
+        out = model(input_ids=ids, use_cache=True)
+        e1.record()
+        torch.cuda.synchronize()
+        prefill_ms = e0.elapsed_time(e1)
+        cache = out.past_key_values
+        nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        e0.record()
+        for _ in range(C3_DECODE):
+            out = model(input_ids=nxt, past_key_values=cache, use_cache=True)
+            cache = out.past_key_values
+            nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        e1.record()
+        torch.cuda.synchronize()
+        decode_ms = e0.elapsed_time(e1)
+    _native.check_device_errors(dev)
+    clk.stop()
+    tokens = C3_B * C3_T
+    line = {"metric": METRIC_C3, "value": round(tokens / (ms / 1000.0), 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (uniform token ids, random init)", "config": config_obj(world, "c3"),
+            "prefill": {"tokens_per_s": round(tokens / (prefill_ms / 1000.0), 1), "ms": round(prefill_ms, 3),
+                        "tokens": tokens},
+            "decode": {"tokens_per_s": round(C3_B * C3_DECODE / (decode_ms / 1000.0), 1),
+                       "ms_per_token_step": round(decode_ms / C3_DECODE, 4), "batch": C3_B, "steps": C3_DECODE},
+            "e2e": {"value": round(tokens / (e2e_ms / 1000.0), 1), "unit": UNIT,
+                    "h2d_bytes_per_step": ids.numel() * ids.element_size(), "d2h_bytes_per_step": 4,
+                    "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": None if launches is None else launches * args.steps, "gpu_launches_per_step": launches,
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -766,8 +872,9 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2", "c1", "c4"],
-                    help="c2: the PKM layer (default); c1: the embedding bag alone; c4: the fast-weight memory")
+    ap.add_argument("--workload", default="c2", choices=["c2", "c1", "c3", "c4"],
+                    help="c2: the PKM layer (default); c1: the embedding bag alone; c3: the Qwen3-PKM model "
+                         "(train step, prefill, decode); c4: the fast-weight memory")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--grad-exchange", default="fused", choices=["fused", "nccl", "owner"],
                     help="data-parallel exchange of the value-table gradient (N > 1); owner: the table's "
@@ -800,6 +907,8 @@ def main():
             run_ours_c1(args, rank, world, local_rank)
         elif args.workload == "c4":
             run_ours_c4(args, rank, world, local_rank)
+        elif args.workload == "c3":
+            run_ours_c3(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:
