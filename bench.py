@@ -593,6 +593,9 @@ def run_ours_c3(args, rank, world, local_rank):
         raise SystemExit("--workload c3 runs on one GPU")
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    # cuDNN's attention plans each new KV length on the host (milliseconds a
+    # decode step); the flash backend does not
+    torch.backends.cuda.enable_cudnn_sdp(False)
     clk = Clocks(local_rank).start()
     model = build_qwen3_pkm(device=dev, dtype=torch.bfloat16).train()
     g = torch.Generator(device=dev).manual_seed(0)
