@@ -502,26 +502,33 @@ def run_ours_c1(args, rank, world, local_rank):
 
 
 def run_ours_c4(args, rank, world, local_rank):
-    """Config 4 on one GPU: the fast-weight memory's chunked forward with its
-    inner updates, then the outer backward through them."""
+    """Config 4: the fast-weight memory's chunked forward with its inner
+    updates, then the outer backward through them; at N GPUs every rank runs
+    its own 8 sequences (weak scaling) with the fast weights replicated and
+    updated from the whole batch (``FastWeightProductKeyMemory.data_parallel``)."""
     import torch
 
     from modelos_b200 import _native
     from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
     from modelos_b200.pkm.memory import linear
 
-    if world > 1:
-        raise SystemExit("--workload c4 runs on one GPU")
+    import torch.distributed as dist
+
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     clk = Clocks(local_rank).start()
-    torch.manual_seed(0)
+    torch.manual_seed(0)  # identical parameters on every rank
     m = FastWeightProductKeyMemory(**C4_FW).to(dev).train()
     m.reset_parameters()
     wq = torch.nn.Linear(1024, 2048).to(dev, torch.bfloat16)
     wv = torch.nn.Linear(1024, 1024).to(dev, torch.bfloat16)
+    proj = list(wq.parameters()) + list(wv.parameters())
+    if world > 1:
+        # batch split over the ranks, fast weights replicated, every inner
+        # update from the whole batch's gradient (differentiable all-reduces)
+        m.data_parallel(dist.group.WORLD)
     keys0, values0 = m.keys.detach().clone(), m.values.detach().clone()
-    g = torch.Generator(device=dev).manual_seed(1000)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
     x = torch.randn((C4_B, C4_T, 1024), generator=g, device=dev).to(torch.bfloat16)
     x_host = x.cpu().pin_memory()
 
@@ -539,6 +546,10 @@ def run_ours_c4(args, rank, world, local_rank):
         res = m(q, ref_v, None, C4_CHUNK)
         loss = (res["output"].float() ** 2).sum()
         loss.backward()
+        if world > 1:
+            m.reduce_grads()
+            for p in proj:
+                dist.all_reduce(p.grad)
         return loss
 
     for _ in range(args.warmup):
@@ -546,6 +557,9 @@ def run_ours_c4(args, rank, world, local_rank):
     torch.cuda.synchronize()
     _native.check_device_errors(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     t0 = time.time()
     e0.record()
     for _ in range(args.steps):
@@ -553,7 +567,12 @@ def run_ours_c4(args, rank, world, local_rank):
     e1.record()
     torch.cuda.synchronize()
     clk.mark(t0, time.time())
-    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
     d_x = torch.empty_like(x)
     torch.cuda.synchronize()
     w0 = time.perf_counter()
@@ -561,11 +580,17 @@ def run_ours_c4(args, rank, world, local_rank):
         d_x.copy_(x_host, non_blocking=True)
         lv = step(d_x).item()
     e2e_ms = (time.perf_counter() - w0) * 1000.0 / args.steps
+    t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
     assert math.isfinite(lv)
     launches = count_launches(step, x)
     _native.check_device_errors(dev)
     clk.stop()
-    tokens = C4_B * C4_T
+    if rank != 0:
+        return
+    tokens = C4_B * C4_T * world
     line = {"metric": METRIC_C4, "value": round(tokens / (ms / 1000.0), 1), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 inputs, fp32 fast weights",
@@ -576,7 +601,11 @@ def run_ours_c4(args, rank, world, local_rank):
                     "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": None if launches is None else launches * args.steps, "gpu_launches_per_step": launches,
             "clocks": clk.summary()}
-    if not args.no_cpu_baseline:
+    if world > 1:
+        line["config"]["exchange"] = ("per chunk: differentiable all-reduces of the fast-weight gradients (fp32 "
+                                      "values 1 GiB, keys) and of the addressing loss's row sums, all-gather of the "
+                                      "slot indices; after the step, all-reduce of the parameters' gradients")
+    if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = ref_fw_rate()
     print(json.dumps(line), flush=True)
 

@@ -317,14 +317,67 @@ class FastWeightProductKeyMemory(nn.Module):
         return ScoreTransform.apply(rows, float(self.score_temperature), self.score_nonlinear).view(scores.shape)
 
     def compute_marginal_entropy(self, M, epsilon=1e-8):
-        """Entropy of the batch-mean of a top-k-thresholded softmax of M [N, K]."""
+        """Entropy of the batch-mean of a top-k-thresholded softmax of M [N, K].
+        Split over data-parallel ranks, the batch mean is over every rank's
+        rows (a differentiable all-reduce of the row sums)."""
         in_dtype = M.dtype
         if self.addr_loss_weight == 0.0:
             return torch.tensor(0.0, device=M.device, dtype=in_dtype)
         kth = torch.topk(M, self.topk, dim=1).values[:, -1:]
         M = torch.where(M >= kth, M, torch.full_like(M, float("-inf"))).float()
-        P_bar = F.softmax(M, dim=1).mean(dim=0)
+        world, group = self._dp()
+        if world == 1:
+            P_bar = F.softmax(M, dim=1).mean(dim=0)
+        else:
+            from torch.distributed.nn.functional import all_reduce
+            P_bar = all_reduce(F.softmax(M, dim=1).sum(dim=0), group=group) / (M.shape[0] * world)
         return (-(P_bar * torch.log(P_bar + epsilon)).sum()).to(in_dtype)
+
+    # ------------------------------------------------------------------
+    # data parallelism over the batch (replicated fast weights)
+    # ------------------------------------------------------------------
+    def data_parallel(self, group=None):
+        """Split the batch over the ranks of ``group`` (every rank passes the
+        same number of sequences and the same parameters).  The fast weights
+        stay replicated and every inner update uses the gradient of the whole
+        batch: per chunk the memorisation loss is each rank's share of the
+        global mean, the value and key gradients are summed over the ranks
+        with differentiable all-reduces (so the outer backward, second
+        derivatives included, is the single-process one), the slot counts
+        come from every rank's indices, and the addressing loss's batch mean
+        covers every rank's rows.  After the outer backward, ``reduce_grads``
+        sums the parameters' gradients over the ranks."""
+        self.dp_group = group
+        return self
+
+    def _dp(self):
+        group = getattr(self, "dp_group", None)
+        if group is None:
+            return 1, None
+        import torch.distributed as dist
+        if not dist.is_initialized():
+            return 1, None
+        return dist.get_world_size(group), group
+
+    def reduce_grads(self):
+        """Sum the fast-weight parameters' gradients over the data-parallel ranks."""
+        world, group = self._dp()
+        if world == 1:
+            return
+        import torch.distributed as dist
+        for p in (self.keys, self.values):
+            if p.grad is not None:
+                dist.all_reduce(p.grad, group=group)
+
+    def _all_indices(self, indices):
+        """Every rank's slot indices of this chunk (for the global bincount)."""
+        world, group = self._dp()
+        if world == 1:
+            return indices
+        import torch.distributed as dist
+        parts = [torch.empty_like(indices) for _ in range(world)]
+        dist.all_gather(parts, indices.contiguous(), group=group)
+        return torch.cat([t.reshape(-1) for t in parts])
 
     def retrieve_values(self, query: torch.Tensor, fw_named_params: OrderedDict):
         B, T = query.shape[:2]
@@ -386,6 +439,13 @@ class FastWeightProductKeyMemory(nn.Module):
         else:
             loss = mem_loss if addr_loss is None else mem_loss + addr_loss
             grads = list(torch.autograd.grad(loss, params, create_graph=self.training))
+        world, group = self._dp()
+        if world > 1:
+            # each rank holds its batch share's gradient: sum them (the
+            # all-reduce is differentiable, so the outer backward sees the sum)
+            from torch.distributed.nn.functional import all_reduce
+            grads = [None if g is None else all_reduce(g, group=group) for g in grads]
+            indices = self._all_indices(indices)
         # the value gradient is a sum over samples, features, heads and top-k,
         # shared out over the times each slot was read; its scaling, the
         # bincount, the clamp and the SGD step run as one fused kernel pass
@@ -429,8 +489,18 @@ class FastWeightProductKeyMemory(nn.Module):
         """Targets shifted by ``lookahead`` tokens (``fwpkm/fwpkm.py:472-480``)."""
         return ref if self.lookahead == 0 else ref[:, self.lookahead:]
 
+    def _global_count(self, n: int) -> int:
+        world, group = self._dp()
+        if world == 1:
+            return n
+        import torch.distributed as dist
+        t = torch.tensor([n], dtype=torch.int64, device=self.keys.device)
+        dist.all_reduce(t, group=group)
+        return int(t.item())
+
     def forward_wo_past(self, q, ref_v, chunk_size, gates=None, loss_mask=None, token_ids=None):
         B, T = q.shape[:2]
+        world, _ = self._dp()
         input_dtype = q.dtype
         if self.fp32_fw:
             q = q.float()
@@ -465,7 +535,15 @@ class FastWeightProductKeyMemory(nn.Module):
                 addr_loss = self.compute_addr_loss(r["sub_indices1"], r["sub_indices2"], r["all_sub_scores1"],
                                                    r["all_sub_scores2"])
                 num_samples = (upd_mask > 0).sum().item() if upd_mask is not None else B * cT
-                new_params, grads = self.update_fw(cur, num_samples, r["indices"], mem_losses.mean(), addr_loss)
+                mem_loss = mem_losses.mean()
+                if world > 1:
+                    # this rank's share of the batch mean and of the batch's samples
+                    mem_loss = mem_loss / world
+                    num_samples = self._global_count(num_samples)
+                    addr_loss = None if addr_loss is None else addr_loss / world
+                new_params, grads = self.update_fw(cur, num_samples, r["indices"], mem_loss, addr_loss)
+                if world > 1 and addr_loss is not None:
+                    addr_loss = addr_loss * world
                 if self.ob_mode:
                     self.write_ob_log(cids.view(B, cT), r["indices"].view(B, cT, -1), cgates.view(B, cT, -1))
                 all_grads.append([None if g is None else g.detach() for g in grads])

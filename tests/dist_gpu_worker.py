@@ -183,3 +183,51 @@ def run_owner(rank: int, world: int, port: int, out_dir: str, dtype_name: str):
         del owner
     finally:
         dist.destroy_process_group()
+
+
+def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str, backend: str = "nccl"):
+    """One rank of the data-parallel fast-weight memory on the GPU kernels
+    (fp32, tiny geometry): half of the batch, fast weights replicated."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", rank if backend == "nccl" else 0)
+    torch.cuda.set_device(dev)
+    kw = dict(rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    if backend == "nccl":
+        kw["device_id"] = dev
+    dist.init_process_group(backend, **kw)
+    try:
+        import dist_worker
+        keys, values, q, ref_v = dist_worker.fwpkm_dp_case()
+        per = q.shape[0] // world
+        sl = slice(rank * per, (rank + 1) * per)
+        out = fwpkm_gpu_run(q[sl], ref_v[sl], keys, values, dev, dist.group.WORLD)
+        torch.save(out, os.path.join(out_dir, f"fwdp{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def fwpkm_gpu_run(q, ref_v, keys, values, dev, group=None):
+    import torch
+
+    import dist_worker
+    from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
+    m = FastWeightProductKeyMemory(**dist_worker.FW_DP_KW).to(dev).train()
+    with torch.no_grad():
+        m.keys.copy_(keys)
+        m.values.copy_(values)
+    if group is not None:
+        m.data_parallel(group)
+    q = q.to(dev).requires_grad_(True)
+    ref_v = ref_v.to(dev).requires_grad_(True)
+    res = m(q, ref_v, None, 8)
+    (res["output"] ** 2).sum().backward()
+    m.reduce_grads()
+    torch.cuda.synchronize()
+    return {k: v.detach().cpu() for k, v in (("out", res["output"]), ("q_grad", q.grad), ("ref_v_grad", ref_v.grad),
+                                             ("keys", m.keys), ("values", m.values), ("keys_grad", m.keys.grad),
+                                             ("values_grad", m.values.grad), ("indices", res["indices"]))}

@@ -123,3 +123,58 @@ def run_sharded(rank: int, world: int, port: int, out_dir: str, bad_rank=None):
                    os.path.join(out_dir, f"shard{rank}.pt"))
     finally:
         dist.destroy_process_group()
+
+
+FW_DP_KW = dict(mem_k_dim=16, mem_v_dim=32, mem_heads=2, mem_topk=4, mem_n_subkeys=16, lookahead=1,
+                learning_rate=0.1)
+
+
+def fwpkm_dp_case():
+    import cases
+    return cases.fwpkm_case(0, B=4, T=16)
+
+
+def fwpkm_run(q, ref_v, keys, values, group=None):
+    """``forward_wo_past`` and the outer backward of ``sum(out^2)`` for the
+    sequences given (all of them, or one rank's share with ``group``)."""
+    from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
+    import torch
+    m = FastWeightProductKeyMemory(**FW_DP_KW).train()
+    with torch.no_grad():
+        m.keys.copy_(keys)
+        m.values.copy_(values)
+    if group is not None:
+        m.data_parallel(group)
+    q = q.clone().requires_grad_(True)
+    ref_v = ref_v.clone().requires_grad_(True)
+    res = m(q, ref_v, None, 8)
+    (res["output"] ** 2).sum().backward()
+    m.reduce_grads()
+    return {"out": res["output"].detach(), "q_grad": q.grad, "ref_v_grad": ref_v.grad, "keys": m.keys.detach(),
+            "values": m.values.detach(), "keys_grad": m.keys.grad, "values_grad": m.values.grad,
+            "losses": res["losses"], "addr_loss": res["addr_loss"], "indices": res["indices"],
+            "grad_norms": torch.stack(res["grad_norms"])}
+
+
+def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str):
+    """One rank of the data-parallel fast-weight memory (gloo, CPU stand-ins)."""
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        import fake_native
+
+        class _Set:
+            setattr = staticmethod(setattr)
+        fake_native.install(_Set())
+        install_cpu_kernels()
+        keys, values, q, ref_v = fwpkm_dp_case()
+        per = q.shape[0] // world
+        sl = slice(rank * per, (rank + 1) * per)
+        out = fwpkm_run(q[sl], ref_v[sl], keys, values, dist.group.WORLD)
+        torch.save(out, os.path.join(out_dir, f"fwdp{rank}.pt"))
+    finally:
+        dist.destroy_process_group()

@@ -113,3 +113,47 @@ def test_row_sharded_bad_index_raises_on_every_rank(tmp_path):
     msgs = [torch.load(os.path.join(tmp_path, f"bad{r}.pt"))["raised"] for r in range(2)]
     assert msgs[1] == "row index outside the sharded table"
     assert msgs[0] is not None and "rank(s) [1]" in msgs[0]
+
+
+def test_fwpkm_data_parallel_equals_one_process(tmp_path, monkeypatch):
+    """The fast-weight memory with its batch split over two gloo ranks
+    (``data_parallel``): outputs, losses, indices, final fast weights and
+    every outer gradient equal one process running the whole batch (fp32,
+    1e-5; the sums only change order)."""
+    import numpy as np
+
+    import dist_worker
+    import fake_native
+    os.environ["PYTHONPATH"] = os.pathsep.join([HERE, os.path.dirname(HERE), os.environ.get("PYTHONPATH", "")])
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=dist_worker.run_fwpkm_dp, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert [p.exitcode for p in procs] == [0, 0]
+    fake_native.install(monkeypatch)
+    dist_worker.install_cpu_kernels(monkeypatch.setattr)
+    keys, values, q, ref_v = dist_worker.fwpkm_dp_case()
+    full = dist_worker.fwpkm_run(q, ref_v, keys, values)
+
+    def rel(a, b):
+        a, b = np.asarray(a, dtype=np.float64), np.asarray(b, dtype=np.float64)
+        return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+    parts = [torch.load(os.path.join(tmp_path, f"fwdp{r}.pt")) for r in range(2)]
+    for key in ("out", "q_grad", "ref_v_grad", "losses", "indices"):
+        got = torch.cat([p[key] for p in parts], 0)
+        if key == "indices":
+            assert torch.equal(got, full[key])
+        else:
+            assert rel(got.numpy(), full[key].numpy()) < 1e-5, key
+    for p in parts:
+        for key in ("keys", "values", "keys_grad", "values_grad", "grad_norms"):
+            assert rel(p[key].numpy(), full[key].numpy()) < 1e-5, key
+        assert abs(p["addr_loss"].item() - full["addr_loss"].item()) <= 1e-5 * abs(full["addr_loss"].item())

@@ -181,3 +181,49 @@ def test_row_owner_sgd(tmp_path, dtype_name, world):
             if i == 0:  # the first update: same gradient, one rounding apart at most
                 assert ((got - ref).abs() <= ref.abs() * ulp + 1e-30).all()
             assert ((got - ref).abs().max() / ref.abs().max()).item() < tol
+
+
+@pytest.mark.parametrize("backend,world", [("gloo", 2), ("nccl", 2)])
+def test_fwpkm_data_parallel_equals_one_gpu(tmp_path, backend, world):
+    """The fast-weight memory with its batch split over ranks
+    (``data_parallel``) on the GPU kernels equals one GPU running the whole
+    batch: outputs, indices, final fast weights and outer gradients (fp32,
+    1e-5).  gloo: the ranks share GPU 0; nccl: one GPU per rank."""
+    if backend == "nccl" and torch.cuda.device_count() < world:
+        pytest.skip("needs two GPUs")
+    import numpy as np
+    import torch.multiprocessing as mp
+    sys.path.insert(0, HERE)
+    import dist_gpu_worker
+    import dist_worker
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=dist_gpu_worker.run_fwpkm_dp, args=(r, world, port, str(tmp_path), backend))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert [p.exitcode for p in procs] == [0] * world
+    keys, values, q, ref_v = dist_worker.fwpkm_dp_case()
+    full = dist_gpu_worker.fwpkm_gpu_run(q, ref_v, keys, values, torch.device("cuda", 0))
+
+    def rel(a, b):
+        a, b = np.asarray(a, dtype=np.float64), np.asarray(b, dtype=np.float64)
+        return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+    parts = [torch.load(os.path.join(tmp_path, f"fwdp{r}.pt")) for r in range(world)]
+    for key in ("out", "q_grad", "ref_v_grad", "indices"):
+        got = torch.cat([p[key] for p in parts], 0)
+        if key == "indices":
+            assert torch.equal(got, full[key])
+        else:
+            assert rel(got.numpy(), full[key].numpy()) < 1e-5, key
+    for p in parts:
+        for key in ("keys", "values", "keys_grad", "values_grad"):
+            assert rel(p[key].numpy(), full[key].numpy()) < 1e-5, key
