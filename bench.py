@@ -510,7 +510,7 @@ def run_ours_c4(args, rank, world, local_rank):
 
     from modelos_b200 import _native
     from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
-    from modelos_b200.pkm.memory import linear
+    from modelos_b200.pkm.memory import LinearColsumBias
 
     import torch.distributed as dist
 
@@ -541,8 +541,8 @@ def run_ours_c4(args, rank, world, local_rank):
         for p in list(m.parameters()) + list(wq.parameters()) + list(wv.parameters()):
             p.grad = None
         xf = xin.view(-1, 1024)
-        q = linear(xf, wq.weight, wq.bias).view(C4_B, C4_T, -1)
-        ref_v = linear(xf, wv.weight, wv.bias).view(C4_B, C4_T, -1)
+        q = LinearColsumBias.apply(xf, wq.weight, wq.bias).view(C4_B, C4_T, -1)
+        ref_v = LinearColsumBias.apply(xf, wv.weight, wv.bias).view(C4_B, C4_T, -1)
         res = m(q, ref_v, None, C4_CHUNK)
         loss = (res["output"].float() ** 2).sum()
         loss.backward()
