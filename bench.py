@@ -622,9 +622,6 @@ def run_ours_c3(args, rank, world, local_rank):
         raise SystemExit("--workload c3 runs on one GPU")
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    # cuDNN's attention plans each new KV length on the host (milliseconds a
-    # decode step); the flash backend does not
-    torch.backends.cuda.enable_cudnn_sdp(False)
     clk = Clocks(local_rank).start()
     model = build_qwen3_pkm(device=dev, dtype=torch.bfloat16).train()
     g = torch.Generator(device=dev).manual_seed(0)
@@ -677,6 +674,9 @@ def run_ours_c3(args, rank, world, local_rank):
         prefill_ms = e0.elapsed_time(e1)
         cache = out.past_key_values
         nxt = out.logits[:, -1].argmax(-1, keepdim=True)
+        # cuDNN's attention plans every new KV length on the host
+        # (milliseconds a decode step); decode on the flash backend
+        torch.backends.cuda.enable_cudnn_sdp(False)
         e0.record()
         for _ in range(C3_DECODE):
             out = model(input_ids=nxt, past_key_values=cache, use_cache=True)
