@@ -207,6 +207,10 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     steps, warmup = max(args.steps, 1), max(args.warmup, 0)
+    if args.workload == "gemm":
+        print(json.dumps({"impl": "reference", "unavailable": "the GEMM comparison times torch's cuBLAS beside "
+                          "this library's kernel in the same line", "metric": "dense GEMM TFLOP/s"}), flush=True)
+        return
     if args.workload == "c3":
         print(json.dumps({"impl": "reference", "unavailable": "config 3 runs the reference's model file "
                           "(modeling_qwen3pkm.py), which is not on the benchmark machine; the PKM layer it "
@@ -704,6 +708,83 @@ def run_ours_c3(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+GEMM_SHAPES = (  # the dense GEMMs of one c2 step: name, M, N, K, A MN-major, B MN-major
+    ("query fwd", 16384, 2048, 1024, False, False), ("swilu/value fwd", 16384, 1024, 1024, False, False),
+    ("query dgrad", 16384, 1024, 2048, False, True), ("swilu/value dgrad", 16384, 1024, 1024, False, True),
+    ("query wgrad", 2048, 1024, 16384, True, True), ("swilu/value wgrad", 1024, 1024, 16384, True, True))
+
+
+def run_ours_gemm(args, rank, world, local_rank):
+    """The dense GEMM shapes of one c2 step on this library's tensor-core
+    GEMM and on torch's matmul (cuBLAS), device-timed; one line with the
+    per-shape times and rates."""
+    import torch
+
+    from modelos_b200 import _native
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    bf = torch.bfloat16
+    torch.manual_seed(0)
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps * 1000.0
+
+    rows, ours_total, torch_total, flops = [], 0.0, 0.0, 0.0
+    for name, M, N, K, amn, bmn in GEMM_SHAPES:
+        a = torch.randn((K, M) if amn else (M, K), device=dev, dtype=bf)
+        b = torch.randn((K, N) if bmn else (N, K), device=dev, dtype=bf)
+        A, Bt = (a.t() if amn else a), (b if bmn else b.t())
+        uo = timed(lambda: _native.gemm(a, b, a_mn=amn, b_mn=bmn))
+        ut = timed(lambda: A @ Bt)
+        f = 2.0 * M * N * K
+        rows.append({"gemm": name, "M": M, "N": N, "K": K, "ours_us": round(uo, 1), "torch_us": round(ut, 1),
+                     "ours_tflops": round(f / uo / 1e6, 1), "torch_tflops": round(f / ut / 1e6, 1)})
+        ours_total += uo
+        torch_total += ut
+        flops += f
+    T, G, n, half = 16384, 8, 512, 256
+    dS = torch.randn(T, G * n, device=dev, dtype=bf)
+    keys = torch.randn(G * n, half, device=dev, dtype=bf)
+    q = torch.randn(T, G * half, device=dev, dtype=bf)
+    dq = torch.empty(T, G * half, device=dev, dtype=bf)
+    dk = torch.empty(G * n, half, device=dev, dtype=bf)
+    u1 = timed(lambda: _native.gemm(dS, keys, b_mn=True, batch=G, M=T, N=half, K=n, a_batch=(n, 0), b_batch=(0, n),
+                                    out=dq, c_batch_stride=half))
+    u2 = timed(lambda: _native.gemm(dS, q, a_mn=True, b_mn=True, batch=G, M=n, N=half, K=T, a_batch=(n, 0),
+                                    b_batch=(half, 0), out=dk, c_batch_stride=n * half))
+    dSv = dS.view(T, G, n)
+    dqv = torch.empty(T, G, half, device=dev, dtype=bf)
+    t1 = timed(lambda: torch.bmm(dSv.transpose(0, 1), keys.view(G, n, half), out=dqv.transpose(0, 1)))
+    t2 = timed(lambda: torch.bmm(dSv.permute(1, 2, 0), q.view(T, G, half).transpose(0, 1)))
+    fb = 2.0 * T * G * n * half
+    rows.append({"gemm": "score dq (batched 8)", "ours_us": round(u1, 1), "torch_us": round(t1, 1),
+                 "ours_tflops": round(fb / u1 / 1e6, 1), "torch_tflops": round(fb / t1 / 1e6, 1)})
+    rows.append({"gemm": "score dk (batched 8)", "ours_us": round(u2, 1), "torch_us": round(t2, 1),
+                 "ours_tflops": round(fb / u2 / 1e6, 1), "torch_tflops": round(fb / t2 / 1e6, 1)})
+    _native.check_device_errors(dev)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        peak = 1590.0
+    rate = flops / ours_total / 1e6
+    print(json.dumps({"metric": "dense GEMM TFLOP/s over the c2 step's projection shapes", "value": round(rate, 1),
+                      "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "higher_is_better": True, "dtype": "bf16",
+                      "roofline": {"bound": "tensor", "achieved": round(rate, 1), "peak": peak, "unit": "TFLOP/s",
+                                   "frac": round(rate / peak, 4), "peak_source": "measured cuBLAS bf16 burst"},
+                      "torch_cublas_tflops": round(flops / torch_total / 1e6, 1), "shapes": rows}), flush=True)
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -904,9 +985,10 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c2", "c1", "c3", "c4"],
+    ap.add_argument("--workload", default="c2", choices=["c2", "c1", "c3", "c4", "gemm"],
                     help="c2: the PKM layer (default); c1: the embedding bag alone; c3: the Qwen3-PKM model "
-                         "(train step, prefill, decode); c4: the fast-weight memory")
+                         "(train step, prefill, decode); c4: the fast-weight memory; gemm: the c2 step's GEMM "
+                         "shapes on this library's GEMM and on cuBLAS")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--grad-exchange", default="fused", choices=["fused", "nccl", "owner"],
                     help="data-parallel exchange of the value-table gradient (N > 1); owner: the table's "
@@ -941,6 +1023,8 @@ def main():
             run_ours_c4(args, rank, world, local_rank)
         elif args.workload == "c3":
             run_ours_c3(args, rank, world, local_rank)
+        elif args.workload == "gemm":
+            run_ours_gemm(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:
