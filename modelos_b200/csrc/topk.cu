@@ -362,10 +362,13 @@ __device__ void stage2_merge(float v1, uint32_t i1, const uint32_t* idx2, const 
 }
 
 constexpr int kTopkWarps = 8;
+#ifndef PKM_TOPK_MINB
+#define PKM_TOPK_MINB 3  // resident blocks per SM the register budget is sized for
+#endif
 constexpr int kPairCap = 128;  // candidate pairs for knn <= 32 (119 at knn = 32)
 
 template <typename T, int EPL>
-__global__ void __launch_bounds__(kTopkWarps * 32, 3) product_topk_kernel(const T* __restrict__ scores, int64_t rows,
+__global__ void __launch_bounds__(kTopkWarps * 32, PKM_TOPK_MINB) product_topk_kernel(const T* __restrict__ scores, int64_t rows,
                                                                         int n, int knn,
                                                                         int64_t* __restrict__ out_idx,
                                                                         T* __restrict__ out_scores,
