@@ -807,6 +807,8 @@ def run_ours(args, rank, world, local_rank):
     reducer = None
     owner = None
     exchange = "none"
+    exchanges = []
+    waits = []  # (before, after) events around the caller's wait for the gradient exchange
     if world > 1:
         from modelos_b200.dist import GradReducer, RowOwnerSGD, ShardedTableGrad
         if args.grad_exchange == "owner":
@@ -821,6 +823,7 @@ def run_ours(args, rank, world, local_rank):
             # the bag backward computes it; owners reduce and all-gather beside
             # the rest of the backward
             ex = ShardedTableGrad(m.values.weight)
+            exchanges.append(ex)
             reducer = GradReducer(params, sharded=[ex])
             exchange = {"nvls": "fused nvls: in-switch multimem all-reduce of the table gradient beside the backward",
                         "p2p": "fused p2p: segment-pass stores to row owners + owner reduce/all-gather"}[ex.mode]
@@ -834,6 +837,8 @@ def run_ours(args, rank, world, local_rank):
         dense = [p for p in params if owner is None or p is not m.values.weight]
         opt = torch.optim.SGD(dense, lr=args.lr, foreach=True)
 
+    timing_on = [False]
+
     def step(xin):
         for p in params:
             p.grad = None
@@ -841,7 +846,14 @@ def run_ours(args, rank, world, local_rank):
         loss = (y.float() ** 2).sum()
         loss.backward()
         if reducer is not None:
+            if timing_on[0]:
+                a = torch.cuda.Event(enable_timing=True)
+                a.record()
             reducer.finish()
+            if timing_on[0]:
+                b = torch.cuda.Event(enable_timing=True)
+                b.record()
+                waits.append((a, b))
         if opt is not None:
             opt.step()
         if owner is not None:
@@ -857,6 +869,9 @@ def run_ours(args, rank, world, local_rank):
     names = ["pkm_bag_fwd", "pkm_bag_bwd", "pkm_bag_bwd_sort", "pkm_bag_bwd_rows"]
     probe = _native.EventProbe(names, min_rows=m.values.weight.shape[0])
     _native.set_probe(probe)
+    timing_on[0] = True
+    for ex in exchanges:
+        ex.timing = True
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -870,9 +885,15 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     clk.mark(t0, time.time())
     _native.set_probe(None)
+    timing_on[0] = False
+    for ex in exchanges:
+        ex.timing = False
     if world > 1:
         dist.barrier()
     ms = e0.elapsed_time(e1) / args.steps
+    ex_ms = [e.exchange_ms() for e in exchanges]
+    ex_ms = ex_ms[0] if ex_ms and ex_ms[0] is not None else None
+    wait_ms = sum(a.elapsed_time(b) for a, b in waits) / len(waits) if waits else None
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -972,6 +993,11 @@ def run_ours(args, rank, world, local_rank):
         "roofline_other": {k: v for k, v in rl.items() if k != dom},
         "clocks": clk.summary(),
     }
+    if world > 1:
+        # the table gradient's exchange on its side stream, and the part of
+        # it (with the small gradients' NCCL all-reduce) the step waits for
+        line["exchange_ms"] = None if ex_ms is None else round(ex_ms, 4)
+        line["exchange_exposed_ms"] = None if wait_ms is None else round(wait_ms, 4)
     if emb is not None:
         line["emb_bag"] = dict(emb, metric=METRIC_C1, config=config_obj(1, "c1")["workload"])
     if world == 1 and not args.no_cpu_baseline:

@@ -120,6 +120,11 @@ class ShardedTableGrad:
         self.flag = torch.zeros(1, device=dev)
         self.done = None
         self.weight = weight
+        # with `timing` set, each step's side-stream exchange is bracketed by
+        # CUDA events (start of its first transfer, end of the last barrier)
+        self.timing = False
+        self.timed = []
+        self._t0 = None
         weight._pkm_grad_exchange = self
 
     def _offset(self, h, t) -> int:
@@ -141,6 +146,7 @@ class ShardedTableGrad:
             for r0, r1 in zip(bounds[:-1], bounds[1:]):
                 ph.rows(r0, r1, self.local[: self.K])
                 self.side.wait_stream(main)
+                self._mark_start()
                 with torch.cuda.stream(self.side):
                     dist.all_reduce(self.flag, group=self.group)  # every rank's rows [r0, r1) are written
                     _native.grad_multimem_allreduce(self.mc_local, self.mc_full, weight.dtype, self.K, self.D,
@@ -151,15 +157,30 @@ class ShardedTableGrad:
             dpsw = _native.bag_bwd_sharded(indices, weight, psw, grad_out, self.recv_ptrs, self.rank,
                                            self.shard_rows, need_dpsw=need_dpsw)
             self.side.wait_stream(main)
+            self._mark_start()
             with torch.cuda.stream(self.side):
                 dist.all_reduce(self.flag, group=self.group)  # every rank's rows are in the receive buffers
                 _native.grad_shard_reduce(self.recv, self.K, self.rank, self.shard_rows, self.full_ptrs,
                                           self.scale, self.max_blocks)
         with torch.cuda.stream(self.side):
             dist.all_reduce(self.flag, group=self.group)  # every shard is in every rank's gradient
-            self.done = torch.cuda.Event()
+            self.done = torch.cuda.Event(enable_timing=self.timing)
             self.done.record(self.side)
+            if self.timing and self._t0 is not None:
+                self.timed.append((self._t0, self.done))
+            self._t0 = None
         return self.full[: self.K], dpsw
+
+    def _mark_start(self):
+        if self.timing and self._t0 is None:
+            self._t0 = torch.cuda.Event(enable_timing=True)
+            self._t0.record(self.side)
+
+    def exchange_ms(self):
+        """Mean side-stream time of the timed steps' exchanges (ms), or None."""
+        if not self.timed:
+            return None
+        return sum(a.elapsed_time(b) for a, b in self.timed) / len(self.timed)
 
     def wait(self):
         """Order the current stream after this step's exchange."""
