@@ -275,6 +275,16 @@ PKM_API int pkm_gemm_swiglu_bwd(const void* dy, int64_t ldy, const void* wv, int
  */
 PKM_API int pkm_debug_set_wait_limit(int64_t polls);
 
+/*
+ * Test hook, no counterpart in the reference: which form pkm_gemm_bf16 (and
+ * the fused SwiGLU GEMMs) run.  -1 (default): CTA pairs (clusters of two
+ * CTAs sharing one 256-row MMA tile) when M > 128, single CTAs otherwise;
+ * 0: single CTAs always; 1: CTA pairs always.  Both forms give the same
+ * results; the split count, and with it pkm_gemm_workspace, may differ.
+ * Read by later calls.
+ */
+PKM_API int pkm_debug_gemm_pair(int mode);
+
 PKM_API int pkm_score_transform_fwd(const void* scores, int dtype, int64_t rows, int64_t width,
                                     double temperature, int mode, void* out, void* stream);
 PKM_API int pkm_score_transform_bwd(const void* scores, const void* out, const void* grad_out, int dtype,

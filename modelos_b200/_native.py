@@ -45,6 +45,7 @@ _SIGS = {
     "pkm_gemm_bf16": ([_P, _I, _I64, _I64, _I64, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                        _I64, _I64, _P, _I, _P, _I, _I64, _I64, _P, ctypes.c_size_t, _P, _P], _I),
     "pkm_debug_set_wait_limit": ([_I64], _I),
+    "pkm_debug_gemm_pair": ([_I], _I),
     "pkm_gemm_f32": ([_P, _I, _I64, _I64, _I64, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                       _I64, _I64, _P, _I64, _I64, _P], _I),
     "pkm_gemm_swiglu_fwd": ([_P, _I64, _P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P], _I),
@@ -625,6 +626,12 @@ def set_wait_limit(polls: int):
     """Test hook: the pipeline wait limit of the GEMM kernel (negative: the
     default; 0: every wait gives up at once)."""
     _check(lib().pkm_debug_set_wait_limit(int(polls)), "pkm_debug_set_wait_limit")
+
+
+def set_gemm_pair(mode: int):
+    """Test hook: the GEMM's form (-1: CTA pairs when M > 128; 0: single
+    CTAs; 1: CTA pairs)."""
+    _check(lib().pkm_debug_gemm_pair(int(mode)), "pkm_debug_gemm_pair")
 
 
 TRANSFORM_MODES = {"softmax": 0, "silu": 1, "relu": 2}

@@ -22,6 +22,15 @@
 //             columns each; tcgen05.ld of the next 32 columns in flight
 //             while the current ones get their bias, rounding and 16-byte
 //             stores (or fp32 partials), one output row per thread.
+// GEMMs of more than 128 rows run as CTA pairs (clusters of two,
+// tcgen05.mma.cta_group::2): a pair computes 256 x 256 tiles, each CTA
+// stages its 128 rows of A and half of the tile's 256 rows of B (6 stages
+// of 32 KiB) and holds 128 accumulator rows; rank 0's warp 1 issues the
+// 256x256x16 MMAs, its commits reach the mbarriers of both CTAs, both CTAs'
+// copies complete on rank 0's stage barriers, and the epilogue warps of both
+// CTAs release an accumulator on rank 0's barrier.  Per output element a
+// pair stages a third less operand data than two single CTAs, which is what
+// bounds the single form (its operand copies, not the tensor pipe).
 // When the tiles alone cannot fill the SMs (weight gradients, K = tokens),
 // the K range is split over several CTAs that write fp32 partials; a second
 // kernel sums them in split order (deterministic) and applies the epilogue.
@@ -29,20 +38,35 @@
 // drains its own outstanding copies / MMAs before TMEM is released.
 #include <algorithm>
 #include <atomic>
+#include <cstring>
 
 #include "umma.cuh"
 
 namespace pkm {
 
-constexpr int GM_BM = 128, GM_BN = 256, GM_BK = 64, GM_STAGES = 4;
-constexpr int GM_A_BYTES = GM_BM * GM_BK * 2;  // 16 KiB
-constexpr int GM_B_BYTES = GM_BN * GM_BK * 2;  // 32 KiB
-constexpr int GM_STAGE = GM_A_BYTES + GM_B_BYTES;
+constexpr int GM_BM = 128, GM_BN = 256, GM_BK = 64;
 constexpr int GM_EPI_WARPS = 8;  // two per TMEM lane quarter, 128 columns each
 constexpr int GM_THREADS = 64 + GM_EPI_WARPS * 32;
-constexpr int GM_SMEM = GM_STAGES * GM_STAGE + 1024 + 256;
 constexpr int GM_MN_BOX = 64;                   // MN-major tiles arrive as 64-wide boxes
 constexpr int GM_MN_BOX_BYTES = GM_MN_BOX * GM_BK * 2;  // 8 KiB
+
+// Tile geometry of the single-CTA form and of the CTA-pair form.  Every CTA
+// holds 128 accumulator rows x 256 columns; a pair's tile is 256 x 256, each
+// CTA staging its 128 rows of A and 128 of the 256 rows of B, so a pair
+// stages a third less operand data per output element than two single CTAs.
+template <bool PAIR>
+struct GmTile {
+  static constexpr int TM = PAIR ? 2 * GM_BM : GM_BM;  // tile rows
+  static constexpr int BROWS = PAIR ? GM_BN / 2 : GM_BN;  // B rows staged per CTA
+  static constexpr int STAGES = PAIR ? 6 : 4;
+  static constexpr int A_BYTES = GM_BM * GM_BK * 2;  // 16 KiB
+  static constexpr int B_BYTES = BROWS * GM_BK * 2;  // 16 or 32 KiB
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  // per epilogue warp, one 32-row x 128-byte box of output staged for a
+  // TMA store (128-byte swizzle)
+  static constexpr int STAGING = GM_EPI_WARPS * 4096;
+  static constexpr int SMEM = STAGES * STAGE + STAGING + 1024 + 256;
+};
 
 struct GemmArgs {
   int M, N, K, batch;
@@ -65,6 +89,12 @@ struct GemmArgs {
   const __nv_bfloat16* aux_h;  // the gate projection's output h (backward)
   __nv_bfloat16* aux_out;      // z (forward) or da (backward, may be NULL)
   int64_t ld_aux;
+  // st_tma: the epilogue writes whole 32-row boxes of C (or of the split
+  // partials) through TMA stores, the box of split s, batch b, rows m.., and
+  // columns n.. at x = b * st_bx + n, y = s * st_sy + b * st_by + m; boxes
+  // that cross the edge of M or N are stored directly
+  int st_tma;
+  int st_bx, st_by, st_sy;
 };
 
 // Rounding to bf16 and back (each step of the gate is rounded where torch's
@@ -98,9 +128,12 @@ __device__ __forceinline__ void gm_gate8(const GemmArgs& a, int64_t x0, const fl
   }
 }
 
+// Bounded wait; CL: an acquire at cluster scope (arrivals from the other
+// CTA of a pair).
+template <bool CL = false>
 __device__ __forceinline__ bool gm_wait(uint64_t* bar, uint32_t parity, const GemmArgs& a, volatile int* abort_flag) {
   for (uint32_t i = 0; i < a.wait_limit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (CL ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
     if ((i & 1023) == 1023 && *abort_flag) return false;
   }
   raise_err(a.err, PKM_DEVERR_TIMEOUT);
@@ -164,29 +197,38 @@ __device__ __forceinline__ void gm_bias32(const GemmArgs& a, int n0, float* f) {
   }
 }
 
+// PAIR: launched as clusters of two CTAs; rank 0 of each pair issues the
+// pair's MMAs (M = 256), both CTAs load their halves of the operands and run
+// the epilogue on their own 128 accumulator rows.
+template <bool PAIR>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                     const GemmArgs a) {
+                     const __grid_constant__ CUtensorMap tc, const GemmArgs a) {
+  using G = GmTile<PAIR>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GM_STAGES * GM_STAGE);
-  uint64_t* empty = full + GM_STAGES;
-  uint64_t* tfull = empty + GM_STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::STAGES * G::STAGE + G::STAGING);
+  uint64_t* empty = full + G::STAGES;
+  uint64_t* tfull = empty + G::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int64_t cta0 = PAIR ? (int64_t)(blockIdx.x >> 1) : (int64_t)blockIdx.x;  // first unit
+  const int64_t ctas = PAIR ? (int64_t)(gridDim.x >> 1) : (int64_t)gridDim.x;    // unit stride
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GM_STAGES; ++s) {
+    for (int s = 0; s < G::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], GM_EPI_WARPS * 32);
+      // pair: one arrival per epilogue warp of both CTAs (rank 0's barrier)
+      mbar_init(&tempty[i], PAIR ? 2 * GM_EPI_WARPS : GM_EPI_WARPS * 32);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -194,57 +236,80 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     fence_proxy_async_smem();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 512);
+      tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&ta);
     prefetch_tmap(&tb);
+    if (a.st_tma) prefetch_tmap(&tc);
   }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();  // barrier.cluster is warp-aligned
+  if constexpr (PAIR)
+    cluster_sync_all();  // both CTAs' barriers are initialised before any copy or arrival reaches them
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
+      // rank 0's full barriers count the copies of both CTAs of a pair
+      const uint32_t full0 = PAIR ? mapa_shared(smem_u32(full), 0) : smem_u32(full);
       uint32_t u = 0;
-      for (int64_t unit = blockIdx.x; unit < a.units && !*abort_flag; unit += gridDim.x) {
+      for (int64_t unit = cta0; unit < a.units && !*abort_flag; unit += ctas) {
         int b, mt, nt, s, kb0, kb1;
         gm_decode(a, unit, b, mt, nt, s);
         gm_krange(a, s, kb0, kb1);
+        const int m0 = mt * G::TM + (int)rank * GM_BM;   // this CTA's A rows
+        const int n0 = nt * GM_BN + (int)rank * G::BROWS;  // this CTA's B rows
         for (int kb = kb0; kb < kb1; ++kb, ++u) {
-          const int st = (int)(u % GM_STAGES);
-          if (!gm_wait(&empty[st], ((u / GM_STAGES) & 1) ^ 1, a, abort_flag)) break;
-          unsigned char* sa = smem + st * GM_STAGE;
-          unsigned char* sb = sa + GM_A_BYTES;
-          mbar_arrive_expect_tx(&full[st], GM_STAGE);
+          const int st = (int)(u % G::STAGES);
+          if (!gm_wait(&empty[st], ((u / G::STAGES) & 1) ^ 1, a, abort_flag)) break;
+          unsigned char* sa = smem + st * G::STAGE;
+          unsigned char* sb = sa + G::A_BYTES;
+          if (rank == 0) mbar_arrive_expect_tx(&full[st], PAIR ? 2 * G::STAGE : G::STAGE);
+          const uint32_t fb = full0 + (uint32_t)st * 8u;
+          auto load = [&](void* dst, const CUtensorMap* map, int x, int y) {
+            if constexpr (PAIR)
+              tma_load_2d_pair(dst, map, x, y, fb);
+            else
+              tma_load_2d(dst, map, x, y, &full[st]);
+          };
           const int k0 = kb * GM_BK;
           if (a.a_mn) {
 #pragma unroll
             for (int i = 0; i < GM_BM / GM_MN_BOX; ++i)
-              tma_load_2d(sa + i * GM_MN_BOX_BYTES, &ta, mt * GM_BM + i * GM_MN_BOX + b * a.a_bx, k0 + b * a.a_by,
-                          &full[st]);
+              load(sa + i * GM_MN_BOX_BYTES, &ta, m0 + i * GM_MN_BOX + b * a.a_bx, k0 + b * a.a_by);
           } else {
-            tma_load_2d(sa, &ta, k0 + b * a.a_bx, mt * GM_BM + b * a.a_by, &full[st]);
+            load(sa, &ta, k0 + b * a.a_bx, m0 + b * a.a_by);
           }
           if (a.b_mn) {
 #pragma unroll
-            for (int i = 0; i < GM_BN / GM_MN_BOX; ++i)
-              tma_load_2d(sb + i * GM_MN_BOX_BYTES, &tb, nt * GM_BN + i * GM_MN_BOX + b * a.b_bx, k0 + b * a.b_by,
-                          &full[st]);
+            for (int i = 0; i < G::BROWS / GM_MN_BOX; ++i)
+              load(sb + i * GM_MN_BOX_BYTES, &tb, n0 + i * GM_MN_BOX + b * a.b_bx, k0 + b * a.b_by);
           } else {
-            tma_load_2d(sb, &tb, k0 + b * a.b_bx, nt * GM_BN + b * a.b_by, &full[st]);
+            load(sb, &tb, k0 + b * a.b_bx, n0 + b * a.b_by);
           }
         }
       }
-      // the copies in flight must land before the block exits (full wait limit)
-      for (uint32_t j = (u > (uint32_t)GM_STAGES ? u - GM_STAGES : 0u); j < u; ++j)
-        if (!mbar_wait(&full[j % GM_STAGES], (j / GM_STAGES) & 1, nullptr)) break;
+      // the copies in flight must land before the block exits (full wait
+      // limit); in a pair, rank 0's barriers count both CTAs' copies and the
+      // final cluster barrier holds rank 1 until rank 0 has seen them land
+      if (rank == 0)
+        for (uint32_t j = (u > (uint32_t)G::STAGES ? u - G::STAGES : 0u); j < u; ++j)
+          if (!mbar_wait(&full[j % G::STAGES], (j / G::STAGES) & 1, nullptr)) break;
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16(GM_BM, GM_BN) | ((uint32_t)a.a_mn << 15) | ((uint32_t)a.b_mn << 16);
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc =
+          umma_idesc_bf16(G::TM, GM_BN) | ((uint32_t)a.a_mn << 15) | ((uint32_t)a.b_mn << 16);
       // descriptor step per 16-element K slice: 32 bytes along a K-major row,
       // 16 rows of 128 bytes in an MN-major box
       const uint64_t a_step = a.a_mn ? (16 * 128) >> 4 : 32 >> 4;
@@ -252,48 +317,76 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       uint32_t u = 0;
       int li = 0;
       bool ok = true;
-      for (int64_t unit = blockIdx.x; unit < a.units && ok && !*abort_flag; unit += gridDim.x, ++li) {
+      for (int64_t unit = cta0; unit < a.units && ok && !*abort_flag; unit += ctas, ++li) {
         int b, mt, nt, s, kb0, kb1;
         gm_decode(a, unit, b, mt, nt, s);
         gm_krange(a, s, kb0, kb1);
         const int acc = li & 1;
-        if (!gm_wait(&tempty[acc], ((li >> 1) & 1) ^ 1, a, abort_flag)) break;
+        if (!gm_wait<PAIR>(&tempty[acc], ((li >> 1) & 1) ^ 1, a, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * GM_BN);
         for (int kb = kb0; kb < kb1; ++kb, ++u) {
-          const int st = (int)(u % GM_STAGES);
-          if (!gm_wait(&full[st], (u / GM_STAGES) & 1, a, abort_flag)) {
+          const int st = (int)(u % G::STAGES);
+          if (!gm_wait(&full[st], (u / G::STAGES) & 1, a, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const unsigned char* sa = smem + st * GM_STAGE;
+          const unsigned char* sa = smem + st * G::STAGE;
           const uint64_t ad = a.a_mn ? umma_desc_mn_sw128(sa) : umma_desc_k_sw128(sa);
-          const uint64_t bd = a.b_mn ? umma_desc_mn_sw128(sa + GM_A_BYTES) : umma_desc_k_sw128(sa + GM_A_BYTES);
+          const uint64_t bd =
+              a.b_mn ? umma_desc_mn_sw128(sa + G::A_BYTES) : umma_desc_k_sw128(sa + G::A_BYTES);
 #pragma unroll
-          for (int k = 0; k < GM_BK / 16; ++k)
-            umma_bf16(d_tmem, ad + a_step * k, bd + b_step * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
-          umma_commit(&empty[st]);
+          for (int k = 0; k < GM_BK / 16; ++k) {
+            const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
+            if constexpr (PAIR)
+              umma_bf16_pair(d_tmem, ad + a_step * k, bd + b_step * k, idesc, accum);
+            else
+              umma_bf16(d_tmem, ad + a_step * k, bd + b_step * k, idesc, accum);
+          }
+          // the stage is free in both CTAs once these MMAs have read it
+          if constexpr (PAIR)
+            umma_commit_pair(&empty[st], 3);
+          else
+            umma_commit(&empty[st]);
         }
-        if (ok) umma_commit(&tfull[acc]);
+        if (ok) {
+          if constexpr (PAIR)
+            umma_commit_pair(&tfull[acc], 3);
+          else
+            umma_commit(&tfull[acc]);
+        }
       }
       // every MMA issued here completes before TMEM is released
-      umma_commit(drain);
+      if constexpr (PAIR)
+        umma_commit_pair(drain, 1);
+      else
+        umma_commit(drain);
       mbar_wait(drain, 0, nullptr);
     }
   } else {
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;       // which 128 of the tile's 256 columns
     constexpr int HC = GM_BN / 2 / 32;      // 32-column chunks per warp
-    const int row = q * 32 + lane;
+    // pair: the accumulator-empty barriers of rank 0
+    const uint32_t tempty0 = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0u;
+    // TMA store boxes are 32 rows x 128 bytes: 32 fp32 columns (one chunk)
+    // or 64 bf16 columns (two chunks)
+    const bool f32box = a.splits > 1 || a.c_dtype == PKM_DT_F32;
+    unsigned char* stg = smem + G::STAGES * G::STAGE + (warp - 2) * 4096;
+    unsigned char* stg_row = stg + lane * 128;
     int li = 0;
-    for (int64_t unit = blockIdx.x; unit < a.units; unit += gridDim.x, ++li) {
+    for (int64_t unit = cta0; unit < a.units; unit += ctas, ++li) {
       const int acc = li & 1;
-      if (!gm_wait(&tfull[acc], (li >> 1) & 1, a, abort_flag)) break;
+      // the warp leaves together (tcgen05.ld is warp-collective)
+      const bool got = gm_wait(&tfull[acc], (li >> 1) & 1, a, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       int b, mt, nt, s;
       gm_decode(a, unit, b, mt, nt, s);
-      const int m = mt * GM_BM + row;
+      const int mw = mt * G::TM + (int)rank * GM_BM + q * 32;  // the warp's first row
+      const int m = mw + lane;
+      const bool rows_in = mw + 32 <= a.M;
       const uint32_t tbase =
           tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * GM_BN + half * (GM_BN / 2));
       // two register buffers: the load of chunk c + 1 is in flight while
@@ -306,7 +399,55 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         if (c + 1 < HC) tmem_ld_32x32b_x32(tbase + (uint32_t)((c + 1) * 32), r[(c + 1) & 1]);
         const uint32_t* rc = r[c & 1];
         const int n0 = nt * GM_BN + half * (GM_BN / 2) + c * 32;
-        if (m < a.M && n0 < a.N) {
+        const int nb = f32box ? n0 : n0 - (c & 1) * 32;  // the box's first column
+        if (a.st_tma && rows_in && nb + (f32box ? 32 : 64) <= a.N) {
+          // into the staging box (row = lane, 16-byte chunk j at j ^ (row & 7))
+          if (f32box || (c & 1) == 0) {
+            if (lane == 0) bulk_wait_read_all();  // the previous box has left shared memory
+            __syncwarp();
+          }
+          if (a.splits > 1) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<uint4*>(stg_row + ((j ^ (lane & 7)) << 4)) =
+                  make_uint4(rc[4 * j], rc[4 * j + 1], rc[4 * j + 2], rc[4 * j + 3]);
+          } else {
+            float f[32];
+            gm_bias32(a, n0, f);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] += __uint_as_float(rc[j]);
+            if (f32box) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                *reinterpret_cast<uint4*>(stg_row + ((j ^ (lane & 7)) << 4)) =
+                    make_uint4(__float_as_uint(f[4 * j]), __float_as_uint(f[4 * j + 1]),
+                               __float_as_uint(f[4 * j + 2]), __float_as_uint(f[4 * j + 3]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint4 v;
+                __nv_bfloat162 h;
+                h = __floats2bfloat162_rn(f[8 * j], f[8 * j + 1]);
+                v.x = *reinterpret_cast<uint32_t*>(&h);
+                h = __floats2bfloat162_rn(f[8 * j + 2], f[8 * j + 3]);
+                v.y = *reinterpret_cast<uint32_t*>(&h);
+                h = __floats2bfloat162_rn(f[8 * j + 4], f[8 * j + 5]);
+                v.z = *reinterpret_cast<uint32_t*>(&h);
+                h = __floats2bfloat162_rn(f[8 * j + 6], f[8 * j + 7]);
+                v.w = *reinterpret_cast<uint32_t*>(&h);
+                *reinterpret_cast<uint4*>(stg_row + ((((c & 1) * 4 + j) ^ (lane & 7)) << 4)) = v;
+              }
+            }
+          }
+          if (f32box || (c & 1) == 1) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tc, stg, b * a.st_bx + nb, s * a.st_sy + b * a.st_by + mw);
+              bulk_commit_group();
+            }
+          }
+        } else if (m < a.M && n0 < a.N) {
           if (a.splits > 1) {
             float* dst = a.ws + (((int64_t)s * a.batch + b) * a.M + m) * (int64_t)a.N + n0;
 #pragma unroll
@@ -341,13 +482,28 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         tmem_ld_wait();
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      if constexpr (PAIR) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(tempty0 + (uint32_t)acc * 8u);
+      } else {
+        mbar_arrive(&tempty[acc]);
+      }
     }
+    if (lane == 0) bulk_wait_all();  // this warp's boxes are written
   }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  if constexpr (PAIR)
+    cluster_sync_all();  // no copy, MMA or arrival of either CTA is still aimed at the other
+  else
+    __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, 512);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, 512);
+    else
+      tmem_dealloc(tmem_base, 512);
+  }
 }
 
 // out[b][m][n] = sum_s ws[s][b][m][n] + bias[n], summed in split order.
@@ -381,21 +537,64 @@ static std::atomic<int64_t> g_gemm_wait_limit{-1};
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_stride_bytes,
                       uint32_t box_cols, uint32_t box_rows);
 
+// -1: CTA pairs whenever the tile has more than 128 rows; 0: never; 1:
+// always (a test hook: both forms run every shape).
+static std::atomic<int> g_gemm_pair{-1};
+
+static bool gemm_use_pair(int64_t M) {
+  const int mode = g_gemm_pair.load();
+  return mode == 1 || (mode < 0 && M > GM_BM);
+}
+
+// Clusters of two CTAs resident at once (the pair kernel's persistent grid),
+// cached per device ordinal.
+static int gemm_pair_slots() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
+    v = num_sms() / 2;
+    if (cudaFuncSetAttribute(gemm_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             GmTile<true>::SMEM) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(2 * std::max(1, num_sms() / 2)));
+      cfg.blockDim = dim3(GM_THREADS);
+      cfg.dynamicSmemBytes = GmTile<true>::SMEM;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_bf16_kernel<true>, &cfg) == cudaSuccess && n > 0) v = n;
+    }
+    cudaGetLastError();  // a failed query leaves the fallback and no sticky error
+    v = std::max(v, 1);
+    cache[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
 // Split count: the K range is divided while the tiles alone would leave
-// SMs idle and every split keeps at least four 64-deep K blocks.
-static int gemm_splits(int64_t tiles, int64_t k_blocks) {
-  const int64_t sms = num_sms();
+// CTAs (or CTA pairs) idle and every split keeps at least four 64-deep K
+// blocks.
+static int gemm_splits(int64_t tiles, int64_t k_blocks, int64_t slots) {
   int s = 1;
-  while (tiles * s * 2 <= sms && k_blocks / (s * 2) >= 4 && s < 16) s *= 2;
+  while (tiles * s * 2 <= slots && k_blocks / (s * 2) >= 4 && s < 16) s *= 2;
   return s;
 }
 
-static void gemm_shape(int64_t batch, int64_t M, int64_t N, int64_t K, int64_t& mt, int64_t& nt, int64_t& kb,
-                       int& splits) {
-  mt = (M + GM_BM - 1) / GM_BM;
+static void gemm_shape(int64_t batch, int64_t M, int64_t N, int64_t K, bool pair, int64_t& mt, int64_t& nt,
+                       int64_t& kb, int& splits) {
+  const int64_t tm = pair ? 2 * GM_BM : GM_BM;
+  mt = (M + tm - 1) / tm;
   nt = (N + GM_BN - 1) / GM_BN;
   kb = (K + GM_BK - 1) / GM_BK;
-  splits = gemm_splits(batch * mt * nt, kb);
+  splits = gemm_splits(batch * mt * nt, kb, pair ? gemm_pair_slots() : num_sms());
 }
 
 struct GateArgs {
@@ -421,8 +620,14 @@ extern "C" int pkm_gemm_workspace(int64_t batch, int64_t M, int64_t N, int64_t K
   if (batch < 0 || M < 0 || N < 0 || K < 0) return fail(PKM_ERR_INVALID_ARG, "negative size");
   int64_t mt, nt, kb;
   int s;
-  gemm_shape(batch, M, N, K, mt, nt, kb, s);
+  gemm_shape(batch, M, N, K, gemm_use_pair(M), mt, nt, kb, s);
   *bytes = s > 1 ? (size_t)s * batch * M * N * sizeof(float) : 0;
+  return PKM_OK;
+}
+
+extern "C" int pkm_debug_gemm_pair(int mode) {
+  if (mode < -1 || mode > 1) return fail(PKM_ERR_INVALID_ARG, "mode must be -1, 0 or 1");
+  g_gemm_pair.store(mode);
   return PKM_OK;
 }
 
@@ -514,9 +719,10 @@ int pkm::gemm_launch(const void* A, int a_mn_major, int64_t a_rows, int64_t a_co
   if (a_rows > INT32_MAX || a_cols > INT32_MAX || b_rows > INT32_MAX || b_cols > INT32_MAX)
     return fail(PKM_ERR_UNSUPPORTED, "operand extent above 2^31");
 
+  const bool pair = gemm_use_pair(M);
   int64_t mt, nt, kb;
   int splits;
-  gemm_shape(batch, M, N, K, mt, nt, kb, splits);
+  gemm_shape(batch, M, N, K, pair, mt, nt, kb, splits);
   if (gate.epi) {
     if (batch != 1) return fail(PKM_ERR_INVALID_ARG, "the fused gate takes one GEMM");
     splits = 1;
@@ -531,7 +737,7 @@ int pkm::gemm_launch(const void* A, int a_mn_major, int64_t a_rows, int64_t a_co
                              a_mn_major ? GM_MN_BOX : GM_BK, a_mn_major ? GM_BK : GM_BM);
   if (rc) return rc;
   rc = make_tmap_bf16_2d(&tb, B, (uint64_t)b_cols, (uint64_t)b_rows, (uint64_t)(ldb * 2),
-                         b_mn_major ? GM_MN_BOX : GM_BK, b_mn_major ? GM_BK : GM_BN);
+                         b_mn_major ? GM_MN_BOX : GM_BK, b_mn_major ? GM_BK : (pair ? GM_BN / 2 : GM_BN));
   if (rc) return rc;
   GemmArgs a{};
   a.M = (int)M;
@@ -562,13 +768,76 @@ int pkm::gemm_launch(const void* A, int a_mn_major, int64_t a_rows, int64_t a_co
   a.aux_h = static_cast<const __nv_bfloat16*>(gate.h);
   a.aux_out = static_cast<__nv_bfloat16*>(gate.out);
   a.ld_aux = gate.ld;
+  // the epilogue's TMA store map: the split partials [splits * batch * M, N]
+  // fp32, or C viewed as one matrix holding every batch (batches offset by
+  // whole rows or by columns within a row); anything else stores directly
+  CUtensorMap tcm;
+  memset(&tcm, 0, sizeof(tcm));
+  a.st_tma = 0;
+  if (!gate.epi) {
+    int64_t rows = 0, cols = 0, bx = 0, by = 0, sy = 0;
+    if (splits > 1) {
+      rows = (int64_t)splits * batch * M;
+      cols = N;
+      by = M;
+      sy = batch * M;
+    } else if (batch == 1) {
+      rows = M;
+      cols = N;
+    } else if (c_batch_stride % ldc == 0) {
+      by = c_batch_stride / ldc;
+      rows = (batch - 1) * by + M;
+      cols = N;
+    } else if ((batch - 1) * c_batch_stride + N <= ldc) {
+      bx = c_batch_stride;
+      rows = M;
+      cols = (batch - 1) * c_batch_stride + N;
+    }
+    if (rows > 0 && rows < INT32_MAX && cols < INT32_MAX) {
+      const bool ws32 = splits > 1;
+      const int dt = ws32 ? PKM_DT_F32 : c_dtype;
+      const int64_t pitch = ws32 ? N * 4 : ldc * dtype_size(c_dtype);
+      if (make_tmap_2d(&tcm, ws32 ? workspace : C, dt, (uint64_t)cols, (uint64_t)rows, (uint64_t)pitch,
+                       dt == PKM_DT_F32 ? 32 : 64, 32) == PKM_OK) {
+        a.st_tma = 1;
+        a.st_bx = (int)bx;
+        a.st_by = (int)by;
+        a.st_sy = (int)sy;
+      }
+    }
+  }
   const int64_t wl = g_gemm_wait_limit.load();
   a.wait_limit = wl < 0 ? kWaitLimit : (uint32_t)wl;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM) != cudaSuccess)
-    return check_cuda("cudaFuncSetAttribute(gemm_bf16)");
-  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(a.units, num_sms()));
-  gemm_bf16_kernel<<<(unsigned)grid, GM_THREADS, GM_SMEM, st>>>(ta, tb, a);
+  if (pair) {
+    if (cudaFuncSetAttribute(gemm_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             GmTile<true>::SMEM) != cudaSuccess)
+      return check_cuda("cudaFuncSetAttribute(gemm_bf16 pair)");
+    const int64_t clusters = std::max<int64_t>(1, std::min<int64_t>(a.units, gemm_pair_slots()));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * clusters));
+    cfg.blockDim = dim3(GM_THREADS);
+    cfg.dynamicSmemBytes = GmTile<true>::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<true>, ta, tb, tcm, a);
+    if (le != cudaSuccess) {
+      cudaGetLastError();
+      return fail(PKM_ERR_CUDA, std::string("gemm_bf16_kernel (pair) launch: ") + cudaGetErrorString(le));
+    }
+  } else {
+    if (cudaFuncSetAttribute(gemm_bf16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             GmTile<false>::SMEM) != cudaSuccess)
+      return check_cuda("cudaFuncSetAttribute(gemm_bf16)");
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(a.units, num_sms()));
+    gemm_bf16_kernel<false><<<(unsigned)grid, GM_THREADS, GmTile<false>::SMEM, st>>>(ta, tb, tcm, a);
+  }
   rc = check_cuda("gemm_bf16_kernel");
   if (rc || splits == 1) return rc;
   const int64_t per = batch * M * (N / 4);

@@ -5,7 +5,9 @@ matrix, split K, and the batched forms the scoring backward uses.  fp32
 outputs within 1e-5 (only the summation order differs), bf16 outputs within
 one bf16 rounding (2^-8) normwise.  Also the bounded-wait path: with a wait
 limit of zero polls every pipeline wait gives up, the kernel reports
-PKM_DEVERR_TIMEOUT, drains and returns, and the next call is correct."""
+PKM_DEVERR_TIMEOUT, drains and returns, and the next call is correct.
+Each of these runs in both forms of the kernel: single CTAs and CTA pairs
+(clusters of two sharing a 256-row MMA tile, forced even where M <= 128)."""
 from __future__ import annotations
 
 import numpy as np
@@ -20,6 +22,14 @@ def rel_err(a, b):
     a = a.double().cpu()
     b = b.double().cpu()
     return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+@pytest.fixture(params=[0, 1], ids=["single", "pair"])
+def form(request):
+    from modelos_b200 import _native
+    _native.set_gemm_pair(request.param)
+    yield request.param
+    _native.set_gemm_pair(-1)
 
 
 def _operand(rows, cols, g, pitch_extra=0):
@@ -42,7 +52,7 @@ CASES = [
 
 
 @pytest.mark.parametrize("M,N,K,a_mn,b_mn,bias,dt,pitch", CASES)
-def test_gemm_matches_torch(M, N, K, a_mn, b_mn, bias, dt, pitch):
+def test_gemm_matches_torch(M, N, K, a_mn, b_mn, bias, dt, pitch, form):
     from modelos_b200 import _native
     g = torch.Generator().manual_seed(M + N + K)
     a = _operand(K, M, g, pitch) if a_mn else _operand(M, K, g, pitch)
@@ -61,7 +71,7 @@ def test_gemm_matches_torch(M, N, K, a_mn, b_mn, bias, dt, pitch):
     assert rel_err(c, ref) < tol
 
 
-def test_gemm_batched_scoring_backward_forms():
+def test_gemm_batched_scoring_backward_forms(form):
     """The two batched GEMMs of the scoring backward over (head, half) groups:
     dq[t, g, :] = dS[t, g, :] @ keys_g and dk_g = dS[:, g, :].T @ q[:, g, :]."""
     from modelos_b200 import _native
@@ -98,7 +108,7 @@ def test_gemm_rejects_bad_arguments():
         _native.gemm(a, b)  # N = 12
 
 
-def test_gemm_bounded_waits_time_out_and_recover():
+def test_gemm_bounded_waits_time_out_and_recover(form):
     """Zero polls per pipeline wait: the kernel sets PKM_DEVERR_TIMEOUT,
     drains its copies and MMAs, releases TMEM and returns; with the default
     limit restored the same call on the same context is correct again."""
@@ -121,7 +131,7 @@ def test_gemm_bounded_waits_time_out_and_recover():
     assert np.isfinite(c.cpu().numpy()).all()
 
 
-def test_fused_swiglu_gemms_equal_unfused_kernels():
+def test_fused_swiglu_gemms_equal_unfused_kernels(form):
     """The gate in the GEMM epilogues (``pkm_gemm_swiglu_fwd/bwd``) gives the
     same bits as the GEMM followed by the standalone gate kernels, and
     matches the reference's op sequence in fp32 within bf16 tolerance."""
@@ -152,6 +162,26 @@ def test_fused_swiglu_gemms_equal_unfused_kernels():
     sig = torch.sigmoid(hr)
     assert rel_err(da, dzr * F.silu(hr)) < 2e-2
     assert rel_err(dh, dzr * a.float() * sig * (1 + hr * (1 - sig))) < 2e-2
+
+
+def test_gemm_pair_equals_single_without_split():
+    """Where neither form splits K, the pair form's 256-row MMAs sum every
+    output in the same K order as the single form's 128-row MMAs: the same
+    bits."""
+    from modelos_b200 import _native
+    g = torch.Generator().manual_seed(5)
+    outs = []
+    a = torch.randn(4096, 1024, generator=g).to(torch.bfloat16).to(DEV)
+    b = torch.randn(2048, 1024, generator=g).to(torch.bfloat16).to(DEV)
+    try:
+        for mode in (0, 1):
+            _native.set_gemm_pair(mode)
+            outs.append(_native.gemm(a, b, out_dtype=torch.float32))
+    finally:
+        _native.set_gemm_pair(-1)
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    assert torch.equal(outs[0], outs[1])
 
 
 F32_CASES = [
