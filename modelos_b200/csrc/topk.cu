@@ -5,7 +5,9 @@
 // rows).  Stage 1 selects the knn best sub-keys of each half: a bitwise radix
 // select on order-preserving integer keys finds the knn-th largest key T,
 // the keys above T and the lowest-index keys equal to T are compacted, and a
-// warp bitonic network sorts them (score descending, index ascending).
+// warp bitonic network sorts them (score descending, index ascending).  Full
+// bf16 rows first try a shorter route (a bound from each lane's best two, a
+// few dozen candidates placed by their ranks; stage1_select_bf16).
 //
 // Stage 2 needs the knn best sums s1[i] + s2[j] (rounded to the score dtype)
 // of the knn x knn product.  With both lists sorted, the pair (i, j) is
@@ -19,8 +21,8 @@
 // whether row i has such a pair; if any row has one (rare), the row is
 // finished by an exact k-way merge of the knn sorted rows instead.  Pairs
 // equal to T are taken in ascending slot order (slot = i1 * n + i2), as
-// many as the top knn has room for.  Nothing of the product is
-// materialised.
+// many as the top knn has room for; the knn selected pairs are placed in
+// the output by their ranks.  Nothing of the product is materialised.
 //
 // Non-finite scores (a diverged model) keep every index a valid slot: NaN
 // ranks above +inf, as in torch.topk, in both stages.
@@ -226,9 +228,22 @@ __device__ __forceinline__ uint32_t unkey16_bits(uint32_t k) { return (k & 0x800
 // l*EPL+EPL-1, word k = elements 2k and 2k+1): the same selection as
 // stage1_select, with every count taken by packed bf16x2 comparisons
 // (two elements per instruction, -0 equal to +0 as in the key order).
+//
+// Most rows take a shorter route first.  The knn-th largest L of the 64
+// values {best two of each lane} is a lower bound of the knn-th largest
+// score T (at least knn distinct elements are >= L), and on scores of
+// trained or random layers only ~36 of 512 elements reach it.  Those are
+// compacted as 32-bit composites (key << 16 | 0xffff - index: larger is
+// better, all distinct), each one's rank among them is counted, and the
+// knn of rank < knn land in rank order: sorted, ties at T taken by lowest
+// index, exactly the selection below.  Rows with more than 64 elements at
+// or above L (wide ties) take the radix select.
+constexpr int kCandCap = 64;
+
 template <int EPL>
 __device__ __forceinline__ void stage1_select_bf16(const uint32_t (&w)[EPL / 2], int knn, uint32_t* s_key,
-                                                   uint32_t* s_idx, uint32_t& okey, uint32_t& oidx) {
+                                                   uint32_t* s_idx, uint32_t* s_comp, uint32_t& okey,
+                                                   uint32_t& oidx) {
   constexpr int NW = EPL / 2;
   static_assert(NW <= 8, "mask_count takes at most 8 masks");
   const int lane = threadIdx.x & 31;
@@ -246,6 +261,64 @@ __device__ __forceinline__ void stage1_select_bf16(const uint32_t (&w)[EPL / 2],
   }
   const uint32_t lmax = max(key16(mw & 0xffffu), key16(mw >> 16));
   const uint32_t lo = __reduce_min_sync(0xffffffffu, lmax), hi = __reduce_max_sync(0xffffffffu, lmax);
+  {
+    // the lane's best two (even and odd elements apart, then merged)
+    __nv_bfloat162 t1 = bf2(w[0]), t2 = bf2(0xff80ff80u);
+#pragma unroll
+    for (int k = 1; k < NW; ++k) {
+      const __nv_bfloat162 x = bf2(w[k]);
+      t2 = __hmax2(t2, __hmin2(t1, x));
+      t1 = __hmax2(t1, x);
+    }
+    const uint32_t t1w = *reinterpret_cast<uint32_t*>(&t1), t2w = *reinterpret_cast<uint32_t*>(&t2);
+    const uint32_t ka = key16(t1w & 0xffffu), kb = key16(t1w >> 16);
+    const uint32_t two[2] = {max(ka, kb), max(min(ka, kb), max(key16(t2w & 0xffffu), key16(t2w >> 16)))};
+    const uint32_t L = warp_kth_key<2>(two, knn, lo, hi);
+    const uint32_t lb = unkey16_bits(L);
+    const __nv_bfloat162 l2 = bf2(lb | (lb << 16));
+    uint32_t gem[NW];
+    uint32_t gacc = 0;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+      gem[k] = __hge2_mask(bf2(w[k]), l2);
+      gacc += gem[k];
+    }
+    const int cnt = mask_count(gacc);
+    const int total = __reduce_add_sync(0xffffffffu, cnt);
+    if (total <= kCandCap) {
+      int pos = warp_excl_prefix(cnt);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        if ((gem[e >> 1] >> ((e & 1) ? 31 : 15)) & 1u) {
+          const uint32_t kk = key16((e & 1) ? (w[e >> 1] >> 16) : (w[e >> 1] & 0xffffu));
+          s_comp[pos++] = (kk << 16) | (0xffffu - (uint32_t)(lane * EPL + e));
+        }
+      }
+      if (lane < 4) s_comp[total + lane] = 0u;  // pads the last 16-byte group; no element's composite is 0
+      __syncwarp();
+      const uint32_t c0 = lane < total ? s_comp[lane] : 0u;
+      const uint32_t c1 = lane + 32 < total ? s_comp[lane + 32] : 0u;
+      int r0 = 0, r1 = 0;
+      for (int i = 0; i < total; i += 4) {
+        const uint4 x = *reinterpret_cast<const uint4*>(s_comp + i);
+        r0 += (x.x > c0) + (x.y > c0) + (x.z > c0) + (x.w > c0);
+        r1 += (x.x > c1) + (x.y > c1) + (x.z > c1) + (x.w > c1);
+      }
+      if (lane < total && r0 < knn) {
+        s_key[r0] = c0 >> 16;
+        s_idx[r0] = 0xffffu - (c0 & 0xffffu);
+      }
+      if (lane + 32 < total && r1 < knn) {
+        s_key[r1] = c1 >> 16;
+        s_idx[r1] = 0xffffu - (c1 & 0xffffu);
+      }
+      __syncwarp();
+      okey = lane < knn ? s_key[lane] : 0u;
+      oidx = lane < knn ? s_idx[lane] : 0xffffffffu;
+      __syncwarp();
+      return;
+    }
+  }
   uint32_t T = lo;
   if (lo != hi) {
     const int top = 31 - __clz(lo ^ hi);
@@ -375,13 +448,14 @@ __global__ void __launch_bounds__(kTopkWarps * 32, PKM_TOPK_MINB) product_topk_k
                                                                         T* __restrict__ out_psw,
                                                                         int64_t* __restrict__ sub1,
                                                                         int64_t* __restrict__ sub2, bool vec_ok) {
-  __shared__ uint32_t sh_key[kTopkWarps][32];
-  __shared__ uint32_t sh_idx[kTopkWarps][32];
+  __shared__ __align__(16) uint32_t sh_key[kTopkWarps][32];
+  __shared__ __align__(16) uint32_t sh_idx[kTopkWarps][32];
   __shared__ float sh_v1[kTopkWarps][32];
   __shared__ uint32_t sh_i1[kTopkWarps][32];
   __shared__ float sh_v2[kTopkWarps][32];
   __shared__ uint32_t sh_i2[kTopkWarps][32];
   __shared__ uint16_t sh_pair[kTopkWarps][kPairCap];
+  __shared__ __align__(16) uint32_t sh_comp[kTopkWarps][kCandCap + 4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int KB = ScoreT<T>::KEYBITS;
   constexpr int PV = ScoreT<T>::PER_VEC;
@@ -423,7 +497,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32, PKM_TOPK_MINB) product_topk_k
           w[4 * v + 2] = q.z;
           w[4 * v + 3] = q.w;
         }
-        stage1_select_bf16<EPL>(w, knn, s_key, s_idx, ok, oi);
+        stage1_select_bf16<EPL>(w, knn, s_key, s_idx, sh_comp[warp], ok, oi);
         if (p == 0) {
           k1 = ok;
           i1 = oi;
@@ -551,12 +625,34 @@ __global__ void __launch_bounds__(kTopkWarps * 32, PKM_TOPK_MINB) product_topk_k
           ++pos;
         }
       }
+      if (!live) {
+        s_key[lane] = 0u;  // pads to 32 entries; no selected pair has key 0
+        s_idx[lane] = 0xffffffffu;
+      }
       __syncwarp();
-      uint32_t ok = live ? s_key[lane] : 0u;
+      // each pair's rank among the knn (sum descending, slot ascending; the
+      // slots are distinct) is its place in the output
+      const uint32_t ok = s_key[lane], os = s_idx[lane];
+      const float ov = sh_v1[warp][lane];
+      int rk = 0;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const uint4 kq = *reinterpret_cast<const uint4*>(s_key + i);
+        const uint4 sq = *reinterpret_cast<const uint4*>(s_idx + i);
+        rk += (kq.x > ok) + (kq.x == ok && sq.x < os);
+        rk += (kq.y > ok) + (kq.y == ok && sq.y < os);
+        rk += (kq.z > ok) + (kq.z == ok && sq.z < os);
+        rk += (kq.w > ok) + (kq.w == ok && sq.w < os);
+      }
+      __syncwarp();
+      if (live) {
+        s_idx[rk] = os;
+        sh_v1[warp][rk] = ov;
+      }
+      __syncwarp();
       my_slot = live ? s_idx[lane] : 0xffffffffu;
       my_val = live ? sh_v1[warp][lane] : -INFINITY;
       __syncwarp();
-      warp_sort_desc(ok, my_slot, my_val);
     }
     // outputs + per-row softmax (fp32, stored in the score dtype)
     if (live) {

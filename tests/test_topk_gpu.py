@@ -75,7 +75,8 @@ def test_scores_bf16_tensor_cores(N, H, kd, n):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("n,knn", [(128, 32), (512, 32), (100, 7), (16, 4), (1024, 32), (33, 1)])
+@pytest.mark.parametrize("n,knn", [(128, 32), (512, 32), (512, 7), (256, 32), (256, 8), (100, 7), (16, 4),
+                                   (1024, 32), (33, 1)])
 def test_product_topk_bit_exact(dtype, n, knn):
     from modelos_b200 import _native
     g = torch.Generator().manual_seed(n * 100 + knn)
