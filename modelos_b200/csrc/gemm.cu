@@ -95,6 +95,10 @@ struct GemmArgs {
   // that cross the edge of M or N are stored directly
   int st_tma;
   int st_bx, st_by, st_sy;
+  // gt_tma: the gate epilogue moves whole 32 x 32 boxes through TMA: a (and
+  // h) loaded, h / dh and z / da stored (64-byte swizzle, two 2 KiB boxes
+  // per warp); boxes crossing the edge of M or N use direct accesses
+  int gt_tma;
 };
 
 // Rounding to bf16 and back (each step of the gate is rounded where torch's
@@ -105,10 +109,9 @@ __device__ __forceinline__ float rb16(float x) { return __bfloat162float(__float
 // projection's output), s = silu(h), z = a * s.  Backward: g = acc (the
 // gradient of z), da = g * s, ds = g * a, dh = ds * sig * (1 + h (1 - sig)).
 // `o` receives h (forward) or dh (backward), `o2` z or da.
-__device__ __forceinline__ void gm_gate8(const GemmArgs& a, int64_t x0, const float* acc, float* o, float* o2) {
-  float av[8], hv[8];
-  VecTraits<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(a.aux_a + x0), av);
-  if (a.epi == 1) {
+__device__ __forceinline__ void gate8(int epi, const float* av, const float* hv, const float* acc, float* o,
+                                      float* o2) {
+  if (epi == 1) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const float h = rb16(acc[k]);
@@ -116,7 +119,6 @@ __device__ __forceinline__ void gm_gate8(const GemmArgs& a, int64_t x0, const fl
       o2[k] = rb16(av[k] * rb16(h / (1.f + expf(-h))));
     }
   } else {
-    VecTraits<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(a.aux_h + x0), hv);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const float g = rb16(acc[k]);
@@ -126,6 +128,19 @@ __device__ __forceinline__ void gm_gate8(const GemmArgs& a, int64_t x0, const fl
       o[k] = rb16(rb16(g * av[k]) * sig * (1.f + hv[k] * (1.f - sig)));
     }
   }
+}
+
+// The same with a and h read from global memory.
+__device__ __forceinline__ void gm_gate8(const GemmArgs& a, int64_t x0, const float* acc, float* o, float* o2) {
+  float av[8], hv[8];
+  VecTraits<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(a.aux_a + x0), av);
+  if (a.epi == 2) VecTraits<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(a.aux_h + x0), hv);
+  gate8(a.epi, av, hv, acc, o, o2);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
 }
 
 // Bounded wait; CL: an acquire at cluster scope (arrivals from the other
@@ -203,7 +218,9 @@ __device__ __forceinline__ void gm_bias32(const GemmArgs& a, int n0, float* f) {
 template <bool PAIR>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                     const __grid_constant__ CUtensorMap tc, const GemmArgs a) {
+                     const __grid_constant__ CUtensorMap tc, const __grid_constant__ CUtensorMap tx_a,
+                     const __grid_constant__ CUtensorMap tx_h, const __grid_constant__ CUtensorMap tx_o,
+                     const GemmArgs a) {
   using G = GmTile<PAIR>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -213,7 +230,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   uint64_t* tfull = empty + G::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* ebar = drain + 1;  // one per epilogue warp: its gate-input boxes
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + GM_EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -231,6 +249,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       mbar_init(&tempty[i], PAIR ? 2 * GM_EPI_WARPS : GM_EPI_WARPS * 32);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < GM_EPI_WARPS; ++i) mbar_init(&ebar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -247,7 +266,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&ta);
     prefetch_tmap(&tb);
-    if (a.st_tma) prefetch_tmap(&tc);
+    if (a.st_tma || a.gt_tma) prefetch_tmap(&tc);
+    if (a.gt_tma) {
+      prefetch_tmap(&tx_a);
+      if (a.epi == 2) prefetch_tmap(&tx_h);
+      if (a.aux_out) prefetch_tmap(&tx_o);
+    }
   }
   tc_fence_before();
   __syncwarp();  // barrier.cluster is warp-aligned
@@ -375,6 +399,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     const bool f32box = a.splits > 1 || a.c_dtype == PKM_DT_F32;
     unsigned char* stg = smem + G::STAGES * G::STAGE + (warp - 2) * 4096;
     unsigned char* stg_row = stg + lane * 128;
+    // gate boxes: 32 rows x 64 bytes each, 16-byte chunk j of row r at
+    // j ^ ((r >> 1) & 3) (64-byte swizzle); box A holds a, then z / da;
+    // box H holds h (backward), then h / dh
+    unsigned char* gbox_a = stg;
+    unsigned char* gbox_h = stg + 2048;
+    const uint32_t g_sw = (uint32_t)((lane >> 1) & 3);
+    uint64_t* my_ebar = &ebar[warp - 2];
+    uint32_t eph = 0;  // loads completed on my_ebar
     int li = 0;
     for (int64_t unit = cta0; unit < a.units; unit += ctas, ++li) {
       const int acc = li & 1;
@@ -394,13 +426,54 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       uint32_t r[2][32];
       tmem_ld_32x32b_x32(tbase, r[0]);
       tmem_ld_wait();
+      bool gate_fail = false;  // a gate box never arrived: the warp leaves (the error is raised)
 #pragma unroll
       for (int c = 0; c < HC; ++c) {
         if (c + 1 < HC) tmem_ld_32x32b_x32(tbase + (uint32_t)((c + 1) * 32), r[(c + 1) & 1]);
         const uint32_t* rc = r[c & 1];
         const int n0 = nt * GM_BN + half * (GM_BN / 2) + c * 32;
         const int nb = f32box ? n0 : n0 - (c & 1) * 32;  // the box's first column
-        if (a.st_tma && rows_in && nb + (f32box ? 32 : 64) <= a.N) {
+        if (a.gt_tma && rows_in && n0 + 32 <= a.N) {
+          // the gate through TMA boxes
+          if (lane == 0) {
+            bulk_wait_read_all();  // the previous boxes have left shared memory
+            mbar_arrive_expect_tx(my_ebar, a.epi == 2 ? 4096u : 2048u);
+            tma_load_2d(gbox_a, &tx_a, n0, mw, my_ebar);
+            if (a.epi == 2) tma_load_2d(gbox_h, &tx_h, n0, mw, my_ebar);
+          }
+          const bool got_box = gm_wait(my_ebar, eph & 1u, a, abort_flag);
+          ++eph;
+          if (!__all_sync(0xffffffffu, got_box)) {
+            tmem_ld_wait();
+            gate_fail = true;
+            break;
+          }
+          float f[32];
+          gm_bias32(a, n0, f);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] += __uint_as_float(rc[j]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t off = (uint32_t)lane * 64u + ((((uint32_t)j) ^ g_sw) << 4);
+            float av[8], hv[8], o[8], o2[8];
+            VecTraits<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(gbox_a + off), av);
+            if (a.epi == 2) VecTraits<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(gbox_h + off), hv);
+            gate8(a.epi, av, hv, f + 8 * j, o, o2);
+            *reinterpret_cast<uint4*>(gbox_h + off) =
+                make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                           pack_bf16x2(o[6], o[7]));
+            *reinterpret_cast<uint4*>(gbox_a + off) =
+                make_uint4(pack_bf16x2(o2[0], o2[1]), pack_bf16x2(o2[2], o2[3]), pack_bf16x2(o2[4], o2[5]),
+                           pack_bf16x2(o2[6], o2[7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tc, gbox_h, n0, mw);
+            if (a.aux_out) tma_store_2d(&tx_o, gbox_a, n0, mw);
+            bulk_commit_group();
+          }
+        } else if (a.st_tma && rows_in && nb + (f32box ? 32 : 64) <= a.N) {
           // into the staging box (row = lane, 16-byte chunk j at j ^ (row & 7))
           if (f32box || (c & 1) == 0) {
             if (lane == 0) bulk_wait_read_all();  // the previous box has left shared memory
@@ -481,6 +554,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         }
         tmem_ld_wait();
       }
+      if (gate_fail) break;
       tc_fence_before();
       if constexpr (PAIR) {
         __syncwarp();
@@ -771,9 +845,26 @@ int pkm::gemm_launch(const void* A, int a_mn_major, int64_t a_rows, int64_t a_co
   // the epilogue's TMA store map: the split partials [splits * batch * M, N]
   // fp32, or C viewed as one matrix holding every batch (batches offset by
   // whole rows or by columns within a row); anything else stores directly
-  CUtensorMap tcm;
+  CUtensorMap tcm, txa, txh, txo;
   memset(&tcm, 0, sizeof(tcm));
+  memset(&txa, 0, sizeof(txa));
+  memset(&txh, 0, sizeof(txh));
+  memset(&txo, 0, sizeof(txo));
   a.st_tma = 0;
+  a.gt_tma = 0;
+  if (gate.epi && M < INT32_MAX) {
+    // the gate's operands are [M, N] bf16: C at pitch ldc, a / h / aux_out at
+    // the gate pitch; boxes of 32 columns x 32 rows, 64-byte swizzle
+    const int64_t lg = gate.ld * 2;
+    bool ok = make_tmap_2d(&tcm, C, PKM_DT_BF16, (uint64_t)N, (uint64_t)M, (uint64_t)(ldc * 2), 32, 32, 64) ==
+                  PKM_OK &&
+              make_tmap_2d(&txa, gate.a, PKM_DT_BF16, (uint64_t)N, (uint64_t)M, (uint64_t)lg, 32, 32, 64) == PKM_OK;
+    if (ok && gate.epi == 2)
+      ok = make_tmap_2d(&txh, gate.h, PKM_DT_BF16, (uint64_t)N, (uint64_t)M, (uint64_t)lg, 32, 32, 64) == PKM_OK;
+    if (ok && gate.out)
+      ok = make_tmap_2d(&txo, gate.out, PKM_DT_BF16, (uint64_t)N, (uint64_t)M, (uint64_t)lg, 32, 32, 64) == PKM_OK;
+    a.gt_tma = ok ? 1 : 0;
+  }
   if (!gate.epi) {
     int64_t rows = 0, cols = 0, bx = 0, by = 0, sy = 0;
     if (splits > 1) {
@@ -798,7 +889,7 @@ int pkm::gemm_launch(const void* A, int a_mn_major, int64_t a_rows, int64_t a_co
       const int dt = ws32 ? PKM_DT_F32 : c_dtype;
       const int64_t pitch = ws32 ? N * 4 : ldc * dtype_size(c_dtype);
       if (make_tmap_2d(&tcm, ws32 ? workspace : C, dt, (uint64_t)cols, (uint64_t)rows, (uint64_t)pitch,
-                       dt == PKM_DT_F32 ? 32 : 64, 32) == PKM_OK) {
+                       dt == PKM_DT_F32 ? 32 : 64, 32, 128) == PKM_OK) {
         a.st_tma = 1;
         a.st_bx = (int)bx;
         a.st_by = (int)by;
@@ -826,7 +917,7 @@ int pkm::gemm_launch(const void* A, int a_mn_major, int64_t a_rows, int64_t a_co
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t le = cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<true>, ta, tb, tcm, a);
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<true>, ta, tb, tcm, txa, txh, txo, a);
     if (le != cudaSuccess) {
       cudaGetLastError();
       return fail(PKM_ERR_CUDA, std::string("gemm_bf16_kernel (pair) launch: ") + cudaGetErrorString(le));
@@ -836,7 +927,8 @@ int pkm::gemm_launch(const void* A, int a_mn_major, int64_t a_rows, int64_t a_co
                              GmTile<false>::SMEM) != cudaSuccess)
       return check_cuda("cudaFuncSetAttribute(gemm_bf16)");
     const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(a.units, num_sms()));
-    gemm_bf16_kernel<false><<<(unsigned)grid, GM_THREADS, GmTile<false>::SMEM, st>>>(ta, tb, tcm, a);
+    gemm_bf16_kernel<false><<<(unsigned)grid, GM_THREADS, GmTile<false>::SMEM, st>>>(ta, tb, tcm, txa, txh, txo,
+                                                                                       a);
   }
   rc = check_cuda("gemm_bf16_kernel");
   if (rc || splits == 1) return rc;

@@ -225,7 +225,7 @@ static EncodeTiledFn encode_fn() {
 }
 
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t cols, uint64_t rows,
-                 uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows) {
+                 uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows, int swizzle_bytes) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(PKM_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   if (dtype != PKM_DT_BF16 && dtype != PKM_DT_F32) return fail(PKM_ERR_INVALID_ARG, "tensor map dtype");
@@ -235,7 +235,8 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t cols, u
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r =
       fn(map, dtype == PKM_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
-         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(PKM_ERR_INVALID_ARG, "cuTensorMapEncodeTiled rejected the operand");
   return PKM_OK;
@@ -243,7 +244,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t cols, u
 
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_stride_bytes,
                       uint32_t box_cols, uint32_t box_rows) {
-  return make_tmap_2d(map, base, PKM_DT_BF16, cols, rows, row_stride_bytes, box_cols, box_rows);
+  return make_tmap_2d(map, base, PKM_DT_BF16, cols, rows, row_stride_bytes, box_cols, box_rows, 128);
 }
 
 bool subkey_scores_tc_eligible(int64_t heads, int64_t k_dim, int64_t n_keys, const void* query, const void* keys,

@@ -207,8 +207,9 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 // `row_stride_bytes`, box [box_rows, box_cols] and 128-byte swizzle.
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_stride_bytes,
                       uint32_t box_cols, uint32_t box_rows);
-// The same for bf16 or fp32 elements (PKM_DT_BF16 / PKM_DT_F32).
+// The same for bf16 or fp32 elements (PKM_DT_BF16 / PKM_DT_F32) and a 128-
+// or 64-byte swizzle (the box's rows must then be that many bytes wide).
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t cols, uint64_t rows,
-                 uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows);
+                 uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
 
 }  // namespace pkm

@@ -220,16 +220,25 @@ class LinearColsumBias(torch.autograd.Function):
 class SwiGLUProjection(torch.autograd.Function):
     """``value_proj(a * silu(swilu_projection(x)))`` of ``HashingMemory.forward``
     (``pkm/memory.py:226-229``): both projections and their gradients on the
-    library's GEMM (bf16), the gate in the epilogues of the gate projection's
-    GEMM (forward: h and z) and of the value projection's data-gradient GEMM
-    (backward: da and dh); the bias gradients are column sums.  Other
-    dtypes run the gate as one pass each way (``pkm_swiglu_fwd`` /
-    ``pkm_swiglu_bwd``)."""
+    library's GEMM (bf16); the gate as one pass each way (``pkm_swiglu_fwd``,
+    ``pkm_swiglu_bwd``, the latter with the gate projection's bias gradient).
+
+    With ``FUSE_GATE`` the gate rides in the GEMM epilogues instead (forward:
+    h and z from the gate projection's GEMM; backward: da and dh from the
+    value projection's data-gradient GEMM), with the same bits.  It is off by
+    default: the gate's exact exp and divisions on the epilogue's eight warps
+    per SM take longer than the tile's MMAs, and the HashingMemory step at
+    config 2 measured 2.88 ms fused against 2.71 ms with the gate pass."""
+
+    # whether the gate rides in the GEMM epilogues (else GEMM, then the gate
+    # kernel; the two give the same bits)
+    FUSE_GATE = False
 
     @staticmethod
     def _fused(a, x, ws, wv):
         # the gate rides in the GEMM epilogues (bf16, N a multiple of 8)
-        return _tc(a, x, ws, wv) and ws.shape[0] % 8 == 0 and a.shape == (x.shape[0], ws.shape[0])
+        return (SwiGLUProjection.FUSE_GATE and _tc(a, x, ws, wv) and ws.shape[0] % 8 == 0
+                and a.shape == (x.shape[0], ws.shape[0]))
 
     @staticmethod
     def forward(ctx, a, x, ws, bs, wv, bv):

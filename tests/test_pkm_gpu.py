@@ -169,3 +169,36 @@ def test_eval_mode_usage_statistics():
     assert li.device.type == "cpu" and li.shape == (8, 4, 32)
     assert torch.equal(li.reshape(8, -1), idx.view(8, -1).cpu())
     assert m.last_scores.dtype == torch.float32
+
+
+def test_fused_gate_path_equals_default_layer_step():
+    """``SwiGLUProjection.FUSE_GATE`` (the gate in the GEMM epilogues) gives
+    the same bits as the default (GEMM, then the gate kernel) through a whole
+    bf16 layer step: output and every parameter and input gradient (the gate
+    projection's bias gradient within a bf16 rounding).  4096
+    tokens and 256-wide projections keep every unfused GEMM from splitting K
+    (the same summation order)."""
+    from modelos_b200.pkm import memory
+    cfg = dict(cases.CONFIG2)
+    cfg.update(input_dim=256, output_dim=256, mem_v_dim=256, mem_n_keys=64)
+    runs = []
+    try:
+        for fuse in (False, True):
+            memory.SwiGLUProjection.FUSE_GATE = fuse
+            m = build(cfg, 0, torch.bfloat16)
+            x = cases.pkm_input((2, 2048, 256), 0).to(DEV, torch.bfloat16).requires_grad_(True)
+            out, _ = m(x)
+            (out.float() ** 2).sum().backward()
+            got = {"out": out.detach(), "x": x.grad}
+            got.update({n: p.grad for n, p in m.named_parameters()})
+            runs.append(got)
+    finally:
+        memory.SwiGLUProjection.FUSE_GATE = False
+    torch.cuda.synchronize()
+    for name, a in runs[0].items():
+        b = runs[1][name]
+        if name == "swilu_projection.bias":
+            # a column sum of the same dh by another kernel (another order)
+            assert rel_err(a.float().cpu().numpy(), b.float().cpu().numpy()) < 2.0 ** -8, name
+        else:
+            assert torch.equal(a, b), name
