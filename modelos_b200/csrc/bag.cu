@@ -2,6 +2,7 @@
 // (K4) and the double-backward of the weight gradient (K5), with their C ABI
 // entry points.
 #include <algorithm>
+#include <type_traits>
 #include <string>
 
 #include "gather.cuh"
@@ -456,7 +457,7 @@ static BwdLayout bwd_layout(int64_t M, int64_t K, int64_t D) {
     return at;
   };
   const int64_t tiles = sort_tiles(M);
-  const int64_t nh = (int64_t)kRadix * tiles;
+  const int64_t nh = (int64_t)kRadixMax * tiles;
   const int64_t max_items = K + (M + kChunk - 1) / kChunk + 1;
   const int64_t max_partial = 2 * ((M + kChunk - 1) / kChunk) + 2;
   L.counts = take(sizeof(int32_t) * (K + 1));
@@ -704,7 +705,8 @@ static int bag_bwd_impl(const int64_t* indices, const void* psw, int psw_dtype, 
   float* partials = reinterpret_cast<float*>(ws + L.partials);
 
   const int nsm = num_sms();
-  const int sort_passes = (bits_for(K) + 7) / 8;
+  int sort_rb, sort_passes;
+  sort_plan(bits_for(K), sort_rb, sort_passes);
   if (phase == kBwdRows) {
     int32_t* sorted = sort_passes & 1 ? vals_a : vals_b;  // where the last radix pass wrote the values
     return bag_bwd_rows(grad_out, weight, weight_dtype, n_bags, bag_size, K, D, dest, grad_weight_dtype, grad_psw,
@@ -722,8 +724,8 @@ static int bag_bwd_impl(const int64_t* indices, const void* psw, int psw_dtype, 
   scan_exclusive<I4>(RowScanLoad{counts, K, kChunk}, K + 1, offs, sums_4, st);
   // 3. stable radix sort of occurrence ids by row (sentinel row K included)
   {
-    const int bits = bits_for(K);
-    const int passes = (bits + 7) / 8;
+    const int passes = sort_passes;
+    const int rb = sort_rb;
     const int64_t tiles = sort_tiles(M);
     const uint32_t* kin = keys_a;
     const int32_t* vin = nullptr;
@@ -731,12 +733,23 @@ static int bag_bwd_impl(const int64_t* indices, const void* psw, int psw_dtype, 
     int32_t* vbuf[2] = {vals_a, vals_b};
     for (int p = 0; p < passes; ++p) {
       const bool last = p == passes - 1;
-      radix_upsweep_kernel<<<(unsigned)tiles, kSortThreads, 0, st>>>(kin, M, 8 * p, hist, tiles);
-      scan_exclusive<int>(IntLoad{hist}, (int64_t)kRadix * tiles, hist, sums_i, st);
       uint32_t* kout = last ? nullptr : kbuf[p & 1];
       int32_t* vout = vbuf[p & 1];
-      radix_downsweep_kernel<<<(unsigned)tiles, kSortThreads, 0, st>>>(
-          kin, vin, M, 8 * p, hist, tiles, kout, vout, last ? psw : nullptr, psw_dtype, last ? w_sorted : nullptr);
+      const int shift = rb * p;
+      auto pass = [&](auto rbc) {
+        constexpr int RB = decltype(rbc)::value;
+        radix_upsweep_kernel<RB><<<(unsigned)tiles, kSortThreads, 0, st>>>(kin, M, shift, hist, tiles);
+        scan_exclusive<int>(IntLoad{hist}, (int64_t)(1 << RB) * tiles, hist, sums_i, st);
+        radix_downsweep_kernel<RB><<<(unsigned)tiles, kSortThreads, 0, st>>>(
+            kin, vin, M, shift, hist, tiles, kout, vout, last ? psw : nullptr, psw_dtype,
+            last ? w_sorted : nullptr);
+      };
+      if (rb == 10)
+        pass(std::integral_constant<int, 10>{});
+      else if (rb == 9)
+        pass(std::integral_constant<int, 9>{});
+      else
+        pass(std::integral_constant<int, 8>{});
       kin = kout;
       vin = vout;
     }

@@ -28,6 +28,8 @@
 // one program per row and an fp32 accumulator.
 #pragma once
 
+#include <type_traits>
+
 #include "gather.cuh"
 
 namespace pkm {
@@ -98,6 +100,22 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
+
+// f(std::integral_constant<int, i>{}) for i = 0 .. N-1, unrolled at compile
+// time (immediate address offsets in inline PTX need constants).
+template <int I, int N>
+struct StaticFor {
+  template <class F>
+  __device__ __forceinline__ static void run(F&& f) {
+    f(std::integral_constant<int, I>{});
+    StaticFor<I + 1, N>::run(f);
+  }
+};
+template <int N>
+struct StaticFor<N, N> {
+  template <class F>
+  __device__ __forceinline__ static void run(F&&) {}
+};
 
 // Shared-memory bytes of one warp of the segment pass.
 __host__ __device__ constexpr int64_t seg_warp_smem(int64_t rb, int depth, bool dot) {
@@ -325,42 +343,51 @@ __global__ void __launch_bounds__(NW * 32, 1) seg_direct_kernel(const __grid_con
       const uint32_t slot = ring_lane + cslot * rb;
       const float w = m_w[e & (kMetaRing - 1)];
       const uint64_t w2 = pack2(__float_as_uint(w), __float_as_uint(w));
-      uint64_t ds[2] = {0ull, 0ull};  // dot accumulators of the even and the odd vectors
+      uint64_t ds[VPL];  // dot accumulators, one per vector (short dependency chains)
+      // the entry's vectors, at immediate offsets from the slot
+      uint4 raw[VPL];
+      StaticFor<0, VPL>::run([&](auto vc) {
+        constexpr int v = decltype(vc)::value;
+        if (FULL || (v * 32 + lane) * 16 < rb)
+          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4+%5];"
+                       : "=r"(raw[v].x), "=r"(raw[v].y), "=r"(raw[v].z), "=r"(raw[v].w)
+                       : "r"(slot), "n"(v * 512));
+      });
 #pragma unroll
       for (int v = 0; v < VPL; ++v) {
+        ds[v] = 0ull;
         if (FULL || (v * 32 + lane) * 16 < rb) {
-          uint4 raw;
-          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w)
-                       : "r"(slot + v * 512));
           uint64_t f[NP];
-          Pairs<RowT>::unpack(raw, f);
+          Pairs<RowT>::unpack(raw[v], f);
 #pragma unroll
           for (int t = 0; t < NP; ++t) {
             ffma2(acc[v][t], w2, f[t]);
-            if (DOT) ffma2(ds[v & 1], dv[v][t], f[t]);
+            if (DOT) ffma2(ds[v], dv[v][t], f[t]);
           }
         }
       }
       // the slot's values are in registers: refill it with entry e + DEPTH
       if (all_issue) {
         const char* src = src_lane + (int64_t)m_sp[(e + DEPTH) & (kMetaRing - 1)].x * RB;
-#pragma unroll
-        for (int v = 0; v < VPL; ++v) {
+        StaticFor<0, VPL>::run([&](auto vc) {
+          constexpr int v = decltype(vc)::value;
           if (FULL || (v * 32 + lane) * 16 < rb)
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(slot + v * 512), "l"(src + v * 512)
+            asm volatile("cp.async.cg.shared.global [%0+%2], [%1+%2], 16;" ::"r"(slot), "l"(src), "n"(v * 512)
                          : "memory");
-        }
+        });
         cp_async_commit();
       } else {
         issue(e + DEPTH, cslot);
       }
       cslot = cslot + 1 == DEPTH ? 0 : cslot + 1;
       if (DOT) {
-        uint64_t d2;
-        asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d2) : "l"(ds[0]), "l"(ds[1]));
+        // pairwise over the vectors, then the two halves of the pair
+#pragma unroll
+        for (int h = 1; h < VPL; h <<= 1)
+#pragma unroll
+          for (int v = 0; v + h < VPL; v += 2 * h) asm("add.rn.f32x2 %0, %0, %1;" : "+l"(ds[v]) : "l"(ds[v + h]));
         float x0, x1;
-        unpack2(d2, x0, x1);
+        unpack2(ds[0], x0, x1);
         m_dot[e & 31][lane] = x0 + x1;
       }
     }

@@ -163,10 +163,13 @@ void scan_exclusive(Load ld, int64_t n, T* out, T* block_sums, cudaStream_t st) 
 }
 
 // ---------------------------------------------------------------------------
-// Stable LSD radix sort, 8-bit digits.  A tile of kSortTile items is ranked
-// by one block: warp w owns items [w*32*kSortIpt, (w+1)*32*kSortIpt) in
-// rounds of 32, so (warp, round, lane) order is item order, and equal digits
-// keep their order through __match_any_sync ranks.
+// Stable LSD radix sort, RB-bit digits (8, or 9 or 10 where that saves a
+// pass: the row keys of a 2^18-row table, its sentinel row included, have
+// 19 bits and sort in two 10-bit passes instead of three 8-bit ones).
+// A tile of kSortTile items is ranked by one block: warp w owns items
+// [w*32*kSortIpt, (w+1)*32*kSortIpt) in rounds of 32, so (warp, round, lane)
+// order is item order, and equal digits keep their order through
+// __match_any_sync ranks.
 // ---------------------------------------------------------------------------
 #ifndef PKM_SORT_THREADS
 #define PKM_SORT_THREADS 256
@@ -178,10 +181,13 @@ constexpr int kSortThreads = PKM_SORT_THREADS;
 constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kSortIpt = PKM_SORT_IPT;
 constexpr int kSortTile = kSortThreads * kSortIpt;
-constexpr int kRadix = 256;
+constexpr int kRadix = 256;     // 8-bit digits
+constexpr int kRadixMax = 1024;  // the widest digit (10 bits)
 
+template <int RB = 8>
 static __global__ void __launch_bounds__(kSortThreads) radix_upsweep_kernel(const uint32_t* keys, int64_t n, int shift,
                                                                      int* hist, int64_t tiles) {
+  constexpr int kRadix = 1 << RB;
   __shared__ int cnt[kRadix];
   for (int i = threadIdx.x; i < kRadix; i += kSortThreads) cnt[i] = 0;
   __syncthreads();
@@ -197,9 +203,11 @@ static __global__ void __launch_bounds__(kSortThreads) radix_upsweep_kernel(cons
 // vals_in == nullptr: the values are the item positions (first pass).
 // keys_out == nullptr: keys are not written (last pass).
 // w != nullptr: also writes w_out[pos] = float(w[value]) (last pass).
+template <int RB = 8>
 static __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
     const uint32_t* keys_in, const int32_t* vals_in, int64_t n, int shift, const int* hist_scan,
     int64_t tiles, uint32_t* keys_out, int32_t* vals_out, const void* w, int w_dtype, float* w_out) {
+  constexpr int kRadix = 1 << RB;
   __shared__ int wcnt[kSortWarps][kRadix];
   __shared__ int tbase[kRadix];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -250,5 +258,13 @@ static __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
 }
 
 inline int64_t sort_tiles(int64_t n) { return (n + kSortTile - 1) / kSortTile; }
+
+// Digit width and pass count for keys of `bits` bits: the fewest passes of
+// at most 10-bit digits, each as narrow as that allows.
+inline void sort_plan(int bits, int& rb, int& passes) {
+  passes = (bits + 9) / 10;
+  rb = (bits + passes - 1) / passes;
+  if (rb < 8) rb = 8;
+}
 
 }  // namespace pkm

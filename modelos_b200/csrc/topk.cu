@@ -456,6 +456,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32, PKM_TOPK_MINB) product_topk_k
   __shared__ uint32_t sh_i2[kTopkWarps][32];
   __shared__ uint16_t sh_pair[kTopkWarps][kPairCap];
   __shared__ __align__(16) uint32_t sh_comp[kTopkWarps][kCandCap + 4];
+  __shared__ __align__(16) unsigned long long sh_comp64[kTopkWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int KB = ScoreT<T>::KEYBITS;
   constexpr int PV = ScoreT<T>::PER_VEC;
@@ -475,6 +476,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32, PKM_TOPK_MINB) product_topk_k
   }
   uint32_t* s_key = sh_key[warp];
   uint32_t* s_idx = sh_idx[warp];
+  unsigned long long* s_comp64 = sh_comp64[warp];
 
   const int64_t warps_total = (int64_t)gridDim.x * kTopkWarps;
   for (int64_t r = (int64_t)blockIdx.x * kTopkWarps + warp; r < rows; r += warps_total) {
@@ -625,26 +627,22 @@ __global__ void __launch_bounds__(kTopkWarps * 32, PKM_TOPK_MINB) product_topk_k
           ++pos;
         }
       }
-      if (!live) {
-        s_key[lane] = 0u;  // pads to 32 entries; no selected pair has key 0
-        s_idx[lane] = 0xffffffffu;
-      }
-      __syncwarp();
       // each pair's rank among the knn (sum descending, slot ascending; the
-      // slots are distinct) is its place in the output
-      const uint32_t ok = s_key[lane], os = s_idx[lane];
-      const float ov = sh_v1[warp][lane];
+      // slots are distinct) is its place in the output: one 64-bit compare
+      // per pair of composites key << 32 | ~slot (padding 0 ranks last)
+      __syncwarp();  // the compacted pairs are visible to every lane
+      const uint32_t ok = live ? s_key[lane] : 0u, os = live ? s_idx[lane] : 0xffffffffu;
+      const float ov = live ? sh_v1[warp][lane] : -INFINITY;
+      const unsigned long long mine = ((unsigned long long)ok << 32) | (uint32_t)~os;
+      __syncwarp();
+      s_comp64[lane] = live ? mine : 0ull;
+      __syncwarp();
       int rk = 0;
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const uint4 kq = *reinterpret_cast<const uint4*>(s_key + i);
-        const uint4 sq = *reinterpret_cast<const uint4*>(s_idx + i);
-        rk += (kq.x > ok) + (kq.x == ok && sq.x < os);
-        rk += (kq.y > ok) + (kq.y == ok && sq.y < os);
-        rk += (kq.z > ok) + (kq.z == ok && sq.z < os);
-        rk += (kq.w > ok) + (kq.w == ok && sq.w < os);
+      for (int i = 0; i < 32; i += 2) {
+        const ulonglong2 cq = *reinterpret_cast<const ulonglong2*>(s_comp64 + i);
+        rk += (cq.x > mine) + (cq.y > mine);
       }
-      __syncwarp();
       if (live) {
         s_idx[rk] = os;
         sh_v1[warp][rk] = ov;
