@@ -508,8 +508,10 @@ def run_ours_c1(args, rank, world, local_rank):
 def run_ours_c4(args, rank, world, local_rank):
     """Config 4: the fast-weight memory's chunked forward with its inner
     updates, then the outer backward through them; at N GPUs every rank runs
-    its own 8 sequences (weak scaling) with the fast weights replicated and
-    updated from the whole batch (``FastWeightProductKeyMemory.data_parallel``)."""
+    its own 8 sequences (weak scaling) and the inner updates use the whole
+    batch, with the value table split by rows over the ranks
+    (``row_sharded``, the default) or replicated (``data_parallel``,
+    ``--fw-table replicated``)."""
     import torch
 
     from modelos_b200 import _native
@@ -528,9 +530,14 @@ def run_ours_c4(args, rank, world, local_rank):
     wv = torch.nn.Linear(1024, 1024).to(dev, torch.bfloat16)
     proj = list(wq.parameters()) + list(wv.parameters())
     if world > 1:
-        # batch split over the ranks, fast weights replicated, every inner
-        # update from the whole batch's gradient (differentiable all-reduces)
-        m.data_parallel(dist.group.WORLD)
+        if args.fw_table == "sharded":
+            # batch split over the ranks, value rows split over the ranks:
+            # lookups and their gradients travel to the rows' owners
+            m.row_sharded(dist.group.WORLD)
+        else:
+            # batch split over the ranks, fast weights replicated, every inner
+            # update from the whole batch's gradient (differentiable all-reduces)
+            m.data_parallel(dist.group.WORLD)
     keys0, values0 = m.keys.detach().clone(), m.values.detach().clone()
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     x = torch.randn((C4_B, C4_T, 1024), generator=g, device=dev).to(torch.bfloat16)
@@ -605,7 +612,16 @@ def run_ours_c4(args, rank, world, local_rank):
                     "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": None if launches is None else launches * args.steps, "gpu_launches_per_step": launches,
             "clocks": clk.summary()}
-    if world > 1:
+    if world > 1 and args.fw_table == "sharded":
+        line["config"]["fw_table"] = "value rows split over the ranks (row_sharded)"
+        line["config"]["exchange"] = ("per chunk: all-to-alls of the lookups to the rows' owners and of the owners' "
+                                      "partial bag sums back, in the backward of the upstream rows to the owners "
+                                      "and of the weight gradients back (twice more for the double backward); "
+                                      "differentiable all-reduces of the key gradients and of the addressing "
+                                      "loss's row sums; no value-table gradient crosses the links; after the "
+                                      "step, all-reduce of the keys' and the projections' gradients")
+    elif world > 1:
+        line["config"]["fw_table"] = "replicated (data_parallel)"
         line["config"]["exchange"] = ("per chunk: differentiable all-reduces of the fast-weight gradients (fp32 "
                                       "values 1 GiB, keys) and of the addressing loss's row sums, all-gather of the "
                                       "slot indices; after the step, all-reduce of the parameters' gradients")
@@ -1016,6 +1032,8 @@ def main():
                          "(train step, prefill, decode); c4: the fast-weight memory; gemm: the c2 step's GEMM "
                          "shapes on this library's GEMM and on cuBLAS")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fw-table", default="sharded", choices=["sharded", "replicated"],
+                    help="c4 at N > 1: the fast-weight value table split by rows over the ranks, or replicated")
     ap.add_argument("--grad-exchange", default="fused", choices=["fused", "nccl", "owner"],
                     help="data-parallel exchange of the value-table gradient (N > 1); owner: the table's "
                          "optimizer sharded by rows (needs --optimizer sgd)")

@@ -350,6 +350,36 @@ class FastWeightProductKeyMemory(nn.Module):
         self.dp_group = group
         return self
 
+    def row_sharded(self, group=None):
+        """Split the batch over the ranks of ``group`` as ``data_parallel``
+        does, and split the value table by rows instead of replicating it:
+        this rank keeps rows ``[rank*S, rank*S + S)`` (``S = ceil(n^2 /
+        world)``, the last shard zero-padded) of the current ``values``.
+        Lookups go to the rows' owners and come back as partial bag sums;
+        each owner computes the value gradient of its rows from every rank's
+        lookups (nothing of the table is all-reduced), updates its rows with
+        the slot counts of the lookups it served, and carries the double
+        backward of its rows.  The keys stay replicated; their gradients are
+        summed over the ranks.  Every rank must call it, with the same
+        parameters."""
+        import torch.distributed as dist
+        self.dp_group = group if group is not None else dist.group.WORLD
+        world = dist.get_world_size(self.dp_group)
+        rank = dist.get_rank(self.dp_group)
+        S = -(-self.size // world)
+        self.shard_rows = S
+        with torch.no_grad():
+            full = self.values.detach()
+            shard = torch.zeros((S, full.shape[1]), dtype=full.dtype, device=full.device)
+            r0, r1 = rank * S, min((rank + 1) * S, self.size)
+            if r1 > r0:
+                shard[: r1 - r0].copy_(full[r0:r1])
+        self.values = nn.Parameter(shard)
+        return self
+
+    def _sharded(self) -> bool:
+        return getattr(self, "shard_rows", None) is not None and self._dp()[0] > 1
+
     def _dp(self):
         group = getattr(self, "dp_group", None)
         if group is None:
@@ -365,7 +395,7 @@ class FastWeightProductKeyMemory(nn.Module):
         if world == 1:
             return
         import torch.distributed as dist
-        for p in (self.keys, self.values):
+        for p in (self.keys,) if self._sharded() else (self.keys, self.values):
             if p.grad is not None:
                 dist.all_reduce(p.grad, group=group)
 
@@ -384,12 +414,19 @@ class FastWeightProductKeyMemory(nn.Module):
         scores, indices, indices1, indices2, all_scores1, all_scores2 = self.get_indices(
             query.view(B * T, self.heads, self.k_dim), fw_named_params["keys"])
         normed_scores = self.score_transform(scores.view(B * T, self.heads * self.topk))
-        vals = xformers_embedding_bag(
-            indices=indices.view(B * T, self.heads * self.topk),
-            weight=fw_named_params["values"],
-            per_sample_weights=normed_scores,
-        )
+        route = None
+        if self._sharded():
+            from ..sharded import fw_sharded_bag
+            vals, route = fw_sharded_bag(indices.view(B * T, self.heads * self.topk), fw_named_params["values"],
+                                         normed_scores, self.shard_rows, self._dp()[1])
+        else:
+            vals = xformers_embedding_bag(
+                indices=indices.view(B * T, self.heads * self.topk),
+                weight=fw_named_params["values"],
+                per_sample_weights=normed_scores,
+            )
         return {
+            "route": route,
             "retireved_values": vals,
             "scores": scores,
             "normed_scores": normed_scores,
@@ -424,8 +461,11 @@ class FastWeightProductKeyMemory(nn.Module):
             raise NotImplementedError(f"Optimizer {self.optimizer_type} not implemented.")
         return p - lr * (g + wd * p)
 
-    def update_fw(self, fw_named_params, num_samples, indices, mem_loss, addr_loss=None):
-        """One SGD step on the fast weights (``fwpkm/fwpkm.py:274-367``)."""
+    def update_fw(self, fw_named_params, num_samples, indices, mem_loss, addr_loss=None, route=None):
+        """One SGD step on the fast weights (``fwpkm/fwpkm.py:274-367``).
+        With a row-split table (``route`` of the chunk's lookups) the value
+        gradient is already this rank's rows' sum over every rank, and the
+        slot counts are those of the lookups this rank served."""
         mem_loss = mem_loss * 0.5
         names = list(fw_named_params.keys())
         params = tuple(fw_named_params.values())
@@ -440,12 +480,15 @@ class FastWeightProductKeyMemory(nn.Module):
             loss = mem_loss if addr_loss is None else mem_loss + addr_loss
             grads = list(torch.autograd.grad(loss, params, create_graph=self.training))
         world, group = self._dp()
+        sharded = route is not None
         if world > 1:
             # each rank holds its batch share's gradient: sum them (the
-            # all-reduce is differentiable, so the outer backward sees the sum)
+            # all-reduce is differentiable, so the outer backward sees the sum);
+            # a row-split value table's gradient is complete on its owner
             from torch.distributed.nn.functional import all_reduce
-            grads = [None if g is None else all_reduce(g, group=group) for g in grads]
-            indices = self._all_indices(indices)
+            grads = [g if g is None or (sharded and n == "values") else all_reduce(g, group=group)
+                     for n, g in zip(names, grads)]
+            indices = route.r_row.long() if sharded else self._all_indices(indices)
         # the value gradient is a sum over samples, features, heads and top-k,
         # shared out over the times each slot was read; its scaling, the
         # bincount, the clamp and the SGD step run as one fused kernel pass
@@ -541,7 +584,8 @@ class FastWeightProductKeyMemory(nn.Module):
                     mem_loss = mem_loss / world
                     num_samples = self._global_count(num_samples)
                     addr_loss = None if addr_loss is None else addr_loss / world
-                new_params, grads = self.update_fw(cur, num_samples, r["indices"], mem_loss, addr_loss)
+                new_params, grads = self.update_fw(cur, num_samples, r["indices"], mem_loss, addr_loss,
+                                                   route=r["route"])
                 if world > 1 and addr_loss is not None:
                     addr_loss = addr_loss * world
                 if self.ob_mode:
@@ -557,8 +601,20 @@ class FastWeightProductKeyMemory(nn.Module):
         losses = torch.cat(losses, dim=1)
         addr_loss = torch.stack(addr_losses).mean() if addr_losses is not None else None
         with torch.no_grad():
-            grad_norms = [torch.stack([g[i].norm() if g[i] is not None else torch.zeros((), device=q.device)
-                                       for g in all_grads]).mean() for i in range(len(fw_params[0]))]
+            names0 = list(fw_params[0].keys())
+
+            def _norm(g, n):
+                if g is None:
+                    return torch.zeros((), device=q.device)
+                if n == "values" and self._sharded():
+                    # the norm of the whole table's gradient from the shards'
+                    import torch.distributed as dist
+                    sq = g.double().pow(2).sum()
+                    dist.all_reduce(sq, group=self._dp()[1])
+                    return sq.sqrt().to(g.dtype)
+                return g.norm()
+            grad_norms = [torch.stack([_norm(g[i], names0[i]) for g in all_grads]).mean()
+                          for i in range(len(fw_params[0]))]
             final = fw_params[-1]
             for n, p in self.named_parameters():
                 if n in final:
@@ -575,6 +631,8 @@ class FastWeightProductKeyMemory(nn.Module):
 
     def forward_w_past(self, q, ref_v, gates, chunk_size, loss_mask=None, past_key_values=None, token_ids=None):
         """Streaming read/update with a carried signal queue (``fwpkm/fwpkm.py:560-820``)."""
+        if self._sharded():
+            raise NotImplementedError("forward_w_past with a row-split value table")
         B, T = q.shape[:2]
         input_dtype = q.dtype
         if self.fp32_fw:

@@ -157,3 +157,126 @@ class RowShardedEmbeddingBag(nn.Module):
     def forward(self, indices: torch.Tensor, per_sample_weights: torch.Tensor) -> torch.Tensor:
         return _RowShardedBag.apply(indices.contiguous(), per_sample_weights.contiguous(), self.weight,
                                     self.shard_rows, self.group)
+
+
+# ---------------------------------------------------------------------------
+# the fast-weight memory's value table, split by rows
+# ---------------------------------------------------------------------------
+class FwRoute:
+    """The routing of one chunk's lookups ``indices [B, L]`` (weights
+    ``psw [B, L]``) to the owners of their rows, built once per chunk and
+    shared by the forward, the backward and the double backward of
+    :func:`fw_sharded_bag`.  Every rank of ``group`` builds its route in the
+    same step (collectives)."""
+
+    def __init__(self, indices: torch.Tensor, psw: torch.Tensor, shard_rows: int, group):
+        self.group = group
+        world = dist.get_world_size(group)
+        self.world = world
+        B, L = indices.shape
+        self.B, self.L = B, L
+        n = B * L
+        send_t, order, local_row, bag, w = _native.route_pack(indices.contiguous(), psw.detach().contiguous(),
+                                                              shard_rows, world)
+        _, _, my_seg_bag, back_recv_t = _native.route_segments(bag, send_t, world)
+        valid = (send_t.sum() == n).to(torch.int64).expand(world)
+        recv2 = _exchange_counts(torch.stack([send_t, valid], 1), group)
+        recv_t = recv2[:, 0].contiguous()
+        counts = torch.cat([send_t, recv2[:, 0], recv2[:, 1], back_recv_t]).tolist()
+        self.send, self.recv = counts[:world], counts[world:2 * world]
+        senders_ok, self.back_recv = counts[2 * world:3 * world], counts[3 * world:]
+        if not all(senders_ok):
+            if sum(self.send) != n:
+                if indices.is_cuda:
+                    _native.read_device_errors(indices.device)
+                raise IndexError("row index outside the sharded table")
+            raise IndexError(f"row index outside the sharded table on rank(s) "
+                             f"{[r for r, ok in enumerate(senders_ok) if not ok]}")
+        self.order = order.long()
+        self.r_row = _all_to_all(local_row, self.send, self.recv, group)
+        self.r_w = _all_to_all(w, self.send, self.recv, group)
+        r_bag = _all_to_all(bag, self.send, self.recv, group)
+        self.r_seg_of, r_seg_start, _, back_send_t = _native.route_segments(r_bag, recv_t, world)
+        self.back_send = back_send_t.tolist()
+        self.r_seg_start = r_seg_start[:sum(self.back_send) + 1]
+        self.my_seg_bag = my_seg_bag[:sum(self.back_recv)]
+        self.back_recv_t = back_recv_t
+
+    def bag(self, table: torch.Tensor) -> torch.Tensor:
+        """``[B, D]`` weighted bag sums over ``table`` (this rank's rows of a
+        row-split table): the owners' partial sums, combined per bag."""
+        partial = _native.segment_sum(table.contiguous(), self.r_row, self.r_w, self.r_seg_start,
+                                      out_dtype=table.dtype)
+        got = _all_to_all(partial, self.back_send, self.back_recv, self.group)
+        return _native.route_combine(got, self.my_seg_bag, self.back_recv_t, self.world, self.B,
+                                     out_dtype=table.dtype)
+
+    def rows_to_owners(self, d_out: torch.Tensor, dtype) -> torch.Tensor:
+        """The rows of ``d_out [B, D]`` that each owner's segments read."""
+        rows = d_out.to(dtype).contiguous().index_select(0, self.my_seg_bag.long())
+        return _all_to_all(rows, self.back_recv, self.back_send, self.group)
+
+    def entries_home(self, vals: torch.Tensor) -> torch.Tensor:
+        """Per-entry values computed by the owners, back in ``[B, L]`` order."""
+        back = _all_to_all(vals, self.recv, self.send, self.group)
+        flat = torch.empty(self.B * self.L, dtype=vals.dtype, device=vals.device)
+        flat[self.order] = back
+        return flat.view(self.B, self.L)
+
+
+class _FwShardedBagBW(torch.autograd.Function):
+    """The owner's table gradient ``dW[k] = sum psw[b,j] d_out[b]`` as a
+    differentiable function of ``psw`` and ``d_out`` (the double backward
+    of the sharded bag, as ``EmbeddingBagBW`` is for the whole table):
+    ``d(d_out)[b] = sum_j psw[b,j] gbar[idx[b,j]]`` is the sharded bag over
+    ``gbar``, ``d(psw)[b,j] = <gbar[idx[b,j]], d_out[b]>`` the owners'
+    per-entry dot products."""
+
+    @staticmethod
+    def forward(ctx, psw, d_out, route, rows_in, dW):
+        ctx.route = route
+        ctx.save_for_backward(rows_in)
+        ctx.psw_dtype, ctx.dout_dtype = psw.dtype, d_out.dtype
+        return dW
+
+    @staticmethod
+    def backward(ctx, g_bar):
+        (rows_in,) = ctx.saved_tensors
+        route = ctx.route
+        g_bar = g_bar.contiguous()
+        d_psw = d_dout = None
+        if ctx.needs_input_grad[1]:
+            d_dout = route.bag(g_bar).to(ctx.dout_dtype)
+        if ctx.needs_input_grad[0]:
+            _, dots = _native.bag_bwd_ragged(route.r_row, route.r_seg_of, route.r_w, g_bar, rows_in, need_dpsw=True)
+            d_psw = route.entries_home(dots).to(ctx.psw_dtype)
+        return d_psw, d_dout, None, None, None
+
+
+class _FwShardedBag(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, shard, psw, route):
+        ctx.route = route
+        ctx.save_for_backward(shard, psw)
+        return route.bag(shard)
+
+    @staticmethod
+    def backward(ctx, d_out):
+        shard, psw = ctx.saved_tensors
+        route = ctx.route
+        rows_in = route.rows_to_owners(d_out, shard.dtype)
+        dW, dots = _native.bag_bwd_ragged(route.r_row, route.r_seg_of, route.r_w, shard.detach(), rows_in,
+                                          need_dpsw=ctx.needs_input_grad[1])
+        d_psw = route.entries_home(dots).to(psw.dtype) if ctx.needs_input_grad[1] else None
+        grad_shard = _FwShardedBagBW.apply(psw, d_out, route, rows_in, dW) if ctx.needs_input_grad[0] else None
+        return grad_shard, d_psw, None
+
+
+def fw_sharded_bag(indices: torch.Tensor, shard: torch.Tensor, psw: torch.Tensor, shard_rows: int, group):
+    """Weighted bag sums ``[B, D]`` of ``indices [B, L]`` over a row-split
+    table of which this rank holds ``shard`` (rows ``[rank*S, rank*S + S)``),
+    with a table gradient that is differentiable once more (the fast-weight
+    memory's inner update).  Returns ``(out, route)``; ``route.r_row`` are
+    the shard rows of the entries this rank served (its slot counts)."""
+    route = FwRoute(indices, psw, shard_rows, group)
+    return _FwShardedBag.apply(shard, psw, route), route

@@ -185,9 +185,10 @@ def run_owner(rank: int, world: int, port: int, out_dir: str, dtype_name: str):
         dist.destroy_process_group()
 
 
-def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str, backend: str = "nccl"):
+def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str, backend: str = "nccl", sharded: bool = False):
     """One rank of the data-parallel fast-weight memory on the GPU kernels
-    (fp32, tiny geometry): half of the batch, fast weights replicated."""
+    (fp32, tiny geometry): half of the batch, fast weights replicated or the
+    value table split by rows."""
     import datetime
 
     import torch
@@ -205,13 +206,13 @@ def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str, backend: str = 
         keys, values, q, ref_v = dist_worker.fwpkm_dp_case()
         per = q.shape[0] // world
         sl = slice(rank * per, (rank + 1) * per)
-        out = fwpkm_gpu_run(q[sl], ref_v[sl], keys, values, dev, dist.group.WORLD)
-        torch.save(out, os.path.join(out_dir, f"fwdp{rank}.pt"))
+        out = fwpkm_gpu_run(q[sl], ref_v[sl], keys, values, dev, dist.group.WORLD, sharded=sharded)
+        torch.save(out, os.path.join(out_dir, f"{'fwsh' if sharded else 'fwdp'}{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
-def fwpkm_gpu_run(q, ref_v, keys, values, dev, group=None):
+def fwpkm_gpu_run(q, ref_v, keys, values, dev, group=None, sharded=False):
     import torch
 
     import dist_worker
@@ -221,13 +222,31 @@ def fwpkm_gpu_run(q, ref_v, keys, values, dev, group=None):
         m.keys.copy_(keys)
         m.values.copy_(values)
     if group is not None:
-        m.data_parallel(group)
+        if sharded:
+            m.row_sharded(group)
+        else:
+            m.data_parallel(group)
     q = q.to(dev).requires_grad_(True)
     ref_v = ref_v.to(dev).requires_grad_(True)
     res = m(q, ref_v, None, 8)
     (res["output"] ** 2).sum().backward()
     m.reduce_grads()
+    vals, vgrad = m.values.detach(), m.values.grad
+    if sharded:
+        import torch.distributed as dist
+        world = dist.get_world_size(group)
+
+        def gather(t):
+            parts = [torch.empty_like(t) for _ in range(world)]
+            if dist.get_backend(group) == "nccl":
+                dist.all_gather(parts, t.contiguous(), group=group)
+            else:
+                host = [torch.empty_like(t, device="cpu") for _ in range(world)]
+                dist.all_gather(host, t.detach().cpu().contiguous(), group=group)
+                parts = [h.to(t.device) for h in host]
+            return torch.cat(parts)[: m.size]
+        vals, vgrad = gather(vals), gather(vgrad)
     torch.cuda.synchronize()
     return {k: v.detach().cpu() for k, v in (("out", res["output"]), ("q_grad", q.grad), ("ref_v_grad", ref_v.grad),
-                                             ("keys", m.keys), ("values", m.values), ("keys_grad", m.keys.grad),
-                                             ("values_grad", m.values.grad), ("indices", res["indices"]))}
+                                             ("keys", m.keys), ("values", vals), ("keys_grad", m.keys.grad),
+                                             ("values_grad", vgrad), ("indices", res["indices"]))}

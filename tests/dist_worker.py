@@ -134,9 +134,11 @@ def fwpkm_dp_case():
     return cases.fwpkm_case(0, B=4, T=16)
 
 
-def fwpkm_run(q, ref_v, keys, values, group=None):
+def fwpkm_run(q, ref_v, keys, values, group=None, sharded=False):
     """``forward_wo_past`` and the outer backward of ``sum(out^2)`` for the
-    sequences given (all of them, or one rank's share with ``group``)."""
+    sequences given (all of them, or one rank's share with ``group``; with
+    ``sharded`` the value table is split by rows over the group, and the
+    returned values and value gradient are the gathered whole tables)."""
     from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
     import torch
     m = FastWeightProductKeyMemory(**FW_DP_KW).train()
@@ -144,20 +146,34 @@ def fwpkm_run(q, ref_v, keys, values, group=None):
         m.keys.copy_(keys)
         m.values.copy_(values)
     if group is not None:
-        m.data_parallel(group)
+        if sharded:
+            m.row_sharded(group)
+        else:
+            m.data_parallel(group)
     q = q.clone().requires_grad_(True)
     ref_v = ref_v.clone().requires_grad_(True)
     res = m(q, ref_v, None, 8)
     (res["output"] ** 2).sum().backward()
     m.reduce_grads()
+    vals, vgrad = m.values.detach(), m.values.grad
+    if sharded:
+        import torch.distributed as dist
+        world = dist.get_world_size(group)
+
+        def gather(t):
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t.contiguous(), group=group)
+            return torch.cat(parts)[: m.size]
+        vals, vgrad = gather(vals), gather(vgrad)
     return {"out": res["output"].detach(), "q_grad": q.grad, "ref_v_grad": ref_v.grad, "keys": m.keys.detach(),
-            "values": m.values.detach(), "keys_grad": m.keys.grad, "values_grad": m.values.grad,
+            "values": vals, "keys_grad": m.keys.grad, "values_grad": vgrad,
             "losses": res["losses"], "addr_loss": res["addr_loss"], "indices": res["indices"],
             "grad_norms": torch.stack(res["grad_norms"])}
 
 
-def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str):
-    """One rank of the data-parallel fast-weight memory (gloo, CPU stand-ins)."""
+def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str, sharded: bool = False):
+    """One rank of the data-parallel fast-weight memory (gloo, CPU stand-ins),
+    with a replicated or a row-split value table."""
     import torch
     import torch.distributed as dist
 
@@ -174,7 +190,7 @@ def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str):
         keys, values, q, ref_v = fwpkm_dp_case()
         per = q.shape[0] // world
         sl = slice(rank * per, (rank + 1) * per)
-        out = fwpkm_run(q[sl], ref_v[sl], keys, values, dist.group.WORLD)
-        torch.save(out, os.path.join(out_dir, f"fwdp{rank}.pt"))
+        out = fwpkm_run(q[sl], ref_v[sl], keys, values, dist.group.WORLD, sharded=sharded)
+        torch.save(out, os.path.join(out_dir, f"{'fwsh' if sharded else 'fwdp'}{rank}.pt"))
     finally:
         dist.destroy_process_group()

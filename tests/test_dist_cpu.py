@@ -115,11 +115,7 @@ def test_row_sharded_bad_index_raises_on_every_rank(tmp_path):
     assert msgs[0] is not None and "rank(s) [1]" in msgs[0]
 
 
-def test_fwpkm_data_parallel_equals_one_process(tmp_path, monkeypatch):
-    """The fast-weight memory with its batch split over two gloo ranks
-    (``data_parallel``): outputs, losses, indices, final fast weights and
-    every outer gradient equal one process running the whole batch (fp32,
-    1e-5; the sums only change order)."""
+def _fwpkm_dp_check(tmp_path, monkeypatch, sharded):
     import numpy as np
 
     import dist_worker
@@ -127,7 +123,8 @@ def test_fwpkm_data_parallel_equals_one_process(tmp_path, monkeypatch):
     os.environ["PYTHONPATH"] = os.pathsep.join([HERE, os.path.dirname(HERE), os.environ.get("PYTHONPATH", "")])
     port = _free_port()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=dist_worker.run_fwpkm_dp, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    procs = [ctx.Process(target=dist_worker.run_fwpkm_dp, args=(r, 2, port, str(tmp_path), sharded))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -146,7 +143,8 @@ def test_fwpkm_data_parallel_equals_one_process(tmp_path, monkeypatch):
         a, b = np.asarray(a, dtype=np.float64), np.asarray(b, dtype=np.float64)
         return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
 
-    parts = [torch.load(os.path.join(tmp_path, f"fwdp{r}.pt")) for r in range(2)]
+    tag = "fwsh" if sharded else "fwdp"
+    parts = [torch.load(os.path.join(tmp_path, f"{tag}{r}.pt")) for r in range(2)]
     for key in ("out", "q_grad", "ref_v_grad", "losses", "indices"):
         got = torch.cat([p[key] for p in parts], 0)
         if key == "indices":
@@ -157,3 +155,20 @@ def test_fwpkm_data_parallel_equals_one_process(tmp_path, monkeypatch):
         for key in ("keys", "values", "keys_grad", "values_grad", "grad_norms"):
             assert rel(p[key].numpy(), full[key].numpy()) < 1e-5, key
         assert abs(p["addr_loss"].item() - full["addr_loss"].item()) <= 1e-5 * abs(full["addr_loss"].item())
+
+
+def test_fwpkm_data_parallel_equals_one_process(tmp_path, monkeypatch):
+    """The fast-weight memory with its batch split over two gloo ranks
+    (``data_parallel``): outputs, losses, indices, final fast weights and
+    every outer gradient equal one process running the whole batch (fp32,
+    1e-5; the sums only change order)."""
+    _fwpkm_dp_check(tmp_path, monkeypatch, sharded=False)
+
+
+def test_fwpkm_row_sharded_equals_one_process(tmp_path, monkeypatch):
+    """The same with the value table split by rows over the two ranks
+    (``row_sharded``: lookups served by the rows' owners, the value update
+    and its double backward on the owners): outputs, losses, indices, the
+    final fast weights (the shards gathered), every outer gradient and the
+    gradient norms equal one process on the whole table."""
+    _fwpkm_dp_check(tmp_path, monkeypatch, sharded=True)

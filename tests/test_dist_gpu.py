@@ -183,12 +183,15 @@ def test_row_owner_sgd(tmp_path, dtype_name, world):
             assert ((got - ref).abs().max() / ref.abs().max()).item() < tol
 
 
+@pytest.mark.parametrize("sharded", [False, True], ids=["replicated", "row_sharded"])
 @pytest.mark.parametrize("backend,world", [("gloo", 2), ("nccl", 2)])
-def test_fwpkm_data_parallel_equals_one_gpu(tmp_path, backend, world):
-    """The fast-weight memory with its batch split over ranks
-    (``data_parallel``) on the GPU kernels equals one GPU running the whole
-    batch: outputs, indices, final fast weights and outer gradients (fp32,
-    1e-5).  gloo: the ranks share GPU 0; nccl: one GPU per rank."""
+def test_fwpkm_data_parallel_equals_one_gpu(tmp_path, backend, world, sharded):
+    """The fast-weight memory with its batch split over ranks on the GPU
+    kernels equals one GPU running the whole batch: outputs, indices, final
+    fast weights and outer gradients (fp32, 1e-5), with the value table
+    replicated (``data_parallel``) or split by rows (``row_sharded``: the
+    route, segment-sum and ragged-backward kernels, the owners' double
+    backward).  gloo: the ranks share GPU 0; nccl: one GPU per rank."""
     if backend == "nccl" and torch.cuda.device_count() < world:
         pytest.skip("needs two GPUs")
     import numpy as np
@@ -199,7 +202,8 @@ def test_fwpkm_data_parallel_equals_one_gpu(tmp_path, backend, world):
     torch.backends.cuda.matmul.allow_tf32 = False
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=dist_gpu_worker.run_fwpkm_dp, args=(r, world, port, str(tmp_path), backend))
+    procs = [ctx.Process(target=dist_gpu_worker.run_fwpkm_dp,
+                         args=(r, world, port, str(tmp_path), backend, sharded))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -217,7 +221,7 @@ def test_fwpkm_data_parallel_equals_one_gpu(tmp_path, backend, world):
         a, b = np.asarray(a, dtype=np.float64), np.asarray(b, dtype=np.float64)
         return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
 
-    parts = [torch.load(os.path.join(tmp_path, f"fwdp{r}.pt")) for r in range(world)]
+    parts = [torch.load(os.path.join(tmp_path, f"{'fwsh' if sharded else 'fwdp'}{r}.pt")) for r in range(world)]
     for key in ("out", "q_grad", "ref_v_grad", "indices"):
         got = torch.cat([p[key] for p in parts], 0)
         if key == "indices":
