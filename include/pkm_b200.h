@@ -232,7 +232,7 @@ PKM_API int pkm_gemm_bf16(const void* A, int a_mn_major, int64_t a_rows, int64_t
                           size_t workspace_bytes, uint32_t* dev_err, void* stream);
 /*
  * fp32 GEMM on the CUDA cores, same operand views and batching as
- * pkm_gemm_bf16 (no bias, fp32 C, any K, no workspace):
+ * pkm_gemm_bf16 (no bias, fp32 C, any K, unsplit: no workspace):
  *   C[b][m, n] = sum_k A[b][m, k] * B[b][n, k]
  * Replaces the fp32 einsum / cdist gradients of the fast-weight memory's
  * sub-key scores (fwpkm/fwpkm.py:853-869: dS @ K and dS^T @ Q per (head, half)
@@ -244,6 +244,18 @@ PKM_API int pkm_gemm_f32(const float* A, int a_mn_major, int64_t a_rows, int64_t
                          int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_batch_x, int64_t a_batch_y,
                          int64_t b_batch_x, int64_t b_batch_y, float* C, int64_t ldc, int64_t c_batch_stride,
                          void* stream);
+/*
+ * The same with a workspace from pkm_gemm_f32_workspace: grids that the
+ * tiles alone cannot fill split K into fp32 partials summed in split order
+ * (the same results for every split count up to fp32 summation order; a
+ * workspace smaller than the query's runs unsplit).
+ */
+PKM_API int pkm_gemm_f32_workspace(int64_t batch, int64_t M, int64_t N, int64_t K, size_t* bytes);
+PKM_API int pkm_gemm_f32_ws(const float* A, int a_mn_major, int64_t a_rows, int64_t a_cols, int64_t lda,
+                            const float* B, int b_mn_major, int64_t b_rows, int64_t b_cols, int64_t ldb,
+                            int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_batch_x, int64_t a_batch_y,
+                            int64_t b_batch_x, int64_t b_batch_y, float* C, int64_t ldc, int64_t c_batch_stride,
+                            void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * The SwiLU-gated value projection's GEMMs with the gate in their epilogue

@@ -48,6 +48,9 @@ _SIGS = {
     "pkm_debug_gemm_pair": ([_I], _I),
     "pkm_gemm_f32": ([_P, _I, _I64, _I64, _I64, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                       _I64, _I64, _P, _I64, _I64, _P], _I),
+    "pkm_gemm_f32_workspace": ([_I64, _I64, _I64, _I64, ctypes.POINTER(ctypes.c_size_t)], _I),
+    "pkm_gemm_f32_ws": ([_P, _I, _I64, _I64, _I64, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                         _I64, _I64, _P, _I64, _I64, _P, ctypes.c_size_t, _P], _I),
     "pkm_gemm_swiglu_fwd": ([_P, _I64, _P, _P, _I, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P], _I),
     "pkm_gemm_swiglu_bwd": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P], _I),
     "pkm_score_transform_bwd": ([_P, _P, _P, _I, _I64, _I64, ctypes.c_double, _I, _P, _P], _I),
@@ -584,10 +587,13 @@ def gemm_f32(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool
         assert batch == 1
         out = torch.empty((M, N), dtype=torch.float32, device=a.device)
     assert out.dtype == torch.float32 and out.stride(-1) == 1
-    rc = lib().pkm_gemm_f32(_ptr(a), int(a_mn), ar, ac, lda, _ptr(b), int(b_mn), br, bc, ldb, batch, M, N, K,
-                            a_batch[0], a_batch[1], b_batch[0], b_batch[1], _ptr(out), out.stride(-2), c_batch_stride,
-                            _stream(a.device))
-    _check(rc, "pkm_gemm_f32")
+    nb = ctypes.c_size_t(0)
+    _check(lib().pkm_gemm_f32_workspace(batch, M, N, K, ctypes.byref(nb)), "pkm_gemm_f32_workspace")
+    ws = torch.empty(int(nb.value), dtype=torch.uint8, device=a.device) if nb.value else None
+    rc = lib().pkm_gemm_f32_ws(_ptr(a), int(a_mn), ar, ac, lda, _ptr(b), int(b_mn), br, bc, ldb, batch, M, N, K,
+                               a_batch[0], a_batch[1], b_batch[0], b_batch[1], _ptr(out), out.stride(-2),
+                               c_batch_stride, _ptr(ws), 0 if ws is None else ws.numel(), _stream(a.device))
+    _check(rc, "pkm_gemm_f32_ws")
     return out
 
 

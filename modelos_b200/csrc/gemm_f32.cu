@@ -10,8 +10,12 @@
 // shifting the operands by (column, row) offsets, the same views as the
 // tensor-core GEMM.  128 x 128 output tiles, 256 threads, 8 x 8 outputs per
 // thread in two 4-wide groups 64 apart (conflict-free 16-byte shared loads),
-// K in slices of 8 through a double-buffered shared tile; fp32 FMAs,
-// ascending k within a thread.
+// K in slices of 8 through a double-buffered shared tile: the next slice is
+// fetched into registers (16-byte loads where its four elements are inside
+// and aligned) while the current one is multiplied, then stored; fp32 FMAs,
+// ascending k within a thread.  Grids the tiles alone cannot fill split K
+// (with a workspace): fp32 partials per split, summed in split order by a
+// second kernel (deterministic).
 #include <algorithm>
 
 #include "common.cuh"
@@ -26,10 +30,12 @@ struct GemmF32Args {
   float* C;
   int64_t lda, ldb, ldc;
   int a_mn, b_mn;
+  int vec_a, vec_b;  // 16-byte loads allowed (aligned base, pitch and batch offsets)
   int M, N, K;
   int64_t a_rows, a_cols, b_rows, b_cols;
   int64_t a_bx, a_by, b_bx, b_by, c_bs;
-  int m_tiles, n_tiles;
+  int m_tiles, n_tiles, batch, splits;
+  float* ws;  // split partials [splits][batch][M][N]
 };
 
 // Element (i along M or N, k) of an operand view, 0 outside the matrix.
@@ -39,35 +45,56 @@ __device__ __forceinline__ float f_at(const float* P, int64_t ld, int mn_major, 
   return (r < rows && c < cols) ? __ldg(P + r * ld + c) : 0.f;
 }
 
-// Load one operand's 8 x 128 slice [k][i] into shared memory: 4 elements
-// per thread, coalesced along the operand's contiguous dimension.
-__device__ __forceinline__ void f_load(const float* P, int64_t ld, int mn_major, int64_t rows, int64_t cols,
-                                       int64_t bx, int64_t by, int64_t i0, int64_t k0, int lim_i, int lim_k,
-                                       float (*S)[F_BM + 4]) {
+// This thread's 4 elements of one operand's 8 x 128 slice, into registers:
+// MN-major: (k = t / 32, i = (t % 32) * 4 .. +3); K-major: (i = t / 2,
+// k = (t % 2) * 4 .. +3); both runs are contiguous in memory.
+__device__ __forceinline__ void f_fetch(const float* P, int64_t ld, int mn_major, int vec, int64_t rows, int64_t cols,
+                                        int64_t bx, int64_t by, int64_t i0, int64_t k0, int lim_i, int lim_k,
+                                        float (&r)[4]) {
   const int t = threadIdx.x;
   if (mn_major) {
-    // rows are k: thread -> (k = t / 32, i = (t % 32) * 4 .. +3)
-    const int k = t >> 5, i = (t & 31) * 4;
+    const int64_t k = k0 + (t >> 5), i = i0 + (t & 31) * 4;
+    if (vec && k < lim_k && i + 3 < lim_i) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(P + (k + by) * ld + i + bx));
+      r[0] = v.x;
+      r[1] = v.y;
+      r[2] = v.z;
+      r[3] = v.w;
+    } else {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const bool in = (k0 + k < lim_k) && (i0 + i + j < lim_i);
-      S[k][i + j] = in ? f_at(P, ld, 1, rows, cols, bx, by, i0 + i + j, k0 + k) : 0.f;
+      for (int j = 0; j < 4; ++j) r[j] = (k < lim_k && i + j < lim_i) ? f_at(P, ld, 1, rows, cols, bx, by, i + j, k) : 0.f;
     }
   } else {
-    // rows are i: thread -> (i = t / 2, k = (t % 2) * 4 .. +3)
+    const int64_t i = i0 + (t >> 1), k = k0 + (t & 1) * 4;
+    if (vec && i < lim_i && k + 3 < lim_k) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(P + (i + by) * ld + k + bx));
+      r[0] = v.x;
+      r[1] = v.y;
+      r[2] = v.z;
+      r[3] = v.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = (i < lim_i && k + j < lim_k) ? f_at(P, ld, 0, rows, cols, bx, by, i, k + j) : 0.f;
+    }
+  }
+}
+
+__device__ __forceinline__ void f_store(int mn_major, const float (&r)[4], float (*S)[F_BM + 4]) {
+  const int t = threadIdx.x;
+  if (mn_major) {
+    *reinterpret_cast<float4*>(&S[t >> 5][(t & 31) * 4]) = make_float4(r[0], r[1], r[2], r[3]);
+  } else {
     const int i = t >> 1, k = (t & 1) * 4;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const bool in = (k0 + k + j < lim_k) && (i0 + i < lim_i);
-      S[k + j][i] = in ? f_at(P, ld, 0, rows, cols, bx, by, i0 + i, k0 + k + j) : 0.f;
-    }
+    for (int j = 0; j < 4; ++j) S[k + j][i] = r[j];
   }
 }
 
 __global__ void __launch_bounds__(F_THREADS) gemm_f32_kernel(const GemmF32Args a) {
   __shared__ __align__(16) float As[2][F_BK][F_BM + 4];
   __shared__ __align__(16) float Bs[2][F_BK][F_BN + 4];
-  const int64_t tile = blockIdx.x;
+  const int s = (int)(blockIdx.x % a.splits);
+  const int64_t tile = blockIdx.x / a.splits;
   const int nt = (int)(tile % a.n_tiles);
   const int mt = (int)((tile / a.n_tiles) % a.m_tiles);
   const int b = (int)(tile / ((int64_t)a.n_tiles * a.m_tiles));
@@ -82,14 +109,24 @@ __global__ void __launch_bounds__(F_THREADS) gemm_f32_kernel(const GemmF32Args a
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
 
   const int nk = (a.K + F_BK - 1) / F_BK;
-  f_load(a.A, a.lda, a.a_mn, a.a_rows, a.a_cols, abx, aby, m0, 0, a.M, a.K, As[0]);
-  f_load(a.B, a.ldb, a.b_mn, a.b_rows, a.b_cols, bbx, bby, n0, 0, a.N, a.K, Bs[0]);
+  const int kt0 = (int)((int64_t)nk * s / a.splits), kt1 = (int)((int64_t)nk * (s + 1) / a.splits);
+  float ra[4], rb[4];
+  if (kt0 < kt1) {
+    f_fetch(a.A, a.lda, a.a_mn, a.vec_a, a.a_rows, a.a_cols, abx, aby, m0, (int64_t)kt0 * F_BK, a.M, a.K, ra);
+    f_fetch(a.B, a.ldb, a.b_mn, a.vec_b, a.b_rows, a.b_cols, bbx, bby, n0, (int64_t)kt0 * F_BK, a.N, a.K, rb);
+    f_store(a.a_mn, ra, As[0]);
+    f_store(a.b_mn, rb, Bs[0]);
+  }
   __syncthreads();
-  for (int kt = 0; kt < nk; ++kt) {
-    const int cur = kt & 1;
-    if (kt + 1 < nk) {
-      f_load(a.A, a.lda, a.a_mn, a.a_rows, a.a_cols, abx, aby, m0, (int64_t)(kt + 1) * F_BK, a.M, a.K, As[cur ^ 1]);
-      f_load(a.B, a.ldb, a.b_mn, a.b_rows, a.b_cols, bbx, bby, n0, (int64_t)(kt + 1) * F_BK, a.N, a.K, Bs[cur ^ 1]);
+  for (int kt = kt0; kt < kt1; ++kt) {
+    const int cur = (kt - kt0) & 1;
+    const bool more = kt + 1 < kt1;
+    if (more) {
+      // in flight while this slice is multiplied
+      f_fetch(a.A, a.lda, a.a_mn, a.vec_a, a.a_rows, a.a_cols, abx, aby, m0, (int64_t)(kt + 1) * F_BK, a.M, a.K,
+              ra);
+      f_fetch(a.B, a.ldb, a.b_mn, a.vec_b, a.b_rows, a.b_cols, bbx, bby, n0, (int64_t)(kt + 1) * F_BK, a.N, a.K,
+              rb);
     }
 #pragma unroll
     for (int k = 0; k < F_BK; ++k) {
@@ -107,13 +144,19 @@ __global__ void __launch_bounds__(F_THREADS) gemm_f32_kernel(const GemmF32Args a
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
+    if (more) {
+      // the other buffer was last read before the previous barrier
+      f_store(a.a_mn, ra, As[cur ^ 1]);
+      f_store(a.b_mn, rb, Bs[cur ^ 1]);
+    }
     __syncthreads();
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int64_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
     if (m >= a.M) continue;
-    float* crow = a.C + b * a.c_bs + m * a.ldc;
+    float* crow = a.splits > 1 ? a.ws + (((int64_t)s * a.batch + b) * a.M + m) * a.N
+                               : a.C + b * a.c_bs + m * a.ldc;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int64_t n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
@@ -122,15 +165,45 @@ __global__ void __launch_bounds__(F_THREADS) gemm_f32_kernel(const GemmF32Args a
   }
 }
 
+// C[b][m][n] = sum over s of the split partials, in split order.
+__global__ void gemm_f32_reduce_kernel(const GemmF32Args a) {
+  const int64_t per = (int64_t)a.batch * a.M * a.N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = a.ws[i];
+    for (int s = 1; s < a.splits; ++s) acc += a.ws[s * per + i];
+    const int64_t n = i % a.N, r = i / a.N;
+    const int64_t m = r % a.M, b = r / a.M;
+    a.C[b * a.c_bs + m * a.ldc + n] = acc;
+  }
+}
+
+// Splits of K: while the tiles would leave SMs idle (two blocks each) and
+// every split keeps at least 32 slices of 8.
+static int gemm_f32_splits(int64_t tiles, int64_t K) {
+  const int64_t nk = (K + F_BK - 1) / F_BK, target = 2 * (int64_t)num_sms();
+  int s = 1;
+  while (tiles * s * 2 <= target && nk / (s * 2) >= 32 && s < 16) s *= 2;
+  return s;
+}
+
 }  // namespace pkm
 
 using namespace pkm;
 
-extern "C" int pkm_gemm_f32(const float* A, int a_mn_major, int64_t a_rows, int64_t a_cols, int64_t lda,
-                            const float* B, int b_mn_major, int64_t b_rows, int64_t b_cols, int64_t ldb,
-                            int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_batch_x, int64_t a_batch_y,
-                            int64_t b_batch_x, int64_t b_batch_y, float* C, int64_t ldc, int64_t c_batch_stride,
-                            void* stream) {
+extern "C" int pkm_gemm_f32_workspace(int64_t batch, int64_t M, int64_t N, int64_t K, size_t* bytes) {
+  if (!bytes) return fail(PKM_ERR_INVALID_ARG, "null bytes");
+  if (batch < 0 || M < 0 || N < 0 || K < 0) return fail(PKM_ERR_INVALID_ARG, "negative size");
+  const int64_t tiles = batch * ((M + F_BM - 1) / F_BM) * ((N + F_BN - 1) / F_BN);
+  const int s = gemm_f32_splits(tiles, K);
+  *bytes = s > 1 ? (size_t)s * batch * M * N * sizeof(float) : 0;
+  return PKM_OK;
+}
+
+extern "C" int pkm_gemm_f32_ws(const float* A, int a_mn_major, int64_t a_rows, int64_t a_cols, int64_t lda,
+                               const float* B, int b_mn_major, int64_t b_rows, int64_t b_cols, int64_t ldb,
+                               int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_batch_x,
+                               int64_t a_batch_y, int64_t b_batch_x, int64_t b_batch_y, float* C, int64_t ldc,
+                               int64_t c_batch_stride, void* workspace, size_t workspace_bytes, void* stream) {
   if (batch < 0 || M < 0 || N < 0 || K < 0) return fail(PKM_ERR_INVALID_ARG, "negative size");
   if (batch == 0 || M == 0 || N == 0) return PKM_OK;
   if (!A || !B || !C) return fail(PKM_ERR_INVALID_ARG, "null operand");
@@ -154,6 +227,8 @@ extern "C" int pkm_gemm_f32(const float* A, int a_mn_major, int64_t a_rows, int6
   a.ldc = ldc;
   a.a_mn = a_mn_major ? 1 : 0;
   a.b_mn = b_mn_major ? 1 : 0;
+  a.vec_a = aligned16(A) && lda % 4 == 0 && a_batch_x % 4 == 0;
+  a.vec_b = aligned16(B) && ldb % 4 == 0 && b_batch_x % 4 == 0;
   a.M = (int)M;
   a.N = (int)N;
   a.K = (int)K;
@@ -168,8 +243,29 @@ extern "C" int pkm_gemm_f32(const float* A, int a_mn_major, int64_t a_rows, int6
   a.c_bs = c_batch_stride;
   a.m_tiles = (int)((M + F_BM - 1) / F_BM);
   a.n_tiles = (int)((N + F_BN - 1) / F_BN);
+  a.batch = (int)batch;
   const int64_t tiles = batch * a.m_tiles * a.n_tiles;
-  if (tiles > INT32_MAX) return fail(PKM_ERR_UNSUPPORTED, "too many tiles");
-  gemm_f32_kernel<<<(unsigned)tiles, F_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  return check_cuda("gemm_f32_kernel");
+  int splits = gemm_f32_splits(tiles, K);
+  const size_t need = splits > 1 ? (size_t)splits * batch * M * N * sizeof(float) : 0;
+  if (splits > 1 && (!workspace || workspace_bytes < need || !aligned16(workspace))) splits = 1;
+  a.splits = splits;
+  a.ws = static_cast<float*>(workspace);
+  if (tiles * splits > INT32_MAX) return fail(PKM_ERR_UNSUPPORTED, "too many tiles");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  gemm_f32_kernel<<<(unsigned)(tiles * splits), F_THREADS, 0, st>>>(a);
+  int rc = check_cuda("gemm_f32_kernel");
+  if (rc || splits == 1) return rc;
+  const int64_t per = batch * M * N;
+  const int64_t rgrid = std::max<int64_t>(1, std::min<int64_t>((per + 255) / 256, (int64_t)num_sms() * 8));
+  gemm_f32_reduce_kernel<<<(unsigned)rgrid, 256, 0, st>>>(a);
+  return check_cuda("gemm_f32_reduce_kernel");
+}
+
+extern "C" int pkm_gemm_f32(const float* A, int a_mn_major, int64_t a_rows, int64_t a_cols, int64_t lda,
+                            const float* B, int b_mn_major, int64_t b_rows, int64_t b_cols, int64_t ldb,
+                            int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_batch_x, int64_t a_batch_y,
+                            int64_t b_batch_x, int64_t b_batch_y, float* C, int64_t ldc, int64_t c_batch_stride,
+                            void* stream) {
+  return pkm_gemm_f32_ws(A, a_mn_major, a_rows, a_cols, lda, B, b_mn_major, b_rows, b_cols, ldb, batch, M, N, K,
+                         a_batch_x, a_batch_y, b_batch_x, b_batch_y, C, ldc, c_batch_stride, nullptr, 0, stream);
 }

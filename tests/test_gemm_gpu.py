@@ -192,6 +192,9 @@ F32_CASES = [
     (256, 256, 4096, True, True),
     (1000, 136, 512, False, True),
     (7, 5, 3, True, False),
+    (512, 256, 8192, True, True),     # few tiles, deep K: split K (workspace, fixed-order reduction)
+    (130, 70, 3001, False, False),    # split K with ragged M, N and K
+    (257, 129, 1029, True, False),    # odd pitches: scalar loads
 ]
 
 
@@ -206,6 +209,22 @@ def test_gemm_f32_matches_torch(M, N, K, a_mn, b_mn):
     c = _native.gemm_f32(a, b, a_mn=a_mn, b_mn=b_mn)
     ref = (a.T if a_mn else a).double() @ (b.T if b_mn else b).double().T
     assert rel_err(c, ref) < 1e-5
+
+
+def test_gemm_f32_batched_split_matches_torch():
+    """The fast-weight scoring backward's dK form, batched over (head, half)
+    groups with few tiles and a deep K (split K): dk_g = dS[:, g, :].T @ q_g."""
+    from modelos_b200 import _native
+    torch.backends.cuda.matmul.allow_tf32 = False
+    g = torch.Generator().manual_seed(13)
+    T, G, n, half = 4096, 4, 256, 128
+    dS = torch.randn(T, G * n, generator=g).to(DEV)
+    q = torch.randn(T, G * half, generator=g).to(DEV)
+    dk = torch.empty(G * n, half, dtype=torch.float32, device=DEV)
+    _native.gemm_f32(dS, q, a_mn=True, b_mn=True, batch=G, M=n, N=half, K=T, a_batch=(n, 0), b_batch=(half, 0),
+                     out=dk, c_batch_stride=n * half)
+    ref = torch.einsum("tgn,tgh->gnh", dS.double().view(T, G, n), q.double().view(T, G, half)).reshape(G * n, half)
+    assert rel_err(dk, ref) < 1e-5
 
 
 def test_group_mm_second_derivatives_match_einsum():
