@@ -11,11 +11,15 @@
 //             one of two 256-column TMEM accumulators, tcgen05.commit frees
 //             each stage and hands finished accumulators to the epilogue;
 //   warps 2-5 epilogue: tcgen05.ld of the accumulator rows (one token row
-//             per thread), round to bf16, store into [N, H, 2, n].
+//             per thread, the next 32 columns in flight), round to bf16
+//             into a swizzled 32-token x 64-key staging box per warp, one
+//             TMA store per box into [N, H, 2, n] (viewed as [N, H*2*n]);
+//             boxes at a ragged edge are stored directly.
 // Two accumulators let the epilogue of one tile overlap the MMAs of the next.
 // Every wait is bounded; a timeout raises PKM_DEVERR_TIMEOUT and each role
 // drains its own outstanding work before TMEM is released.
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "umma.cuh"
@@ -27,7 +31,8 @@ constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;
 constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;
 constexpr int TC_STAGE = TC_A_BYTES + TC_B_BYTES;
 constexpr int TC_THREADS = 192;
-constexpr int TC_SMEM = TC_STAGES * TC_STAGE + 1024 + 256;
+constexpr int TC_STAGING = 4 * 4096;  // per epilogue warp: 32 rows x 128 bytes
+constexpr int TC_SMEM = TC_STAGES * TC_STAGE + TC_STAGING + 1024 + 256;
 
 struct TcScoreArgs {
   int64_t n_tokens;
@@ -40,6 +45,7 @@ struct TcScoreArgs {
   int64_t n_tile_total;
   __nv_bfloat16* out;
   uint32_t* err;
+  int st_tma;  // the output map is valid: whole boxes leave by TMA stores
 };
 
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort_flag) {
@@ -54,11 +60,11 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, uint32_t
 
 __global__ void __launch_bounds__(TC_THREADS, 1)
     subkey_scores_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                            const TcScoreArgs a) {
+                            const __grid_constant__ CUtensorMap to, const TcScoreArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE + TC_STAGING);
   uint64_t* empty = full + TC_STAGES;
   uint64_t* tfull = empty + TC_STAGES;
   uint64_t* tempty = tfull + 2;
@@ -88,6 +94,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tq);
     prefetch_tmap(&tk);
+    if (a.st_tma) prefetch_tmap(&to);
   }
   tc_fence_before();
   __syncthreads();
@@ -156,47 +163,85 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;
     const int64_t H2 = (int64_t)a.heads * 2;
+    // staging box: row = lane, 16-byte chunk j at j ^ (lane & 7) (128-byte swizzle)
+    unsigned char* stg = smem + TC_STAGES * TC_STAGE + (warp - 2) * 4096;
+    unsigned char* stg_row = stg + lane * 128;
     int li = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++li) {
       const int acc = li & 1;
-      if (!tc_wait(&tfull[acc], (li >> 1) & 1, a.err, abort_flag)) break;
+      // the warp leaves together (tcgen05.ld is warp-collective)
+      const bool got = tc_wait(&tfull[acc], (li >> 1) & 1, a.err, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       int hp, mt, nt;
       decode(tile, hp, mt, nt);
-      const int64_t t = (int64_t)mt * TC_BM + row;
+      const int64_t mw = (int64_t)mt * TC_BM + q * 32;  // the warp's first token
+      const int64_t t = mw + lane;
+      const bool rows_in = mw + 32 <= a.n_tokens;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TC_BN);
       __nv_bfloat16* orow = a.out + (t * H2 + hp) * (int64_t)a.n_keys;
-#pragma unroll 1
+      uint32_t r[2][32];
+      tmem_ld_32x32b_x32(tbase, r[0]);
+      tmem_ld_wait();
+#pragma unroll
       for (int c = 0; c < TC_BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
-        tmem_ld_wait();
+        if (c + 1 < TC_BN / 32) tmem_ld_32x32b_x32(tbase + (uint32_t)((c + 1) * 32), r[(c + 1) & 1]);
+        const uint32_t* rc = r[c & 1];
         const int col0 = nt * TC_BN + c * 32;
-        if (t < a.n_tokens) {
+        const int nb = col0 - (c & 1) * 32;  // the 64-key box's first key
+        if (a.st_tma && rows_in && nb + 64 <= a.n_keys) {
+          if ((c & 1) == 0) {
+            if (lane == 0) bulk_wait_read_all();  // the previous box has left shared memory
+            __syncwarp();
+          }
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 o;
+            __nv_bfloat162 h;
+            h = __floats2bfloat162_rn(__uint_as_float(rc[v * 8 + 0]), __uint_as_float(rc[v * 8 + 1]));
+            o.x = *reinterpret_cast<uint32_t*>(&h);
+            h = __floats2bfloat162_rn(__uint_as_float(rc[v * 8 + 2]), __uint_as_float(rc[v * 8 + 3]));
+            o.y = *reinterpret_cast<uint32_t*>(&h);
+            h = __floats2bfloat162_rn(__uint_as_float(rc[v * 8 + 4]), __uint_as_float(rc[v * 8 + 5]));
+            o.z = *reinterpret_cast<uint32_t*>(&h);
+            h = __floats2bfloat162_rn(__uint_as_float(rc[v * 8 + 6]), __uint_as_float(rc[v * 8 + 7]));
+            o.w = *reinterpret_cast<uint32_t*>(&h);
+            *reinterpret_cast<uint4*>(stg_row + ((((c & 1) * 4 + v) ^ (lane & 7)) << 4)) = o;
+          }
+          if ((c & 1) == 1) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&to, stg, (int32_t)(hp * a.n_keys + nb), (int32_t)mw);
+              bulk_commit_group();
+            }
+          }
+        } else if (t < a.n_tokens) {
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             const int col = col0 + v * 8;
             if (col + 8 <= a.n_keys) {
               uint4 o;
               __nv_bfloat162 h;
-              h = __floats2bfloat162_rn(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+              h = __floats2bfloat162_rn(__uint_as_float(rc[v * 8 + 0]), __uint_as_float(rc[v * 8 + 1]));
               o.x = *reinterpret_cast<uint32_t*>(&h);
-              h = __floats2bfloat162_rn(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+              h = __floats2bfloat162_rn(__uint_as_float(rc[v * 8 + 2]), __uint_as_float(rc[v * 8 + 3]));
               o.y = *reinterpret_cast<uint32_t*>(&h);
-              h = __floats2bfloat162_rn(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+              h = __floats2bfloat162_rn(__uint_as_float(rc[v * 8 + 4]), __uint_as_float(rc[v * 8 + 5]));
               o.z = *reinterpret_cast<uint32_t*>(&h);
-              h = __floats2bfloat162_rn(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+              h = __floats2bfloat162_rn(__uint_as_float(rc[v * 8 + 6]), __uint_as_float(rc[v * 8 + 7]));
               o.w = *reinterpret_cast<uint32_t*>(&h);
               *reinterpret_cast<uint4*>(orow + col) = o;
             }
           }
         }
+        tmem_ld_wait();
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) bulk_wait_all();  // this warp's boxes are written
   }
   tc_fence_before();
   __syncthreads();
@@ -277,11 +322,18 @@ int subkey_scores_tc(const void* query, const void* keys, int64_t n_tokens, int6
   a.n_tile_total = (int64_t)a.m_tiles * a.n_tiles * heads * 2;
   a.out = static_cast<__nv_bfloat16*>(scores);
   a.err = err;
+  // the scores [N, H*2*n] for the epilogue's TMA stores: boxes of 64 keys x
+  // 32 tokens (a failed encode leaves the direct stores)
+  CUtensorMap to;
+  memset(&to, 0, sizeof(to));
+  a.st_tma = n_tokens < INT32_MAX && 2 * heads * n_keys < INT32_MAX &&
+             make_tmap_2d(&to, scores, PKM_DT_BF16, (uint64_t)(2 * heads * n_keys), (uint64_t)n_tokens,
+                          (uint64_t)(2 * heads * n_keys * 2), 64, 32, 128) == PKM_OK;
   if (cudaFuncSetAttribute(subkey_scores_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) !=
       cudaSuccess)
     return check_cuda("cudaFuncSetAttribute(subkey_scores_tc)");
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(a.n_tile_total, num_sms()));
-  subkey_scores_tc_kernel<<<(unsigned)grid, TC_THREADS, TC_SMEM, st>>>(tq, tk, a);
+  subkey_scores_tc_kernel<<<(unsigned)grid, TC_THREADS, TC_SMEM, st>>>(tq, tk, to, a);
   return check_cuda("subkey_scores_tc_kernel");
 }
 
