@@ -316,14 +316,22 @@ class FastWeightProductKeyMemory(nn.Module):
         rows = scores.reshape(-1, scores.shape[-1])
         return ScoreTransform.apply(rows, float(self.score_temperature), self.score_nonlinear).view(scores.shape)
 
-    def compute_marginal_entropy(self, M, epsilon=1e-8):
+    def compute_marginal_entropy(self, M, epsilon=1e-8, sorted_idx=None):
         """Entropy of the batch-mean of a top-k-thresholded softmax of M [N, K].
         Split over data-parallel ranks, the batch mean is over every rank's
-        rows (a differentiable all-reduce of the row sums)."""
+        rows (a differentiable all-reduce of the row sums).  ``sorted_idx``
+        [N, topk], when given, are each row's topk best columns, best first
+        (the product top-k's stage-1 lists of these very scores): the
+        threshold, the topk-th largest value, is then read at its last
+        column instead of running a top-k again (equal values tie, so the
+        value is the same whichever tied column holds it)."""
         in_dtype = M.dtype
         if self.addr_loss_weight == 0.0:
             return torch.tensor(0.0, device=M.device, dtype=in_dtype)
-        kth = torch.topk(M, self.topk, dim=1).values[:, -1:]
+        if sorted_idx is not None:
+            kth = M.gather(1, sorted_idx.reshape(M.shape[0], -1)[:, self.topk - 1:self.topk].long())
+        else:
+            kth = torch.topk(M, self.topk, dim=1).values[:, -1:]
         M = torch.where(M >= kth, M, torch.full_like(M, float("-inf"))).float()
         world, group = self._dp()
         if world == 1:
@@ -454,7 +462,12 @@ class FastWeightProductKeyMemory(nn.Module):
             raise NotImplementedError(f"Addressing loss {self.addr_loss} not implemented.")
         s1 = all_sub_scores1.reshape(-1, self.subsize)
         s2 = all_sub_scores2.reshape(-1, self.subsize)
-        return self.addr_loss_weight * (-self.compute_marginal_entropy(s1) - self.compute_marginal_entropy(s2))
+        i1 = sub_indices1.reshape(s1.shape[0], -1) if sub_indices1 is not None else None
+        i2 = sub_indices2.reshape(s2.shape[0], -1) if sub_indices2 is not None else None
+        if i1 is not None and (i1.shape[1] != self.topk or i2 is None or i2.shape[1] != self.topk):
+            i1 = i2 = None
+        return self.addr_loss_weight * (-self.compute_marginal_entropy(s1, sorted_idx=i1)
+                                        - self.compute_marginal_entropy(s2, sorted_idx=i2))
 
     def update_fw_param(self, p, g, lr, wd):
         if self.optimizer_type != "sgd":

@@ -55,7 +55,9 @@ def pin_pkm_selection(monkeypatch, native, ref_idx: torch.Tensor):
 def pin_fwpkm_selection(monkeypatch, native, ref_idx: torch.Tensor, chunk: int):
     """FwPKM's lookup of chunk c takes the reference's indices of that chunk
     (``ref_idx`` [B, T, H, knn]); the module re-forms the scores from its
-    own sub-key scores."""
+    own sub-key scores.  The per-half lists are each half's knn best
+    sub-keys, best first, as the product top-k returns them (the addressing
+    loss reads its threshold there)."""
     calls = [0]
     B, T, H, knn = ref_idx.shape
 
@@ -64,8 +66,9 @@ def pin_fwpkm_selection(monkeypatch, native, ref_idx: torch.Tensor, chunk: int):
         calls[0] += 1
         idx = ref_idx[:, c * chunk:(c + 1) * chunk].reshape(-1, knn).to(scores.device)
         assert idx.shape[0] == scores.shape[0] and k == knn
-        n = scores.shape[-1]
-        return idx.clone(), None, None, idx // n, idx % n
+        s1 = torch.topk(scores[:, 0].float(), k, dim=1).indices
+        s2 = torch.topk(scores[:, 1].float(), k, dim=1).indices
+        return idx.clone(), None, None, s1, s2
 
     monkeypatch.setattr(native, "product_topk", forced)
     return calls
