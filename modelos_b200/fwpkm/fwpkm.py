@@ -241,8 +241,16 @@ class FusedValueUpdate(torch.autograd.Function):
         scale, lr, wd, clip = ctx.args
         if d_new is None:
             d_new = torch.zeros_like(d_scaled)
-        dv, dg = _native.fw_update_bwd(d_new, d_scaled, scaled, counts, scale, lr, wd, clip,
-                                       need_values=ctx.needs_input_grad[0], need_grad=ctx.needs_input_grad[1])
+        # d_values = d_new * (1 - lr * wd): without weight decay that is
+        # d_new itself, passed on rather than copied (1 GiB at config 4)
+        pass_through = ctx.needs_input_grad[0] and wd == 0.0
+        dv = dg = None
+        if (ctx.needs_input_grad[0] and not pass_through) or ctx.needs_input_grad[1]:
+            dv, dg = _native.fw_update_bwd(d_new, d_scaled, scaled, counts, scale, lr, wd, clip,
+                                           need_values=ctx.needs_input_grad[0] and not pass_through,
+                                           need_grad=ctx.needs_input_grad[1])
+        if pass_through:
+            dv = d_new
         return dv, dg, None, None, None, None, None
 
 
