@@ -353,6 +353,80 @@ def bag_bytes(N, L, D, K, s_v=2, s_idx=8, s_w=2, s_out=2):
     return fwd, bwd
 
 
+def e2e_graph(step, x, x_host, steps, dev):
+    """The c2 end-to-end loop with the step (the layer's forward and
+    backward and the loss, all through the public modules) captured once in
+    a CUDA graph and replayed: every step still copies its batch from
+    pinned host memory (side stream, two device buffers, then a
+    device-to-device copy into the graph's input) and reads its loss back.
+    Returns ``(ms_per_step, None)``, or ``(None, reason)`` when the capture
+    fails or its first replay does not give the eager step's loss bit for
+    bit (the eager loop's number then stands)."""
+    import torch
+    compute = torch.cuda.current_stream(dev)
+    try:
+        static_x = torch.empty_like(x)
+        static_x.copy_(x)
+        # the reference step and the warm-up on a side stream, so that the
+        # leaves' gradient accumulators are recreated off the default stream
+        # (an accumulator made there would sync with it inside the capture)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(compute)
+        with torch.cuda.stream(side):
+            ref = step(static_x).detach().clone()
+            for _ in range(2):
+                step(static_x)
+        compute.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_loss = step(static_x)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        if not torch.equal(static_loss, ref):
+            return None, "the graph's loss differs from the eager step's"
+    except Exception as e:  # the eager loop's number stands
+        return None, f"capture failed ({type(e).__name__}: {str(e).splitlines()[0][:160] if str(e) else ''})"
+    copy_stream = torch.cuda.Stream(dev)
+    bufs = [torch.empty_like(x), torch.empty_like(x)]
+    slots = [torch.empty_like(static_loss), torch.empty_like(static_loss)]
+    ready = [torch.cuda.Event(), torch.cuda.Event()]
+    free = [torch.cuda.Event(), torch.cuda.Event()]
+    for ev in free:
+        ev.record(compute)
+    torch.cuda.synchronize(dev)
+
+    def h2d(b):
+        copy_stream.wait_event(free[b])
+        with torch.cuda.stream(copy_stream):
+            bufs[b].copy_(x_host, non_blocking=True)
+            ready[b].record(copy_stream)
+
+    w0 = time.perf_counter()
+    h2d(0)
+    pending = None
+    lv = None
+    for i in range(steps):
+        b = i & 1
+        compute.wait_event(ready[b])
+        static_x.copy_(bufs[b])
+        free[b].record(compute)
+        if i + 1 < steps:
+            h2d(b ^ 1)
+        graph.replay()
+        slots[b].copy_(static_loss)  # the next replay overwrites the graph's loss
+        if pending is not None:
+            lv = pending.item()
+        pending = slots[b]
+    lv = pending.item()
+    torch.cuda.synchronize(dev)
+    ms = (time.perf_counter() - w0) * 1000.0 / steps
+    del graph
+    if not math.isfinite(lv):
+        return None, "non-finite loss in the graph loop"
+    return ms, None
+
+
 def count_launches(step, *a):
     """Kernels of libpkm_b200 launched by one step (profiled outside timing)."""
     import torch
@@ -971,6 +1045,13 @@ def run_ours(args, rank, world, local_rank):
         del bufs
         emb, _ = measure_c1(dev, max(args.steps, 20), max(args.warmup, 3))
     clk.stop()
+    # last, so that a capture that went wrong can cost nothing else
+    graph_ms, graph_note = (None, "not attempted (N > 1 or --no-graph)")
+    if world == 1 and not args.no_graph:
+        # no loss of an earlier step may keep its autograd graph, and with it
+        # the gradient accumulators made on the default stream, alive
+        loss = pending = None
+        graph_ms, graph_note = e2e_graph(step, x, x_host, args.steps, dev)
 
     if rank != 0:
         return
@@ -1000,9 +1081,16 @@ def run_ours(args, rank, world, local_rank):
         "config": dict(config_obj(world), grad_exchange=exchange,
                        **({} if opt is None else {"optimizer": f"sgd lr {args.lr} (foreach; table rows by owner "
                                                                 f"with --grad-exchange owner)"})),
-        "e2e": {"value": round(B * T * world / (e2e_ms / 1000.0), 1), "unit": UNIT,
-                "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4,
-                "ms_per_step": round(e2e_ms, 4)},
+        "e2e": ({"value": round(B * T * world / (graph_ms / 1000.0), 1), "unit": UNIT,
+                 "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4,
+                 "ms_per_step": round(graph_ms, 4),
+                 "graph": "the step captured once in a CUDA graph, replayed per step (its first replay's loss "
+                          "equals the eager step's bit for bit)",
+                 "eager": {"value": round(B * T * world / (e2e_ms / 1000.0), 1), "ms_per_step": round(e2e_ms, 4)}}
+                if graph_ms is not None else
+                {"value": round(B * T * world / (e2e_ms / 1000.0), 1), "unit": UNIT,
+                 "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4,
+                 "ms_per_step": round(e2e_ms, 4), "graph": graph_note}),
         "gpu_launches": None if launches_per_step is None else launches_per_step * args.steps,
         "gpu_launches_per_step": launches_per_step,
         "roofline": dict(rl[dom], kernel=dom) if dom else None,
@@ -1032,6 +1120,8 @@ def main():
                          "(train step, prefill, decode); c4: the fast-weight memory; gemm: the c2 step's GEMM "
                          "shapes on this library's GEMM and on cuBLAS")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="c2 at N=1: the end-to-end loop without the CUDA-graph replay")
     ap.add_argument("--fw-table", default="sharded", choices=["sharded", "replicated"],
                     help="c4 at N > 1: the fast-weight value table split by rows over the ranks, or replicated")
     ap.add_argument("--grad-exchange", default="fused", choices=["fused", "nccl", "owner"],
