@@ -65,7 +65,7 @@ def test_indices_other_seeds_tie_aware():
         total_tie += n_tie
         assert n_exact + n_tie == 1024
     # near-tie reorderings between MKL's blocked sums and the sequential sum
-    # are rare (the survey measured 1 in 1024 rows at seed 1)
+    # are rare (about 1 in 1024 rows at seed 1)
     assert total_tie <= 8
 
 
