@@ -201,9 +201,11 @@ class ScoreTransform(torch.autograd.Function):
     """``score_transform`` (``fwpkm/fwpkm.py:105-115``) on the library's
     kernel: softmax / silu / relu of ``scores / temperature`` over each row
     of ``[tokens, H*knn]`` (jointly over the heads), in the scores' dtype.
-    The outer backward needs this transform's first derivative only (the
-    inner updates differentiate the bag, not the weights' normalisation), so
-    the backward is one kernel and is not itself differentiable."""
+    The backward is one kernel.  When it runs under ``create_graph`` (an
+    inner update whose loss reaches the keys through the weights:
+    ``mem_grad_to_values_only=False``) it is the same derivative in tensor
+    ops instead, so that the outer backward can differentiate it again, as
+    torch's own softmax backward can be."""
 
     @staticmethod
     def forward(ctx, scores, temperature, mode):
@@ -214,11 +216,21 @@ class ScoreTransform(torch.autograd.Function):
         return y
 
     @staticmethod
-    @torch.autograd.function.once_differentiable
     def backward(ctx, dy):
         s, y = ctx.saved_tensors
         temperature, mode = ctx.args
-        return _native.score_transform_bwd(s, y, dy, temperature, mode), None, None
+        if not torch.is_grad_enabled():
+            return _native.score_transform_bwd(s, y, dy, temperature, mode), None, None
+        if mode == "softmax":
+            dx = y * (dy - (dy * y).sum(-1, keepdim=True)) / temperature
+        else:
+            z = s / temperature
+            if mode == "silu":
+                sg = torch.sigmoid(z)
+                dx = dy * sg * (1 + z * (1 - sg)) / temperature
+            else:
+                dx = dy * (z > 0).to(dy.dtype) / temperature
+        return dx, None, None
 
 
 class FusedValueUpdate(torch.autograd.Function):

@@ -134,14 +134,17 @@ def fwpkm_dp_case():
     return cases.fwpkm_case(0, B=4, T=16)
 
 
-def fwpkm_run(q, ref_v, keys, values, group=None, sharded=False):
+FW_VARIANT_KW = dict(mem_grad_to_values_only=False, weight_decay=0.01, grad_clip=True)
+
+
+def fwpkm_run(q, ref_v, keys, values, group=None, sharded=False, extra_kw=None):
     """``forward_wo_past`` and the outer backward of ``sum(out^2)`` for the
     sequences given (all of them, or one rank's share with ``group``; with
     ``sharded`` the value table is split by rows over the group, and the
     returned values and value gradient are the gathered whole tables)."""
     from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
     import torch
-    m = FastWeightProductKeyMemory(**FW_DP_KW).train()
+    m = FastWeightProductKeyMemory(**dict(FW_DP_KW, **(extra_kw or {}))).train()
     with torch.no_grad():
         m.keys.copy_(keys)
         m.values.copy_(values)
@@ -171,7 +174,7 @@ def fwpkm_run(q, ref_v, keys, values, group=None, sharded=False):
             "grad_norms": torch.stack(res["grad_norms"])}
 
 
-def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str, sharded: bool = False):
+def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str, sharded: bool = False, variant: bool = False):
     """One rank of the data-parallel fast-weight memory (gloo, CPU stand-ins),
     with a replicated or a row-split value table."""
     import torch
@@ -190,7 +193,8 @@ def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str, sharded: bool =
         keys, values, q, ref_v = fwpkm_dp_case()
         per = q.shape[0] // world
         sl = slice(rank * per, (rank + 1) * per)
-        out = fwpkm_run(q[sl], ref_v[sl], keys, values, dist.group.WORLD, sharded=sharded)
+        out = fwpkm_run(q[sl], ref_v[sl], keys, values, dist.group.WORLD, sharded=sharded,
+                        extra_kw=FW_VARIANT_KW if variant else None)
         torch.save(out, os.path.join(out_dir, f"{'fwsh' if sharded else 'fwdp'}{rank}.pt"))
     finally:
         dist.destroy_process_group()

@@ -7,6 +7,8 @@ product package never imports it.
 """
 from __future__ import annotations
 
+import functools
+
 import numpy as np
 import torch
 
@@ -204,6 +206,23 @@ def read_device_errors(dev=None, reset=True):
 
 def check_device_errors(dev=None):
     return None
+
+
+def _kernel(f):
+    """A stand-in for a CUDA kernel: its outputs carry no autograd graph (a
+    kernel's never do), even when it is called inside a backward that runs
+    with ``create_graph``."""
+    @functools.wraps(f)
+    def run(*args, **kwargs):
+        with torch.no_grad():
+            return f(*args, **kwargs)
+    return run
+
+
+for _name in ("bag_fwd", "bag_bwd", "bag_bwd2", "subkey_scores", "product_topk", "score_grad_dense", "fw_update",
+              "fw_update_bwd", "swiglu_fwd", "swiglu_bwd", "colsum", "segment_sum", "bag_bwd_ragged", "route_pack",
+              "route_segments", "route_combine", "score_transform_fwd", "score_transform_bwd"):
+    globals()[_name] = _kernel(globals()[_name])
 
 
 def install(monkeypatch):

@@ -115,7 +115,7 @@ def test_row_sharded_bad_index_raises_on_every_rank(tmp_path):
     assert msgs[0] is not None and "rank(s) [1]" in msgs[0]
 
 
-def _fwpkm_dp_check(tmp_path, monkeypatch, sharded):
+def _fwpkm_dp_check(tmp_path, monkeypatch, sharded, variant=False):
     import numpy as np
 
     import dist_worker
@@ -123,7 +123,7 @@ def _fwpkm_dp_check(tmp_path, monkeypatch, sharded):
     os.environ["PYTHONPATH"] = os.pathsep.join([HERE, os.path.dirname(HERE), os.environ.get("PYTHONPATH", "")])
     port = _free_port()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=dist_worker.run_fwpkm_dp, args=(r, 2, port, str(tmp_path), sharded))
+    procs = [ctx.Process(target=dist_worker.run_fwpkm_dp, args=(r, 2, port, str(tmp_path), sharded, variant))
              for r in range(2)]
     for p in procs:
         p.start()
@@ -137,7 +137,7 @@ def _fwpkm_dp_check(tmp_path, monkeypatch, sharded):
     fake_native.install(monkeypatch)
     dist_worker.install_cpu_kernels(monkeypatch.setattr)
     keys, values, q, ref_v = dist_worker.fwpkm_dp_case()
-    full = dist_worker.fwpkm_run(q, ref_v, keys, values)
+    full = dist_worker.fwpkm_run(q, ref_v, keys, values, extra_kw=dist_worker.FW_VARIANT_KW if variant else None)
 
     def rel(a, b):
         a, b = np.asarray(a, dtype=np.float64), np.asarray(b, dtype=np.float64)
@@ -172,3 +172,11 @@ def test_fwpkm_row_sharded_equals_one_process(tmp_path, monkeypatch):
     final fast weights (the shards gathered), every outer gradient and the
     gradient norms equal one process on the whole table."""
     _fwpkm_dp_check(tmp_path, monkeypatch, sharded=True)
+
+
+def test_fwpkm_row_sharded_variant_equals_one_process(tmp_path, monkeypatch):
+    """The row-split table with the memorisation loss reaching the keys too
+    (``mem_grad_to_values_only=False``), weight decay (the value update's
+    backward then scales the incoming gradient rather than passing it on)
+    and gradient clipping: the same comparison with one process."""
+    _fwpkm_dp_check(tmp_path, monkeypatch, sharded=True, variant=True)
