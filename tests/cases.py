@@ -96,6 +96,29 @@ def fwpkm_case(seed: int = 0, B=2, T=16, heads=2, k_dim=16, v_dim=32, n_sub=16, 
     return keys, values, q, ref_v
 
 
+# Non-default module options, each fixture a combination the defaults
+# leave untested: the transform (silu / relu, temperature), the keys trained
+# by the memorisation loss too, gradient clipping, weight decay, no
+# look-ahead, no addressing loss, per-token gates and a loss mask.
+FW_VARIANTS = {
+    "fwpkm_var_silu.npz": (dict(qk_score_type="idw", score_nonlinear="silu", score_temperature=0.5,
+                                mem_grad_to_values_only=False, grad_clip=True, weight_decay=0.01),
+                           True, True),
+    "fwpkm_var_relu.npz": (dict(qk_score_type="dot_product", score_nonlinear="relu", lookahead=0, addr_loss=None,
+                                mem_grad_to_values_only=False),
+                           False, True),
+    "fwpkm_var_keys.npz": (dict(qk_score_type="dot_product", mem_grad_to_values_only=False), False, False),
+}
+
+
+def fw_variant_inputs(B, T, with_gates, with_mask, seed=5):
+    """Per-token gates in (0, 1) and a 0/1 loss mask for a variant run."""
+    g = torch.Generator().manual_seed(40_000 + seed)
+    gates = torch.rand((B, T), generator=g) if with_gates else None
+    mask = (torch.rand((B, T), generator=g) > 0.25).float() if with_mask else None
+    return gates, mask
+
+
 # Benchmark config 4 geometry (FwPKM): k_dim 512, v_dim 1024, 4 heads x top-32
 # over 512^2 fp32 fast-weight slots; the module's other defaults (idw,
 # softmax, addressing loss "me", lookahead 1, fp32 fast weights).
@@ -232,3 +255,39 @@ def run_stream(m, q, ref_v, d, rel_err, tol=1e-5):
             for got, key in pairs:
                 assert rel_err(got.detach().float().cpu().numpy(), d[f"c{c}_{key}"]) < tol, (c, key)
             np.testing.assert_array_equal(past[5].cpu().numpy(), d[f"c{c}_past_ids"])
+
+
+def run_fw_variant(cls, fw_kw, name, d, rel_err, tol=1e-5, device="cpu"):
+    """One training call of a ``FW_VARIANTS`` module on ``fwpkm_case(2)``
+    (gates and loss mask as the variant asks), loss = sum(output^2) plus the
+    addressing loss when there is one, checked against the fixture ``d``:
+    indices exactly, outputs, losses, updated fast weights and every
+    gradient to ``tol``."""
+    kw, with_gates, with_mask = FW_VARIANTS[name]
+    m = cls(**dict(fw_kw, **kw)).to(device).train()
+    keys, values, q, ref_v = fwpkm_case(2)
+    gates, mask = fw_variant_inputs(q.shape[0], q.shape[1], with_gates, with_mask)
+    with torch.no_grad():
+        m.keys.copy_(keys)
+        m.values.copy_(values)
+    q = q.to(device).requires_grad_(True)
+    ref_v = ref_v.to(device).requires_grad_(True)
+    gates = None if gates is None else gates.to(device)
+    mask = None if mask is None else mask.to(device)
+    res = m(q, ref_v, gates, 8, loss_mask=mask)
+    loss = (res["output"] ** 2).sum()
+    assert (res["addr_loss"] is None) == ("addr_loss" not in d)
+    if res["addr_loss"] is not None:
+        loss = loss + res["addr_loss"]
+        ref_addr = float(d["addr_loss"])
+        assert abs(res["addr_loss"].item() - ref_addr) <= tol * abs(ref_addr) + 1e-7
+    loss.backward()
+    np.testing.assert_array_equal(res["indices"].cpu().numpy(), d["indices"])
+    assert (m.keys.grad is None) == ("keys_grad" not in d)
+    pairs = [(res["output"], "output"), (res["losses"], "losses"), (m.keys, "final_keys"),
+             (m.values, "final_values"), (q.grad, "q_grad"), (ref_v.grad, "ref_v_grad"),
+             (m.values.grad, "values_grad")]
+    if m.keys.grad is not None:
+        pairs.append((m.keys.grad, "keys_grad"))
+    for got, key in pairs:
+        assert rel_err(got.detach().float().cpu().numpy(), d[key]) < tol, key

@@ -218,6 +218,59 @@ def gen_fwpkm(fw, name, score_type, seed=0):
     print("wrote", name)
 
 
+def gen_fwpkm_variant(fw, gw, name):
+    """The reference's first-order bag backward (``bw_kernel`` of
+    ``fwpkm/xformer_embeddingbag_grad_wrapper.py:128``) is a Triton kernel on
+    CUDA (``fwpkm/xformer_embeddingbag_legacy.py:177-220``): its score-weight
+    gradient carries no autograd graph.  Its CPU stand-in
+    (``_embedding_bag_bw_native``, ``:147-167``) computes that gradient in
+    torch ops, which under a ``create_graph`` backward do build a graph, so
+    with ``mem_grad_to_values_only=False`` a CPU run gains second-order terms
+    the CUDA path does not have.  These fixtures run the stand-in under
+    ``no_grad`` to follow the CUDA path, as that function's own docstring
+    says it runs."""
+    kw, with_gates, with_mask = cases.FW_VARIANTS[name]
+    orig_bw = gw.embedding_bag_bw_rev_indices
+    gw.embedding_bag_bw_rev_indices = torch.no_grad()(orig_bw)
+    try:
+        _gen_fwpkm_variant(fw, name, kw, with_gates, with_mask)
+    finally:
+        gw.embedding_bag_bw_rev_indices = orig_bw
+
+
+def _gen_fwpkm_variant(fw, name, kw, with_gates, with_mask):
+    torch.manual_seed(0)
+    m = fw.FastWeightProductKeyMemory(**dict(FW_KW, **kw)).train()
+    keys, values, q, ref_v = cases.fwpkm_case(2)
+    gates, mask = cases.fw_variant_inputs(q.shape[0], q.shape[1], with_gates, with_mask)
+    with torch.no_grad():
+        m.keys.copy_(keys)
+        m.values.copy_(values)
+    q = q.clone().requires_grad_(True)
+    ref_v = ref_v.clone().requires_grad_(True)
+    res = m(q, ref_v, gates, 8, loss_mask=mask)
+    loss = (res["output"] ** 2).sum()
+    if res["addr_loss"] is not None:
+        loss = loss + res["addr_loss"]
+    loss.backward()
+    out = {
+        "output": _np(res["output"]),
+        "indices": res["indices"].numpy(),
+        "losses": _np(res["losses"]),
+        "final_keys": _np(m.keys),
+        "final_values": _np(m.values),
+        "q_grad": _np(q.grad),
+        "ref_v_grad": _np(ref_v.grad),
+        "values_grad": _np(m.values.grad),
+    }
+    if m.keys.grad is not None:
+        out["keys_grad"] = _np(m.keys.grad)
+    if res["addr_loss"] is not None:
+        out["addr_loss"] = np.array(res["addr_loss"].item())
+    np.savez_compressed(os.path.join(HERE, name), **out)
+    print("wrote", name)
+
+
 def gen_fwpkm_stream(fw, name, score_type, seed=1):
     """``forward_w_past`` (``fwpkm/fwpkm.py:560-820``) over three successive
     calls that carry the signal queue: the first only queues, the second
@@ -414,6 +467,8 @@ def main():
     gen_c2_full(mem, "c2_full_bf16.npz")
     gen_fwpkm_c4(fw, "fwpkm_c4_dot.npz", "dot_product")
     gen_fwpkm_c4(fw, "fwpkm_c4_idw.npz", "idw")
+    for vname in cases.FW_VARIANTS:
+        gen_fwpkm_variant(fw, gw, vname)
 
 
 if __name__ == "__main__":
@@ -423,6 +478,10 @@ if __name__ == "__main__":
                 gen_addr_stats("addr_stats.npz")
             elif arg == "c2_full":
                 gen_c2_full(_import_ref()[0], "c2_full_bf16.npz")
+            elif arg == "fwpkm_var":
+                ref = _import_ref()
+                for vname in cases.FW_VARIANTS:
+                    gen_fwpkm_variant(ref[2], ref[3], vname)
             elif arg == "fwpkm_c4":
                 fw = _import_ref()[2]
                 gen_fwpkm_c4(fw, "fwpkm_c4_dot.npz", "dot_product")

@@ -55,6 +55,18 @@ def test_forward_wo_past_matches_reference(score_type, fname):
     assert rel_err(m.values.grad.cpu().numpy(), d["values_grad"]) < tol
 
 
+@pytest.mark.parametrize("fname", sorted(cases.FW_VARIANTS))
+def test_variant_matches_reference(fname):
+    """Non-default options (silu / relu transforms, temperature, keys trained
+    by the memorisation loss, clipping, weight decay, no look-ahead, no
+    addressing loss, gates, loss mask) through the kernels against the
+    reference's run, to 1e-5 of each tensor's largest magnitude."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
+    cases.run_fw_variant(FastWeightProductKeyMemory, FW_KW, fname, np.load(os.path.join(GOLD, fname)), rel_err,
+                         tol=1e-5, device=DEV)
+
+
 def test_double_backward_wrapper_gradgradcheck():
     """EmbeddingBagBW (K5) against autograd's numerical second derivatives of
     the bag in float64-accumulated fp32 (small shapes)."""

@@ -71,6 +71,15 @@ def test_fwpkm_streaming_matches_reference(cpu_kernels, score_type, fname):
     cases.run_stream(m, q, ref_v, d, rel_err)
 
 
+@pytest.mark.parametrize("fname", sorted(cases.FW_VARIANTS))
+def test_fwpkm_variant_matches_reference(cpu_kernels, fname):
+    """Non-default options (silu / relu transforms, temperature, keys trained
+    by the memorisation loss, clipping, weight decay, no look-ahead, no
+    addressing loss, gates, loss mask) against the reference's run."""
+    from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
+    cases.run_fw_variant(FastWeightProductKeyMemory, FW_KW, fname, np.load(os.path.join(GOLD, fname)), rel_err)
+
+
 def test_fwpkm_without_addressing_loss_keeps_keys(cpu_kernels):
     from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
     m = FastWeightProductKeyMemory(addr_loss=None, **FW_KW).train()
