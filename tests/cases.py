@@ -99,16 +99,23 @@ def fwpkm_case(seed: int = 0, B=2, T=16, heads=2, k_dim=16, v_dim=32, n_sub=16, 
 # Non-default module options, each fixture a combination the defaults
 # leave untested: the transform (silu / relu, temperature), the keys trained
 # by the memorisation loss too, gradient clipping, weight decay, no
-# look-ahead, no addressing loss, per-token gates and a loss mask.
+# look-ahead, no addressing loss, per-token gates and a loss mask.  Each
+# entry: module options, with gates, with a loss mask, and the dtype of the
+# module and its inputs ("bf16": the model's setting, bf16 parameters with
+# the fast weights in fp32 copies, ``fp32_fw``).
 FW_VARIANTS = {
     "fwpkm_var_silu.npz": (dict(qk_score_type="idw", score_nonlinear="silu", score_temperature=0.5,
                                 mem_grad_to_values_only=False, grad_clip=True, weight_decay=0.01),
-                           True, True),
+                           True, True, "f32"),
     "fwpkm_var_relu.npz": (dict(qk_score_type="dot_product", score_nonlinear="relu", lookahead=0, addr_loss=None,
                                 mem_grad_to_values_only=False),
-                           False, True),
-    "fwpkm_var_keys.npz": (dict(qk_score_type="dot_product", mem_grad_to_values_only=False), False, False),
+                           False, True, "f32"),
+    "fwpkm_var_keys.npz": (dict(qk_score_type="dot_product", mem_grad_to_values_only=False), False, False, "f32"),
+    "fwpkm_var_bf16.npz": (dict(qk_score_type="dot_product", addr_loss_weight=0.5), True, False, "bf16"),
 }
+# normwise tolerance by variant dtype: fp32, and one bf16 rounding of
+# results computed in fp32 on both sides
+FW_VARIANT_TOL = {"f32": 1e-5, "bf16": 1e-2}
 
 
 def fw_variant_inputs(B, T, with_gates, with_mask, seed=5):
@@ -259,14 +266,16 @@ def run_stream(m, q, ref_v, d, rel_err, tol=1e-5):
 
 def run_fw_variant(cls, fw_kw, name, d, rel_err, tol=1e-5, device="cpu"):
     """One training call of a ``FW_VARIANTS`` module on ``fwpkm_case(2)``
-    (gates and loss mask as the variant asks), loss = sum(output^2) plus the
+    (gates, loss mask and dtype as the variant asks), loss = sum(output^2) plus the
     addressing loss when there is one, checked against the fixture ``d``:
     indices exactly, outputs, losses, updated fast weights and every
     gradient to ``tol``."""
-    kw, with_gates, with_mask = FW_VARIANTS[name]
-    m = cls(**dict(fw_kw, **kw)).to(device).train()
-    keys, values, q, ref_v = fwpkm_case(2)
-    gates, mask = fw_variant_inputs(q.shape[0], q.shape[1], with_gates, with_mask)
+    kw, with_gates, with_mask, dt = FW_VARIANTS[name]
+    dt = torch.bfloat16 if dt == "bf16" else torch.float32
+    m = cls(**dict(fw_kw, **kw)).to(device=device, dtype=dt).train()
+    keys, values, q, ref_v = (t.to(dt) for t in fwpkm_case(2))
+    gates, mask = (None if t is None else t.to(dt)
+                   for t in fw_variant_inputs(q.shape[0], q.shape[1], with_gates, with_mask))
     with torch.no_grad():
         m.keys.copy_(keys)
         m.values.copy_(values)

@@ -229,20 +229,21 @@ def gen_fwpkm_variant(fw, gw, name):
     the CUDA path does not have.  These fixtures run the stand-in under
     ``no_grad`` to follow the CUDA path, as that function's own docstring
     says it runs."""
-    kw, with_gates, with_mask = cases.FW_VARIANTS[name]
+    kw, with_gates, with_mask, dt = cases.FW_VARIANTS[name]
     orig_bw = gw.embedding_bag_bw_rev_indices
     gw.embedding_bag_bw_rev_indices = torch.no_grad()(orig_bw)
     try:
-        _gen_fwpkm_variant(fw, name, kw, with_gates, with_mask)
+        _gen_fwpkm_variant(fw, name, kw, with_gates, with_mask, torch.bfloat16 if dt == "bf16" else torch.float32)
     finally:
         gw.embedding_bag_bw_rev_indices = orig_bw
 
 
-def _gen_fwpkm_variant(fw, name, kw, with_gates, with_mask):
+def _gen_fwpkm_variant(fw, name, kw, with_gates, with_mask, dt):
     torch.manual_seed(0)
-    m = fw.FastWeightProductKeyMemory(**dict(FW_KW, **kw)).train()
-    keys, values, q, ref_v = cases.fwpkm_case(2)
-    gates, mask = cases.fw_variant_inputs(q.shape[0], q.shape[1], with_gates, with_mask)
+    m = fw.FastWeightProductKeyMemory(**dict(FW_KW, **kw)).to(dt).train()
+    keys, values, q, ref_v = (t.to(dt) for t in cases.fwpkm_case(2))
+    gates, mask = (None if t is None else t.to(dt)
+                   for t in cases.fw_variant_inputs(q.shape[0], q.shape[1], with_gates, with_mask))
     with torch.no_grad():
         m.keys.copy_(keys)
         m.values.copy_(values)

@@ -75,9 +75,11 @@ def test_fwpkm_streaming_matches_reference(cpu_kernels, score_type, fname):
 def test_fwpkm_variant_matches_reference(cpu_kernels, fname):
     """Non-default options (silu / relu transforms, temperature, keys trained
     by the memorisation loss, clipping, weight decay, no look-ahead, no
-    addressing loss, gates, loss mask) against the reference's run."""
+    addressing loss, gates, loss mask, a bf16 module) against the
+    reference's run."""
     from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
-    cases.run_fw_variant(FastWeightProductKeyMemory, FW_KW, fname, np.load(os.path.join(GOLD, fname)), rel_err)
+    cases.run_fw_variant(FastWeightProductKeyMemory, FW_KW, fname, np.load(os.path.join(GOLD, fname)), rel_err,
+                         tol=cases.FW_VARIANT_TOL[cases.FW_VARIANTS[fname][3]])
 
 
 def test_fwpkm_without_addressing_loss_keeps_keys(cpu_kernels):
