@@ -64,6 +64,62 @@ def pkm_state(cfg: dict, seed: int = 0) -> dict:
     return st
 
 
+# ``HashingMemory`` option sets beyond the benchmark configs, on a small
+# geometry: the gate, no query bias, no query norm, the value projection
+# without the SwiLU branch, no projection at all, three heads, eval mode
+# (``last_indices`` / ``last_scores``).  Each entry: options, training mode.
+PKM_VARIANT_BASE = dict(input_dim=64, output_dim=64, mem_k_dim=32, mem_v_dim=-1, mem_heads=2, mem_knn=4,
+                        mem_n_keys=16)
+PKM_VARIANTS = {
+    "pkm_var_gated.npz": (dict(mem_gated=True, mem_v_dim=48, mem_query_bias=False), True),
+    "pkm_var_plain.npz": (dict(swilu_projection=False, mem_query_rmsnorm=False, mem_gated=True, mem_heads=3,
+                               mem_knn=8), True),
+    "pkm_var_vproj.npz": (dict(swilu_projection=False, mem_v_dim=48), True),
+    "pkm_var_eval.npz": (dict(), False),
+}
+
+
+def pkm_variant_state(shapes: dict, seed: int = 0) -> dict:
+    """Parameters for a ``PKM_VARIANTS`` module from its state-dict names and
+    shapes, filled in sorted-name order from one seeded generator: keys
+    U(+-1/sqrt(2·cols)), weight matrices N(0, cols^-1/2), biases
+    U(+-1/sqrt(64)), the RMS-norm scale 1 + N(0, 0.1)."""
+    g = torch.Generator().manual_seed(50_000 + seed)
+    st = {}
+    for name in sorted(shapes):
+        shape = tuple(shapes[name])
+        if name == "keys":
+            st[name] = _u(g, shape, 1 / math.sqrt(2 * shape[1]))
+        elif name.endswith("norm.weight"):
+            st[name] = 1 + _n(g, shape, 0.1)
+        elif len(shape) == 2:
+            st[name] = _n(g, shape, shape[1] ** -0.5)
+        else:
+            st[name] = _u(g, shape, 0.125)
+    return st
+
+
+def run_pkm_variant(module, name, seed=0, device="cpu"):
+    """Load ``pkm_variant_state`` into ``module`` (built with the variant's
+    options), run one forward + backward of loss = sum(out^2) on a seeded
+    [2, 8, input_dim] input and return every output: out, indices, the input
+    gradient, each parameter's gradient (``g_<name>``) and, in eval mode,
+    ``last_indices`` / ``last_scores``."""
+    kw, train = PKM_VARIANTS[name]
+    module.load_state_dict(pkm_variant_state({k: v.shape for k, v in module.state_dict().items()}, seed))
+    module = module.to(device).train(train)
+    g = torch.Generator().manual_seed(60_000 + seed)
+    x = torch.randn((2, 8, module.input_dim), generator=g).to(device).requires_grad_(True)
+    y, idx = module(x)
+    (y ** 2).sum().backward()
+    out = {"out": y, "indices": idx, "x_grad": x.grad}
+    out.update({"g_" + k: p.grad for k, p in module.named_parameters() if p.grad is not None})
+    if not train:
+        out["last_indices"] = module.last_indices
+        out["last_scores"] = module.last_scores
+    return out
+
+
 def pkm_input(shape, seed: int = 0) -> torch.Tensor:
     g = torch.Generator().manual_seed(10_000 + seed)
     return torch.randn(shape, generator=g, dtype=torch.float32)
@@ -300,3 +356,16 @@ def run_fw_variant(cls, fw_kw, name, d, rel_err, tol=1e-5, device="cpu"):
         pairs.append((m.keys.grad, "keys_grad"))
     for got, key in pairs:
         assert rel_err(got.detach().float().cpu().numpy(), d[key]) < tol, key
+
+
+def check_pkm_variant(res, d, rel_err, tol=1e-5):
+    """``run_pkm_variant`` results against the reference's fixture ``d``:
+    the same set of outputs and gradients, indices exactly, the rest to
+    ``tol`` of each tensor's largest magnitude."""
+    assert sorted(res) == sorted(d), (sorted(res), sorted(d))
+    for key, got in res.items():
+        got = got.detach().cpu()
+        if got.dtype == torch.long:
+            np.testing.assert_array_equal(got.numpy(), d[key], err_msg=key)
+        else:
+            assert rel_err(got.float().numpy(), d[key]) < tol, key

@@ -95,6 +95,16 @@ def gen_pkm(mem, cfg, name, batch_shape, dtype, seed=0):
     print("wrote", name)
 
 
+def gen_pkm_variant(mem, name):
+    kw, _ = cases.PKM_VARIANTS[name]
+    torch.manual_seed(0)
+    m = mem.HashingMemory(**dict(cases.PKM_VARIANT_BASE, **kw))
+    res = cases.run_pkm_variant(m, name)
+    np.savez_compressed(os.path.join(HERE, name),
+                        **{k: (v.numpy() if v.dtype == torch.long else _np(v)) for k, v in res.items()})
+    print("wrote", name)
+
+
 def gen_indices_seeds(mem, name, seeds=(1, 2)):
     cfg = cases.CONFIG0
     out = {}
@@ -470,6 +480,8 @@ def main():
     gen_fwpkm_c4(fw, "fwpkm_c4_idw.npz", "idw")
     for vname in cases.FW_VARIANTS:
         gen_fwpkm_variant(fw, gw, vname)
+    for vname in cases.PKM_VARIANTS:
+        gen_pkm_variant(mem, vname)
 
 
 if __name__ == "__main__":
@@ -479,6 +491,10 @@ if __name__ == "__main__":
                 gen_addr_stats("addr_stats.npz")
             elif arg == "c2_full":
                 gen_c2_full(_import_ref()[0], "c2_full_bf16.npz")
+            elif arg == "pkm_var":
+                mem = _import_ref()[0]
+                for vname in cases.PKM_VARIANTS:
+                    gen_pkm_variant(mem, vname)
             elif arg == "fwpkm_var":
                 ref = _import_ref()
                 for vname in cases.FW_VARIANTS:

@@ -95,6 +95,17 @@ def test_fwpkm_without_addressing_loss_keeps_keys(cpu_kernels):
     assert not torch.equal(m.values.detach(), values)
 
 
+@pytest.mark.parametrize("fname", sorted(cases.PKM_VARIANTS))
+def test_hashing_memory_variant_matches_reference(cpu_kernels, fname):
+    """``HashingMemory`` options beyond the benchmark configs (gate, no query
+    bias, no query norm, value projection without SwiLU, no projection,
+    three heads, eval mode) against the reference's run."""
+    from modelos_b200.pkm.memory import HashingMemory
+    kw, _ = cases.PKM_VARIANTS[fname]
+    m = HashingMemory(**dict(cases.PKM_VARIANT_BASE, **kw))
+    cases.check_pkm_variant(cases.run_pkm_variant(m, fname), np.load(os.path.join(GOLD, fname)), rel_err)
+
+
 def test_hashing_memory_config0_matches_reference(cpu_kernels):
     from modelos_b200.pkm.memory import HashingMemory
     c0 = np.load(os.path.join(GOLD, "c0_pkm.npz"))

@@ -160,6 +160,21 @@ def test_config2_geometry_bf16_matches_reference():
         assert rel_err(yo, d["out"].reshape(64, -1)[same]) < 2e-2
 
 
+@pytest.mark.parametrize("fname", sorted(cases.PKM_VARIANTS))
+def test_variant_matches_reference(fname):
+    """Options beyond the benchmark configs (gate, no query bias, no query
+    norm, value projection without SwiLU, no projection, three heads, eval
+    mode's ``last_indices`` / ``last_scores``) in fp32 through the kernels
+    against the reference's run: indices exactly, outputs and every gradient
+    to 1e-5 of each tensor's largest magnitude."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    from modelos_b200.pkm.memory import HashingMemory
+    kw, _ = cases.PKM_VARIANTS[fname]
+    m = HashingMemory(**dict(cases.PKM_VARIANT_BASE, **kw))
+    res = cases.run_pkm_variant(m, fname, device=DEV)
+    cases.check_pkm_variant(res, np.load(os.path.join(GOLD, fname)), rel_err)
+
+
 def test_eval_mode_usage_statistics():
     m = build(cases.CONFIG0, 0, torch.float32).eval()
     x = cases.pkm_input((1, 8, 512), 0).to(DEV)
