@@ -230,7 +230,7 @@ def gen_fwpkm(fw, name, score_type, seed=0):
 
 def gen_fwpkm_variant(fw, gw, name):
     """The reference's first-order bag backward (``bw_kernel`` of
-    ``fwpkm/xformer_embeddingbag_grad_wrapper.py:128``) is a Triton kernel on
+    ``fwpkm/xformer_embeddingbag_grad_wrapper.py:131``) is a Triton kernel on
     CUDA (``fwpkm/xformer_embeddingbag_legacy.py:177-220``): its score-weight
     gradient carries no autograd graph.  Its CPU stand-in
     (``_embedding_bag_bw_native``, ``:147-167``) computes that gradient in
