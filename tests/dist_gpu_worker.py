@@ -185,10 +185,12 @@ def run_owner(rank: int, world: int, port: int, out_dir: str, dtype_name: str):
         dist.destroy_process_group()
 
 
-def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str, backend: str = "nccl", sharded: bool = False):
+def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str, backend: str = "nccl", sharded: bool = False,
+                 variant: bool = False):
     """One rank of the data-parallel fast-weight memory on the GPU kernels
     (fp32, tiny geometry): half of the batch, fast weights replicated or the
-    value table split by rows."""
+    value table split by rows; ``variant`` adds ``FW_VARIANT_KW`` (keys
+    trained by the memorisation loss, weight decay, clipping)."""
     import datetime
 
     import torch
@@ -206,18 +208,19 @@ def run_fwpkm_dp(rank: int, world: int, port: int, out_dir: str, backend: str = 
         keys, values, q, ref_v = dist_worker.fwpkm_dp_case()
         per = q.shape[0] // world
         sl = slice(rank * per, (rank + 1) * per)
-        out = fwpkm_gpu_run(q[sl], ref_v[sl], keys, values, dev, dist.group.WORLD, sharded=sharded)
+        out = fwpkm_gpu_run(q[sl], ref_v[sl], keys, values, dev, dist.group.WORLD, sharded=sharded,
+                            extra_kw=dist_worker.FW_VARIANT_KW if variant else None)
         torch.save(out, os.path.join(out_dir, f"{'fwsh' if sharded else 'fwdp'}{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
-def fwpkm_gpu_run(q, ref_v, keys, values, dev, group=None, sharded=False):
+def fwpkm_gpu_run(q, ref_v, keys, values, dev, group=None, sharded=False, extra_kw=None):
     import torch
 
     import dist_worker
     from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
-    m = FastWeightProductKeyMemory(**dist_worker.FW_DP_KW).to(dev).train()
+    m = FastWeightProductKeyMemory(**dict(dist_worker.FW_DP_KW, **(extra_kw or {}))).to(dev).train()
     with torch.no_grad():
         m.keys.copy_(keys)
         m.values.copy_(values)

@@ -183,15 +183,18 @@ def test_row_owner_sgd(tmp_path, dtype_name, world):
             assert ((got - ref).abs().max() / ref.abs().max()).item() < tol
 
 
-@pytest.mark.parametrize("sharded", [False, True], ids=["replicated", "row_sharded"])
+@pytest.mark.parametrize("sharded,variant", [(False, False), (True, False), (True, True)],
+                         ids=["replicated", "row_sharded", "row_sharded_variant"])
 @pytest.mark.parametrize("backend,world", [("gloo", 2), ("nccl", 2)])
-def test_fwpkm_data_parallel_equals_one_gpu(tmp_path, backend, world, sharded):
+def test_fwpkm_data_parallel_equals_one_gpu(tmp_path, backend, world, sharded, variant):
     """The fast-weight memory with its batch split over ranks on the GPU
     kernels equals one GPU running the whole batch: outputs, indices, final
     fast weights and outer gradients (fp32, 1e-5), with the value table
     replicated (``data_parallel``) or split by rows (``row_sharded``: the
     route, segment-sum and ragged-backward kernels, the owners' double
-    backward).  gloo: the ranks share GPU 0; nccl: one GPU per rank."""
+    backward; ``variant``: keys trained by the memorisation loss, weight
+    decay and clipping as well).  gloo: the ranks share GPU 0; nccl: one GPU
+    per rank."""
     if backend == "nccl" and torch.cuda.device_count() < world:
         pytest.skip("needs two GPUs")
     import numpy as np
@@ -203,7 +206,7 @@ def test_fwpkm_data_parallel_equals_one_gpu(tmp_path, backend, world, sharded):
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=dist_gpu_worker.run_fwpkm_dp,
-                         args=(r, world, port, str(tmp_path), backend, sharded))
+                         args=(r, world, port, str(tmp_path), backend, sharded, variant))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -215,7 +218,8 @@ def test_fwpkm_data_parallel_equals_one_gpu(tmp_path, backend, world, sharded):
             p.join()
     assert [p.exitcode for p in procs] == [0] * world
     keys, values, q, ref_v = dist_worker.fwpkm_dp_case()
-    full = dist_gpu_worker.fwpkm_gpu_run(q, ref_v, keys, values, torch.device("cuda", 0))
+    full = dist_gpu_worker.fwpkm_gpu_run(q, ref_v, keys, values, torch.device("cuda", 0),
+                                         extra_kw=dist_worker.FW_VARIANT_KW if variant else None)
 
     def rel(a, b):
         a, b = np.asarray(a, dtype=np.float64), np.asarray(b, dtype=np.float64)
