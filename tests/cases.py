@@ -296,28 +296,63 @@ def addr_case(name: str, seed: int = 0):
 STREAM_CALLS = ((0, 4), (4, 13), (13, 16))
 
 
-def run_stream(m, q, ref_v, d, rel_err, tol=1e-5):
+# Streaming fixtures: module options, with gates, with a loss mask.  The
+# variant carries gates and a mask through the queues, with a look-ahead of
+# 2, the silu transform and the clipped, decayed update.
+STREAM_FIXTURES = {
+    "fwpkm_stream_dot.npz": (dict(qk_score_type="dot_product"), False, False),
+    "fwpkm_stream_idw.npz": (dict(qk_score_type="idw"), False, False),
+    "fwpkm_stream_var.npz": (dict(qk_score_type="dot_product", score_nonlinear="silu", score_temperature=0.5,
+                                  lookahead=2, grad_clip=True, weight_decay=0.01), True, True),
+}
+
+
+def stream_calls(m, q, ref_v, gates=None, mask=None):
     """Drive ``m`` through ``STREAM_CALLS`` under ``no_grad`` (as generation
-    does) and compare every call with the fixture ``d``."""
+    does), with token ids and the calls' slices of ``gates`` / ``mask``;
+    yields ``(call, result, past_key_values)``."""
     B, T = q.shape[:2]
     ids = torch.arange(B * T, device=q.device).view(B, T)
     past = (None,) * 6
     with torch.no_grad():
         for c, (t0, t1) in enumerate(STREAM_CALLS):
-            res = m(q[:, t0:t1], ref_v[:, t0:t1], None, 8, past_key_values=past, token_ids=ids[:, t0:t1])
+            res = m(q[:, t0:t1], ref_v[:, t0:t1], None if gates is None else gates[:, t0:t1], 8,
+                    loss_mask=None if mask is None else mask[:, t0:t1], past_key_values=past,
+                    token_ids=ids[:, t0:t1])
             past = res["past_key_values"]
-            np.testing.assert_array_equal(res["indices"].cpu().numpy(), d[f"c{c}_indices"])
-            assert (res["losses"] is not None) == bool(d[f"c{c}_updated"]), c
-            pairs = [(res["output"], "output"), (res["scores"], "scores"), (past[0], "past_q"),
-                     (past[1], "past_hyp"), (past[2], "past_ref"), (m.keys, "keys"), (m.values, "values")]
-            if res["losses"] is not None:
-                pairs.append((res["losses"], "losses"))
-                got_addr = res["addr_loss"].item()
-                ref_addr = float(d[f"c{c}_addr_loss"])
-                assert abs(got_addr - ref_addr) <= tol * abs(ref_addr) + 1e-7, c
-            for got, key in pairs:
-                assert rel_err(got.detach().float().cpu().numpy(), d[f"c{c}_{key}"]) < tol, (c, key)
-            np.testing.assert_array_equal(past[5].cpu().numpy(), d[f"c{c}_past_ids"])
+            yield c, res, past
+
+
+def stream_inputs(name, seed=1, device="cpu"):
+    """``(q, ref_v, gates, mask)`` of a ``STREAM_FIXTURES`` entry; keys and
+    values are ``fwpkm_case(seed)``'s."""
+    _, with_gates, with_mask = STREAM_FIXTURES[name]
+    _, _, q, ref_v = fwpkm_case(seed)
+    gates, mask = fw_variant_inputs(q.shape[0], q.shape[1], with_gates, with_mask)
+    return tuple(None if t is None else t.to(device) for t in (q, ref_v, gates, mask))
+
+
+def run_stream(m, q, ref_v, d, rel_err, tol=1e-5, gates=None, mask=None):
+    """``stream_calls`` compared call by call with the fixture ``d``:
+    indices and queued ids exactly; outputs, scores, queues, losses and the
+    fast weights after every call to ``tol``."""
+    for c, res, past in stream_calls(m, q, ref_v, gates, mask):
+        np.testing.assert_array_equal(res["indices"].cpu().numpy(), d[f"c{c}_indices"])
+        assert (res["losses"] is not None) == bool(d[f"c{c}_updated"]), c
+        pairs = [(res["output"], "output"), (res["scores"], "scores"), (past[0], "past_q"),
+                 (past[1], "past_hyp"), (past[2], "past_ref"), (m.keys, "keys"), (m.values, "values")]
+        for t, key in ((past[3], "past_gates"), (past[4], "past_mask")):
+            assert (t is None) == (f"c{c}_{key}" not in d), (c, key)
+            if t is not None:
+                pairs.append((t, key))
+        if res["losses"] is not None:
+            pairs.append((res["losses"], "losses"))
+            got_addr = res["addr_loss"].item()
+            ref_addr = float(d[f"c{c}_addr_loss"])
+            assert abs(got_addr - ref_addr) <= tol * abs(ref_addr) + 1e-7, c
+        for got, key in pairs:
+            assert rel_err(got.detach().float().cpu().numpy(), d[f"c{c}_{key}"]) < tol, (c, key)
+        np.testing.assert_array_equal(past[5].cpu().numpy(), d[f"c{c}_past_ids"])
 
 
 def run_fw_variant(cls, fw_kw, name, d, rel_err, tol=1e-5, device="cpu"):

@@ -282,39 +282,37 @@ def _gen_fwpkm_variant(fw, name, kw, with_gates, with_mask, dt):
     print("wrote", name)
 
 
-def gen_fwpkm_stream(fw, name, score_type, seed=1):
+def gen_fwpkm_stream(fw, name, seed=1):
     """``forward_w_past`` (``fwpkm/fwpkm.py:560-820``) over three successive
     calls that carry the signal queue: the first only queues, the second
-    updates once and queues the rest, the third updates again.  Run under ``no_grad`` as in
-    generation, with token ids (the reference's queue pop indexes them when
-    ``lookahead > 0``)."""
+    updates once and queues the rest, the third updates again.  Run under
+    ``no_grad`` as in generation, with token ids (the reference's queue pop
+    indexes them when ``lookahead > 0``), and with the gates and loss mask
+    the fixture's entry in ``cases.STREAM_FIXTURES`` asks for."""
+    kw, _, _ = cases.STREAM_FIXTURES[name]
     torch.manual_seed(0)
-    m = fw.FastWeightProductKeyMemory(qk_score_type=score_type, **FW_KW).train()
-    keys, values, q, ref_v = cases.fwpkm_case(seed)
+    m = fw.FastWeightProductKeyMemory(**dict(FW_KW, **kw)).train()
+    keys, values, _, _ = cases.fwpkm_case(seed)
+    q, ref_v, gates, mask = cases.stream_inputs(name, seed)
     with torch.no_grad():
         m.keys.copy_(keys)
         m.values.copy_(values)
-    B, T = q.shape[:2]
-    ids = torch.arange(B * T).view(B, T)
-    past = (None,) * 6
     out = {}
-    with torch.no_grad():
-        for c, (t0, t1) in enumerate(cases.STREAM_CALLS):
-            res = m(q[:, t0:t1], ref_v[:, t0:t1], None, 8, past_key_values=past, token_ids=ids[:, t0:t1])
-            past = res["past_key_values"]
-            out[f"c{c}_output"] = _np(res["output"])
-            out[f"c{c}_indices"] = res["indices"].numpy()
-            out[f"c{c}_scores"] = _np(res["scores"])
-            out[f"c{c}_updated"] = np.array(res["losses"] is not None)
-            if res["losses"] is not None:
-                out[f"c{c}_losses"] = _np(res["losses"])
-                out[f"c{c}_addr_loss"] = np.array(res["addr_loss"].item())
-            for k, t in zip(("q", "hyp", "ref"), past[:3]):
+    for c, res, past in cases.stream_calls(m, q, ref_v, gates, mask):
+        out[f"c{c}_output"] = _np(res["output"])
+        out[f"c{c}_indices"] = res["indices"].numpy()
+        out[f"c{c}_scores"] = _np(res["scores"])
+        out[f"c{c}_updated"] = np.array(res["losses"] is not None)
+        if res["losses"] is not None:
+            out[f"c{c}_losses"] = _np(res["losses"])
+            out[f"c{c}_addr_loss"] = np.array(res["addr_loss"].item())
+        for k, t in zip(("q", "hyp", "ref", "gates", "mask"), past[:5]):
+            if t is not None:
                 out[f"c{c}_past_{k}"] = _np(t)
-            out[f"c{c}_past_ids"] = past[5].numpy()
-            # copies: the module updates its parameters in place
-            out[f"c{c}_keys"] = _np(m.keys).copy()
-            out[f"c{c}_values"] = _np(m.values).copy()
+        out[f"c{c}_past_ids"] = past[5].numpy()
+        # copies: the module updates its parameters in place
+        out[f"c{c}_keys"] = _np(m.keys).copy()
+        out[f"c{c}_values"] = _np(m.values).copy()
     np.savez_compressed(os.path.join(HERE, name), **out)
     print("wrote", name)
 
@@ -473,8 +471,8 @@ def main():
     c2.update(mem_n_keys=64)  # same layer, smaller table so the fixture stays small
     gen_pkm(mem, c2, "c2_small_bf16.npz", (2, 32, 1024), torch.bfloat16)
     gen_addr_stats("addr_stats.npz")
-    gen_fwpkm_stream(fw, "fwpkm_stream_dot.npz", "dot_product")
-    gen_fwpkm_stream(fw, "fwpkm_stream_idw.npz", "idw")
+    for sname in cases.STREAM_FIXTURES:
+        gen_fwpkm_stream(fw, sname)
     gen_c2_full(mem, "c2_full_bf16.npz")
     gen_fwpkm_c4(fw, "fwpkm_c4_dot.npz", "dot_product")
     gen_fwpkm_c4(fw, "fwpkm_c4_idw.npz", "idw")
@@ -505,8 +503,8 @@ if __name__ == "__main__":
                 gen_fwpkm_c4(fw, "fwpkm_c4_idw.npz", "idw")
             elif arg == "fwpkm_stream":
                 fw = _import_ref()[2]
-                gen_fwpkm_stream(fw, "fwpkm_stream_dot.npz", "dot_product")
-                gen_fwpkm_stream(fw, "fwpkm_stream_idw.npz", "idw")
+                for sname in cases.STREAM_FIXTURES:
+                    gen_fwpkm_stream(fw, sname)
             else:
                 raise SystemExit(f"unknown fixture {arg}")
     else:

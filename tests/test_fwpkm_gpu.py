@@ -89,21 +89,22 @@ def test_double_backward_wrapper_gradgradcheck():
     assert rel_err(d_a.cpu().numpy(), ref_a.cpu().numpy()) < 1e-6
 
 
-@pytest.mark.parametrize("score_type,fname", [("dot_product", "fwpkm_stream_dot.npz"),
-                                              ("idw", "fwpkm_stream_idw.npz")])
-def test_forward_w_past_matches_reference(score_type, fname):
+@pytest.mark.parametrize("fname", sorted(cases.STREAM_FIXTURES))
+def test_forward_w_past_matches_reference(fname):
     """``forward_w_past`` (``fwpkm/fwpkm.py:560-820``) over three calls that
-    carry the signal queue (queue only; update then queue; update): outputs,
-    indices, losses, queues and fast weights after every call."""
+    carry the signal queue (queue only; update then queue; update; the
+    variant queues gates and a loss mask too): outputs, indices, losses,
+    queues and fast weights after every call."""
     torch.backends.cuda.matmul.allow_tf32 = False
     from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
     d = np.load(os.path.join(GOLD, fname))
-    m = FastWeightProductKeyMemory(qk_score_type=score_type, **FW_KW).to(DEV).train()
-    keys, values, q, ref_v = cases.fwpkm_case(1)
+    m = FastWeightProductKeyMemory(**dict(FW_KW, **cases.STREAM_FIXTURES[fname][0])).to(DEV).train()
+    keys, values, _, _ = cases.fwpkm_case(1)
+    q, ref_v, gates, mask = cases.stream_inputs(fname, device=DEV)
     with torch.no_grad():
         m.keys.copy_(keys)
         m.values.copy_(values)
-    cases.run_stream(m, q.to(DEV), ref_v.to(DEV), d, rel_err)
+    cases.run_stream(m, q, ref_v, d, rel_err, gates=gates, mask=mask)
 
 
 def test_forward_w_past_streaming_runs_and_updates():

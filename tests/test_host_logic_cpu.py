@@ -56,19 +56,20 @@ def test_fwpkm_chunk_loop_matches_reference(cpu_kernels, score_type, fname):
         assert rel_err(got.detach().numpy(), d[key]) < 1e-5, key
 
 
-@pytest.mark.parametrize("score_type,fname", [("dot_product", "fwpkm_stream_dot.npz"),
-                                              ("idw", "fwpkm_stream_idw.npz")])
-def test_fwpkm_streaming_matches_reference(cpu_kernels, score_type, fname):
-    """``forward_w_past`` over three calls carrying the signal queue: outputs,
-    losses, queues and fast weights after every call equal the reference's."""
+@pytest.mark.parametrize("fname", sorted(cases.STREAM_FIXTURES))
+def test_fwpkm_streaming_matches_reference(cpu_kernels, fname):
+    """``forward_w_past`` over three calls carrying the signal queue (gates
+    and a loss mask queued too in the variant): outputs, losses, queues and
+    fast weights after every call equal the reference's."""
     from modelos_b200.fwpkm.fwpkm import FastWeightProductKeyMemory
     d = np.load(os.path.join(GOLD, fname))
-    m = FastWeightProductKeyMemory(qk_score_type=score_type, **FW_KW).train()
-    keys, values, q, ref_v = cases.fwpkm_case(1)
+    m = FastWeightProductKeyMemory(**dict(FW_KW, **cases.STREAM_FIXTURES[fname][0])).train()
+    keys, values, _, _ = cases.fwpkm_case(1)
+    q, ref_v, gates, mask = cases.stream_inputs(fname)
     with torch.no_grad():
         m.keys.copy_(keys)
         m.values.copy_(values)
-    cases.run_stream(m, q, ref_v, d, rel_err)
+    cases.run_stream(m, q, ref_v, d, rel_err, gates=gates, mask=mask)
 
 
 @pytest.mark.parametrize("fname", sorted(cases.FW_VARIANTS))
