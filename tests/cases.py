@@ -142,6 +142,11 @@ def embbag_case(B: int, L: int, K: int, D: int, seed: int = 0, heads: int = 1,
     return idx, psw, W, gout
 
 
+# The small FwPKM geometry of ``fwpkm_case`` (module options).
+FW_KW = dict(mem_k_dim=16, mem_v_dim=32, mem_heads=2, mem_topk=4, mem_n_subkeys=16, lookahead=1,
+             learning_rate=0.1)
+
+
 def fwpkm_case(seed: int = 0, B=2, T=16, heads=2, k_dim=16, v_dim=32, n_sub=16, topk=4):
     """Tiny FwPKM inputs: q [B,T,H*k_dim], ref_v [B,T,v_dim], keys, values."""
     g = torch.Generator().manual_seed(30_000 + seed)

@@ -193,8 +193,7 @@ def gen_embbag(xeb, gw, leg, name):
     print("wrote", name)
 
 
-FW_KW = dict(mem_k_dim=16, mem_v_dim=32, mem_heads=2, mem_topk=4, mem_n_subkeys=16,
-             lookahead=1, learning_rate=0.1)
+FW_KW = cases.FW_KW
 
 
 def gen_fwpkm(fw, name, score_type, seed=0):

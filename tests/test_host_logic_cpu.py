@@ -14,8 +14,7 @@ import cases
 import fake_native
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
-FW_KW = dict(mem_k_dim=16, mem_v_dim=32, mem_heads=2, mem_topk=4, mem_n_subkeys=16, lookahead=1,
-             learning_rate=0.1)
+FW_KW = cases.FW_KW
 
 
 def rel_err(a, b):
